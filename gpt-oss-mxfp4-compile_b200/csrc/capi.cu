@@ -1,0 +1,609 @@
+// extern "C" entry points of libgptoss_moe.so (declared in include/gptoss_moe.h).
+// Validation mirrors the reference's CHECK_* macros (kernels/matmul_mxfp4_cutlass.cu:
+// 1107-1116): every failure becomes a status code plus a thread-local message.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "gptoss_moe.h"
+#include "ptx.cuh"
+#include "numerics.cuh"
+#include "routing.cuh"
+#include "gemm.cuh"
+
+using namespace gptoss;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define GPTOSS_CUDA(call)                                                                    \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return fail(GPTOSS_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_),   \
+                  __FILE__, __LINE__);                                                       \
+  } while (0)
+
+#define GPTOSS_CHECK(cond, ...)                                                              \
+  do {                                                                                       \
+    if (!(cond)) return fail(GPTOSS_ERR_INVALID_ARGUMENT, __VA_ARGS__);                      \
+  } while (0)
+
+#define GPTOSS_TRY(expr)                                                                     \
+  do {                                                                                       \
+    int rc_ = (expr);                                                                        \
+    if (rc_ != GPTOSS_OK) return rc_;                                                        \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  int* status_sink = nullptr;
+};
+
+__device__ int g_status_sink[kMaxDevices];
+
+std::mutex g_dev_mu;
+DeviceInfo g_dev[kMaxDevices];
+bool g_dev_ready[kMaxDevices] = {};
+
+// Makes the device that owns `ptr` current for this runtime and returns its info.
+int bind_device(const void* ptr, const char* name, DeviceInfo* info) {
+  if (ptr == nullptr) return fail(GPTOSS_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  cudaPointerAttributes at{};
+  cudaError_t e = cudaPointerGetAttributes(&at, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(GPTOSS_ERR_INVALID_ARGUMENT, "%s: not a CUDA pointer (%s)", name, cudaGetErrorString(e));
+  }
+  if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)
+    return fail(GPTOSS_ERR_INVALID_ARGUMENT, "%s: must be a CUDA tensor", name);
+  const int dev = at.device;
+  if (dev < 0 || dev >= kMaxDevices) return fail(GPTOSS_ERR_INVALID_ARGUMENT, "%s: bad device %d", name, dev);
+  int cur = -1;
+  GPTOSS_CUDA(cudaGetDevice(&cur));
+  if (cur != dev) GPTOSS_CUDA(cudaSetDevice(dev));
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_dev_ready[dev]) {
+    cudaDeviceProp prop{};
+    GPTOSS_CUDA(cudaGetDeviceProperties(&prop, dev));
+    g_dev[dev].sms = prop.multiProcessorCount;
+    g_dev[dev].major = prop.major;
+    g_dev[dev].minor = prop.minor;
+    void* sink = nullptr;
+    GPTOSS_CUDA(cudaGetSymbolAddress(&sink, g_status_sink));
+    g_dev[dev].status_sink = static_cast<int*>(sink) + dev;
+    g_dev_ready[dev] = true;
+  }
+  *info = g_dev[dev];
+  if (info->major != 10)
+    return fail(GPTOSS_ERR_UNSUPPORTED_DEVICE,
+                "requires an sm_100 (B200-class) GPU, device %d is sm_%d%d", dev, info->major, info->minor);
+  return GPTOSS_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int64_t pad128(int64_t k) { return (k + 127) / 128 * 128; }
+
+// ---------------------------------------------------------------- TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (fn == nullptr) return fail(GPTOSS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(err));
+  *out = fn;
+  return GPTOSS_OK;
+}
+
+// Activations: 2-D [rows, lda] bytes (e4m3), box [box_rows, 128], 128B swizzle.
+int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t lda, int box_rows) {
+  EncodeTiledFn enc;
+  GPTOSS_TRY(get_encode_fn(&enc));
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(lda), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(lda)};
+  cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GPTOSS_ERR_CUDA, "cuTensorMapEncodeTiled(activations) failed: %d", (int)r);
+  return GPTOSS_OK;
+}
+
+// Weights: 3-D [E, N, K] packed E2M1 (K/2 bytes per row); the TMA unit expands each
+// 8-byte group of 16 codes into a 16-byte slot (the 8-bit container kind::mxf8f6f4 reads).
+int make_wgt_map(CUtensorMap* m, const void* base, int E, int64_t N, int64_t K, int box_rows) {
+  EncodeTiledFn enc;
+  GPTOSS_TRY(get_encode_fn(&enc));
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(E)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(N * (K / 2))};
+  cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_rows), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GPTOSS_ERR_CUDA, "cuTensorMapEncodeTiled(weights) failed: %d", (int)r);
+  return GPTOSS_OK;
+}
+
+// ---------------------------------------------------------------- GEMM launch
+struct GemmJob {
+  const uint8_t* act;   // [act_rows, lda] e4m3
+  int64_t act_rows;
+  int64_t lda;
+  const uint8_t* wgt;   // [E, N, K/2]
+  GemmParams p;
+};
+
+template <bool SWAP, int EPI>
+int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t st) {
+  using C = GemmConfig<SWAP>;
+  if (job.act_rows <= 0) return GPTOSS_OK;
+  CUtensorMap ta, tw;
+  GPTOSS_TRY(make_act_map(&ta, job.act, job.act_rows, job.lda, C::kActRows));
+  GPTOSS_TRY(make_wgt_map(&tw, job.wgt, job.p.num_experts, job.p.N, job.p.K, C::kWgtRows));
+  static uint64_t attr_done = 0;   // one bit per device
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_done & (1ull << dev))) {
+      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(C::kSmemBytes)));
+      attr_done |= (1ull << dev);
+    }
+  }
+  GemmParams p = job.p;
+  p.n_tiles = static_cast<int>((p.N + C::kWgtRows - 1) / C::kWgtRows);
+  const int64_t tiles_ub = (job.act_rows / C::kActRows + p.num_experts) * static_cast<int64_t>(p.n_tiles);
+  const int grid = static_cast<int>(std::min<int64_t>(di.sms, tiles_ub));
+  if (grid <= 0) return GPTOSS_OK;
+  moe_gemm_kernel<SWAP, EPI><<<grid, C::kThreads, C::kSmemBytes, st>>>(ta, tw, p);
+  GPTOSS_CUDA(cudaGetLastError());
+  return GPTOSS_OK;
+}
+
+template <int EPI>
+int run_gemm(const GemmJob& job, int mode, const DeviceInfo& di, int dev, cudaStream_t st) {
+  bool swap;
+  if (mode == GPTOSS_GEMM_SWAP) swap = true;
+  else if (mode == GPTOSS_GEMM_TOKENS_M) swap = false;
+  else swap = job.act_rows <= 48LL * job.p.num_experts;
+  return swap ? launch_gemm<true, EPI>(job, di, dev, st) : launch_gemm<false, EPI>(job, di, dev, st);
+}
+
+// ---------------------------------------------------------------- workspace layout
+struct Workspace {
+  size_t sorted_token, sorted_expert, sorted_weight, counts, offsets, sfoff_a, sfoff_b;
+  size_t act_codes, act_sf, inter_codes, inter_sf, router_idx, router_w, total;
+  int64_t act_sf_cap, inter_sf_cap;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+Workspace plan_workspace(int64_t T, int k, int E, int64_t H, int64_t I) {
+  Workspace w{};
+  const int64_t A = T * k;
+  const int64_t blocks = (A + 127) / 128 + E;   // upper bound of sum_e ceil(m_e / 128)
+  w.act_sf_cap = blocks * (pad128(H) / 128) * 512;
+  w.inter_sf_cap = blocks * (pad128(I) / 128) * 512;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t r = o; o = align256(o + bytes); return r; };
+  w.sorted_token = take(sizeof(int64_t) * A);
+  w.sorted_expert = take(sizeof(int64_t) * A);
+  w.sorted_weight = take(sizeof(float) * A);
+  w.counts = take(sizeof(int32_t) * E);
+  w.offsets = take(sizeof(int32_t) * E);
+  w.sfoff_a = take(sizeof(int32_t) * E);
+  w.sfoff_b = take(sizeof(int32_t) * E);
+  w.act_codes = take(static_cast<size_t>(A * H));
+  w.act_sf = take(static_cast<size_t>(w.act_sf_cap));
+  w.inter_codes = take(static_cast<size_t>(A * I));
+  w.inter_sf = take(static_cast<size_t>(w.inter_sf_cap));
+  w.router_idx = take(sizeof(int64_t) * A);
+  w.router_w = take(sizeof(float) * A);
+  w.total = o;
+  return w;
+}
+
+int router_launch(const void* hidden, const void* weight, const void* bias, int64_t T, int64_t H, int E,
+                  int k, int64_t* idx, void* scores, float* wf32, void* logits, void* zero_rows,
+                  int64_t zero_elems, cudaStream_t st) {
+  int tb = T <= 256 ? 1 : (T <= 4096 ? 4 : 16);
+  const size_t smem = sizeof(__nv_bfloat16) * tb * H + sizeof(float) * tb * E;
+  GPTOSS_CHECK(smem <= 200 * 1024, "router: hidden size %lld too large", (long long)H);
+  const int grid = static_cast<int>((T + tb - 1) / tb);
+  auto go = [&](auto kern) -> int {
+    GPTOSS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    kern<<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(weight),
+                                  static_cast<const __nv_bfloat16*>(bias), static_cast<int>(T), static_cast<int>(H), E, k,
+                                  idx, static_cast<__nv_bfloat16*>(scores), wf32, static_cast<__nv_bfloat16*>(logits),
+                                  static_cast<__nv_bfloat16*>(zero_rows), zero_elems);
+    GPTOSS_CUDA(cudaGetLastError());
+    return GPTOSS_OK;
+  };
+  if (tb == 1) return go(router_topk_kernel<1>);
+  if (tb == 4) return go(router_topk_kernel<4>);
+  return go(router_topk_kernel<16>);
+}
+
+struct ExpertWeights {
+  const uint8_t* gu_data; const uint8_t* gu_scales; int64_t ldb_gu; const float* gu_bias;
+  const uint8_t* dn_data; const uint8_t* dn_scales; int64_t ldb_dn; const float* dn_bias;
+};
+
+int check_expert_weights(const ExpertWeights& w, int64_t H, int64_t I, int E) {
+  GPTOSS_CHECK(w.gu_data && w.gu_scales && w.gu_bias && w.dn_data && w.dn_scales && w.dn_bias,
+               "expert weights: null pointer");
+  GPTOSS_CHECK(aligned(w.gu_data, 32) && aligned(w.dn_data, 32), "weight data must be 32-byte aligned");
+  GPTOSS_CHECK(aligned(w.gu_scales, 16) && aligned(w.dn_scales, 16), "weight scales must be 16-byte aligned");
+  GPTOSS_CHECK(w.ldb_gu % 16 == 0 && w.ldb_dn % 16 == 0, "weight scale strides must be multiples of 16");
+  GPTOSS_CHECK(w.ldb_gu >= blocked_sf_cosize(2 * I, static_cast<int>(pad128(H) / 32)),
+               "gate_up scales: %lld bytes per expert, need %lld", (long long)w.ldb_gu,
+               (long long)blocked_sf_cosize(2 * I, static_cast<int>(pad128(H) / 32)));
+  GPTOSS_CHECK(w.ldb_dn >= blocked_sf_cosize(H, static_cast<int>(pad128(I) / 32)),
+               "down scales: %lld bytes per expert, need %lld", (long long)w.ldb_dn,
+               (long long)blocked_sf_cosize(H, static_cast<int>(pad128(I) / 32)));
+  (void)E;
+  return GPTOSS_OK;
+}
+
+// route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch.
+int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E,
+                     int64_t H, int64_t I, const ExpertWeights& w, float sw_alpha, float sw_limit, void* out,
+                     uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
+                     cudaStream_t st, bool out_zeroed) {
+  const int64_t A = T * k;
+  const int64_t Kh = pad128(H), Ki = pad128(I);
+  auto* sorted_token = reinterpret_cast<int64_t*>(ws + L.sorted_token);
+  auto* sorted_expert = reinterpret_cast<int64_t*>(ws + L.sorted_expert);
+  auto* sorted_weight = reinterpret_cast<float*>(ws + L.sorted_weight);
+  auto* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+  auto* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  auto* sfoff_a = reinterpret_cast<int32_t*>(ws + L.sfoff_a);
+  auto* sfoff_b = reinterpret_cast<int32_t*>(ws + L.sfoff_b);
+  uint8_t* act_codes = ws + L.act_codes;
+  uint8_t* act_sf = ws + L.act_sf;
+  uint8_t* inter_codes = ws + L.inter_codes;
+  uint8_t* inter_sf = ws + L.inter_sf;
+
+  RouteSortParams rp{};
+  rp.router_indices = ridx; rp.routing_weights = rw;
+  rp.A = static_cast<int>(A); rp.K = k; rp.E = E;
+  rp.sorted_token = sorted_token; rp.sorted_expert = sorted_expert; rp.sorted_weight = sorted_weight;
+  rp.counts = counts; rp.offsets = offsets;
+  rp.sf_offsets_a = sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = static_cast<int>(H / 32); rp.sf_a = act_sf;
+  rp.sf_offsets_b = sfoff_b; rp.g4_b = static_cast<int>(Ki / 128); rp.groups_b = static_cast<int>(I / 32); rp.sf_b = inter_sf;
+  rp.err = status;
+  route_sort_kernel<<<E, 1024, 0, st>>>(rp);
+  GPTOSS_CUDA(cudaGetLastError());
+
+  const int qblocks = static_cast<int>((A + 7) / 8);
+  gather_quant_kernel<__nv_bfloat16><<<qblocks, 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(hidden), A, static_cast<int>(H), sorted_token, sorted_expert, offsets,
+      sfoff_a, static_cast<int>(Kh / 128), act_codes, act_sf, nullptr);
+  GPTOSS_CUDA(cudaGetLastError());
+  if (!out_zeroed) GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
+
+  GemmJob g1{};
+  g1.act = act_codes; g1.act_rows = A; g1.lda = H; g1.wgt = w.gu_data;
+  g1.p.num_experts = E; g1.p.N = static_cast<int>(2 * I); g1.p.K = static_cast<int>(Kh); g1.p.num_kb = static_cast<int>(Kh / 128);
+  g1.p.m_sizes = counts; g1.p.m_stride = 1; g1.p.row_offsets = offsets; g1.p.sfa_offsets = sfoff_a;
+  g1.p.sfa = act_sf; g1.p.sfb = w.gu_scales; g1.p.sfb_stride = w.ldb_gu; g1.p.err = status;
+  g1.p.out = inter_codes; g1.p.ld_out = I; g1.p.bias = w.gu_bias; g1.p.out_sf = inter_sf;
+  g1.p.out_sf_offsets = sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
+  g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
+  GPTOSS_TRY(run_gemm<kEpiGemm1>(g1, mode, di, dev, st));
+
+  GemmJob g2{};
+  g2.act = inter_codes; g2.act_rows = A; g2.lda = I; g2.wgt = w.dn_data;
+  g2.p.num_experts = E; g2.p.N = static_cast<int>(H); g2.p.K = static_cast<int>(Ki); g2.p.num_kb = static_cast<int>(Ki / 128);
+  g2.p.m_sizes = counts; g2.p.m_stride = 1; g2.p.row_offsets = offsets; g2.p.sfa_offsets = sfoff_b;
+  g2.p.sfa = inter_sf; g2.p.sfb = w.dn_scales; g2.p.sfb_stride = w.ldb_dn; g2.p.err = status;
+  g2.p.out = out; g2.p.ld_out = H; g2.p.bias = w.dn_bias; g2.p.token_idx = sorted_token; g2.p.row_weights = sorted_weight;
+  GPTOSS_TRY(run_gemm<kEpiGemm2>(g2, mode, di, dev, st));
+  return GPTOSS_OK;
+}
+
+int check_dims(int64_t T, int k, int E, int64_t H, int64_t I) {
+  GPTOSS_CHECK(T >= 0, "num_tokens must be >= 0");
+  GPTOSS_CHECK(k >= 1 && k <= kMaxTopK, "top_k must be in [1, %d]", kMaxTopK);
+  GPTOSS_CHECK(E >= 1 && E <= kMaxExperts, "num_experts must be in [1, %d]", kMaxExperts);
+  GPTOSS_CHECK(k <= E, "top_k > num_experts");
+  GPTOSS_CHECK(H > 0 && H % 32 == 0 && I > 0 && I % 32 == 0, "hidden/intermediate sizes must be multiples of 32");
+  GPTOSS_CHECK(T * k < (1LL << 31), "too many assignments");
+  return GPTOSS_OK;
+}
+
+}  // namespace
+
+// ======================================================================= C ABI
+extern "C" {
+
+const char* gptoss_last_error(void) { return g_last_error.c_str(); }
+
+int gptoss_abi_version(void) { return 1; }
+
+int gptoss_read_status(int32_t* status_dev, int32_t* status_host, void* stream) {
+  GPTOSS_CHECK(status_host != nullptr, "status_host is null");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(status_dev, "status", &di));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GPTOSS_CUDA(cudaMemcpyAsync(status_host, status_dev, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  GPTOSS_CUDA(cudaMemsetAsync(status_dev, 0, sizeof(int32_t), st));
+  GPTOSS_CUDA(cudaStreamSynchronize(st));
+  return GPTOSS_OK;
+}
+
+int gptoss_fused_moe_routing(const int64_t* router_indices, const float* routing_weights, int64_t num_tokens,
+                             int top_k, int num_experts, int64_t* sorted_token_idx, int64_t* sorted_expert_idx,
+                             float* sorted_weights, int32_t* expert_counts, int32_t* expert_offsets,
+                             int32_t* status_dev, void* stream) {
+  GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && num_experts >= 1 && num_experts <= kMaxExperts,
+               "fused_moe_routing: bad sizes (T=%lld k=%d E=%d)", (long long)num_tokens, top_k, num_experts);
+  GPTOSS_CHECK(num_tokens * top_k < (1LL << 31), "fused_moe_routing: too many assignments");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(expert_counts, "expert_counts", &di));
+  GPTOSS_CHECK(expert_offsets != nullptr, "expert_offsets is null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t A = num_tokens * top_k;
+  if (A > 0) {
+    GPTOSS_CHECK(router_indices && routing_weights && sorted_token_idx && sorted_expert_idx && sorted_weights,
+                 "fused_moe_routing: null pointer");
+  }
+  RouteSortParams rp{};
+  rp.router_indices = router_indices; rp.routing_weights = routing_weights;
+  rp.A = static_cast<int>(A); rp.K = top_k; rp.E = num_experts;
+  rp.sorted_token = sorted_token_idx; rp.sorted_expert = sorted_expert_idx; rp.sorted_weight = sorted_weights;
+  rp.counts = expert_counts; rp.offsets = expert_offsets;
+  rp.err = status_dev ? status_dev : di.status_sink;
+  route_sort_kernel<<<num_experts, 1024, 0, st>>>(rp);
+  GPTOSS_CUDA(cudaGetLastError());
+  return GPTOSS_OK;
+}
+
+int gptoss_router_topk(const void* hidden, const void* weight, const void* bias, int64_t num_tokens,
+                       int64_t hidden_size, int num_experts, int top_k, int64_t* router_indices, void* router_scores,
+                       float* routing_weights_f32, void* logits, void* stream) {
+  GPTOSS_CHECK(num_tokens >= 0, "router: num_tokens < 0");
+  GPTOSS_CHECK(hidden_size > 0 && hidden_size % 8 == 0, "router: hidden_size must be a positive multiple of 8");
+  GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExperts, "router: num_experts must be in [1, %d]", kMaxExperts);
+  GPTOSS_CHECK(top_k >= 1 && top_k <= kMaxTopK && top_k <= num_experts, "router: bad top_k %d", top_k);
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(weight, "router weight", &di));
+  GPTOSS_CHECK(bias != nullptr && router_indices != nullptr, "router: null pointer");
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(hidden != nullptr && aligned(hidden, 16) && aligned(weight, 16), "router: inputs must be 16-byte aligned");
+  return router_launch(hidden, weight, bias, num_tokens, hidden_size, num_experts, top_k, router_indices,
+                       router_scores, routing_weights_f32, logits, nullptr, 0, static_cast<cudaStream_t>(stream));
+}
+
+int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, uint8_t* codes, uint8_t* scales,
+                        void* stream) {
+  GPTOSS_CHECK(rows >= 0 && cols > 0 && cols % 32 == 0, "quantize: K=%lld must be a positive multiple of 32",
+               (long long)cols);
+  GPTOSS_CHECK(dtype == GPTOSS_DTYPE_BF16 || dtype == GPTOSS_DTYPE_F32, "quantize: dtype must be bf16 or f32");
+  if (rows == 0) return GPTOSS_OK;
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(x, "x", &di));
+  GPTOSS_CHECK(codes && scales && aligned(x, 16) && aligned(codes, 16), "quantize: null or misaligned pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int blocks = static_cast<int>((rows + 7) / 8);
+  if (dtype == GPTOSS_DTYPE_BF16)
+    gather_quant_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows,
+                                                                static_cast<int>(cols), nullptr, nullptr, nullptr,
+                                                                nullptr, 0, codes, nullptr, scales);
+  else
+    gather_quant_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), rows, static_cast<int>(cols),
+                                                        nullptr, nullptr, nullptr, nullptr, 0, codes, nullptr, scales);
+  GPTOSS_CUDA(cudaGetLastError());
+  return GPTOSS_OK;
+}
+
+int gptoss_swiglu(const void* x, int dtype, int64_t rows, int64_t cols, void* out, float alpha, float limit,
+                  void* stream) {
+  GPTOSS_CHECK(rows >= 0 && cols > 0 && cols % 2 == 0, "swiglu: last dimension must be even");
+  GPTOSS_CHECK(dtype == GPTOSS_DTYPE_BF16 || dtype == GPTOSS_DTYPE_F32, "swiglu: dtype must be bf16 or f32");
+  if (rows == 0) return GPTOSS_OK;
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(x, "x", &di));
+  GPTOSS_CHECK(out != nullptr, "swiglu: null output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n = cols / 2;
+  const int blocks = static_cast<int>(std::min<int64_t>((rows * n + 255) / 256, 8192));
+  if (dtype == GPTOSS_DTYPE_F32)
+    swiglu_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), rows, n, static_cast<float*>(out),
+                                                 alpha, limit);
+  else
+    swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, n,
+                                                         static_cast<__nv_bfloat16*>(out), alpha, limit);
+  GPTOSS_CUDA(cudaGetLastError());
+  return GPTOSS_OK;
+}
+
+int64_t gptoss_blocked_scales_bytes(int64_t rows, int64_t k) {
+  if (rows < 0 || k <= 0) return -1;
+  return blocked_sf_cosize(rows, static_cast<int>(k / 32));
+}
+
+int gptoss_convert_scales_blocked(const uint8_t* scales_rowmajor, int64_t rows, int64_t k, uint8_t* blocked,
+                                  int64_t blocked_bytes, void* stream) {
+  GPTOSS_CHECK(rows >= 0 && k > 0 && k % 32 == 0, "convert_scales: K=%lld must be a multiple of 32", (long long)k);
+  const int G = static_cast<int>(k / 32);
+  const int64_t need = blocked_sf_cosize(rows, G);
+  GPTOSS_CHECK(blocked_bytes >= need, "convert_scales: output holds %lld bytes, need %lld", (long long)blocked_bytes,
+               (long long)need);
+  if (need == 0) return GPTOSS_OK;
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(blocked, "blocked", &di));
+  GPTOSS_CHECK(scales_rowmajor != nullptr, "convert_scales: null input");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int g4 = (G + 3) / 4;
+  const int64_t total = ((rows + 127) / 128 * 128) * g4 * 4;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  convert_scales_kernel<<<blocks, 256, 0, st>>>(scales_rowmajor, rows, G, g4, blocked);
+  GPTOSS_CUDA(cudaGetLastError());
+  return GPTOSS_OK;
+}
+
+int64_t gptoss_batch_blocked_scales_capacity(int64_t total_rows, int num_experts, int64_t k) {
+  if (total_rows < 0 || num_experts < 1 || k <= 0) return -1;
+  return ((total_rows + 127) / 128 + num_experts) * ((k / 32 + 3) / 4) * 512;
+}
+
+int gptoss_batch_convert_a_scales(const uint8_t* scales_rowmajor, const int32_t* expert_counts,
+                                  const int32_t* expert_offsets, int num_experts, int64_t k, uint8_t* blocked,
+                                  int64_t capacity, int32_t* sf_offsets, void* stream) {
+  GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExperts, "batch_convert: bad num_experts");
+  GPTOSS_CHECK(k > 0 && k % 32 == 0, "batch_convert: K must be a multiple of 32");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(sf_offsets, "sf_offsets", &di));
+  GPTOSS_CHECK(expert_counts && expert_offsets && blocked && capacity >= 0, "batch_convert: null pointer");
+  const int G = static_cast<int>(k / 32);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  batch_convert_scales_kernel<<<num_experts, 256, 0, st>>>(scales_rowmajor, expert_counts, expert_offsets, num_experts,
+                                                           G, (G + 3) / 4, blocked, sf_offsets);
+  GPTOSS_CUDA(cudaGetLastError());
+  return GPTOSS_OK;
+}
+
+int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t lda, const uint8_t* b, int num_experts,
+                        int64_t n, int64_t k, const uint8_t* a_blockscale, const uint8_t* b_blockscales,
+                        int64_t ldb_blockscale, const float* alphas, const int32_t* problem_sizes,
+                        const int32_t* expert_offsets, const int32_t* sf_offsets, int gemm_mode, int32_t* status_dev,
+                        void* stream) {
+  GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExpertsGemm, "fp4_group_mm: num_experts must be in [1, %d]",
+               kMaxExpertsGemm);
+  GPTOSS_CHECK(k > 0 && k % 128 == 0, "fp4_group_mm: K=%lld must be a multiple of 128 (pad with pad_k_to_tile)",
+               (long long)k);
+  GPTOSS_CHECK(n > 0 && n % 8 == 0 && n < (1LL << 31), "fp4_group_mm: N=%lld must be a positive multiple of 8",
+               (long long)n);
+  GPTOSS_CHECK(m_total >= 0 && lda > 0 && lda <= k && lda % 16 == 0, "fp4_group_mm: a must be [M, lda<=K], lda %% 16 == 0");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "fp4_group_mm: bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(b, "b", &di));
+  GPTOSS_CHECK(aligned(b, 32), "fp4_group_mm: b must be 32-byte aligned");
+  GPTOSS_CHECK(ldb_blockscale >= blocked_sf_cosize(n, static_cast<int>(k / 32)) && ldb_blockscale % 16 == 0,
+               "fp4_group_mm: b_blockscales holds %lld bytes per expert, need %lld (multiple of 16)",
+               (long long)ldb_blockscale, (long long)blocked_sf_cosize(n, static_cast<int>(k / 32)));
+  GPTOSS_CHECK(problem_sizes && expert_offsets && sf_offsets && b_blockscales, "fp4_group_mm: null pointer");
+  if (m_total == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(a && out && a_blockscale && aligned(a, 16) && aligned(out, 16) && aligned(a_blockscale, 16) &&
+                   aligned(b_blockscales, 16),
+               "fp4_group_mm: null or misaligned pointer");
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  GemmJob job{};
+  job.act = a; job.act_rows = m_total; job.lda = lda; job.wgt = b;
+  job.p.num_experts = num_experts; job.p.N = static_cast<int>(n); job.p.K = static_cast<int>(k);
+  job.p.num_kb = static_cast<int>(k / 128); job.p.m_sizes = problem_sizes; job.p.m_stride = 3;
+  job.p.row_offsets = expert_offsets; job.p.sfa_offsets = sf_offsets; job.p.sfa = a_blockscale;
+  job.p.sfb = b_blockscales; job.p.sfb_stride = ldb_blockscale;
+  job.p.err = status_dev ? status_dev : di.status_sink;
+  job.p.out = out; job.p.ld_out = n; job.p.alphas = alphas;
+  return run_gemm<kEpiPlain>(job, gemm_mode, di, dev, static_cast<cudaStream_t>(stream));
+}
+
+size_t gptoss_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                                  int64_t intermediate_size) {
+  if (num_tokens < 0 || top_k < 1 || num_experts < 1 || hidden_size <= 0 || intermediate_size <= 0) return 0;
+  return plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size).total;
+}
+
+int gptoss_moe_experts_forward(const void* hidden, const int64_t* router_indices, const float* routing_weights,
+                               int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                               int64_t intermediate_size, const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                               int64_t ldb_gate_up, const float* gate_up_bias, const uint8_t* down_data,
+                               const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                               float swiglu_alpha, float swiglu_limit, void* out, void* workspace,
+                               size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                  down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(w, hidden_size, intermediate_size, num_experts));
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(hidden && router_indices && routing_weights && out && workspace, "experts_forward: null pointer");
+  GPTOSS_CHECK(aligned(hidden, 16) && aligned(out, 16) && aligned(workspace, 256), "experts_forward: misaligned pointer");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total)
+    return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  return experts_pipeline(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
+                          intermediate_size, w, swiglu_alpha, swiglu_limit, out, static_cast<uint8_t*>(workspace), L,
+                          gemm_mode, status_dev ? status_dev : di.status_sink, di, dev,
+                          static_cast<cudaStream_t>(stream), false);
+}
+
+int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, const void* router_bias,
+                             int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                             int64_t intermediate_size, const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                             int64_t ldb_gate_up, const float* gate_up_bias, const uint8_t* down_data,
+                             const uint8_t* down_scales, int64_t ldb_down, const float* down_bias, float swiglu_alpha,
+                             float swiglu_limit, void* out, int64_t* router_indices_out, void* router_scores_out,
+                             void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
+                             void* stream) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(hidden_size % 8 == 0, "hidden size must be a multiple of 8");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                  down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(w, hidden_size, intermediate_size, num_experts));
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(hidden && router_weight && router_bias && out && workspace, "layer_forward: null pointer");
+  GPTOSS_CHECK(aligned(hidden, 16) && aligned(router_weight, 16) && aligned(out, 16) && aligned(workspace, 256),
+               "layer_forward: misaligned pointer");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total)
+    return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int64_t* ridx = router_indices_out ? router_indices_out : reinterpret_cast<int64_t*>(ws + L.router_idx);
+  float* rw = reinterpret_cast<float*>(ws + L.router_w);
+  GPTOSS_TRY(router_launch(hidden, router_weight, router_bias, num_tokens, hidden_size, num_experts, top_k, ridx,
+                           router_scores_out, rw, nullptr, out, hidden_size, st));
+  return experts_pipeline(hidden, ridx, rw, num_tokens, top_k, num_experts, hidden_size, intermediate_size, w,
+                          swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode, status_dev ? status_dev : di.status_sink,
+                          di, dev, st, true);
+}
+
+}  // extern "C"

@@ -1,0 +1,479 @@
+// Grouped W4A8 GEMM for sm_100a: FP8 e4m3 activations x E2M1 weights, UE8M0 1x32 block
+// scales, fp32 accumulation in TMEM via tcgen05.mma kind::mxf8f6f4.block_scale.
+//
+// One persistent CTA per SM walks a ragged tile list built on the device from the
+// per-expert row counts (no host sync). Warp roles (192 threads):
+//   warp 0     TMA producer: activation tile (2-D map, fp8), weight tile (3-D map,
+//              packed e2m1 expanded to the 8-bit smem container by the TMA unit),
+//              plus the 512-byte blocked scale chunks (plain bulk copies).
+//   warp 1     TMEM allocator + single-thread MMA issuer: tcgen05.cp of the scale chunks
+//              into TMEM, then 4 MMAs (K = 32 each) per 128-deep K block.
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator and one of three fused tails.
+//
+// Two orientations:
+//   SWAP = false  M = 128 activation rows, N = 192 weight rows (prefill-sized groups).
+//   SWAP = true   M = 128 weight rows,     N = 32 activation rows (decode: the weights
+//                 stream through the M side so a group of ~4 rows wastes little MMA).
+//
+// Epilogues (all restate cutlass_experts.py:414-450 for the rows a tile owns):
+//   kEpiPlain  D = bf16(alpha[e] * acc) stored row-major (the fp4_group_mm op,
+//              matmul_mxfp4_cutlass.cu:1118-1171 with beta = 0).
+//   kEpiGemm1  h = swiglu(float(bf16(acc)) + b_gu[e]) on (even, odd) column pairs,
+//              then FP8 + UE8M0 requantisation written as the next GEMM's A operand
+//              (codes compact row-major, scales in the blocked layout).
+//   kEpiGemm2  y = bf16((float(bf16(acc)) + b_dn[e]) * w_row) added into out[token]
+//              with bf16x2 vector reductions (the scatter_add_ of :445-450).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include "ptx.cuh"
+#include "numerics.cuh"
+
+namespace gptoss {
+
+enum EpilogueKind : int { kEpiPlain = 0, kEpiGemm1 = 1, kEpiGemm2 = 2 };
+
+struct GemmParams {
+  int num_experts;
+  int N;                        // weight rows (output features) per expert
+  int K;                        // padded reduction depth, multiple of 128
+  int num_kb;                   // K / 128
+  const int32_t* m_sizes;       // rows of expert e at m_sizes[e * m_stride]
+  int m_stride;
+  const int32_t* row_offsets;   // first activation / output row of each expert
+  const int32_t* sfa_offsets;   // byte offset of each expert's activation scales
+  const uint8_t* sfa;           // activation scales, blocked layout
+  const uint8_t* sfb;           // weight scales, blocked layout
+  int64_t sfb_stride;           // bytes between experts in sfb
+  int n_tiles;                  // ceil(N / weight rows per tile)
+  int* err;                     // device status word (0 = ok)
+  // epilogue
+  void* out;
+  int64_t ld_out;               // elements per output row
+  const float* alphas;          // kEpiPlain
+  const float* bias;            // [E, N] fp32 (kEpiGemm1, kEpiGemm2)
+  uint8_t* out_sf;              // kEpiGemm1: blocked scales of the intermediate
+  const int32_t* out_sf_offsets;
+  int out_g4;
+  int out_features;             // kEpiGemm1: intermediate width (N / 2)
+  const int64_t* token_idx;     // kEpiGemm2
+  const float* row_weights;     // kEpiGemm2
+  float swiglu_alpha, swiglu_limit;
+};
+
+template <bool SWAP>
+struct GemmConfig {
+  static constexpr int kWgtRows = SWAP ? 128 : 192;   // weight rows per tile
+  static constexpr int kActRows = SWAP ? 32 : 128;    // activation rows per tile
+  static constexpr int kMmaM = 128;
+  static constexpr int kMmaN = SWAP ? kActRows : kWgtRows;
+  static constexpr int kStages = SWAP ? 10 : 5;
+  static constexpr int kAccBufs = SWAP ? 4 : 2;
+  static constexpr int kAccCols = kMmaN;              // fp32 columns per accumulator
+  static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
+  static constexpr uint32_t kWgtTileBytes = kWgtRows * 128;   // 8-bit container in smem
+  static constexpr uint32_t kActTileBytes = kActRows * 128;
+  static constexpr uint32_t kSfActBytes = 512;
+  static constexpr uint32_t kSfWgtBytes = 512 * kWgtSfChunks;
+  static constexpr uint32_t kStageBytes =
+      ((kWgtTileBytes + kActTileBytes + kSfActBytes + kSfWgtBytes + 1023) / 1024) * 1024;
+  static constexpr uint32_t kTmemAccCols = kAccBufs * kAccCols;
+  static constexpr uint32_t kSfActCol = kTmemAccCols;           // 4 columns
+  static constexpr uint32_t kSfWgtCol = kTmemAccCols + 4;       // 4 per chunk
+  static constexpr uint32_t kTmemCols = (kSfWgtCol + 4 * kWgtSfChunks) <= 128 ? 128
+                                        : (kSfWgtCol + 4 * kWgtSfChunks) <= 256 ? 256 : 512;
+  static constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + 2 * kAccBufs + 1) + 16;
+  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 2048;
+  static constexpr int kThreads = 192;
+};
+
+constexpr int kMaxExpertsGemm = 256;
+
+template <bool SWAP, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,
+                    const __grid_constant__ CUtensorMap tm_wgt, const GemmParams p) {
+  using C = GemmConfig<SWAP>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ int s_chunk_prefix[kMaxExpertsGemm + 1];
+  __shared__ int s_chunks[kMaxExpertsGemm];
+  __shared__ uint32_t s_tmem_base;
+  __shared__ float s_amax[4][32];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t bar_base = smem_base + C::kStages * C::kStageBytes;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (C::kStages + s); };
+  auto accf_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + b); };
+  auto acce_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + C::kAccBufs + b); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * C::kStages + 2 * C::kAccBufs);
+
+  // ---- per-CTA tile map from the device-side counts
+  for (int i = threadIdx.x; i < p.num_experts; i += blockDim.x) {
+    const int m = p.m_sizes[i * p.m_stride];
+    s_chunks[i] = m > 0 ? (m + C::kActRows - 1) / C::kActRows : 0;
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_act);
+    tma_prefetch_desc(&tm_wgt);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < C::kAccBufs; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 4);
+    }
+    mbar_init(drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&s_tmem_base), C::kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < p.num_experts; ++e) { s_chunk_prefix[e] = acc; acc += s_chunks[e]; }
+    s_chunk_prefix[p.num_experts] = acc;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem_base;
+  const int total_tiles = s_chunk_prefix[p.num_experts] * p.n_tiles;
+
+  // tile t -> (expert, weight tile, activation chunk)
+  auto decode = [&](int t, int& e, int& nt, int& ch) {
+    const int cidx = t / p.n_tiles;           // global chunk-major index
+    int lo = 0, hi = p.num_experts - 1;
+    while (lo < hi) {                         // last e with prefix[e] <= cidx
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_chunk_prefix[mid] <= cidx) lo = mid; else hi = mid - 1;
+    }
+    e = lo;
+    const int local = t - s_chunk_prefix[e] * p.n_tiles;
+    const int nch = s_chunks[e];
+    nt = local / nch;
+    ch = local - nt * nch;
+  };
+
+  if (warp == 0) {
+    // ================================================================ producer
+    if (elect_one()) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int e, nt, ch;
+        decode(t, e, nt, ch);
+        const int act_row0 = p.row_offsets[e] + ch * C::kActRows;
+        const int wgt_row0 = nt * C::kWgtRows;
+        const int act_blk = (ch * C::kActRows) >> 7;
+        const uint8_t* sfa_src = p.sfa + p.sfa_offsets[e] + static_cast<int64_t>(act_blk) * p.num_kb * 512;
+        const int wblk0 = wgt_row0 >> 7;
+        const int nwblk_total = (p.N + 127) >> 7;
+        const int nwchunks = min(C::kWgtSfChunks, nwblk_total - wblk0);
+        const uint8_t* sfb_src = p.sfb + static_cast<int64_t>(e) * p.sfb_stride +
+                                 static_cast<int64_t>(wblk0) * p.num_kb * 512;
+        const uint32_t tx = C::kActTileBytes + C::kWgtRows * 64 + C::kSfActBytes + 512u * nwchunks;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.err, kDevTimeoutProducer)) { ok = false; break; }
+          const uint32_t sb = smem_base + stage * C::kStageBytes;
+          const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
+          const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
+          mbar_arrive_expect_tx(full_bar(stage), tx);
+          tma_load_2d(s_a, &tm_act, full_bar(stage), kb * 128, act_row0, pol_a);
+          tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
+          bulk_load(s_sfa, sfa_src + kb * 512, 512, full_bar(stage), pol_a);
+          for (int c = 0; c < nwchunks; ++c)
+            bulk_load(s_sfw + 512u * c, sfb_src + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512, 512,
+                      full_bar(stage), pol_w);
+          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: make sure no copy is still landing in shared memory before exit.
+      for (int s = 0; s < C::kStages; ++s) {
+        // Stage s last received the load of phase (phase if s < stage else phase ^ 1).
+        const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
+        (void)mbar_wait(full_bar(s), ph, p.err, kDevTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        int e, nt, ch;
+        decode(t, e, nt, ch);
+        const int b = local % C::kAccBufs;
+        const uint32_t acc_phase = static_cast<uint32_t>(local / C::kAccBufs) & 1u;
+        if (!mbar_wait(acce_bar(b), acc_phase ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * C::kAccCols;
+        // Column shift selecting the 32-row groups this tile starts at inside the
+        // copied 128-row scale blocks.
+        const uint32_t wshift = SWAP ? 0u : static_cast<uint32_t>(((nt * C::kWgtRows) & 127) >> 5);
+        const uint32_t ashift = SWAP ? static_cast<uint32_t>(((ch * C::kActRows) & 127) >> 5) : 0u;
+        const uint32_t t_sfa = tmem_base + C::kSfActCol;
+        const uint32_t t_sfw = tmem_base + C::kSfWgtCol;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, p.err, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sb = smem_base + stage * C::kStageBytes;
+          const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
+          const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
+          tc_cp_32x128b_warpx4(t_sfa, desc_sf_block(s_sfa));
+#pragma unroll
+          for (int c = 0; c < C::kWgtSfChunks; ++c)
+            tc_cp_32x128b_warpx4(t_sfw + 4u * c, desc_sf_block(s_sfw + 512u * c));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t da = desc_kmajor_sw128(s_a + 32u * k);
+            const uint64_t dw = desc_kmajor_sw128(s_w + 32u * k);
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (SWAP) {
+              // A = weights (E2M1), B = activations (E4M3)
+              mma_mxf8f6f4(d_tmem, dw, da, idesc_mxf8f6f4(5, 0, C::kMmaM, C::kMmaN, k, k),
+                           t_sfw, t_sfa + ashift, acc);
+            } else {
+              // A = activations (E4M3), B = weights (E2M1)
+              mma_mxf8f6f4(d_tmem, da, dw, idesc_mxf8f6f4(0, 5, C::kMmaM, C::kMmaN, k, k),
+                           t_sfa, t_sfw + wshift, acc);
+            }
+          }
+          tc_commit(empty_bar(stage));
+          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit(accf_bar(b));
+      }
+      // Wait for every tcgen05 operation this thread issued before TMEM is released.
+      tc_commit(drain_bar);
+      (void)mbar_wait(drain_bar, 0u, p.err, kDevTimeoutDrain);
+    }
+  } else {
+    // ================================================================ epilogue
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    int local = 0;
+    bool ok = true;   // after a timeout keep walking the tiles (named barriers stay
+                      // matched across the four warps) but touch no TMEM or memory
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      int e, nt, ch;
+      decode(t, e, nt, ch);
+      const int b = local % C::kAccBufs;
+      const uint32_t acc_phase = static_cast<uint32_t>(local / C::kAccBufs) & 1u;
+      if (ok) ok = mbar_wait(accf_bar(b), acc_phase, p.err, kDevTimeoutEpilogue);
+      if (!ok) {
+        if constexpr (SWAP && EPI == kEpiGemm1) {
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        continue;
+      }
+      tc_fence_after();
+      const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + b * C::kAccCols;
+      const int m_e = p.m_sizes[e * p.m_stride];
+      const int row0 = p.row_offsets[e];
+      if constexpr (!SWAP) {
+        // thread <-> activation row
+        const int r_in = ch * C::kActRows + 32 * q + lane;   // row inside the expert
+        const bool vrow = r_in < m_e;
+        const int64_t grow = static_cast<int64_t>(row0) + r_in;
+        const int n_tile0 = nt * C::kWgtRows;
+        if constexpr (EPI == kEpiGemm1) {
+#pragma unroll 1
+          for (int gi = 0; gi < C::kWgtRows / 64; ++gi) {
+            float h[32];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              uint32_t r[32];
+              __syncwarp();
+              tmem_ld_32x32b_x32(t_acc + (2 * gi + half) * 32, r);
+              tmem_ld_wait();
+              const int nb = n_tile0 + (2 * gi + half) * 32;
+              const float* bs = p.bias + static_cast<int64_t>(e) * p.N + nb;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const bool in = nb + 2 * j + 1 < p.N;
+                const float g = __fadd_rn(bf16_round(__uint_as_float(r[2 * j])), in ? bs[2 * j] : 0.0f);
+                const float u = __fadd_rn(bf16_round(__uint_as_float(r[2 * j + 1])), in ? bs[2 * j + 1] : 0.0f);
+                h[half * 16 + j] = swiglu_pair(g, u, p.swiglu_alpha, p.swiglu_limit);
+              }
+            }
+            const int f0 = (n_tile0 >> 1) + 32 * gi;   // first intermediate feature
+            if (vrow && f0 < p.out_features) {
+              uint32_t codes[8];
+              const uint8_t s = quantize_group32(h, codes);
+              uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + grow * p.ld_out + f0);
+              o[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+              o[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+              p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(r_in, f0 >> 5, p.out_g4)] = s;
+            }
+          }
+        } else {
+          float alpha = 1.0f, wrow = 0.0f;
+          int64_t tok = 0;
+          if constexpr (EPI == kEpiPlain) alpha = p.alphas ? p.alphas[e] : 1.0f;
+          if constexpr (EPI == kEpiGemm2) {
+            if (vrow) { tok = p.token_idx[grow]; wrow = p.row_weights[grow]; }
+          }
+#pragma unroll 1
+          for (int c = 0; c < C::kWgtRows / 32; ++c) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_acc + c * 32, r);
+            tmem_ld_wait();
+            const int nb = n_tile0 + c * 32;
+            if (vrow && nb < p.N) {
+            const bool full = nb + 32 <= p.N;
+            if constexpr (EPI == kEpiPlain) {
+              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + grow * p.ld_out + nb;
+              if (full) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const __nv_bfloat162 v2 = __floats2bfloat162_rn(__fmul_rn(alpha, __uint_as_float(r[2 * j])),
+                                                                  __fmul_rn(alpha, __uint_as_float(r[2 * j + 1])));
+                  pk[j] = *reinterpret_cast<const uint32_t*>(&v2);
+                }
+                uint4* o4 = reinterpret_cast<uint4*>(o);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+              } else {
+                for (int j = 0; j < 32 && nb + j < p.N; ++j)
+                  o[j] = __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
+              }
+            } else {  // kEpiGemm2
+              const float* bs = p.bias + static_cast<int64_t>(e) * p.N + nb;
+              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + tok * p.ld_out + nb;
+              uint32_t pk[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const bool in0 = nb + 2 * j < p.N, in1 = nb + 2 * j + 1 < p.N;
+                const float y0 = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[2 * j])), in0 ? bs[2 * j] : 0.f), wrow);
+                const float y1 = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[2 * j + 1])), in1 ? bs[2 * j + 1] : 0.f), wrow);
+                const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
+                pk[j] = *reinterpret_cast<const uint32_t*>(&v2);
+              }
+              if (full) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(o + 8 * j),
+                               "r"(pk[4 * j]), "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
+                               : "memory");
+              } else {
+                for (int j = 0; j < 16 && nb + 2 * j < p.N; ++j) {
+                  const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
+                  if (nb + 2 * j + 1 < p.N) {
+                    atomicAdd(reinterpret_cast<__nv_bfloat162*>(o + 2 * j), v2);
+                  } else {
+                    atomicAdd(o + 2 * j, v2.x);
+                  }
+                }
+              }
+            }
+            }  // vrow && nb < N
+          }
+        }
+      } else {
+        // thread <-> weight row (output feature); 32 columns = 32 activation rows
+        const int wrow_i = nt * C::kWgtRows + 32 * q + lane;    // weight row / feature
+        const bool vcol = wrow_i < p.N;
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(t_acc, r);
+        tmem_ld_wait();
+        const int a0 = ch * C::kActRows;                        // first row inside expert
+        if constexpr (EPI == kEpiPlain) {
+          const float alpha = p.alphas ? p.alphas[e] : 1.0f;
+          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (vcol && a0 + j < m_e)
+              o[(static_cast<int64_t>(row0) + a0 + j) * p.ld_out + wrow_i] =
+                  __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
+          }
+        } else if constexpr (EPI == kEpiGemm2) {
+          const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
+          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            const bool vr = a0 + j < m_e;                       // warp-uniform
+            if (!vr) break;
+            const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
+            const int64_t tok = p.token_idx[grow];
+            const float wr = p.row_weights[grow];
+            const float y = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[j])), bsv), wr);
+            const float yo = __shfl_xor_sync(0xffffffffu, y, 1);
+            if ((lane & 1) == 0 && vcol) {
+              __nv_bfloat16* dst = o + tok * p.ld_out + wrow_i;
+              if (wrow_i + 1 < p.N) atomicAdd(reinterpret_cast<__nv_bfloat162*>(dst), __floats2bfloat162_rn(y, yo));
+              else atomicAdd(dst, __float2bfloat16_rn(y));
+            }
+          }
+        } else {  // kEpiGemm1: lanes (2f, 2f+1) hold gate / up of feature f
+          const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
+          const int f = wrow_i >> 1;                            // intermediate feature
+          const int grp = f >> 5;                               // quant group (2 warps)
+          float hv[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float v = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
+            const float up = __shfl_xor_sync(0xffffffffu, v, 1);
+            hv[j] = swiglu_pair(v, up, p.swiglu_alpha, p.swiglu_limit);   // valid on even lanes
+          }
+          // group absmax over the 32 features held by the even lanes of warps (q, q^1)
+#pragma unroll 1
+          for (int j = 0; j < 32; ++j) {
+            float a = (lane & 1) == 0 ? fabsf(hv[j]) : 0.0f;
+            if (hv[j] != hv[j] && (lane & 1) == 0) a = hv[j];
+#pragma unroll
+            for (int o2 = 2; o2 < 32; o2 <<= 1) {
+              const float ob = __shfl_xor_sync(0xffffffffu, a, o2);
+              a = (ob > a || ob != ob) ? ob : a;
+            }
+            if (lane == 0) s_amax[q][j] = a;
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int qp = q ^ 1;
+          uint8_t* codes_out = static_cast<uint8_t*>(p.out);
+#pragma unroll 1
+          for (int j = 0; j < 32; ++j) {
+            if (a0 + j >= m_e) break;
+            const float a_self = s_amax[q][j], a_pair = s_amax[qp][j];
+            const float amax = (a_pair > a_self || a_pair != a_pair) ? a_pair : a_self;
+            const uint32_t rb = ue8m0_rounded_bits(amax);
+            const float scale = scale_from_bits(rb);
+            const float qv = clamp_fp8(__fdiv_rn(hv[j], scale));
+            const uint16_t c2 = cvt_e4m3x2(qv, 0.0f);
+            const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
+            if ((lane & 1) == 0 && vcol && f < p.out_features)
+              codes_out[grow * p.ld_out + f] = static_cast<uint8_t>(c2 & 0xFFu);
+            if (lane == 0 && (q & 1) == 0 && f < p.out_features)
+              p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(a0 + j, grp, p.out_g4)] =
+                  static_cast<uint8_t>((rb >> 23) & 0xFFu);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(b));
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace gptoss

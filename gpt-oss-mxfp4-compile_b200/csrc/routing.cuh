@@ -1,0 +1,357 @@
+// Routing kernels of the MoE expert path.
+//
+//  router_topk_kernel   logits = x W^T + b (bf16 out, fp32 accumulate), top-k, softmax
+//                       over the k selected logits; HF GptOssTopKRouter semantics
+//                       (F.linear -> torch.topk -> softmax(dtype=bf16)).
+//  route_sort_kernel    one CTA per expert: histogram of all assignments, exclusive
+//                       offsets, then a stable compaction of this expert's assignments
+//                       in (token, k) order. Replaces the reference's atomic-slot
+//                       counting sort (kernels/matmul_mxfp4_cutlass.cu:1010-1095); the
+//                       result equals torch.argsort(stable=True), the order
+//                       benchmark_optimizations.py:170-187 uses.
+//  gather_quant_kernel  hidden[sorted_token] -> FP8 rows + UE8M0 scales written straight
+//                       into the blocked layout the MMA reads
+//                       (cutlass_experts.py:405-408 + matmul_mxfp4_cutlass.cu:881-908).
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include "ptx.cuh"
+#include "numerics.cuh"
+
+namespace gptoss {
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 8;
+
+// ----------------------------------------------------------------------------------
+// Router: each CTA owns TB tokens; their rows are staged in shared memory, each warp
+// walks a subset of experts and every lane accumulates an 8-wide strided slice of the
+// dot product in a fixed order (deterministic), followed by a fixed-order warp tree.
+template <int TB>
+__global__ void __launch_bounds__(256) router_topk_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const __nv_bfloat16* __restrict__ bias, int T, int H, int E, int K,
+    int64_t* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_scores,
+    float* __restrict__ out_weights_f32, __nv_bfloat16* __restrict__ out_logits,
+    __nv_bfloat16* __restrict__ zero_rows, int64_t zero_row_elems) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);      // [TB][H]
+  float* logits = reinterpret_cast<float*>(smem_raw + sizeof(__nv_bfloat16) * TB * H);  // [TB][E]
+
+  const int t0 = blockIdx.x * TB;
+  const int ntok = min(TB, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Stage the token rows (H multiple of 8 is checked on the host).
+  const int vec_per_row = H >> 3;
+  for (int i = threadIdx.x; i < ntok * vec_per_row; i += blockDim.x) {
+    const int t = i / vec_per_row, v = i - t * vec_per_row;
+    reinterpret_cast<uint4*>(xs + t * H)[v] =
+        reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + t) * H)[v];
+  }
+  // Optionally zero the output rows of these tokens (the combine adds into them).
+  if (zero_rows != nullptr) {
+    const int64_t vz = zero_row_elems >> 3;
+    uint4 z = make_uint4(0, 0, 0, 0);
+    for (int64_t i = threadIdx.x; i < ntok * vz; i += blockDim.x)
+      reinterpret_cast<uint4*>(zero_rows + static_cast<int64_t>(t0) * zero_row_elems)[i] = z;
+  }
+  __syncthreads();
+
+  for (int e = warp; e < E; e += blockDim.x >> 5) {
+    float acc[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
+    const __nv_bfloat16* wr = w + static_cast<int64_t>(e) * H;
+    for (int v = lane; v < vec_per_row; v += 32) {
+      const uint4 wv = reinterpret_cast<const uint4*>(wr)[v];
+      const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int t = 0; t < TB; ++t) {
+        if (t < ntok) {
+          const uint4 xv = reinterpret_cast<const uint4*>(xs + t * H)[v];
+          const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
+          float a = acc[t];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            a = fmaf(bf16_bits_lo(xq[j]), bf16_bits_lo(wq[j]), a);
+            a = fmaf(bf16_bits_hi(xq[j]), bf16_bits_hi(wq[j]), a);
+          }
+          acc[t] = a;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+      float a = acc[t];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0 && t < ntok) {
+        // F.linear in bf16: fp32 accumulate, add the bias, round once to bf16.
+        const float l = bf16_round(a + __bfloat162float(bias[e]));
+        logits[t * E + e] = l;
+      }
+    }
+  }
+  __syncthreads();
+
+  // Top-k (ties -> lower expert index first) and softmax over the selected logits.
+  if (threadIdx.x < ntok) {
+    const int t = threadIdx.x;
+    const float* lg = logits + t * E;
+    int sel[kMaxTopK];
+    float val[kMaxTopK];
+    for (int j = 0; j < K; ++j) {
+      int best = -1;
+      float bv = 0.0f;
+      for (int e = 0; e < E; ++e) {
+        bool taken = false;
+        for (int q = 0; q < j; ++q) taken |= (sel[q] == e);
+        if (taken) continue;
+        const float v = lg[e];
+        if (best < 0 || v > bv || (v != v && bv == bv)) { best = e; bv = v; }
+      }
+      sel[j] = best;
+      val[j] = bv;
+    }
+    const float m = val[0];
+    float ex[kMaxTopK], s = 0.0f;
+    for (int j = 0; j < K; ++j) { ex[j] = expf(__fsub_rn(val[j], m)); s = __fadd_rn(s, ex[j]); }
+    const float inv = __fdiv_rn(1.0f, s);
+    const int64_t tg = t0 + t;
+    for (int j = 0; j < K; ++j) {
+      const __nv_bfloat16 p = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
+      out_idx[tg * K + j] = sel[j];
+      if (out_scores) out_scores[tg * K + j] = p;
+      if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(p);
+    }
+    if (out_logits)
+      for (int e = 0; e < E; ++e) out_logits[tg * E + e] = __float2bfloat16_rn(lg[e]);
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Per-expert stable counting sort. blockDim = 1024, gridDim = E.
+struct RouteSortParams {
+  const int64_t* router_indices;   // [A] expert of assignment i = t*K + k
+  const float* routing_weights;    // [A]
+  int A, K, E;
+  int64_t* sorted_token;           // [A]
+  int64_t* sorted_expert;          // [A]
+  float* sorted_weight;            // [A]
+  int32_t* counts;                 // [E]
+  int32_t* offsets;                // [E]
+  // Optional blocked-scale bookkeeping for the fused path (nullptr to skip).
+  int32_t* sf_offsets_a;           // [E] bytes, act layout with g4_a k-atoms
+  int g4_a, groups_a;              // k-atoms / valid groups of the GEMM1 A operand
+  uint8_t* sf_a;                   // zero the padding of this buffer
+  int32_t* sf_offsets_b;           // [E] bytes, intermediate layout
+  int g4_b, groups_b;
+  uint8_t* sf_b;
+  int* err;                        // set if an index is outside [0, E)
+};
+
+__global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
+  __shared__ int hist[kMaxExperts];
+  __shared__ int warp_cnt[32];
+  __shared__ int s_base;
+  const int e = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < p.E; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  // Pass 1: full histogram (every CTA builds it; A is small next to the GEMMs).
+  for (int i = tid; i < p.A; i += blockDim.x) {
+    const int64_t ex = p.router_indices[i];
+    if (ex < 0 || ex >= p.E) {
+      if (p.err) atomicCAS(p.err, 0, 0x201);
+      continue;
+    }
+    atomicAdd(&hist[ex], 1);
+  }
+  __syncthreads();
+  int off = 0;
+  for (int q = 0; q < e; ++q) off += hist[q];
+  const int cnt = hist[e];
+  if (tid == 0) {
+    p.counts[e] = cnt;
+    p.offsets[e] = off;
+    s_base = 0;
+  }
+  if (p.sf_offsets_a != nullptr && tid == 0) {
+    int64_t sa = 0, sb = 0;
+    for (int q = 0; q < e; ++q) {
+      sa += blocked_sf_cosize(hist[q], p.g4_a * 4);
+      sb += blocked_sf_cosize(hist[q], p.g4_b * 4);
+    }
+    p.sf_offsets_a[e] = static_cast<int32_t>(sa);
+    p.sf_offsets_b[e] = static_cast<int32_t>(sb);
+    s_base = 0;
+  }
+  __syncthreads();
+  // Zero the padding of this expert's blocked scale buffers: rows [cnt, pad128(cnt))
+  // and k-groups past the valid ones. The quantisers write the valid entries.
+  if (p.sf_offsets_a != nullptr) {
+    const int rows_pad = (cnt + 127) & ~127;
+    for (int pass = 0; pass < 2; ++pass) {
+      uint8_t* buf = pass == 0 ? p.sf_a : p.sf_b;
+      const int g4 = pass == 0 ? p.g4_a : p.g4_b;
+      const int gv = pass == 0 ? p.groups_a : p.groups_b;
+      if (buf == nullptr) continue;
+      const int gp = g4 * 4;
+      int64_t base = 0;
+      for (int q = 0; q < e; ++q) base += blocked_sf_cosize(hist[q], gp);
+      const int64_t total = static_cast<int64_t>(rows_pad) * gp;
+      for (int64_t i = tid; i < total; i += blockDim.x) {
+        const int r = static_cast<int>(i / gp), g = static_cast<int>(i - static_cast<int64_t>(r) * gp);
+        if (r >= cnt || g >= gv) buf[base + blocked_sf_offset(r, g, g4)] = 0;
+      }
+    }
+  }
+  // Pass 2: stable compaction of this expert's assignments, 1024 at a time.
+  for (int c0 = 0; c0 < p.A; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    const bool mine = (i < p.A) && (p.router_indices[i] == e);
+    const unsigned bal = __ballot_sync(0xffffffffu, mine);
+    if (lane == 0) warp_cnt[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0;
+    for (int q = 0; q < warp; ++q) before += warp_cnt[q];
+    int chunk_total = 0;
+    if (tid == 0)
+      for (int q = 0; q < 32; ++q) chunk_total += warp_cnt[q];
+    if (mine) {
+      const int pos = off + s_base + before + __popc(bal & ((1u << lane) - 1u));
+      p.sorted_token[pos] = i / p.K;
+      p.sorted_expert[pos] = e;
+      p.sorted_weight[pos] = p.routing_weights[i];
+    }
+    __syncthreads();
+    if (tid == 0) s_base += chunk_total;
+    __syncthreads();
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Gather + quantise: one warp per sorted row; lane l handles k-groups l, l+32, ...
+// Writes FP8 codes into a compact [A, H] buffer and the UE8M0 scales into the blocked
+// layout at sf_offsets[expert] (row index = position inside the expert's group).
+// When sorted_token is null the rows are taken in order (plain quantiser) and scales
+// go row-major into sf_rowmajor.
+template <typename InT>
+__global__ void __launch_bounds__(256) gather_quant_kernel(
+    const InT* __restrict__ src, int64_t rows, int H, const int64_t* __restrict__ sorted_token,
+    const int64_t* __restrict__ sorted_expert, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ sf_offsets, int g4, uint8_t* __restrict__ out_codes,
+    uint8_t* __restrict__ sf_blocked, uint8_t* __restrict__ sf_rowmajor) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int G = H >> 5;
+  int64_t src_row = row;
+  int64_t sf_base = 0, r_in = 0;
+  if (sorted_token != nullptr) {
+    src_row = sorted_token[row];
+    const int ex = static_cast<int>(sorted_expert[row]);
+    r_in = row - offsets[ex];
+    sf_base = sf_offsets[ex];
+  }
+  const InT* xr = src + src_row * H;
+  uint8_t* orow = out_codes + row * H;
+  for (int g = lane; g < G; g += 32) {
+    float v[32];
+    if constexpr (sizeof(InT) == 2) {
+      const uint4* p = reinterpret_cast<const uint4*>(xr + g * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = p[q];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[q * 8 + 2 * j] = bf16_bits_lo(w4[j]);
+          v[q * 8 + 2 * j + 1] = bf16_bits_hi(w4[j]);
+        }
+      }
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(xr + g * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = p[q];
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+      }
+    }
+    uint32_t codes[8];
+    const uint8_t s = quantize_group32(v, codes);
+    uint4* o = reinterpret_cast<uint4*>(orow + g * 32);
+    o[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+    o[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+    if (sorted_token != nullptr) sf_blocked[sf_base + blocked_sf_offset(r_in, g, g4)] = s;
+    else sf_rowmajor[row * G + g] = s;
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Row-major [rows, G] scales -> one blocked buffer (zero padded), grid-stride over the
+// padded domain. Restates convert_scales_w4a8_impl (matmul_mxfp4_cutlass.cu:666-749).
+__global__ void convert_scales_kernel(const uint8_t* __restrict__ in, int64_t rows, int G, int g4,
+                                      uint8_t* __restrict__ out) {
+  const int gp = g4 * 4;
+  const int64_t total = ((rows + 127) & ~int64_t(127)) * gp;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / gp;
+    const int g = static_cast<int>(i - r * gp);
+    out[blocked_sf_offset(r, g, g4)] = (r < rows && g < G) ? in[r * G + g] : 0;
+  }
+}
+
+// Per-expert blocked conversion (batch_convert_a_scales_for_w4a8_gpu,
+// matmul_mxfp4_cutlass.cu:881-1004) with the per-expert byte offsets computed on the
+// device. grid = E, block = 256.
+__global__ void batch_convert_scales_kernel(const uint8_t* __restrict__ in,
+                                            const int32_t* __restrict__ counts,
+                                            const int32_t* __restrict__ offsets, int E, int G,
+                                            int g4, uint8_t* __restrict__ out,
+                                            int32_t* __restrict__ sf_offsets) {
+  const int e = blockIdx.x;
+  const int gp = g4 * 4;
+  int64_t base = 0;
+  for (int q = 0; q < e; ++q) base += blocked_sf_cosize(counts[q], gp);
+  if (threadIdx.x == 0) sf_offsets[e] = static_cast<int32_t>(base);
+  const int m = counts[e];
+  const int64_t total = static_cast<int64_t>((m + 127) & ~127) * gp;
+  const int64_t in_base = static_cast<int64_t>(offsets[e]) * G;
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    const int64_t r = i / gp;
+    const int g = static_cast<int>(i - r * gp);
+    out[base + blocked_sf_offset(r, g, g4)] = (r < m && g < G) ? in[in_base + r * G + g] : 0;
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Standalone SwiGLU (cutlass_experts.py:258-276) for [rows, 2n] interleaved gate/up.
+// bf16 inputs follow torch's per-op rounding (every elementwise op of the reference
+// rounds its bf16 result); fp32 inputs use swiglu_pair.
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ in, int64_t rows, int64_t n, T* __restrict__ out,
+                              float alpha, float limit) {
+  const int64_t total = rows * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / n, c = i - r * n;
+    const T* row = in + r * 2 * n;
+    if constexpr (sizeof(T) == 4) {
+      out[i] = swiglu_pair(row[2 * c], row[2 * c + 1], alpha, limit);
+    } else {
+      float g = __bfloat162float(row[2 * c]), u = __bfloat162float(row[2 * c + 1]);
+      g = g > limit ? limit : g;
+      u = u < -limit ? -limit : (u > limit ? limit : u);
+      const float ga = bf16_round(__fmul_rn(g, alpha));
+      const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-ga))));
+      const float gs = bf16_round(__fmul_rn(g, sg));
+      const float u1 = bf16_round(__fadd_rn(u, 1.0f));
+      out[i] = __float2bfloat16_rn(__fmul_rn(gs, u1));
+    }
+  }
+}
+
+}  // namespace gptoss

@@ -1,0 +1,384 @@
+"""Tensor-level wrappers over the C ABI and their torch.library registrations.
+
+Every function takes CUDA tensors, validates them the way the reference's CHECK_*
+macros do (kernels/matmul_mxfp4_cutlass.cu:1107-1116: "must be a CUDA tensor", "must be
+contiguous", dtype checks -> RuntimeError) and enqueues work on the current stream.
+No function here computes anything on the host.
+
+Registered ops (all with register_fake, static output shapes, no host sync unless noted):
+  cutlass::fp4_group_mm        same schema as kernels/cutlass_experts.py:147-166
+  cutlass::fused_moe_routing   same schema as kernels/cutlass_experts.py:168-188
+  gptoss::quantize_fp8, gptoss::swiglu, gptoss::router_topk,
+  gptoss::moe_experts_forward  (the whole CutlassGptOssExperts.forward)
+  gptoss::moe_layer_forward    (router + experts)
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+GEMM_AUTO, GEMM_TOKENS_M, GEMM_SWAP = 0, 1, 2
+DTYPE_BF16, DTYPE_F32 = 0, 1
+
+_status = {}
+_status_lock = threading.Lock()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _cuda(t: torch.Tensor, name: str):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name}: must be a CUDA tensor.")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name}: must be contiguous.")
+
+
+def _dtype(t: torch.Tensor, allowed, name: str):
+    if t.dtype not in allowed:
+        raise RuntimeError(f"{name}: Inconsistency of Tensor type: got {t.dtype}, expected one of {allowed}")
+
+
+def status_tensor(device) -> torch.Tensor:
+    """Per-device int32 word the kernels set on a timed-out wait or a bad index."""
+    device = torch.device(device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    with _status_lock:
+        t = _status.get(key)
+        if t is None:
+            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+            _status[key] = t
+        return t
+
+
+def read_status(device) -> int:
+    """Returns and clears the device status word (synchronises the current stream)."""
+    t = status_tensor(device)
+    out = ctypes.c_int32(0)
+    _lib.call("gptoss_read_status", t.data_ptr(), ctypes.addressof(out), _stream(t.device))
+    return int(out.value)
+
+
+# ------------------------------------------------------------------ plain ops
+def quantize_fp8(x: torch.Tensor):
+    """BF16/FP32 [M, K] -> (float8_e4m3fn [M, K], uint8 UE8M0 [M, K/32]), bit-exact with
+    quantize_activations_to_fp8 (kernels/cutlass_experts.py:197-251)."""
+    if x.dim() != 2:
+        raise RuntimeError(f"Expected 2D tensor, got {x.dim()}D")
+    _cuda(x, "x")
+    _dtype(x, (torch.bfloat16, torch.float32), "x")
+    M, K = x.shape
+    if K % 32 != 0:
+        raise RuntimeError(f"K={K} must be divisible by 32")
+    codes = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    scales = torch.empty((M, K // 32), dtype=torch.uint8, device=x.device)
+    _lib.call("gptoss_quantize_fp8", x.data_ptr(), DTYPE_BF16 if x.dtype == torch.bfloat16 else DTYPE_F32,
+              M, K, codes.data_ptr(), scales.data_ptr(), _stream(x.device))
+    return codes, scales
+
+
+def swiglu(gate_up: torch.Tensor, alpha: float = 1.702, limit: float = 7.0) -> torch.Tensor:
+    """SwiGLU over interleaved gate (even) / up (odd) columns (cutlass_experts.py:258-276)."""
+    _cuda(gate_up, "gate_up")
+    _dtype(gate_up, (torch.bfloat16, torch.float32), "gate_up")
+    if gate_up.shape[-1] % 2:
+        raise RuntimeError("swiglu: last dimension must be even")
+    rows = gate_up.numel() // gate_up.shape[-1]
+    out = torch.empty((*gate_up.shape[:-1], gate_up.shape[-1] // 2), dtype=gate_up.dtype, device=gate_up.device)
+    _lib.call("gptoss_swiglu", gate_up.data_ptr(), DTYPE_BF16 if gate_up.dtype == torch.bfloat16 else DTYPE_F32,
+              rows, gate_up.shape[-1], out.data_ptr(), float(alpha), float(limit), _stream(gate_up.device))
+    return out
+
+
+def blocked_scales_bytes(rows: int, k: int) -> int:
+    return int(_lib.query("gptoss_blocked_scales_bytes", rows, k))
+
+
+def convert_scales_blocked(scales: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """Row-major [rows, k/32] UE8M0 -> flat blocked buffer (convert_a/b_scales_for_w4a8,
+    kernels/matmul_mxfp4_cutlass.cu:666-759), on the scales' device."""
+    _cuda(scales, "scales")
+    _dtype(scales, (torch.uint8,), "scales")
+    if scales.numel() != rows * (k // 32):
+        raise RuntimeError(f"scales has {scales.numel()} entries, expected rows*K/32 = {rows * (k // 32)}")
+    nbytes = blocked_scales_bytes(rows, k)
+    out = torch.empty(nbytes, dtype=torch.uint8, device=scales.device)
+    if nbytes:
+        _lib.call("gptoss_convert_scales_blocked", scales.data_ptr(), rows, k, out.data_ptr(), nbytes,
+                  _stream(scales.device))
+    return out
+
+
+def batch_convert_a_scales(scales: torch.Tensor, counts: torch.Tensor, offsets: torch.Tensor, k: int,
+                           exact_size: bool = True):
+    """Per-expert blocked activation scales (batch_convert_a_scales_for_w4a8_gpu,
+    kernels/matmul_mxfp4_cutlass.cu:912-1004). With exact_size=True the result is trimmed to
+    the bytes actually used, which (like the reference) needs the counts on the host; with
+    exact_size=False it returns the static-capacity buffer and never syncs."""
+    _cuda(scales, "scales")
+    _cuda(counts, "expert_counts")
+    _cuda(offsets, "expert_offsets")
+    _dtype(counts, (torch.int32,), "expert_counts")
+    _dtype(offsets, (torch.int32,), "expert_offsets")
+    E = counts.numel()
+    rows = scales.shape[0] if scales.dim() else 0
+    cap = int(_lib.query("gptoss_batch_blocked_scales_capacity", rows, E, k))
+    out = torch.empty(max(cap, 1), dtype=torch.uint8, device=scales.device)
+    sf_offsets = torch.empty(E, dtype=torch.int32, device=scales.device)
+    _lib.call("gptoss_batch_convert_a_scales", scales.data_ptr(), counts.data_ptr(), offsets.data_ptr(), E, k,
+              out.data_ptr(), cap, sf_offsets.data_ptr(), _stream(scales.device))
+    if not exact_size:
+        return out[:cap], sf_offsets
+    c = counts.cpu().long()
+    g4 = (k // 32 + 3) // 4
+    total = int((((c + 127) // 128) * g4 * 512).sum())
+    if total == 0:
+        return torch.zeros(0, dtype=torch.uint8, device=scales.device), torch.zeros_like(sf_offsets)
+    return out[:total], sf_offsets
+
+
+def fused_moe_routing_impl(router_indices: torch.Tensor, routing_weights: torch.Tensor, num_experts: int):
+    _cuda(router_indices, "router_indices")
+    _cuda(routing_weights, "routing_weights")
+    _dtype(router_indices, (torch.int64,), "router_indices")
+    _dtype(routing_weights, (torch.float32,), "routing_weights")
+    T, k = router_indices.shape
+    dev = router_indices.device
+    A = T * k
+    st = torch.empty(A, dtype=torch.int64, device=dev)
+    se = torch.empty(A, dtype=torch.int64, device=dev)
+    sw = torch.empty(A, dtype=torch.float32, device=dev)
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    offsets = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    _lib.call("gptoss_fused_moe_routing", router_indices.data_ptr(), routing_weights.data_ptr(), T, k, num_experts,
+              st.data_ptr(), se.data_ptr(), sw.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+              status_tensor(dev).data_ptr(), _stream(dev))
+    return st, se, sw, counts, offsets
+
+
+def fp4_group_mm_impl(output, a, b, a_blockscale, b_blockscales, alphas, problem_sizes, expert_offsets,
+                      sf_offsets, gemm_mode: int = GEMM_AUTO):
+    """W4A8 grouped GEMM into `output` (cutlass_fp4_group_mm, W4A8 mode)."""
+    _cuda(a, "a")
+    if a.dtype == torch.uint8:
+        raise NotImplementedError("fp4_group_mm: the W4A4 (NVFP4 x NVFP4) mode is not implemented on sm_100a; "
+                                  "pass float8_e4m3fn activations (W4A8)")
+    _dtype(a, (torch.float8_e4m3fn,), "a")
+    _cuda(b, "b")
+    _dtype(b, (torch.uint8,), "b")
+    _cuda(a_blockscale, "a_blockscale")
+    _dtype(a_blockscale, (torch.uint8,), "a_blockscale")
+    _cuda(b_blockscales, "b_blockscales")
+    _dtype(b_blockscales, (torch.uint8,), "b_blockscales")
+    _cuda(alphas, "alphas")
+    _dtype(alphas, (torch.float32,), "alphas")
+    _cuda(output, "output")
+    _dtype(output, (torch.bfloat16,), "output")
+    for t, n in ((problem_sizes, "problem_sizes"), (expert_offsets, "expert_offsets"), (sf_offsets, "sf_offsets")):
+        _cuda(t, n)
+        _dtype(t, (torch.int32,), n)
+    if b.dim() != 3:
+        raise RuntimeError("b must be [E, N, K/2]")
+    if b_blockscales.dim() not in (2, 3):
+        raise RuntimeError("Invalid b_blockscales dim (expected 2D [E, converted_size] or 3D [E, N, K_groups])")
+    if problem_sizes.dim() != 2:
+        raise RuntimeError("problem_sizes must be 2D")
+    E, N, K = b.shape[0], b.shape[1], 2 * b.shape[2]
+    M = a.shape[0]
+    if output.shape[0] < M or output.shape[1] != N:
+        raise RuntimeError(f"output must be [M={M}, N={N}], got {tuple(output.shape)}")
+    ldb = b_blockscales.numel() // E
+    _lib.call("gptoss_fp4_group_mm", output.data_ptr(), a.data_ptr(), M, a.shape[1], b.data_ptr(), E, N, K,
+              a_blockscale.data_ptr(), b_blockscales.data_ptr(), ldb, alphas.data_ptr(), problem_sizes.data_ptr(),
+              expert_offsets.data_ptr(), sf_offsets.data_ptr(), int(gemm_mode), status_tensor(a.device).data_ptr(),
+              _stream(a.device))
+
+
+def router_topk_impl(hidden, weight, bias, top_k: int):
+    _cuda(hidden, "hidden_states")
+    _cuda(weight, "router weight")
+    _cuda(bias, "router bias")
+    for t, n in ((hidden, "hidden_states"), (weight, "router weight"), (bias, "router bias")):
+        _dtype(t, (torch.bfloat16,), n)
+    T, H = hidden.shape
+    E = weight.shape[0]
+    dev = hidden.device
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=dev)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
+    logits = torch.empty((T, E), dtype=torch.bfloat16, device=dev)
+    _lib.call("gptoss_router_topk", hidden.data_ptr(), weight.data_ptr(), bias.data_ptr(), T, H, E, top_k,
+              idx.data_ptr(), scores.data_ptr(), None, logits.data_ptr(), _stream(dev))
+    return logits, scores, idx
+
+
+def workspace_bytes(T, k, E, H, I) -> int:
+    return int(_lib.query("gptoss_moe_workspace_bytes", T, k, E, H, I))
+
+
+def _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias):
+    for t, n in ((gu_data, "gate_up_proj_data"), (gu_scales, "gate_up_proj_scales"),
+                 (dn_data, "down_proj_data"), (dn_scales, "down_proj_scales")):
+        _cuda(t, n)
+        _dtype(t, (torch.uint8,), n)
+    for t, n in ((gu_bias, "gate_up_proj_bias"), (dn_bias, "down_proj_bias")):
+        _cuda(t, n)
+        _dtype(t, (torch.float32,), n)
+
+
+def moe_experts_forward_impl(hidden, router_indices, routing_weights, gu_data, gu_scales, gu_bias, dn_data,
+                             dn_scales, dn_bias, alpha: float, limit: float, gemm_mode: int = GEMM_AUTO):
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _cuda(router_indices, "router_indices")
+    _dtype(router_indices, (torch.int64,), "router_indices")
+    _cuda(routing_weights, "routing_weights")
+    _dtype(routing_weights, (torch.float32,), "routing_weights")
+    _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias)
+    T, H = hidden.shape
+    k = router_indices.shape[1]
+    E = gu_data.shape[0]
+    I = gu_data.shape[1] // 2
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=hidden.device)
+    ws = torch.empty(max(workspace_bytes(T, k, E, H, I), 256), dtype=torch.uint8, device=hidden.device)
+    _lib.call("gptoss_moe_experts_forward", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(),
+              T, k, E, H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E, gu_bias.data_ptr(),
+              dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E, dn_bias.data_ptr(), float(alpha),
+              float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), int(gemm_mode),
+              status_tensor(hidden.device).data_ptr(), _stream(hidden.device))
+    return out
+
+
+def moe_layer_forward_impl(hidden, router_weight, router_bias, top_k: int, gu_data, gu_scales, gu_bias, dn_data,
+                           dn_scales, dn_bias, alpha: float, limit: float, gemm_mode: int = GEMM_AUTO):
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _cuda(router_weight, "router weight")
+    _cuda(router_bias, "router bias")
+    _dtype(router_weight, (torch.bfloat16,), "router weight")
+    _dtype(router_bias, (torch.bfloat16,), "router bias")
+    _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias)
+    T, H = hidden.shape
+    E = gu_data.shape[0]
+    I = gu_data.shape[1] // 2
+    dev = hidden.device
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=dev)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(max(workspace_bytes(T, top_k, E, H, I), 256), dtype=torch.uint8, device=dev)
+    _lib.call("gptoss_moe_layer_forward", hidden.data_ptr(), router_weight.data_ptr(), router_bias.data_ptr(), T,
+              top_k, E, H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E, gu_bias.data_ptr(),
+              dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E, dn_bias.data_ptr(), float(alpha),
+              float(limit), out.data_ptr(), idx.data_ptr(), scores.data_ptr(), ws.data_ptr(), ws.numel(),
+              int(gemm_mode), status_tensor(dev).data_ptr(), _stream(dev))
+    return out, scores, idx
+
+
+# ------------------------------------------------------------------ registration
+_registered = False
+_reg_lock = threading.Lock()
+
+
+def register_ops() -> None:
+    """Register every op with torch.library (idempotent)."""
+    global _registered
+    if _registered:
+        return
+    with _reg_lock:
+        if _registered:
+            return
+        _lib.load()   # fail loudly before anything is registered
+
+        @torch.library.custom_op("cutlass::fp4_group_mm", mutates_args=("output",))
+        def fp4_group_mm(output: torch.Tensor, a: torch.Tensor, b: torch.Tensor, a_blockscale: torch.Tensor,
+                         b_blockscales: torch.Tensor, alphas: torch.Tensor, problem_sizes: torch.Tensor,
+                         expert_offsets: torch.Tensor, sf_offsets: torch.Tensor) -> None:
+            fp4_group_mm_impl(output, a, b, a_blockscale, b_blockscales, alphas, problem_sizes, expert_offsets,
+                              sf_offsets)
+
+        @fp4_group_mm.register_fake
+        def _(output, a, b, a_blockscale, b_blockscales, alphas, problem_sizes, expert_offsets, sf_offsets):
+            return None
+
+        @torch.library.custom_op("cutlass::fused_moe_routing", mutates_args=())
+        def fused_moe_routing(router_indices: torch.Tensor, routing_weights: torch.Tensor, num_experts: int
+                              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+            return fused_moe_routing_impl(router_indices, routing_weights, num_experts)
+
+        @fused_moe_routing.register_fake
+        def _(router_indices, routing_weights, num_experts):
+            total = router_indices.shape[0] * router_indices.shape[1]
+            dev = router_indices.device
+            return (torch.empty(total, dtype=torch.int64, device=dev),
+                    torch.empty(total, dtype=torch.int64, device=dev),
+                    torch.empty(total, dtype=torch.float32, device=dev),
+                    torch.empty(num_experts, dtype=torch.int32, device=dev),
+                    torch.empty(num_experts, dtype=torch.int32, device=dev))
+
+        @torch.library.custom_op("gptoss::quantize_fp8", mutates_args=())
+        def quantize_fp8_op(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+            return quantize_fp8(x)
+
+        @quantize_fp8_op.register_fake
+        def _(x):
+            M, K = x.shape
+            return (torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device),
+                    torch.empty((M, K // 32), dtype=torch.uint8, device=x.device))
+
+        @torch.library.custom_op("gptoss::swiglu", mutates_args=())
+        def swiglu_op(gate_up: torch.Tensor, alpha: float, limit: float) -> torch.Tensor:
+            return swiglu(gate_up, alpha, limit)
+
+        @swiglu_op.register_fake
+        def _(gate_up, alpha, limit):
+            return gate_up.new_empty((*gate_up.shape[:-1], gate_up.shape[-1] // 2))
+
+        @torch.library.custom_op("gptoss::router_topk", mutates_args=())
+        def router_topk_op(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, top_k: int
+                           ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+            return router_topk_impl(hidden, weight, bias, top_k)
+
+        @router_topk_op.register_fake
+        def _(hidden, weight, bias, top_k):
+            T = hidden.shape[0]
+            return (hidden.new_empty((T, weight.shape[0])), hidden.new_empty((T, top_k)),
+                    torch.empty((T, top_k), dtype=torch.int64, device=hidden.device))
+
+        @torch.library.custom_op("gptoss::moe_experts_forward", mutates_args=())
+        def moe_experts_forward(hidden: torch.Tensor, router_indices: torch.Tensor, routing_weights: torch.Tensor,
+                                gate_up_data: torch.Tensor, gate_up_scales: torch.Tensor, gate_up_bias: torch.Tensor,
+                                down_data: torch.Tensor, down_scales: torch.Tensor, down_bias: torch.Tensor,
+                                alpha: float, limit: float, gemm_mode: int) -> torch.Tensor:
+            return moe_experts_forward_impl(hidden, router_indices, routing_weights, gate_up_data, gate_up_scales,
+                                            gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode)
+
+        @moe_experts_forward.register_fake
+        def _(hidden, router_indices, routing_weights, gate_up_data, gate_up_scales, gate_up_bias, down_data,
+              down_scales, down_bias, alpha, limit, gemm_mode):
+            return torch.empty_like(hidden)
+
+        @torch.library.custom_op("gptoss::moe_layer_forward", mutates_args=())
+        def moe_layer_forward(hidden: torch.Tensor, router_weight: torch.Tensor, router_bias: torch.Tensor,
+                              top_k: int, gate_up_data: torch.Tensor, gate_up_scales: torch.Tensor,
+                              gate_up_bias: torch.Tensor, down_data: torch.Tensor, down_scales: torch.Tensor,
+                              down_bias: torch.Tensor, alpha: float, limit: float, gemm_mode: int
+                              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+            return moe_layer_forward_impl(hidden, router_weight, router_bias, top_k, gate_up_data, gate_up_scales,
+                                          gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode)
+
+        @moe_layer_forward.register_fake
+        def _(hidden, router_weight, router_bias, top_k, gate_up_data, gate_up_scales, gate_up_bias, down_data,
+              down_scales, down_bias, alpha, limit, gemm_mode):
+            T = hidden.shape[0]
+            return (torch.empty_like(hidden), hidden.new_empty((T, top_k)),
+                    torch.empty((T, top_k), dtype=torch.int64, device=hidden.device))
+
+        _registered = True

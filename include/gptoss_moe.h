@@ -1,0 +1,175 @@
+/*
+ * gptoss_moe.h - C ABI of the B200 (sm_100a) GPT-OSS MXFP4 W4A8 mixture-of-experts
+ * expert path (libgptoss_moe.so).
+ *
+ * Conventions for every entry point
+ *   - Pointers are device pointers unless a parameter says "host".
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Work is enqueued on it;
+ *     no entry point synchronises the stream unless its comment says so.
+ *   - Return 0 on success, or a GPTOSS_ERR_* code; gptoss_last_error() then returns a
+ *     message for the calling thread. No C++ exception crosses this boundary.
+ *   - Tensors are dense and row-major ("contiguous"); shapes are given in elements.
+ *   - FP8 activations are float8_e4m3fn bytes; MXFP4 weights are two E2M1 codes per
+ *     byte (low nibble = even k); scales are UE8M0 bytes (value 2^(s-127)), one per 32
+ *     consecutive k.
+ *   - "Blocked" scales use the 128-row x 4-group atom layout of CUTLASS's
+ *     Sm1xxBlockScaledConfig<32>::tile_atom_to_shape_SFA/SFB:
+ *       off(r, g) = (r/128)*(G4*512) + (g/4)*512 + (r%32)*16 + ((r%128)/32)*4 + g%4
+ *     with G4 = ceil(groups/4); a buffer for `rows` rows holds ceil(rows/128)*G4*512 bytes.
+ *
+ * Reference interfaces replaced are cited as path:line of evil0sheep/gpt-oss-mxfp4-compile.
+ */
+#ifndef GPTOSS_MOE_H
+#define GPTOSS_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  GPTOSS_OK = 0,
+  GPTOSS_ERR_INVALID_ARGUMENT = 1, /* bad shape / dtype / alignment (TORCH_CHECK in the reference) */
+  GPTOSS_ERR_CUDA = 2,             /* a CUDA runtime or driver call failed */
+  GPTOSS_ERR_NOT_IMPLEMENTED = 3,  /* e.g. the W4A4 (NVFP4) mode of fp4_group_mm */
+  GPTOSS_ERR_UNSUPPORTED_DEVICE = 4, /* not a compute-capability 10.x GPU */
+  GPTOSS_ERR_WORKSPACE = 5         /* workspace smaller than gptoss_*_workspace_bytes() */
+};
+
+enum { GPTOSS_DTYPE_BF16 = 0, GPTOSS_DTYPE_F32 = 1 };
+
+/* GEMM orientation: AUTO picks SWAP (weights on the MMA M side) when the average
+ * expert holds <= 48 rows, else TOKENS_M. Results agree to fp32 accumulation order. */
+enum { GPTOSS_GEMM_AUTO = 0, GPTOSS_GEMM_TOKENS_M = 1, GPTOSS_GEMM_SWAP = 2 };
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* gptoss_last_error(void);
+
+/* ABI version of this header (bumped on any signature change). */
+int gptoss_abi_version(void);
+
+/* Copies the 4-byte device status word that kernels set when a bounded wait times out
+ * or an expert index is out of range (0 = ok) into *status_host and clears it.
+ * Synchronises `stream`. */
+int gptoss_read_status(int32_t* status_dev, int32_t* status_host, void* stream);
+
+/* Replaces fused_moe_routing (kernels/matmul_mxfp4_cutlass.cu:1041-1095, registered as
+ * cutlass::fused_moe_routing at kernels/cutlass_experts.py:168-188).
+ * router_indices [T, top_k] int64, routing_weights [T, top_k] f32 ->
+ * sorted_token_idx [T*top_k] int64, sorted_expert_idx [T*top_k] int64,
+ * sorted_weights [T*top_k] f32, expert_counts [E] int32, expert_offsets [E] int32
+ * (exclusive prefix of counts). Deterministic: inside an expert the assignments are in
+ * ascending (token, k) order, i.e. torch.argsort(flat_expert, stable=True).
+ * status_dev may be NULL; otherwise it records out-of-range expert indices. */
+int gptoss_fused_moe_routing(const int64_t* router_indices, const float* routing_weights,
+                             int64_t num_tokens, int top_k, int num_experts,
+                             int64_t* sorted_token_idx, int64_t* sorted_expert_idx,
+                             float* sorted_weights, int32_t* expert_counts,
+                             int32_t* expert_offsets, int32_t* status_dev, void* stream);
+
+/* Router (HF GptOssTopKRouter.forward, modeling_gpt_oss.py; the reference receives its
+ * outputs in CutlassGptOssExperts.forward, kernels/cutlass_experts.py:376-391):
+ * logits = bf16(hidden[T,H] . weight[E,H]^T + bias[E]) (fp32 accumulate), top-k
+ * (ties -> lower expert index), softmax over the k logits rounded to bf16.
+ * Outputs: router_indices [T,k] int64, router_scores [T,k] bf16 (may be NULL),
+ * routing_weights_f32 [T,k] (the scores as f32, may be NULL), logits [T,E] bf16 (may be
+ * NULL). hidden, weight, bias are bf16; H % 8 == 0; E <= 256; k <= 8. */
+int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
+                       int64_t num_tokens, int64_t hidden_size, int num_experts, int top_k,
+                       int64_t* router_indices, void* router_scores,
+                       float* routing_weights_f32, void* logits, void* stream);
+
+/* Replaces quantize_activations_to_fp8 (kernels/cutlass_experts.py:197-251):
+ * x [M,K] (bf16 or f32, `dtype`) -> codes [M,K] e4m3 bytes + scales [M,K/32] UE8M0,
+ * bit-identical to the reference. K % 32 == 0. */
+int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, uint8_t* codes,
+                        uint8_t* scales, void* stream);
+
+/* Replaces swiglu (kernels/cutlass_experts.py:258-276): x [rows, 2n] with gate on even
+ * and up on odd columns -> out [rows, n]; gate clamped to <= limit, up to [-limit, limit],
+ * out = gate * sigmoid(alpha * gate) * (up + 1). bf16 follows torch's per-op rounding. */
+int gptoss_swiglu(const void* x, int dtype, int64_t rows, int64_t cols, void* out, float alpha,
+                  float limit, void* stream);
+
+/* Replaces convert_a_scales_for_w4a8 / convert_b_scales_for_w4a8
+ * (kernels/matmul_mxfp4_cutlass.cu:666-759): row-major scales [rows, K/32] -> one
+ * blocked buffer of blocked bytes (zero padded). `k` is the (padded) K the GEMM uses;
+ * the mapping does not depend on M or N beyond `rows`. */
+int gptoss_convert_scales_blocked(const uint8_t* scales_rowmajor, int64_t rows, int64_t k,
+                                  uint8_t* blocked, int64_t blocked_bytes, void* stream);
+
+/* Bytes one blocked buffer of `rows` rows needs for reduction depth k. Host only. */
+int64_t gptoss_blocked_scales_bytes(int64_t rows, int64_t k);
+
+/* Replaces batch_convert_a_scales_for_w4a8_gpu (kernels/matmul_mxfp4_cutlass.cu:912-1004)
+ * without its host sync: per-expert blocked activation scales laid end to end, expert e
+ * at sf_offsets[e] (bytes, written on the device). counts/offsets are [E] int32 device
+ * arrays. `capacity` must be >= gptoss_batch_blocked_scales_capacity(total_rows, E, k). */
+int gptoss_batch_convert_a_scales(const uint8_t* scales_rowmajor, const int32_t* expert_counts,
+                                  const int32_t* expert_offsets, int num_experts, int64_t k,
+                                  uint8_t* blocked, int64_t capacity, int32_t* sf_offsets,
+                                  void* stream);
+int64_t gptoss_batch_blocked_scales_capacity(int64_t total_rows, int num_experts, int64_t k);
+
+/* Replaces cutlass_fp4_group_mm, W4A8 mode (kernels/matmul_mxfp4_cutlass.cu:1118-1171,
+ * run_w4a8_group_mm_sm120 :471-655; op cutlass::fp4_group_mm, cutlass_experts.py:147-166):
+ * for each expert e with m_e = problem_sizes[3e] rows:
+ *   out[off_e + i, n] = bf16(alphas[e] * sum_k A[off_e + i, k] 2^(sfa) * B[e, n, k] 2^(sfb))
+ * a [M, lda] e4m3 (lda <= K; columns past lda read as zero), b [E, N, K/2] packed E2M1
+ * (K % 128 == 0), a_blockscale blocked per expert at sf_offsets[e] (bytes),
+ * b_blockscales [E, ldb_blockscale] blocked per expert, alphas [E] f32,
+ * problem_sizes [E,3] int32 (m_e, N, K), expert_offsets [E] int32, out [M, N] bf16.
+ * Rows of `out` owned by no expert are left untouched. gemm_mode: GPTOSS_GEMM_*. */
+int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t lda,
+                        const uint8_t* b, int num_experts, int64_t n, int64_t k,
+                        const uint8_t* a_blockscale, const uint8_t* b_blockscales,
+                        int64_t ldb_blockscale, const float* alphas,
+                        const int32_t* problem_sizes, const int32_t* expert_offsets,
+                        const int32_t* sf_offsets, int gemm_mode, int32_t* status_dev,
+                        void* stream);
+
+/* Workspace (device bytes) for gptoss_moe_experts_forward / gptoss_moe_layer_forward. */
+size_t gptoss_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts,
+                                  int64_t hidden_size, int64_t intermediate_size);
+
+/* Replaces CutlassGptOssExperts.forward (kernels/cutlass_experts.py:376-452) as one
+ * stream of kernels with no host synchronisation:
+ *   route (stable counting sort) -> gather + FP8 quantise (blocked scales)
+ *   -> GEMM1 (+bias, SwiGLU, FP8 requantise) -> GEMM2 (+bias, x routing weight,
+ *   bf16 scatter-add into out).
+ * hidden [T,H] bf16; router_indices [T,k] int64; routing_weights [T,k] f32;
+ * gate_up_data [E, 2I, Kh/2] u8, gate_up_scales [E, ldb1] blocked, gate_up_bias [E,2I] f32;
+ * down_data [E, H, Ki/2] u8, down_scales [E, ldb2] blocked, down_bias [E,H] f32;
+ * Kh = pad128(H), Ki = pad128(I); out [T,H] bf16 (overwritten). swiglu: alpha, limit.
+ * status_dev: NULL or a device int32 that records kernel timeouts / bad indices. */
+int gptoss_moe_experts_forward(const void* hidden, const int64_t* router_indices,
+                               const float* routing_weights, int64_t num_tokens, int top_k,
+                               int num_experts, int64_t hidden_size, int64_t intermediate_size,
+                               const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                               int64_t ldb_gate_up, const float* gate_up_bias,
+                               const uint8_t* down_data, const uint8_t* down_scales,
+                               int64_t ldb_down, const float* down_bias, float swiglu_alpha,
+                               float swiglu_limit, void* out, void* workspace,
+                               size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
+                               void* stream);
+
+/* Router + experts (HF GptOssMLP.forward: router then experts): router_weight [E,H] bf16,
+ * router_bias [E] bf16; writes router_indices [T,k] int64 and router_scores [T,k] bf16
+ * (either may be NULL) and out [T,H] bf16. Same weights/workspace as above. */
+int gptoss_moe_layer_forward(const void* hidden, const void* router_weight,
+                             const void* router_bias, int64_t num_tokens, int top_k,
+                             int num_experts, int64_t hidden_size, int64_t intermediate_size,
+                             const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                             int64_t ldb_gate_up, const float* gate_up_bias,
+                             const uint8_t* down_data, const uint8_t* down_scales,
+                             int64_t ldb_down, const float* down_bias, float swiglu_alpha,
+                             float swiglu_limit, void* out, int64_t* router_indices_out,
+                             void* router_scores_out, void* workspace, size_t workspace_bytes,
+                             int gemm_mode, int32_t* status_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPTOSS_MOE_H */

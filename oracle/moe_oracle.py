@@ -1,0 +1,329 @@
+"""CPU restatement of the reference's W4A8 MoE expert path (test infrastructure only).
+
+Byte and integer work (quantisation bit tricks, e4m3 encoding, blocked layout, routing)
+is numpy; floating point that the reference does in torch (bf16 rounding, matmuls,
+scatter_add_) uses torch on the CPU with the same operation order.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+__all__ = [
+    "MXFP_BLOCK", "FP8_MAX", "E2M1_VALUES", "pad_k_to_tile",
+    "e4m3_encode", "e4m3_decode", "quantize_fp8_ue8m0",
+    "blocked_sf_offset", "blocked_sf_cosize", "convert_scales_blocked", "batch_convert_a_scales",
+    "route_stable", "router_topk_hf", "router_logits_fp32",
+    "mxfp4_dequant", "fp8_dequant", "group_mm_bf16", "swiglu_fp32",
+    "w4a8_experts_forward", "dequant_fp32_reference", "synth_layer", "synth_router_bias",
+]
+
+MXFP_BLOCK = 32
+FP8_MAX = 448.0
+# E2M1 code -> value (cutlass_matmul_investigations.md:87-91; low nibble = even k)
+E2M1_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                        -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], dtype=np.float32)
+
+
+def pad_k_to_tile(K: int, tile: int = 128) -> int:
+    """kernels/cutlass_experts.py:28-30."""
+    return (K + tile - 1) // tile * tile
+
+
+# --------------------------------------------------------------------------- FP8
+def e4m3_encode(v: np.ndarray) -> np.ndarray:
+    """float32 -> float8_e4m3fn bytes, round-to-nearest-even, for |v| <= 448 (what the
+    reference's .to(torch.float8_e4m3fn) does after its clamp, cutlass_experts.py:244).
+    NaN -> 0x7F with the sign bit."""
+    v = np.asarray(v, dtype=np.float32)
+    a = np.abs(v).astype(np.float64)
+    sign = (np.signbit(v).astype(np.uint8) << 7)
+    out = np.zeros(v.shape, dtype=np.uint8)
+    nan = np.isnan(v)
+    sub = (a < 2.0 ** -6) & ~nan
+    out[sub] = np.rint(a[sub] * 512.0).astype(np.uint8)          # subnormals (and 2^-6 on carry)
+    nrm = ~sub & ~nan
+    if nrm.any():
+        f, ex = np.frexp(a[nrm])                                  # a = f * 2^ex, f in [0.5, 1)
+        e = ex - 1
+        m = np.rint((2.0 * f - 1.0) * 8.0).astype(np.int64)
+        carry = m == 8
+        e = e + carry
+        m = np.where(carry, 0, m)
+        out[nrm] = (((e + 7) << 3) | m).astype(np.uint8)
+    out[nan] = 0x7F
+    return out | sign
+
+
+def e4m3_decode(codes: np.ndarray) -> np.ndarray:
+    """float8_e4m3fn bytes -> float32."""
+    c = np.asarray(codes, dtype=np.uint8).astype(np.int64)
+    s = np.where(c & 0x80, -1.0, 1.0)
+    e = (c >> 3) & 0xF
+    m = c & 0x7
+    val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * np.exp2(e - 7.0))
+    val = np.where((e == 15) & (m == 7), np.nan, val)
+    return (s * val).astype(np.float32)
+
+
+def quantize_fp8_ue8m0(x) -> tuple[np.ndarray, np.ndarray]:
+    """[M, K] float (bf16 / f32 torch tensor or numpy) -> (e4m3 codes u8 [M, K], UE8M0 u8
+    [M, K/32]); restates kernels/cutlass_experts.py:197-251 step by step."""
+    if isinstance(x, torch.Tensor):
+        x = x.float().numpy()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M, K = x.shape
+    assert K % MXFP_BLOCK == 0
+    xg = x.reshape(M, K // MXFP_BLOCK, MXFP_BLOCK)
+    amax = np.max(np.abs(xg), axis=-1)                                   # :220-221
+    ds = (amax / np.float32(FP8_MAX)).astype(np.float32)                 # :228
+    r = (ds.view(np.uint32) + np.uint32(0x007FFFFF)) & np.uint32(0x7F800000)   # :230-231
+    scale = r.view(np.float32)
+    scale = np.where(scale == 0, np.float32(1.1754944e-38), scale)       # :235-239
+    q = (xg / scale[..., None]).astype(np.float32)                       # :242
+    q = np.clip(q, -FP8_MAX, FP8_MAX)                                    # :244
+    codes = e4m3_encode(q.reshape(M, K))
+    sf = ((r >> 23) & 0xFF).astype(np.uint8)                             # :248
+    return codes, sf
+
+
+def fp8_dequant(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """e4m3 codes [M, K] x UE8M0 [M, K/32] -> float32 [M, K]."""
+    v = e4m3_decode(codes)
+    M, K = v.shape
+    s = np.exp2(scales.astype(np.float64) - 127.0).astype(np.float32)
+    return (v.reshape(M, K // 32, 32) * s[..., None]).reshape(M, K)
+
+
+def mxfp4_dequant(blocks: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """Packed E2M1 [N, K/2] (low nibble = even k) x UE8M0 [N, K/32] -> float32 [N, K]."""
+    b = np.asarray(blocks, dtype=np.uint8)
+    N = b.shape[0]
+    lo = E2M1_VALUES[b & 0xF]
+    hi = E2M1_VALUES[b >> 4]
+    v = np.stack([lo, hi], axis=-1).reshape(N, -1)
+    K = v.shape[1]
+    s = np.exp2(np.asarray(scales, dtype=np.float64)[:, : K // 32] - 127.0).astype(np.float32)
+    return (v.reshape(N, K // 32, 32) * s[..., None]).reshape(N, K)
+
+
+# --------------------------------------------------------------------------- layout
+def blocked_sf_offset(r, g, g4):
+    """Byte offset of scale (row r, k-group g) in one blocked buffer with g4 k-atoms
+    (CuTe Sm1xxBlockScaledConfig<32>::tile_atom_to_shape_SFA/SFB)."""
+    r = np.asarray(r, dtype=np.int64)
+    g = np.asarray(g, dtype=np.int64)
+    return (r // 128) * (g4 * 512) + (g // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + (g % 4)
+
+
+def blocked_sf_cosize(rows: int, groups: int) -> int:
+    return ((rows + 127) // 128) * ((groups + 3) // 4) * 512
+
+
+def convert_scales_blocked(scales_rowmajor: np.ndarray) -> np.ndarray:
+    """Row-major [rows, G] -> blocked flat buffer, zero filled
+    (convert_scales_w4a8_impl, kernels/matmul_mxfp4_cutlass.cu:666-749)."""
+    s = np.asarray(scales_rowmajor, dtype=np.uint8)
+    rows, G = s.shape
+    out = np.zeros(blocked_sf_cosize(rows, G), dtype=np.uint8)
+    r, g = np.meshgrid(np.arange(rows), np.arange(G), indexing="ij")
+    out[blocked_sf_offset(r, g, (G + 3) // 4)] = s
+    return out
+
+
+def batch_convert_a_scales(scales_rowmajor: np.ndarray, counts, offsets) -> tuple[np.ndarray, np.ndarray]:
+    """Per-expert blocked buffers laid end to end + int32 byte offsets
+    (batch_convert_a_scales_for_w4a8, kernels/matmul_mxfp4_cutlass.cu:763-873)."""
+    s = np.asarray(scales_rowmajor, dtype=np.uint8)
+    G = s.shape[1]
+    parts, sf = [], []
+    cur = 0
+    for m, o in zip(np.asarray(counts).tolist(), np.asarray(offsets).tolist()):
+        sf.append(cur)
+        if m == 0:
+            continue
+        blk = convert_scales_blocked(s[o:o + m])
+        parts.append(blk)
+        cur += blk.size
+    flat = np.concatenate(parts) if parts else np.zeros(0, dtype=np.uint8)
+    return flat, np.asarray(sf, dtype=np.int32)
+
+
+# --------------------------------------------------------------------------- routing
+def route_stable(router_indices, routing_weights, num_experts: int):
+    """Stable counting sort of the (token, k) assignments by expert
+    (benchmark_optimizations.py:170-187). Returns numpy arrays
+    (sorted_token i64, sorted_expert i64, sorted_weight f32, counts i32, offsets i32)."""
+    idx = np.asarray(router_indices, dtype=np.int64)
+    w = np.asarray(routing_weights, dtype=np.float32)
+    T, k = idx.shape
+    flat = idx.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    sorted_token = (order // k).astype(np.int64)
+    sorted_expert = flat[order]
+    sorted_weight = w.reshape(-1)[order]
+    counts = np.bincount(flat, minlength=num_experts).astype(np.int32)
+    offsets = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int32)
+    return sorted_token, sorted_expert, sorted_weight, counts, offsets
+
+
+def router_topk_hf(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, top_k: int):
+    """HF GptOssTopKRouter.forward on the CPU: bf16 F.linear, topk, softmax over the k
+    logits in bf16. Returns (logits bf16, scores bf16, indices i64)."""
+    logits = torch.nn.functional.linear(hidden, weight, bias)
+    top_v, top_i = torch.topk(logits, top_k, dim=-1)
+    scores = torch.nn.functional.softmax(top_v, dim=1, dtype=top_v.dtype)
+    return logits, scores, top_i
+
+
+def router_logits_fp32(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """Logits with fp32 accumulation, fp32 bias add and one rounding to bf16."""
+    acc = hidden.float() @ weight.float().T
+    return (acc + bias.float()).to(torch.bfloat16)
+
+
+# --------------------------------------------------------------------------- GEMM
+def group_mm_bf16(a_codes, a_scales_rm, w_blocks, w_scales_rm, counts, offsets, bias=None):
+    """Grouped W4A8 GEMM: rows [off_e, off_e + m_e) of A times expert e's weights,
+    bf16(fp32(A_deq) @ fp32(W_deq)^T); returns a bf16 torch tensor [rows, N]."""
+    A = torch.from_numpy(fp8_dequant(np.asarray(a_codes), np.asarray(a_scales_rm)))
+    rows = A.shape[0]
+    N = w_blocks.shape[1]
+    out = torch.zeros((rows, N), dtype=torch.bfloat16)
+    for e, (m, o) in enumerate(zip(np.asarray(counts).tolist(), np.asarray(offsets).tolist())):
+        if m == 0:
+            continue
+        W = torch.from_numpy(mxfp4_dequant(w_blocks[e], w_scales_rm[e]))
+        K = min(W.shape[1], A.shape[1])
+        out[o:o + m] = (A[o:o + m, :K] @ W[:, :K].T).to(torch.bfloat16)
+    return out
+
+
+def swiglu_fp32(gate_up: torch.Tensor, alpha: float = 1.702, limit: float = 7.0) -> torch.Tensor:
+    """kernels/cutlass_experts.py:272-276."""
+    gate = gate_up[..., ::2]
+    up = gate_up[..., 1::2]
+    gate = gate.clamp(max=limit)
+    up = up.clamp(min=-limit, max=limit)
+    return gate * torch.sigmoid(gate * alpha) * (up + 1)
+
+
+def w4a8_experts_forward(hidden: torch.Tensor, router_indices, routing_weights, w: dict,
+                         alpha: float = 1.702, limit: float = 7.0, return_intermediates: bool = False):
+    """CutlassGptOssExperts.forward (kernels/cutlass_experts.py:393-452) on the CPU with the
+    GEMM replaced by its exact dequantised semantics. `w` holds the row-major weights:
+    gu_blocks [E, 2I, H/2], gu_scales [E, 2I, H/32], gu_bias f32 [E, 2I],
+    dn_blocks [E, H, I/2], dn_scales [E, H, I/32], dn_bias f32 [E, H]."""
+    H = hidden.shape[-1]
+    h = hidden.reshape(-1, H)
+    T = h.shape[0]
+    E = w["gu_blocks"].shape[0]
+    idx = torch.as_tensor(np.asarray(router_indices)).long()
+    rw = torch.as_tensor(np.asarray(routing_weights, dtype=np.float32))
+    st, se, sw, counts, offsets = route_stable(idx.numpy(), rw.numpy(), E)            # :399-402
+    gathered = h[torch.from_numpy(st)]                                                  # :405
+    a_codes, a_sf = quantize_fp8_ue8m0(gathered)                                        # :408
+    gu = group_mm_bf16(a_codes, a_sf, w["gu_blocks"], w["gu_scales"], counts, offsets)  # :414-419
+    gu32 = gu + torch.as_tensor(w["gu_bias"]).float()[torch.from_numpy(se)]             # :422-423
+    inter = swiglu_fp32(gu32, alpha, limit)                                             # :424
+    i_codes, i_sf = quantize_fp8_ue8m0(inter)                                           # :427
+    dn = group_mm_bf16(i_codes, i_sf, w["dn_blocks"], w["dn_scales"], counts, offsets)  # :433-438
+    dn32 = dn + torch.as_tensor(w["dn_bias"]).float()[torch.from_numpy(se)]             # :441-442
+    dn32 = dn32 * torch.from_numpy(sw).unsqueeze(-1)                                    # :443
+    result = torch.zeros((T, H), dtype=hidden.dtype)                                    # :445
+    result.scatter_add_(0, torch.from_numpy(st).unsqueeze(-1).expand(-1, H), dn32.to(hidden.dtype))
+    out = result.view(hidden.shape)
+    if not return_intermediates:
+        return out
+    return out, dict(sorted_token=st, sorted_expert=se, sorted_weight=sw, counts=counts, offsets=offsets,
+                     act_codes=a_codes, act_scales=a_sf, gate_up=gu, inter=inter, inter_codes=i_codes,
+                     inter_scales=i_sf, down=dn)
+
+
+def dequant_fp32_reference(hidden: torch.Tensor, router_indices, routing_weights, w: dict,
+                           alpha: float = 1.702, limit: float = 7.0) -> torch.Tensor:
+    """The dequantised-weight reference of kernels/test_cutlass_experts.py:422-455, batched
+    by expert: x @ W_gu[e] (bf16 matmul) + b (f32) -> SwiGLU f32 -> bf16 -> @ W_dn[e] (bf16)
+    + b (f32), and out[t] += bf16(w * down) in the (token, k) order of the loop."""
+    H = hidden.shape[-1]
+    h = hidden.reshape(-1, H)
+    T = h.shape[0]
+    idx = np.asarray(router_indices, dtype=np.int64)
+    rw = np.asarray(routing_weights, dtype=np.float32)
+    k = idx.shape[1]
+    E = w["gu_blocks"].shape[0]
+    contrib = torch.zeros((T, k, H), dtype=torch.bfloat16)
+    for e in range(E):
+        sel = np.argwhere(idx == e)
+        if sel.size == 0:
+            continue
+        tok, kk = sel[:, 0], sel[:, 1]
+        Wg = torch.from_numpy(mxfp4_dequant(w["gu_blocks"][e], w["gu_scales"][e])).to(torch.bfloat16)  # [2I, H]
+        Wd = torch.from_numpy(mxfp4_dequant(w["dn_blocks"][e], w["dn_scales"][e])).to(torch.bfloat16)  # [H, I]
+        x = h[torch.from_numpy(tok)]
+        gate_up = (x @ Wg[:, :H].T) + torch.as_tensor(w["gu_bias"][e]).float()
+        gate = gate_up[:, ::2].clamp(max=limit)
+        up = gate_up[:, 1::2].clamp(min=-limit, max=limit)
+        inter = (gate * torch.sigmoid(gate * alpha) * (up + 1)).to(torch.bfloat16)
+        down = (inter @ Wd[:, : inter.shape[1]].T) + torch.as_tensor(w["dn_bias"][e]).float()
+        wt = torch.from_numpy(rw[tok, kk]).unsqueeze(-1)
+        contrib[torch.from_numpy(tok), torch.from_numpy(kk)] = (wt * down).to(torch.bfloat16)
+    out = torch.zeros((T, H), dtype=torch.bfloat16)
+    for j in range(k):
+        out += contrib[:, j]
+    return out.view(hidden.shape)
+
+
+# --------------------------------------------------------------------------- inputs
+def synth_router_bias(kind: str, E: int) -> torch.Tensor:
+    """Extra per-expert router bias for the skewed configs (added before the bf16 cast).
+    'prefill': a fixed linear spread so loads vary about +-50% around the mean.
+    'zipf': 1.5 * log of a Zipf(s=1.1) pmf over experts (some experts get no tokens)."""
+    if kind == "prefill":
+        perm = torch.randperm(E, generator=torch.Generator().manual_seed(1234))
+        lin = torch.linspace(-1.0, 1.0, E)[perm]
+        return 0.33 * lin
+    if kind == "zipf":
+        ranks = torch.arange(1, E + 1, dtype=torch.float64)
+        pmf = ranks ** -1.1
+        pmf = pmf / pmf.sum()
+        perm = torch.randperm(E, generator=torch.Generator().manual_seed(4321))
+        return (1.5 * torch.log(pmf)).float()[perm]
+    raise ValueError(kind)
+
+
+def synth_layer(seed: int, E: int = 32, H: int = 2880, I: int = 2880, T: int = 32, skew: str | None = None,
+                with_hidden: bool = True) -> dict:
+    """Seeded synthetic GPT-OSS MoE layer: one CPU generator, fixed draw order:
+    router W [E,H] N(0,0.02) bf16, router b [E] N(0,0.01) bf16, gate_up blocks
+    [E,2I,H/2] u8 uniform, gate_up scales [E,2I,H/32] in [119,123], gate_up bias [E,2I]
+    N(0,0.01) (bf16 values, kept f32), down blocks [E,H,I/2], down scales [E,H,I/32],
+    down bias [E,H], hidden [T,H] N(0,1) bf16."""
+    g = torch.Generator().manual_seed(seed)
+    d = {}
+    d["router_w"] = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    rb = torch.randn(E, generator=g) * 0.01
+    if skew is not None:
+        rb = rb + synth_router_bias(skew, E)
+    d["router_b"] = rb.to(torch.bfloat16)
+    d["gu_blocks"] = torch.randint(0, 256, (E, 2 * I, H // 2), generator=g, dtype=torch.uint8)
+    d["gu_scales"] = torch.randint(119, 124, (E, 2 * I, H // 32), generator=g, dtype=torch.uint8)
+    d["gu_bias"] = (torch.randn(E, 2 * I, generator=g) * 0.01).to(torch.bfloat16).float()
+    d["dn_blocks"] = torch.randint(0, 256, (E, H, I // 2), generator=g, dtype=torch.uint8)
+    d["dn_scales"] = torch.randint(119, 124, (E, H, I // 32), generator=g, dtype=torch.uint8)
+    d["dn_bias"] = (torch.randn(E, H, generator=g) * 0.01).to(torch.bfloat16).float()
+    if with_hidden:
+        d["hidden"] = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    return d
+
+
+def numpy_weights(d: dict) -> dict:
+    """The numpy views group_mm_bf16 / w4a8_experts_forward take."""
+    return {k: (v.numpy() if isinstance(v, torch.Tensor) and v.dtype != torch.bfloat16 else v)
+            for k, v in d.items()}
+
+
+__all__.append("numpy_weights")
+_ = math

@@ -1,0 +1,67 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the header
+declares, answers host-only size queries and rejects bad arguments before touching a
+device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "gptoss_moe.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gptoss_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for must in ("gptoss_fused_moe_routing", "gptoss_fp4_group_mm", "gptoss_moe_experts_forward",
+                 "gptoss_moe_layer_forward", "gptoss_quantize_fp8", "gptoss_router_topk", "gptoss_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in gptoss_moe.h but not exported"
+        assert name in pkg._lib._SIGNATURES, f"{name} has no ctypes signature"
+    raw = ctypes.CDLL(pkg._lib.lib_path())
+    for name in _declared():
+        getattr(raw, name)
+
+
+def test_abi_version(pkg):
+    assert pkg._lib.load().gptoss_abi_version() == pkg._lib.ABI_VERSION
+
+
+def test_host_size_queries(pkg):
+    q = pkg._lib.query
+    assert q("gptoss_blocked_scales_bytes", 2880, 2944) == 270848
+    assert q("gptoss_blocked_scales_bytes", 5760, 2944) == 529920
+    assert q("gptoss_blocked_scales_bytes", 0, 2944) == 0
+    assert q("gptoss_batch_blocked_scales_capacity", 128, 32, 2944) >= 33 * 23 * 512
+    w1 = q("gptoss_moe_workspace_bytes", 32, 4, 32, 2880, 2880)
+    w2 = q("gptoss_moe_workspace_bytes", 8192, 4, 32, 2880, 2880)
+    assert 0 < w1 < w2
+    assert q("gptoss_moe_workspace_bytes", -1, 4, 32, 2880, 2880) == 0
+
+
+def test_argument_errors_before_device_access(pkg):
+    lib = pkg._lib.load()
+    rc = lib.gptoss_quantize_fp8(None, 0, 4, 31, None, None, None)
+    assert rc == 1 and b"multiple of 32" in lib.gptoss_last_error()
+    rc = lib.gptoss_fp4_group_mm(None, None, 4, 512, None, 1, 256, 500, None, None, 0, None, None, None, None, 0,
+                                 None, None)
+    assert rc == 1 and b"multiple of 128" in lib.gptoss_last_error()
+    rc = lib.gptoss_moe_experts_forward(None, None, None, 4, 9, 4, 512, 256, None, None, 0, None, None, None, 0,
+                                        None, 1.702, 7.0, None, None, 0, 0, None, None)
+    assert rc == 1 and b"top_k" in lib.gptoss_last_error()
+
+
+def test_wrapper_raises_on_failure(pkg):
+    with pytest.raises(pkg._lib.GptossError, match="multiple of 32"):
+        pkg._lib.call("gptoss_quantize_fp8", None, 0, 4, 31, None, None, None)
