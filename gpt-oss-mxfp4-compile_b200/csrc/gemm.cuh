@@ -12,7 +12,7 @@
 //
 // Two orientations:
 //   SWAP = false  M = 128 activation rows, N = 192 weight rows (prefill-sized groups).
-//   SWAP = true   M = 128 weight rows,     N = 32 activation rows (decode: the weights
+//   SWAP = true   M = 128 weight rows,     N = 64 activation rows (decode: the weights
 //                 stream through the M side so a group of ~4 rows wastes little MMA).
 //
 // Epilogues (all restate cutlass_experts.py:414-450 for the rows a tile owns):
@@ -65,10 +65,13 @@ struct GemmParams {
 template <bool SWAP>
 struct GemmConfig {
   static constexpr int kWgtRows = SWAP ? 128 : 192;   // weight rows per tile
-  static constexpr int kActRows = SWAP ? 32 : 128;    // activation rows per tile
+  // Activation rows per tile. In SWAP mode a chunk starts 0 or 64 rows into its 128-row
+  // scale block, so the scale TMEM address moves by 0 or 2 columns (the same even
+  // offsets CUTLASS uses for its N=64 / N=192 tiles).
+  static constexpr int kActRows = SWAP ? 64 : 128;
   static constexpr int kMmaM = 128;
   static constexpr int kMmaN = SWAP ? kActRows : kWgtRows;
-  static constexpr int kStages = SWAP ? 10 : 5;
+  static constexpr int kStages = SWAP ? 8 : 5;
   static constexpr int kAccBufs = SWAP ? 4 : 2;
   static constexpr int kAccCols = kMmaN;              // fp32 columns per accumulator
   static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
@@ -272,8 +275,7 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = mbar_wait(accf_bar(b), acc_phase, p.err, kDevTimeoutEpilogue);
       if (!ok) {
         if constexpr (SWAP && EPI == kEpiGemm1) {
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          for (int c = 0; c < 2 * (C::kActRows / 32); ++c) asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         continue;
       }
@@ -383,84 +385,97 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       } else {
-        // thread <-> weight row (output feature); 32 columns = 32 activation rows
+        // thread <-> weight row (output feature); column j = activation row ch*64 + j,
+        // walked in two 32-column halves.
         const int wrow_i = nt * C::kWgtRows + 32 * q + lane;    // weight row / feature
         const bool vcol = wrow_i < p.N;
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(t_acc, r);
-        tmem_ld_wait();
-        const int a0 = ch * C::kActRows;                        // first row inside expert
-        if constexpr (EPI == kEpiPlain) {
-          const float alpha = p.alphas ? p.alphas[e] : 1.0f;
-          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (vcol && a0 + j < m_e)
-              o[(static_cast<int64_t>(row0) + a0 + j) * p.ld_out + wrow_i] =
-                  __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
+        const float bsv = (EPI != kEpiPlain && vcol) ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < C::kActRows / 32; ++c) {
+          const int a0 = ch * C::kActRows + c * 32;             // first row inside expert
+          const bool live = a0 < m_e;                           // uniform over the CTA
+          uint32_t r[32];
+          if (live) {
+            __syncwarp();
+            tmem_ld_32x32b_x32(t_acc + c * 32, r);
+            tmem_ld_wait();
           }
-        } else if constexpr (EPI == kEpiGemm2) {
-          const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
-          __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+          if constexpr (EPI == kEpiPlain) {
+            if (live) {
+              const float alpha = p.alphas ? p.alphas[e] : 1.0f;
+              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (vcol && a0 + j < m_e)
+                  o[(static_cast<int64_t>(row0) + a0 + j) * p.ld_out + wrow_i] =
+                      __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
+              }
+            }
+          } else if constexpr (EPI == kEpiGemm2) {
+            if (live) {
+              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 4
-          for (int j = 0; j < 32; ++j) {
-            const bool vr = a0 + j < m_e;                       // warp-uniform
-            if (!vr) break;
-            const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
-            const int64_t tok = p.token_idx[grow];
-            const float wr = p.row_weights[grow];
-            const float y = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[j])), bsv), wr);
-            const float yo = __shfl_xor_sync(0xffffffffu, y, 1);
-            if ((lane & 1) == 0 && vcol) {
-              __nv_bfloat16* dst = o + tok * p.ld_out + wrow_i;
-              if (wrow_i + 1 < p.N) atomicAdd(reinterpret_cast<__nv_bfloat162*>(dst), __floats2bfloat162_rn(y, yo));
-              else atomicAdd(dst, __float2bfloat16_rn(y));
+              for (int j = 0; j < 32; ++j) {
+                if (a0 + j >= m_e) break;                       // warp-uniform
+                const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
+                const int64_t tok = p.token_idx[grow];
+                const float wr = p.row_weights[grow];
+                const float y = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[j])), bsv), wr);
+                const float yo = __shfl_xor_sync(0xffffffffu, y, 1);
+                if ((lane & 1) == 0 && vcol) {
+                  __nv_bfloat16* dst = o + tok * p.ld_out + wrow_i;
+                  if (wrow_i + 1 < p.N) atomicAdd(reinterpret_cast<__nv_bfloat162*>(dst), __floats2bfloat162_rn(y, yo));
+                  else atomicAdd(dst, __float2bfloat16_rn(y));
+                }
+              }
             }
-          }
-        } else {  // kEpiGemm1: lanes (2f, 2f+1) hold gate / up of feature f
-          const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
-          const int f = wrow_i >> 1;                            // intermediate feature
-          const int grp = f >> 5;                               // quant group (2 warps)
-          float hv[32];
+          } else {  // kEpiGemm1: lanes (2f, 2f+1) hold gate / up of feature f
+            const int f = wrow_i >> 1;                          // intermediate feature
+            const int grp = f >> 5;                             // quant group (2 warps)
+            float hv[32];
+            if (live) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float v = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
-            const float up = __shfl_xor_sync(0xffffffffu, v, 1);
-            hv[j] = swiglu_pair(v, up, p.swiglu_alpha, p.swiglu_limit);   // valid on even lanes
-          }
-          // group absmax over the 32 features held by the even lanes of warps (q, q^1)
+              for (int j = 0; j < 32; ++j) {
+                const float v = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
+                const float up = __shfl_xor_sync(0xffffffffu, v, 1);
+                hv[j] = swiglu_pair(v, up, p.swiglu_alpha, p.swiglu_limit);   // valid on even lanes
+              }
+              // group absmax over the 32 features held by the even lanes of warps (q, q^1)
 #pragma unroll 1
-          for (int j = 0; j < 32; ++j) {
-            float a = (lane & 1) == 0 ? fabsf(hv[j]) : 0.0f;
-            if (hv[j] != hv[j] && (lane & 1) == 0) a = hv[j];
+              for (int j = 0; j < 32; ++j) {
+                float a = (lane & 1) == 0 ? fabsf(hv[j]) : 0.0f;
+                if (hv[j] != hv[j] && (lane & 1) == 0) a = hv[j];
 #pragma unroll
-            for (int o2 = 2; o2 < 32; o2 <<= 1) {
-              const float ob = __shfl_xor_sync(0xffffffffu, a, o2);
-              a = (ob > a || ob != ob) ? ob : a;
+                for (int o2 = 2; o2 < 32; o2 <<= 1) {
+                  const float ob = __shfl_xor_sync(0xffffffffu, a, o2);
+                  a = (ob > a || ob != ob) ? ob : a;
+                }
+                if (lane == 0) s_amax[q][j] = a;
+              }
             }
-            if (lane == 0) s_amax[q][j] = a;
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          const int qp = q ^ 1;
-          uint8_t* codes_out = static_cast<uint8_t*>(p.out);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (live) {
+              const int qp = q ^ 1;
+              uint8_t* codes_out = static_cast<uint8_t*>(p.out);
 #pragma unroll 1
-          for (int j = 0; j < 32; ++j) {
-            if (a0 + j >= m_e) break;
-            const float a_self = s_amax[q][j], a_pair = s_amax[qp][j];
-            const float amax = (a_pair > a_self || a_pair != a_pair) ? a_pair : a_self;
-            const uint32_t rb = ue8m0_rounded_bits(amax);
-            const float scale = scale_from_bits(rb);
-            const float qv = clamp_fp8(__fdiv_rn(hv[j], scale));
-            const uint16_t c2 = cvt_e4m3x2(qv, 0.0f);
-            const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
-            if ((lane & 1) == 0 && vcol && f < p.out_features)
-              codes_out[grow * p.ld_out + f] = static_cast<uint8_t>(c2 & 0xFFu);
-            if (lane == 0 && (q & 1) == 0 && f < p.out_features)
-              p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(a0 + j, grp, p.out_g4)] =
-                  static_cast<uint8_t>((rb >> 23) & 0xFFu);
+              for (int j = 0; j < 32; ++j) {
+                if (a0 + j >= m_e) break;
+                const float a_self = s_amax[q][j], a_pair = s_amax[qp][j];
+                const float amax = (a_pair > a_self || a_pair != a_pair) ? a_pair : a_self;
+                const uint32_t rb = ue8m0_rounded_bits(amax);
+                const float scale = scale_from_bits(rb);
+                const float qv = clamp_fp8(__fdiv_rn(hv[j], scale));
+                const uint16_t c2 = cvt_e4m3x2(qv, 0.0f);
+                const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
+                if ((lane & 1) == 0 && vcol && f < p.out_features)
+                  codes_out[grow * p.ld_out + f] = static_cast<uint8_t>(c2 & 0xFFu);
+                if (lane == 0 && (q & 1) == 0 && f < p.out_features)
+                  p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(a0 + j, grp, p.out_g4)] =
+                      static_cast<uint8_t>((rb >> 23) & 0xFFu);
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
         }
       }
       tc_fence_before();
@@ -471,6 +486,7 @@ __global__ void __launch_bounds__(192, 1)
 
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
   }

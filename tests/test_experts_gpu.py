@@ -1,0 +1,171 @@
+"""CutlassGptOssExperts drop-in parity (kernels/test_cutlass_experts.py tests 5-9 and the
+north-star output gate) against the reference's own outputs (tests/golden) and the
+oracle, in both GEMM orientations."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from golden import make_golden as MG
+from helpers import Cfg, assert_output_tolerance, bf16_from_int16, build_experts, golden, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+MODES = {"auto": 0, "tokens_m": 1, "swap": 2}
+
+
+@pytest.mark.parametrize("mode", list(MODES))
+@pytest.mark.parametrize("name", ["small", "kpad", "decode", "cpu_ref"])
+def test_forward_matches_reference_golden(pkg, dev, name, mode):
+    seed, E, H, I, T, k = MG.LAYERS[name]
+    g = golden(f"layer_{name}.npz")
+    d, idx, w = MG.layer_inputs(name)
+    m = build_experts(pkg, d, dev, E, H, I)
+    m.gemm_mode = MODES[mode]
+    out = m(d["hidden"].to(dev), idx.to(dev), w.to(dev))
+    torch.cuda.synchronize()
+    assert pkg.ops.read_status(dev) == 0
+    ref = bf16_from_int16(g["out"])
+    r, mx = assert_output_tolerance(out.cpu(), ref, f"{name}/{mode}")
+    print(f"{name}/{mode}: rel-L2 {r:.2e} max-abs/rms {mx:.2e}")
+
+
+def test_first_stage_codes_bit_exact(pkg, dev):
+    # routing permutation + gather + FP8 quantisation reproduce the reference's GEMM1
+    # input bytes exactly (sha256 of the codes and scales the reference produced).
+    import hashlib
+    for name in ("small", "decode", "cpu_ref"):
+        g = golden(f"layer_{name}.npz")
+        d, idx, w = MG.layer_inputs(name)
+        E = MG.LAYERS[name][1]
+        st, se, sw, counts, offsets = pkg.get_cutlass_extension().fused_moe_routing(idx.to(dev), w.to(dev), E)
+        q, s = pkg.quantize_activations_to_fp8(d["hidden"].to(dev)[st])
+        assert hashlib.sha256(q.view(torch.uint8).cpu().numpy().tobytes()).hexdigest() == bytes(g["act_codes_sha"]).decode()
+        assert hashlib.sha256(s.cpu().numpy().tobytes()).hexdigest() == bytes(g["act_scales_sha"]).decode()
+        assert np.array_equal(counts.cpu().numpy(), g["counts"])
+
+
+def test_vs_dequantized_fp32_reference(pkg, dev):
+    # Test 5 (kernels/test_cutlass_experts.py:336-471): W4A8 vs dequantised weights,
+    # mean-abs rel < 0.15; the W4A8 error itself comes from FP8 activations, so ours must
+    # sit as close to the dequantised reference as the reference's W4A8 path does.
+    d, idx, w = MG.layer_inputs("small")
+    seed, E, H, I, T, k = MG.LAYERS["small"]
+    m = build_experts(pkg, d, dev, E, H, I)
+    out = m(d["hidden"].to(dev), idx.to(dev), w.to(dev)).cpu()
+    wn = O.numpy_weights(d)
+    deq = O.dequant_fp32_reference(d["hidden"], idx.numpy(), w.numpy(), wn)
+    w4a8 = O.w4a8_experts_forward(d["hidden"], idx.numpy(), w.numpy(), wn)
+    ours = ((out.float() - deq.float()).abs().mean() / deq.float().abs().mean()).item()
+    theirs = ((w4a8.float() - deq.float()).abs().mean() / deq.float().abs().mean()).item()
+    assert ours < 0.15 and abs(ours - theirs) < 0.1 * theirs, (ours, theirs)
+
+
+def _module(pkg, dev, E=4, H=512, I=256, seed=42):
+    d = O.synth_layer(seed, E=E, H=H, I=I, T=1)
+    return build_experts(pkg, d, dev, E, H, I), d
+
+
+def test_edge_cases(pkg, dev):
+    # Test 7 (kernels/test_cutlass_experts.py:545-626) + oracle parity.
+    m, d = _module(pkg, dev)
+    wn = O.numpy_weights(d)
+    g = torch.Generator().manual_seed(1)
+    cases = []
+    cases.append((torch.randn(1, 512, generator=g) * 0.1, torch.tensor([[0, 2]]), torch.tensor([[0.6, 0.4]])))
+    idx = torch.zeros(32, 2, dtype=torch.int64)
+    idx[:, 1] = 1
+    cases.append((torch.randn(32, 512, generator=g) * 0.1, idx, torch.full((32, 2), 0.5)))
+    lg = torch.randn(256, 4, generator=g)
+    wv, ix = torch.topk(lg, 2, dim=-1)
+    cases.append((torch.randn(256, 512, generator=g) * 0.1, ix, torch.softmax(wv, dim=-1)))
+    for h, ix, wv in cases:
+        h = h.to(torch.bfloat16)
+        out = m(h.to(dev), ix.to(dev), wv.to(dev))
+        assert out.shape == h.shape and not torch.isnan(out).any()
+        ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
+        assert_output_tolerance(out.cpu(), ref, f"T={h.shape[0]}")
+
+
+def test_3d_input_equals_2d(pkg, dev):
+    # Test 8 (kernels/test_cutlass_experts.py:633-697)
+    m, d = _module(pkg, dev)
+    g = torch.Generator().manual_seed(123)
+    h3 = (torch.randn(2, 16, 512, generator=g) * 0.1).to(torch.bfloat16).to(dev)
+    wv, ix = torch.topk(torch.randn(32, 4, generator=g), 2, dim=-1)
+    wv = torch.softmax(wv, -1).to(dev)
+    ix = ix.to(dev)
+    o3 = m(h3, ix, wv)
+    o2 = m(h3.reshape(32, 512), ix, wv)
+    assert o3.shape == (2, 16, 512) and o2.shape == (32, 512)
+    # the bf16 combine adds up to k values per element with atomics: order-free to 1 ulp
+    assert (o3.reshape(32, 512).float() - o2.float()).abs().max().item() <= 2 ** -7 * o2.float().abs().max().item()
+
+
+def test_k_padding(pkg, dev):
+    # Test 9 (kernels/test_cutlass_experts.py:704-782): H = I = 288 -> K padded to 384
+    m, d = _module(pkg, dev, E=4, H=288, I=288)
+    assert m.K_hidden_padded == 384 and m.K_inter_padded == 384
+    assert m.gate_up_proj_data.shape == (4, 576, 192) and m.down_proj_data.shape == (4, 288, 192)
+    g = torch.Generator().manual_seed(123)
+    h = (torch.randn(32, 288, generator=g) * 0.1).to(torch.bfloat16)
+    wv, ix = torch.topk(torch.randn(32, 4, generator=g), 2, dim=-1)
+    wv = torch.softmax(wv, -1)
+    out = m(h.to(dev), ix.to(dev), wv.to(dev))
+    assert not torch.isnan(out).any() and not torch.isinf(out).any()
+    ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), O.numpy_weights(d))
+    assert_output_tolerance(out.cpu(), ref, "kpad")
+
+
+def test_scale_buffers_have_reference_shapes(pkg, dev):
+    m, d = _module(pkg, dev, E=2, H=2880, I=2880, seed=3)
+    assert m.gate_up_proj_data.shape == (2, 5760, 1472) and m.gate_up_proj_scales.shape == (2, 529920)
+    assert m.down_proj_data.shape == (2, 2880, 1472) and m.down_proj_scales.shape == (2, 270848)
+    # weight scales equal the oracle's blocked conversion of the zero-padded row-major scales
+    sc = np.pad(d["dn_scales"][1].numpy(), ((0, 0), (0, 2)))
+    assert np.array_equal(m.down_proj_scales[1].cpu().numpy(), O.convert_scales_blocked(sc))
+
+
+def test_torch_compile_fullgraph(pkg, dev):
+    # Test 6 (kernels/test_cutlass_experts.py:474-538), but with fullgraph=True: every
+    # step is a custom op with a fake kernel and no host sync.
+    m, d = _module(pkg, dev)
+    g = torch.Generator().manual_seed(5)
+    h = (torch.randn(64, 512, generator=g) * 0.1).to(torch.bfloat16).to(dev)
+    wv, ix = torch.topk(torch.randn(64, 4, generator=g), 2, dim=-1)
+    wv, ix = torch.softmax(wv, -1).to(dev), ix.to(dev)
+    eager = m(h, ix, wv)
+    compiled = torch.compile(m, fullgraph=True)(h, ix, wv)
+    assert (eager.float() - compiled.float()).abs().max().item() < 0.01 * eager.float().abs().max().item() + 1e-3
+
+
+def test_cuda_graph_capture(pkg, dev):
+    m, d = _module(pkg, dev)
+    g = torch.Generator().manual_seed(6)
+    h = (torch.randn(16, 512, generator=g) * 0.1).to(torch.bfloat16).to(dev)
+    wv, ix = torch.topk(torch.randn(16, 4, generator=g), 2, dim=-1)
+    wv, ix = torch.softmax(wv, -1).to(dev), ix.to(dev)
+    eager = m(h, ix, wv)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        m(h, ix, wv)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = m(h, ix, wv)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert rel_l2(out, eager) < 1e-2
+    del graph
+
+
+def test_empty_batch(pkg, dev):
+    m, d = _module(pkg, dev)
+    out = m(torch.empty(0, 512, dtype=torch.bfloat16, device=dev), torch.empty(0, 2, dtype=torch.int64, device=dev),
+            torch.empty(0, 2, device=dev))
+    assert out.shape == (0, 512)
+
+
+def test_cfg_roundtrip():
+    assert Cfg(4, 8, 8).num_local_experts == 4
