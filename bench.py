@@ -1,0 +1,352 @@
+#!/usr/bin/env python
+"""GPT-OSS-20B MoE layer benchmark on B200 (router + W4A8 experts, one step = one layer
+forward over one batch of synthetic tokens).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config decode|prefill]
+  python bench.py --impl reference ...     CPU baseline arm (rank 0 only)
+
+Workload at N=1 is BASELINE config 1 (decode, T=32 tokens, E=32, H=I=2880, top-4,
+seeded synthetic weights/inputs). Under torchrun every rank runs its own batch of T
+tokens on its own GPU (weak scaling); the reported value is the whole-job tokens/s
+over the max-over-ranks device time.
+
+Timing: W warm-up steps, then exactly K steps, each bracketed by CUDA events on the
+launching stream; before every timed step a 256 MiB buffer is written to flush L2
+(outside the events). Barrier + synchronize on both sides of the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "GPT-OSS-20B MoE layer tokens/s; %HBM roofline (decode), %MMA peak (prefill)"
+
+CONFIGS = {
+    # name: (T, E, H, I, top_k, skew, description)
+    "decode": (32, 32, 2880, 2880, 4, None, "GPT-OSS-20B MoE layer decode, T=32 (BASELINE config 1)"),
+    "prefill": (8192, 32, 2880, 2880, 4, "prefill", "GPT-OSS-20B MoE layer prefill, T=8192, loads +-50% (BASELINE config 2)"),
+}
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from
+# the ncu capture summarised in profiles/ (None until captured for this kernel/config).
+NCU_TRAFFIC_BYTES = {"decode": None, "prefill": None}
+
+KERNELS_PER_STEP = 5   # router, route_sort, gather_quant, gemm1, gemm2
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=list(CONFIGS), default="decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=45.0)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def alg_bytes(counts, T, k, H, I):
+    """Algorithmic HBM bytes of one layer step (unpadded K): weights + scales + fp32
+    biases of every touched expert, router weights, activations in/out and the FP8
+    intermediates written and read once."""
+    touched = sum(1 for c in counts if c > 0)
+    A = T * k
+    gu = touched * (2 * I * (H // 2) + 2 * I * (H // 32) + 2 * I * 4)
+    dn = touched * (H * (I // 2) + H * (I // 32) + H * 4)
+    act = A * H + A * (H // 32)           # FP8 rows + scales (GEMM1 A operand)
+    inter = A * I + A * (I // 32)         # FP8 intermediate (written by GEMM1, read by GEMM2)
+    g1 = gu + act + inter
+    g2 = dn + inter + 2 * T * H           # output rows (read-modify-write counted once)
+    layer = g1 + g2 + 32 * H * 2 + 2 * T * H
+    return g1, g2, layer, touched
+
+
+def clock_sampler_start(dev_index: int):
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    try:
+        return subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100",
+                                 "-i", str(dev_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except Exception:
+        return None
+
+
+def clock_sampler_stop(proc):
+    if proc is None:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    time.sleep(0.25)
+    proc.terminate()
+    try:
+        out, _ = proc.communicate(timeout=5)
+    except Exception:
+        proc.kill()
+        out = ""
+    sm, mx, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in out.strip().splitlines():
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx.append(float(f[2]))
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower().startswith("active"):
+                reasons.add(n)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def cpu_baseline(cfg_name: str, steps_cap: int, budget_s: float):
+    """The reference's dequantised PyTorch CPU path (oracle.DequantCPULayer) on the host
+    cores, bounded to ~budget_s of work."""
+    import torch
+    import oracle as O
+    T, E, H, I, k, skew, _ = CONFIGS[cfg_name]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    d = O.synth_layer(0, E=E, H=H, I=I, T=T, skew=skew)
+    t0 = time.perf_counter()
+    layer = O.DequantCPULayer(d, top_k=k)
+    dequant_s = time.perf_counter() - t0
+    h = d["hidden"]
+    tw = time.perf_counter()
+    layer(h)                                     # warm-up
+    step_est = max(time.perf_counter() - tw, 1e-3)
+    n = max(1, min(steps_cap, int(budget_s / step_est)))
+    times = []
+    for _ in range(n):
+        t = time.perf_counter()
+        layer(h)
+        times.append(time.perf_counter() - t)
+    per = statistics.median(times)
+    return {"value": T / per, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} full {cfg_name} steps (T={T}) of the dequantised bf16 expert path + HF router, "
+                      f"median {per * 1e3:.1f} ms/step; weights dequantised once beforehand ({dequant_s:.1f} s)",
+            "ms_per_step": per * 1e3, "steps_run": n}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    T = CONFIGS[args.config][0]
+    cb = cpu_baseline(args.config, max(1, args.steps), args.cpu_budget_s)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": cb["steps_run"], "warmup": 1, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (dequantised weights), fp32 accumulate",
+            "data": "synthetic (seeded, SURVEY 8(d) recipe)",
+            "config": {"workload": CONFIGS[args.config][6], "T": T, "world_size": world,
+                       "note": "CPU arm runs on rank 0 only"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    import oracle as O
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pkg = ge.load_package()
+    pkg.ensure_custom_op_registered()
+    T, E, H, I, k, skew, desc = CONFIGS[args.config]
+
+    class Cfg:
+        num_local_experts = E
+        hidden_size = H
+        intermediate_size = I
+        num_experts_per_tok = k
+        swiglu_limit = 7.0
+
+    d = O.synth_layer(rank, E=E, H=H, I=I, T=T, skew=skew)
+    layer = pkg.GptOssMoELayer(Cfg()).to(dev)
+    layer.router_weight.data.copy_(d["router_w"])
+    layer.router_bias.data.copy_(d["router_b"])
+    ex = layer.experts
+    ex.gate_up_proj_bias.data.copy_(d["gu_bias"])
+    ex.down_proj_bias.data.copy_(d["dn_bias"])
+    pkg.load_cutlass_weights(ex, d["gu_blocks"], d["gu_scales"], d["dn_blocks"], d["dn_scales"], dev)
+    x = d["hidden"].to(dev)
+    del d
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step():
+        return layer(x)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert pkg.ops.read_status(dev) == 0
+
+    # ---------------------------------------------------------------- headline
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler = clock_sampler_start(dev.index)
+    time.sleep(0.3)
+    for i in range(K):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = clock_sampler_stop(sampler)
+    barrier()
+    ms = sum(s.elapsed_time(e) for s, e in ev) / K
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = T * world / (ms / 1e3)
+
+    # ---------------------------------------------------------------- per-stage (roofline)
+    ws = pkg.ops.ExpertsWorkspace(T, k, E, H, I, dev)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    Ks = min(K, 500)
+    g1_ms, g2_ms, pre_ms = [], [], []
+    for i in range(Ks + 3):
+        flush.zero_()
+        e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+        e0.record(stream)
+        _, sc, ix = layer.route(x)
+        pkg.ops.route_quant(ws, x, ix, sc.float())
+        out.zero_()
+        e1.record(stream)
+        pkg.ops.gemm1(ws, ex.gate_up_proj_data, ex.gate_up_proj_scales, ex.gate_up_proj_bias.data)
+        e2.record(stream)
+        pkg.ops.gemm2(ws, ex.down_proj_data, ex.down_proj_scales, ex.down_proj_bias.data, out)
+        e3.record(stream)
+        if i >= 3:
+            pre_ms.append((e0, e1))
+            g1_ms.append((e1, e2))
+            g2_ms.append((e2, e3))
+    torch.cuda.synchronize(dev)
+    t_pre = statistics.mean(a.elapsed_time(b) for a, b in pre_ms)
+    t_g1 = statistics.mean(a.elapsed_time(b) for a, b in g1_ms)
+    t_g2 = statistics.mean(a.elapsed_time(b) for a, b in g2_ms)
+    counts = ws.counts.cpu().tolist()
+    b_g1, b_g2, b_layer, touched = alg_bytes(counts, T, k, H, I)
+    hbm_peak, bf16_peak, peak_kind = measured_peaks()
+    g1_gbs = b_g1 / (t_g1 / 1e3) / 1e9
+    layer_gbs = b_layer / (ms / 1e3) / 1e9
+    flops = 2 * T * k * (H * 2 * I + I * H)
+
+    # ---------------------------------------------------------------- end to end
+    xh = d_host = x.cpu().pin_memory()
+    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    Ke = min(K, 500)
+    e2e_t = []
+    for i in range(Ke + 3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        flush.zero_()
+        a.record(stream)
+        xd.copy_(xh, non_blocking=True)
+        y, _, _ = layer(xd)
+        oh.copy_(y, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if i >= 3:
+            e2e_t.append(a.elapsed_time(b))
+    e2e_ms = statistics.mean(e2e_t)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    assert pkg.ops.read_status(dev) == 0
+    del d_host
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args.config, 1000, args.cpu_budget_s)
+        cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        traffic = NCU_TRAFFIC_BYTES.get(args.config)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8 e4m3 x fp4 e2m1 (UE8M0 1x32 scales), fp32 accumulate",
+            "data": "synthetic (seeded: random MXFP4 weights, N(0,1) bf16 hidden)",
+            "config": {"workload": desc, "T": T, "E": E, "hidden": H, "intermediate": I, "top_k": k,
+                       "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                       "l2": "256 MiB written before every timed step (outside the events); weights 424 MB > L2",
+                       "experts_touched": touched},
+            "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel (GEMM1 gate_up + SwiGLU + requant)",
+                         "achieved": g1_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": g1_gbs / hbm_peak,
+                         "traffic": traffic, "peak_kind": peak_kind, "alg_bytes_per_launch": b_g1,
+                         "ms_per_launch": t_g1},
+            "layer_hbm": {"alg_bytes": b_layer, "achieved_gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
+                          "stage_ms": {"router+route+quant": t_pre, "gemm1": t_g1, "gemm2": t_g2},
+                          "gemm2_gbs": b_g2 / (t_g2 / 1e3) / 1e9},
+            "mma": {"flops_per_step": flops, "tflops": flops / (ms / 1e3) / 1e12},
+            "clocks": clocks,
+            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
+            "gpu_launches": K * KERNELS_PER_STEP,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -11,6 +11,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "gptoss_moe.h"
 #include "ptx.cuh"
@@ -107,6 +108,25 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 int64_t pad128(int64_t k) { return (k + 127) / 128 * 128; }
 
+// Launch with programmatic stream serialisation: the kernel may be scheduled while the
+// previous kernel on the stream drains; every kernel of this library waits
+// (griddepcontrol.wait) before touching global memory, so ordering is unchanged.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GPTOSS_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  return GPTOSS_OK;
+}
+
 // ---------------------------------------------------------------- TMA descriptors
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -172,8 +192,15 @@ template <bool SWAP, int EPI>
 int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t st) {
   using C = GemmConfig<SWAP>;
   if (job.act_rows <= 0) return GPTOSS_OK;
-  CUtensorMap ta, tw;
+  CUtensorMap ta, ta32, ta16, tw;
   GPTOSS_TRY(make_act_map(&ta, job.act, job.act_rows, job.lda, C::kActRows));
+  if (SWAP) {
+    GPTOSS_TRY(make_act_map(&ta32, job.act, job.act_rows, job.lda, 32));
+    GPTOSS_TRY(make_act_map(&ta16, job.act, job.act_rows, job.lda, 16));
+  } else {
+    ta32 = ta;
+    ta16 = ta;
+  }
   GPTOSS_TRY(make_wgt_map(&tw, job.wgt, job.p.num_experts, job.p.N, job.p.K, C::kWgtRows));
   static uint64_t attr_done = 0;   // one bit per device
   static std::mutex mu;
@@ -190,9 +217,8 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
   const int64_t tiles_ub = (job.act_rows / C::kActRows + p.num_experts) * static_cast<int64_t>(p.n_tiles);
   const int grid = static_cast<int>(std::min<int64_t>(di.sms, tiles_ub));
   if (grid <= 0) return GPTOSS_OK;
-  moe_gemm_kernel<SWAP, EPI><<<grid, C::kThreads, C::kSmemBytes, st>>>(ta, tw, p);
-  GPTOSS_CUDA(cudaGetLastError());
-  return GPTOSS_OK;
+  return launch_pdl(moe_gemm_kernel<SWAP, EPI>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ta, ta32, ta16,
+                    tw, p);
 }
 
 template <int EPI>
@@ -245,14 +271,13 @@ int router_launch(const void* hidden, const void* weight, const void* bias, int6
   const size_t smem = sizeof(__nv_bfloat16) * tb * H + sizeof(float) * tb * E;
   GPTOSS_CHECK(smem <= 200 * 1024, "router: hidden size %lld too large", (long long)H);
   const int grid = static_cast<int>((T + tb - 1) / tb);
+  const int threads = 32 * std::min(16, E);
   auto go = [&](auto kern) -> int {
     GPTOSS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    kern<<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(weight),
-                                  static_cast<const __nv_bfloat16*>(bias), static_cast<int>(T), static_cast<int>(H), E, k,
-                                  idx, static_cast<__nv_bfloat16*>(scores), wf32, static_cast<__nv_bfloat16*>(logits),
-                                  static_cast<__nv_bfloat16*>(zero_rows), zero_elems);
-    GPTOSS_CUDA(cudaGetLastError());
-    return GPTOSS_OK;
+    return launch_pdl(kern, dim3(grid), dim3(threads), smem, st, static_cast<const __nv_bfloat16*>(hidden),
+                      static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
+                      static_cast<int>(T), static_cast<int>(H), E, k, idx, static_cast<__nv_bfloat16*>(scores), wf32,
+                      static_cast<__nv_bfloat16*>(logits), static_cast<__nv_bfloat16*>(zero_rows), zero_elems);
   };
   if (tb == 1) return go(router_topk_kernel<1>);
   if (tb == 4) return go(router_topk_kernel<4>);
@@ -280,61 +305,90 @@ int check_expert_weights(const ExpertWeights& w, int64_t H, int64_t I, int E) {
   return GPTOSS_OK;
 }
 
-// route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch.
-int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E,
-                     int64_t H, int64_t I, const ExpertWeights& w, float sw_alpha, float sw_limit, void* out,
-                     uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
-                     cudaStream_t st, bool out_zeroed) {
+struct WsPtrs {
+  int64_t* sorted_token; int64_t* sorted_expert; float* sorted_weight;
+  int32_t* counts; int32_t* offsets; int32_t* sfoff_a; int32_t* sfoff_b;
+  uint8_t* act_codes; uint8_t* act_sf; uint8_t* inter_codes; uint8_t* inter_sf;
+};
+
+WsPtrs ws_ptrs(uint8_t* ws, const Workspace& L) {
+  WsPtrs w;
+  w.sorted_token = reinterpret_cast<int64_t*>(ws + L.sorted_token);
+  w.sorted_expert = reinterpret_cast<int64_t*>(ws + L.sorted_expert);
+  w.sorted_weight = reinterpret_cast<float*>(ws + L.sorted_weight);
+  w.counts = reinterpret_cast<int32_t*>(ws + L.counts);
+  w.offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  w.sfoff_a = reinterpret_cast<int32_t*>(ws + L.sfoff_a);
+  w.sfoff_b = reinterpret_cast<int32_t*>(ws + L.sfoff_b);
+  w.act_codes = ws + L.act_codes;
+  w.act_sf = ws + L.act_sf;
+  w.inter_codes = ws + L.inter_codes;
+  w.inter_sf = ws + L.inter_sf;
+  return w;
+}
+
+// Stage 1: stable counting sort + gather + FP8 quantisation (blocked scales).
+int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E, int64_t H,
+                      int64_t I, const WsPtrs& w, int* status, cudaStream_t st) {
   const int64_t A = T * k;
   const int64_t Kh = pad128(H), Ki = pad128(I);
-  auto* sorted_token = reinterpret_cast<int64_t*>(ws + L.sorted_token);
-  auto* sorted_expert = reinterpret_cast<int64_t*>(ws + L.sorted_expert);
-  auto* sorted_weight = reinterpret_cast<float*>(ws + L.sorted_weight);
-  auto* counts = reinterpret_cast<int32_t*>(ws + L.counts);
-  auto* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
-  auto* sfoff_a = reinterpret_cast<int32_t*>(ws + L.sfoff_a);
-  auto* sfoff_b = reinterpret_cast<int32_t*>(ws + L.sfoff_b);
-  uint8_t* act_codes = ws + L.act_codes;
-  uint8_t* act_sf = ws + L.act_sf;
-  uint8_t* inter_codes = ws + L.inter_codes;
-  uint8_t* inter_sf = ws + L.inter_sf;
-
   RouteSortParams rp{};
   rp.router_indices = ridx; rp.routing_weights = rw;
   rp.A = static_cast<int>(A); rp.K = k; rp.E = E;
-  rp.sorted_token = sorted_token; rp.sorted_expert = sorted_expert; rp.sorted_weight = sorted_weight;
-  rp.counts = counts; rp.offsets = offsets;
-  rp.sf_offsets_a = sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = static_cast<int>(H / 32); rp.sf_a = act_sf;
-  rp.sf_offsets_b = sfoff_b; rp.g4_b = static_cast<int>(Ki / 128); rp.groups_b = static_cast<int>(I / 32); rp.sf_b = inter_sf;
+  rp.sorted_token = w.sorted_token; rp.sorted_expert = w.sorted_expert; rp.sorted_weight = w.sorted_weight;
+  rp.counts = w.counts; rp.offsets = w.offsets;
+  rp.sf_offsets_a = w.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = static_cast<int>(H / 32); rp.sf_a = w.act_sf;
+  rp.sf_offsets_b = w.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128); rp.groups_b = static_cast<int>(I / 32); rp.sf_b = w.inter_sf;
   rp.err = status;
-  route_sort_kernel<<<E, 1024, 0, st>>>(rp);
-  GPTOSS_CUDA(cudaGetLastError());
+  GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(E), dim3(1024), 0, st, rp));
+  const int tpr = quant_threads_per_row(static_cast<int>(H));
+  const int rpb = 256 / tpr;
+  const int qblocks = static_cast<int>((A + rpb - 1) / rpb);
+  return launch_pdl(gather_quant_kernel<__nv_bfloat16>, dim3(qblocks), dim3(tpr * rpb), 0, st,
+                    static_cast<const __nv_bfloat16*>(hidden), A, static_cast<int>(H), tpr,
+                    static_cast<const int64_t*>(w.sorted_token), static_cast<const int64_t*>(w.sorted_expert),
+                    static_cast<const int32_t*>(w.offsets), static_cast<const int32_t*>(w.sfoff_a),
+                    static_cast<int>(Kh / 128), w.act_codes, w.act_sf, static_cast<uint8_t*>(nullptr));
+}
 
-  const int qblocks = static_cast<int>((A + 7) / 8);
-  gather_quant_kernel<__nv_bfloat16><<<qblocks, 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(hidden), A, static_cast<int>(H), sorted_token, sorted_expert, offsets,
-      sfoff_a, static_cast<int>(Kh / 128), act_codes, act_sf, nullptr);
-  GPTOSS_CUDA(cudaGetLastError());
-  if (!out_zeroed) GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
-
+// Stage 2: GEMM1 + bias + SwiGLU + FP8 requantisation.
+int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit,
+                const WsPtrs& w, int mode, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+  const int64_t Kh = pad128(H), Ki = pad128(I);
   GemmJob g1{};
-  g1.act = act_codes; g1.act_rows = A; g1.lda = H; g1.wgt = w.gu_data;
+  g1.act = w.act_codes; g1.act_rows = A; g1.lda = H; g1.wgt = wt.gu_data;
   g1.p.num_experts = E; g1.p.N = static_cast<int>(2 * I); g1.p.K = static_cast<int>(Kh); g1.p.num_kb = static_cast<int>(Kh / 128);
-  g1.p.m_sizes = counts; g1.p.m_stride = 1; g1.p.row_offsets = offsets; g1.p.sfa_offsets = sfoff_a;
-  g1.p.sfa = act_sf; g1.p.sfb = w.gu_scales; g1.p.sfb_stride = w.ldb_gu; g1.p.err = status;
-  g1.p.out = inter_codes; g1.p.ld_out = I; g1.p.bias = w.gu_bias; g1.p.out_sf = inter_sf;
-  g1.p.out_sf_offsets = sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
+  g1.p.m_sizes = w.counts; g1.p.m_stride = 1; g1.p.row_offsets = w.offsets; g1.p.sfa_offsets = w.sfoff_a;
+  g1.p.sfa = w.act_sf; g1.p.sfb = wt.gu_scales; g1.p.sfb_stride = wt.ldb_gu; g1.p.err = status;
+  g1.p.out = w.inter_codes; g1.p.ld_out = I; g1.p.bias = wt.gu_bias; g1.p.out_sf = w.inter_sf;
+  g1.p.out_sf_offsets = w.sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
   g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
-  GPTOSS_TRY(run_gemm<kEpiGemm1>(g1, mode, di, dev, st));
+  return run_gemm<kEpiGemm1>(g1, mode, di, dev, st);
+}
 
+// Stage 3: GEMM2 + bias, x routing weight, bf16 scatter-add into out (accumulates).
+int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, void* out, const WsPtrs& w,
+                int mode, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+  const int64_t Ki = pad128(I);
   GemmJob g2{};
-  g2.act = inter_codes; g2.act_rows = A; g2.lda = I; g2.wgt = w.dn_data;
+  g2.act = w.inter_codes; g2.act_rows = A; g2.lda = I; g2.wgt = wt.dn_data;
   g2.p.num_experts = E; g2.p.N = static_cast<int>(H); g2.p.K = static_cast<int>(Ki); g2.p.num_kb = static_cast<int>(Ki / 128);
-  g2.p.m_sizes = counts; g2.p.m_stride = 1; g2.p.row_offsets = offsets; g2.p.sfa_offsets = sfoff_b;
-  g2.p.sfa = inter_sf; g2.p.sfb = w.dn_scales; g2.p.sfb_stride = w.ldb_dn; g2.p.err = status;
-  g2.p.out = out; g2.p.ld_out = H; g2.p.bias = w.dn_bias; g2.p.token_idx = sorted_token; g2.p.row_weights = sorted_weight;
-  GPTOSS_TRY(run_gemm<kEpiGemm2>(g2, mode, di, dev, st));
-  return GPTOSS_OK;
+  g2.p.m_sizes = w.counts; g2.p.m_stride = 1; g2.p.row_offsets = w.offsets; g2.p.sfa_offsets = w.sfoff_b;
+  g2.p.sfa = w.inter_sf; g2.p.sfb = wt.dn_scales; g2.p.sfb_stride = wt.ldb_dn; g2.p.err = status;
+  g2.p.out = out; g2.p.ld_out = H; g2.p.bias = wt.dn_bias; g2.p.token_idx = w.sorted_token; g2.p.row_weights = w.sorted_weight;
+  return run_gemm<kEpiGemm2>(g2, mode, di, dev, st);
+}
+
+// route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch.
+int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E,
+                     int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit, void* out,
+                     uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
+                     cudaStream_t st, bool out_zeroed) {
+  const WsPtrs w = ws_ptrs(ws, L);
+  GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, status, st));
+  if (!out_zeroed) GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
+  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, mode, status, di, dev, st));
+  return stage_gemm2(T * k, E, H, I, wt, out, w, mode, status, di, dev, st);
 }
 
 int check_dims(int64_t T, int k, int E, int64_t H, int64_t I) {
@@ -389,9 +443,7 @@ int gptoss_fused_moe_routing(const int64_t* router_indices, const float* routing
   rp.sorted_token = sorted_token_idx; rp.sorted_expert = sorted_expert_idx; rp.sorted_weight = sorted_weights;
   rp.counts = expert_counts; rp.offsets = expert_offsets;
   rp.err = status_dev ? status_dev : di.status_sink;
-  route_sort_kernel<<<num_experts, 1024, 0, st>>>(rp);
-  GPTOSS_CUDA(cudaGetLastError());
-  return GPTOSS_OK;
+  return launch_pdl(route_sort_kernel, dim3(num_experts), dim3(1024), 0, st, rp);
 }
 
 int gptoss_router_topk(const void* hidden, const void* weight, const void* bias, int64_t num_tokens,
@@ -420,16 +472,18 @@ int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, ui
   GPTOSS_TRY(bind_device(x, "x", &di));
   GPTOSS_CHECK(codes && scales && aligned(x, 16) && aligned(codes, 16), "quantize: null or misaligned pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int blocks = static_cast<int>((rows + 7) / 8);
+  const int tpr = quant_threads_per_row(static_cast<int>(cols));
+  const int rpb = 256 / tpr;
+  const int blocks = static_cast<int>((rows + rpb - 1) / rpb);
+  const int64_t* no_i64 = nullptr;
+  const int32_t* no_i32 = nullptr;
+  uint8_t* no_u8 = nullptr;
   if (dtype == GPTOSS_DTYPE_BF16)
-    gather_quant_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows,
-                                                                static_cast<int>(cols), nullptr, nullptr, nullptr,
-                                                                nullptr, 0, codes, nullptr, scales);
-  else
-    gather_quant_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), rows, static_cast<int>(cols),
-                                                        nullptr, nullptr, nullptr, nullptr, 0, codes, nullptr, scales);
-  GPTOSS_CUDA(cudaGetLastError());
-  return GPTOSS_OK;
+    return launch_pdl(gather_quant_kernel<__nv_bfloat16>, dim3(blocks), dim3(tpr * rpb), 0, st,
+                      static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(cols), tpr, no_i64, no_i64, no_i32,
+                      no_i32, 0, codes, no_u8, scales);
+  return launch_pdl(gather_quant_kernel<float>, dim3(blocks), dim3(tpr * rpb), 0, st, static_cast<const float*>(x), rows,
+                    static_cast<int>(cols), tpr, no_i64, no_i64, no_i32, no_i32, 0, codes, no_u8, scales);
 }
 
 int gptoss_swiglu(const void* x, int dtype, int64_t rows, int64_t cols, void* out, float alpha, float limit,
@@ -604,6 +658,83 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, cons
   return experts_pipeline(hidden, ridx, rw, num_tokens, top_k, num_experts, hidden_size, intermediate_size, w,
                           swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode, status_dev ? status_dev : di.status_sink,
                           di, dev, st, true);
+}
+
+
+int gptoss_moe_workspace_layout(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                                int64_t intermediate_size, int64_t* offsets_out) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(offsets_out != nullptr, "offsets_out is null");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  const size_t v[GPTOSS_WS_NUM_REGIONS] = {L.sorted_token, L.sorted_expert, L.sorted_weight, L.counts, L.offsets,
+                                           L.sfoff_a, L.sfoff_b, L.act_codes, L.act_sf, L.inter_codes, L.inter_sf,
+                                           L.router_idx, L.router_w, L.total};
+  for (int i = 0; i < GPTOSS_WS_NUM_REGIONS; ++i) offsets_out[i] = static_cast<int64_t>(v[i]);
+  return GPTOSS_OK;
+}
+
+int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices, const float* routing_weights,
+                           int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                           int64_t intermediate_size, void* workspace, size_t workspace_bytes, int32_t* status_dev,
+                           void* stream) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(workspace, "workspace", &di));
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(hidden && router_indices && routing_weights && aligned(hidden, 16) && aligned(workspace, 256),
+               "route_quant: null or misaligned pointer");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  return stage_route_quant(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
+                           intermediate_size, ws_ptrs(static_cast<uint8_t*>(workspace), L),
+                           status_dev ? status_dev : di.status_sink, static_cast<cudaStream_t>(stream));
+}
+
+int gptoss_moe_gemm1(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size, int64_t intermediate_size,
+                     const uint8_t* gate_up_data, const uint8_t* gate_up_scales, int64_t ldb_gate_up,
+                     const float* gate_up_bias, float swiglu_alpha, float swiglu_limit, void* workspace,
+                     size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  GPTOSS_CHECK(gate_up_scales && gate_up_bias && aligned(gate_up_data, 32) && aligned(gate_up_scales, 16) &&
+                   ldb_gate_up % 16 == 0 &&
+                   ldb_gate_up >= blocked_sf_cosize(2 * intermediate_size, static_cast<int>(pad128(hidden_size) / 32)),
+               "gemm1: bad gate_up weights");
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(workspace && aligned(workspace, 256), "gemm1: null or misaligned workspace");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias, nullptr, nullptr, 0, nullptr};
+  return stage_gemm1(num_tokens * top_k, num_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit,
+                     ws_ptrs(static_cast<uint8_t*>(workspace), L), gemm_mode, status_dev ? status_dev : di.status_sink,
+                     di, dev, static_cast<cudaStream_t>(stream));
+}
+
+int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size, int64_t intermediate_size,
+                     const uint8_t* down_data, const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                     void* out, void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
+                     void* stream) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(down_data, "down_proj_data", &di));
+  GPTOSS_CHECK(down_scales && down_bias && aligned(down_data, 32) && aligned(down_scales, 16) && ldb_down % 16 == 0 &&
+                   ldb_down >= blocked_sf_cosize(hidden_size, static_cast<int>(pad128(intermediate_size) / 32)),
+               "gemm2: bad down weights");
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(out && workspace && aligned(out, 16) && aligned(workspace, 256), "gemm2: null or misaligned pointer");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  ExpertWeights w{nullptr, nullptr, 0, nullptr, down_data, down_scales, ldb_down, down_bias};
+  return stage_gemm2(num_tokens * top_k, num_experts, hidden_size, intermediate_size, w, out,
+                     ws_ptrs(static_cast<uint8_t*>(workspace), L), gemm_mode, status_dev ? status_dev : di.status_sink,
+                     di, dev, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

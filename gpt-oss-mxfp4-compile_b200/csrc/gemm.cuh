@@ -96,6 +96,8 @@ constexpr int kMaxExpertsGemm = 256;
 template <bool SWAP, int EPI>
 __global__ void __launch_bounds__(192, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,
+                    const __grid_constant__ CUtensorMap tm_act32,
+                    const __grid_constant__ CUtensorMap tm_act16,
                     const __grid_constant__ CUtensorMap tm_wgt, const GemmParams p) {
   using C = GemmConfig<SWAP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -113,13 +115,14 @@ __global__ void __launch_bounds__(192, 1)
   auto acce_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + C::kAccBufs + b); };
   const uint32_t drain_bar = bar_base + 8u * (2 * C::kStages + 2 * C::kAccBufs);
 
-  // ---- per-CTA tile map from the device-side counts
-  for (int i = threadIdx.x; i < p.num_experts; i += blockDim.x) {
-    const int m = p.m_sizes[i * p.m_stride];
-    s_chunks[i] = m > 0 ? (m + C::kActRows - 1) / C::kActRows : 0;
-  }
+  pdl_trigger();
+  // ---- barriers, TMEM and descriptor prefetch overlap the previous kernel's tail
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_act);
+    if constexpr (SWAP) {
+      tma_prefetch_desc(&tm_act32);
+      tma_prefetch_desc(&tm_act16);
+    }
     tma_prefetch_desc(&tm_wgt);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(full_bar(s), 1);
@@ -136,6 +139,12 @@ __global__ void __launch_bounds__(192, 1)
     tmem_alloc(smem_u32(&s_tmem_base), C::kTmemCols);
     tmem_relinquish();
   }
+  pdl_wait();
+  // ---- per-CTA tile map from the device-side counts
+  for (int i = threadIdx.x; i < p.num_experts; i += blockDim.x) {
+    const int m = p.m_sizes[i * p.m_stride];
+    s_chunks[i] = m > 0 ? (m + C::kActRows - 1) / C::kActRows : 0;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0;
@@ -146,6 +155,18 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = s_tmem_base;
   const int total_tiles = s_chunk_prefix[p.num_experts] * p.n_tiles;
+
+  // Activation rows a tile loads and multiplies: SWAP tiles load only 16 or 32 rows when
+  // the chunk holds that few (the MMA N follows); the chunk still starts on a 64-row
+  // boundary, so the scale TMEM shift stays 0 or 2 columns.
+  auto act_rows_of = [&](int e, int ch) -> int {
+    if constexpr (!SWAP) {
+      return C::kActRows;
+    } else {
+      const int left = p.m_sizes[e * p.m_stride] - ch * C::kActRows;
+      return left <= 16 ? 16 : (left <= 32 ? 32 : C::kActRows);
+    }
+  };
 
   // tile t -> (expert, weight tile, activation chunk)
   auto decode = [&](int t, int& e, int& nt, int& ch) {
@@ -182,14 +203,16 @@ __global__ void __launch_bounds__(192, 1)
         const int nwchunks = min(C::kWgtSfChunks, nwblk_total - wblk0);
         const uint8_t* sfb_src = p.sfb + static_cast<int64_t>(e) * p.sfb_stride +
                                  static_cast<int64_t>(wblk0) * p.num_kb * 512;
-        const uint32_t tx = C::kActTileBytes + C::kWgtRows * 64 + C::kSfActBytes + 512u * nwchunks;
+        const int arows = act_rows_of(e, ch);
+        const CUtensorMap* amap = arows == 16 ? &tm_act16 : (arows == 32 ? &tm_act32 : &tm_act);
+        const uint32_t tx = arows * 128u + C::kWgtRows * 64 + C::kSfActBytes + 512u * nwchunks;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.err, kDevTimeoutProducer)) { ok = false; break; }
           const uint32_t sb = smem_base + stage * C::kStageBytes;
           const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
           const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
           mbar_arrive_expect_tx(full_bar(stage), tx);
-          tma_load_2d(s_a, &tm_act, full_bar(stage), kb * 128, act_row0, pol_a);
+          tma_load_2d(s_a, amap, full_bar(stage), kb * 128, act_row0, pol_a);
           tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
           bulk_load(s_sfa, sfa_src + kb * 512, 512, full_bar(stage), pol_a);
           for (int c = 0; c < nwchunks; ++c)
@@ -226,6 +249,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ashift = SWAP ? static_cast<uint32_t>(((ch * C::kActRows) & 127) >> 5) : 0u;
         const uint32_t t_sfa = tmem_base + C::kSfActCol;
         const uint32_t t_sfw = tmem_base + C::kSfWgtCol;
+        const uint32_t mma_n = SWAP ? static_cast<uint32_t>(act_rows_of(e, ch)) : static_cast<uint32_t>(C::kMmaN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
@@ -243,11 +267,11 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
             if constexpr (SWAP) {
               // A = weights (E2M1), B = activations (E4M3)
-              mma_mxf8f6f4(d_tmem, dw, da, idesc_mxf8f6f4(5, 0, C::kMmaM, C::kMmaN, k, k),
+              mma_mxf8f6f4(d_tmem, dw, da, idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, k, k),
                            t_sfw, t_sfa + ashift, acc);
             } else {
               // A = activations (E4M3), B = weights (E2M1)
-              mma_mxf8f6f4(d_tmem, da, dw, idesc_mxf8f6f4(0, 5, C::kMmaM, C::kMmaN, k, k),
+              mma_mxf8f6f4(d_tmem, da, dw, idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, k, k),
                            t_sfa, t_sfw + wshift, acc);
             }
           }
@@ -433,16 +457,20 @@ __global__ void __launch_bounds__(192, 1)
             const int f = wrow_i >> 1;                          // intermediate feature
             const int grp = f >> 5;                             // quant group (2 warps)
             float hv[32];
+            const int nv = min(32, m_e - a0);                   // valid rows, warp-uniform
             if (live) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                const float v = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
-                const float up = __shfl_xor_sync(0xffffffffu, v, 1);
-                hv[j] = swiglu_pair(v, up, p.swiglu_alpha, p.swiglu_limit);   // valid on even lanes
+                if (j < nv) {
+                  const float v = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
+                  const float up = __shfl_xor_sync(0xffffffffu, v, 1);
+                  hv[j] = swiglu_pair(v, up, p.swiglu_alpha, p.swiglu_limit);   // valid on even lanes
+                }
               }
               // group absmax over the 32 features held by the even lanes of warps (q, q^1)
-#pragma unroll 1
+#pragma unroll
               for (int j = 0; j < 32; ++j) {
+                if (j >= nv) break;
                 float a = (lane & 1) == 0 ? fabsf(hv[j]) : 0.0f;
                 if (hv[j] != hv[j] && (lane & 1) == 0) a = hv[j];
 #pragma unroll
@@ -457,14 +485,13 @@ __global__ void __launch_bounds__(192, 1)
             if (live) {
               const int qp = q ^ 1;
               uint8_t* codes_out = static_cast<uint8_t*>(p.out);
-#pragma unroll 1
+#pragma unroll
               for (int j = 0; j < 32; ++j) {
-                if (a0 + j >= m_e) break;
+                if (j >= nv) break;
                 const float a_self = s_amax[q][j], a_pair = s_amax[qp][j];
                 const float amax = (a_pair > a_self || a_pair != a_pair) ? a_pair : a_self;
                 const uint32_t rb = ue8m0_rounded_bits(amax);
-                const float scale = scale_from_bits(rb);
-                const float qv = clamp_fp8(__fdiv_rn(hv[j], scale));
+                const float qv = clamp_fp8(__fmul_rn(hv[j], inv_scale(scale_from_bits(rb))));
                 const uint16_t c2 = cvt_e4m3x2(qv, 0.0f);
                 const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
                 if ((lane & 1) == 0 && vcol && f < p.out_features)

@@ -47,6 +47,11 @@ __device__ __forceinline__ float scale_from_bits(uint32_t rbits) {
   return rbits == 0u ? 1.1754944e-38f : __uint_as_float(rbits);
 }
 
+// 1 / scale for a power-of-two scale in [2^-126, 2^127]. The reciprocal is exact
+// (2^-127 is a subnormal, still exact), so x * inv equals the reference's x / scale
+// bit for bit, including results that round into the subnormal range.
+__device__ __forceinline__ float inv_scale(float scale) { return __frcp_rn(scale); }
+
 __device__ __forceinline__ float clamp_fp8(float v) {
   // torch.clamp keeps NaN.
   return v < -kFp8Max ? -kFp8Max : (v > kFp8Max ? kFp8Max : v);
@@ -66,13 +71,13 @@ __device__ __forceinline__ uint8_t quantize_group32(const float (&x)[32], uint32
 #pragma unroll
   for (int i = 0; i < 32; ++i) amax = torch_max_abs(amax, x[i]);
   const uint32_t rb = ue8m0_rounded_bits(amax);
-  const float scale = scale_from_bits(rb);
+  const float inv = inv_scale(scale_from_bits(rb));
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float a = clamp_fp8(__fdiv_rn(x[4 * i + 0], scale));
-    const float b = clamp_fp8(__fdiv_rn(x[4 * i + 1], scale));
-    const float c = clamp_fp8(__fdiv_rn(x[4 * i + 2], scale));
-    const float d = clamp_fp8(__fdiv_rn(x[4 * i + 3], scale));
+    const float a = clamp_fp8(__fmul_rn(x[4 * i + 0], inv));
+    const float b = clamp_fp8(__fmul_rn(x[4 * i + 1], inv));
+    const float c = clamp_fp8(__fmul_rn(x[4 * i + 2], inv));
+    const float d = clamp_fp8(__fmul_rn(x[4 * i + 3], inv));
     out[i] = static_cast<uint32_t>(cvt_e4m3x2(a, b)) | (static_cast<uint32_t>(cvt_e4m3x2(c, d)) << 16);
   }
   return static_cast<uint8_t>((rb >> 23) & 0xFFu);
@@ -82,7 +87,8 @@ __device__ __forceinline__ uint8_t quantize_group32(const float (&x)[32], uint32
 __device__ __forceinline__ float swiglu_pair(float gate, float up, float alpha, float limit) {
   gate = gate > limit ? limit : gate;                       // clamp(max=limit)
   up = up < -limit ? -limit : (up > limit ? limit : up);    // clamp(-limit, limit)
-  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-__fmul_rn(gate, alpha))));
+  // 1 / (1 + e): a correctly rounded reciprocal equals the IEEE quotient 1.0f / y.
+  const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-__fmul_rn(gate, alpha))));
   return __fmul_rn(__fmul_rn(gate, sig), __fadd_rn(up, 1.0f));
 }
 

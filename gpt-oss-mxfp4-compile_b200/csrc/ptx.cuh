@@ -233,6 +233,13 @@ __host__ __device__ constexpr uint32_t idesc_mxf8f6f4(uint32_t a_fmt, uint32_t b
          ((M >> 4) << 24) | (a_sf_id << 29);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels of the pipeline are launched with programmatic stream serialisation: the next
+// kernel may be scheduled while this one drains, and each kernel waits here before its
+// first global-memory access, so only launch latency and set-up overlap.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------- numerics
 // float -> bf16 -> float with round-to-nearest-even (what .to(torch.bfloat16) does).
 __device__ __forceinline__ float bf16_round(float x) {

@@ -24,11 +24,15 @@ constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
 
 // ----------------------------------------------------------------------------------
-// Router: each CTA owns TB tokens; their rows are staged in shared memory, each warp
-// walks a subset of experts and every lane accumulates an 8-wide strided slice of the
-// dot product in a fixed order (deterministic), followed by a fixed-order warp tree.
+// Router: each CTA owns TB tokens; their rows are staged in shared memory. Warp w
+// handles experts w, w + nwarps, ...; lane l accumulates the 8-element slices
+// l, l + 32, ... of the dot product in a fixed order (deterministic), with the weight
+// slices of a chunk loaded before any arithmetic so their latencies overlap, then a
+// fixed-order warp tree.
+constexpr int kRouterVecChunk = 12;   // 8-element slices per lane per pass (H <= 3072 in one pass)
+
 template <int TB>
-__global__ void __launch_bounds__(256) router_topk_kernel(
+__global__ void __launch_bounds__(512) router_topk_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ bias, int T, int H, int E, int K,
     int64_t* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_scores,
@@ -37,47 +41,59 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);      // [TB][H]
   float* logits = reinterpret_cast<float*>(smem_raw + sizeof(__nv_bfloat16) * TB * H);  // [TB][E]
+  pdl_trigger();
+  pdl_wait();
 
   const int t0 = blockIdx.x * TB;
   const int ntok = min(TB, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
 
-  // Stage the token rows (H multiple of 8 is checked on the host).
-  const int vec_per_row = H >> 3;
+  const int vec_per_row = H >> 3;     // H % 8 == 0 (host check)
   for (int i = threadIdx.x; i < ntok * vec_per_row; i += blockDim.x) {
     const int t = i / vec_per_row, v = i - t * vec_per_row;
     reinterpret_cast<uint4*>(xs + t * H)[v] =
         reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + t) * H)[v];
   }
-  // Optionally zero the output rows of these tokens (the combine adds into them).
-  if (zero_rows != nullptr) {
+  if (zero_rows != nullptr) {          // the combine adds into these rows
     const int64_t vz = zero_row_elems >> 3;
-    uint4 z = make_uint4(0, 0, 0, 0);
+    const uint4 z = make_uint4(0, 0, 0, 0);
     for (int64_t i = threadIdx.x; i < ntok * vz; i += blockDim.x)
       reinterpret_cast<uint4*>(zero_rows + static_cast<int64_t>(t0) * zero_row_elems)[i] = z;
   }
   __syncthreads();
 
-  for (int e = warp; e < E; e += blockDim.x >> 5) {
+  for (int e = warp; e < E; e += nwarps) {
     float acc[TB];
 #pragma unroll
     for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
-    const __nv_bfloat16* wr = w + static_cast<int64_t>(e) * H;
-    for (int v = lane; v < vec_per_row; v += 32) {
-      const uint4 wv = reinterpret_cast<const uint4*>(wr)[v];
-      const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+    const uint4* wr = reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * H);
+    for (int v0 = 0; v0 < vec_per_row; v0 += 32 * kRouterVecChunk) {
+      uint4 wv[kRouterVecChunk];
 #pragma unroll
-      for (int t = 0; t < TB; ++t) {
-        if (t < ntok) {
-          const uint4 xv = reinterpret_cast<const uint4*>(xs + t * H)[v];
-          const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
-          float a = acc[t];
+      for (int i = 0; i < kRouterVecChunk; ++i) {
+        const int v = v0 + lane + 32 * i;
+        wv[i] = v < vec_per_row ? __ldg(wr + v) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            a = fmaf(bf16_bits_lo(xq[j]), bf16_bits_lo(wq[j]), a);
-            a = fmaf(bf16_bits_hi(xq[j]), bf16_bits_hi(wq[j]), a);
+      for (int i = 0; i < kRouterVecChunk; ++i) {
+        const int v = v0 + lane + 32 * i;
+        if (v < vec_per_row) {
+          const uint32_t wq[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+          for (int t = 0; t < TB; ++t) {
+            if (t < ntok) {
+              const uint4 xv = reinterpret_cast<const uint4*>(xs + t * H)[v];
+              const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
+              float a = acc[t];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                a = fmaf(bf16_bits_lo(xq[j]), bf16_bits_lo(wq[j]), a);
+                a = fmaf(bf16_bits_hi(xq[j]), bf16_bits_hi(wq[j]), a);
+              }
+              acc[t] = a;
+            }
           }
-          acc[t] = a;
         }
       }
     }
@@ -88,8 +104,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
       for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
       if (lane == 0 && t < ntok) {
         // F.linear in bf16: fp32 accumulate, add the bias, round once to bf16.
-        const float l = bf16_round(a + __bfloat162float(bias[e]));
-        logits[t * E + e] = l;
+        logits[t * E + e] = bf16_round(a + __bfloat162float(bias[e]));
       }
     }
   }
@@ -117,13 +132,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
     const float m = val[0];
     float ex[kMaxTopK], s = 0.0f;
     for (int j = 0; j < K; ++j) { ex[j] = expf(__fsub_rn(val[j], m)); s = __fadd_rn(s, ex[j]); }
-    const float inv = __fdiv_rn(1.0f, s);
+    const float inv = __frcp_rn(s);
     const int64_t tg = t0 + t;
     for (int j = 0; j < K; ++j) {
-      const __nv_bfloat16 p = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
+      const __nv_bfloat16 pr = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
       out_idx[tg * K + j] = sel[j];
-      if (out_scores) out_scores[tg * K + j] = p;
-      if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(p);
+      if (out_scores) out_scores[tg * K + j] = pr;
+      if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(pr);
     }
     if (out_logits)
       for (int e = 0; e < E; ++e) out_logits[tg * E + e] = __float2bfloat16_rn(lg[e]);
@@ -155,6 +170,8 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
   __shared__ int hist[kMaxExperts];
   __shared__ int warp_cnt[32];
   __shared__ int s_base;
+  pdl_trigger();
+  pdl_wait();
   const int e = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < p.E; i += blockDim.x) hist[i] = 0;
@@ -188,23 +205,19 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
     s_base = 0;
   }
   __syncthreads();
-  // Zero the padding of this expert's blocked scale buffers: rows [cnt, pad128(cnt))
-  // and k-groups past the valid ones. The quantisers write the valid entries.
+  // Zero this expert's blocked scale regions (16-byte stores); the quantisers that run
+  // after this kernel overwrite the valid entries, so the padding ends up zero.
   if (p.sf_offsets_a != nullptr) {
-    const int rows_pad = (cnt + 127) & ~127;
     for (int pass = 0; pass < 2; ++pass) {
       uint8_t* buf = pass == 0 ? p.sf_a : p.sf_b;
-      const int g4 = pass == 0 ? p.g4_a : p.g4_b;
-      const int gv = pass == 0 ? p.groups_a : p.groups_b;
+      const int gp = (pass == 0 ? p.g4_a : p.g4_b) * 4;
       if (buf == nullptr) continue;
-      const int gp = g4 * 4;
       int64_t base = 0;
       for (int q = 0; q < e; ++q) base += blocked_sf_cosize(hist[q], gp);
-      const int64_t total = static_cast<int64_t>(rows_pad) * gp;
-      for (int64_t i = tid; i < total; i += blockDim.x) {
-        const int r = static_cast<int>(i / gp), g = static_cast<int>(i - static_cast<int64_t>(r) * gp);
-        if (r >= cnt || g >= gv) buf[base + blocked_sf_offset(r, g, g4)] = 0;
-      }
+      uint4* dst = reinterpret_cast<uint4*>(buf + base);     // base is a multiple of 512
+      const int64_t n16 = blocked_sf_cosize(cnt, gp) >> 4;
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      for (int64_t i = tid; i < n16; i += blockDim.x) dst[i] = z;
     }
   }
   // Pass 2: stable compaction of this expert's assignments, 1024 at a time.
@@ -232,20 +245,23 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
 }
 
 // ----------------------------------------------------------------------------------
-// Gather + quantise: one warp per sorted row; lane l handles k-groups l, l+32, ...
-// Writes FP8 codes into a compact [A, H] buffer and the UE8M0 scales into the blocked
-// layout at sf_offsets[expert] (row index = position inside the expert's group).
-// When sorted_token is null the rows are taken in order (plain quantiser) and scales
-// go row-major into sf_rowmajor.
+// Gather + quantise. `tpr` threads share a row (one 32-element group each per pass);
+// a block of 256 threads covers 256 / tpr rows. Writes FP8 codes into a compact [A, H]
+// buffer and the UE8M0 scales into the blocked layout at sf_offsets[expert] (row index =
+// position inside the expert's group). When sorted_token is null the rows are taken in
+// order (plain quantiser) and scales go row-major into sf_rowmajor.
 template <typename InT>
 __global__ void __launch_bounds__(256) gather_quant_kernel(
-    const InT* __restrict__ src, int64_t rows, int H, const int64_t* __restrict__ sorted_token,
+    const InT* __restrict__ src, int64_t rows, int H, int tpr, const int64_t* __restrict__ sorted_token,
     const int64_t* __restrict__ sorted_expert, const int32_t* __restrict__ offsets,
     const int32_t* __restrict__ sf_offsets, int g4, uint8_t* __restrict__ out_codes,
     uint8_t* __restrict__ sf_blocked, uint8_t* __restrict__ sf_rowmajor) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  pdl_trigger();
+  pdl_wait();
+  const int rows_per_block = blockDim.x / tpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_block + threadIdx.x / tpr;
   if (row >= rows) return;
-  const int lane = threadIdx.x & 31;
+  const int sub = threadIdx.x % tpr;
   const int G = H >> 5;
   int64_t src_row = row;
   int64_t sf_base = 0, r_in = 0;
@@ -257,14 +273,16 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
   }
   const InT* xr = src + src_row * H;
   uint8_t* orow = out_codes + row * H;
-  for (int g = lane; g < G; g += 32) {
+  for (int g = sub; g < G; g += tpr) {
     float v[32];
     if constexpr (sizeof(InT) == 2) {
-      const uint4* p = reinterpret_cast<const uint4*>(xr + g * 32);
+      const uint4* pp = reinterpret_cast<const uint4*>(xr + g * 32);
+      uint4 u[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) u[q] = __ldg(pp + q);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint4 u = p[q];
-        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+        const uint32_t w4[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           v[q * 8 + 2 * j] = bf16_bits_lo(w4[j]);
@@ -272,21 +290,29 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
         }
       }
     } else {
-      const float4* p = reinterpret_cast<const float4*>(xr + g * 32);
+      const float4* pp = reinterpret_cast<const float4*>(xr + g * 32);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const float4 f = p[q];
+        const float4 f = __ldg(pp + q);
         v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
       }
     }
     uint32_t codes[8];
-    const uint8_t s = quantize_group32(v, codes);
+    const uint8_t sc = quantize_group32(v, codes);
     uint4* o = reinterpret_cast<uint4*>(orow + g * 32);
     o[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
     o[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
-    if (sorted_token != nullptr) sf_blocked[sf_base + blocked_sf_offset(r_in, g, g4)] = s;
-    else sf_rowmajor[row * G + g] = s;
+    if (sorted_token != nullptr) sf_blocked[sf_base + blocked_sf_offset(r_in, g, g4)] = sc;
+    else sf_rowmajor[row * G + g] = sc;
   }
+}
+
+// Threads per row for gather_quant_kernel: a multiple of 32 covering the row's groups,
+// at most 128.
+__host__ __forceinline__ int quant_threads_per_row(int H) {
+  const int G = H / 32;
+  const int t = ((G + 31) / 32) * 32;
+  return t > 128 ? 128 : t;
 }
 
 // ----------------------------------------------------------------------------------
@@ -346,7 +372,7 @@ __global__ void swiglu_kernel(const T* __restrict__ in, int64_t rows, int64_t n,
       g = g > limit ? limit : g;
       u = u < -limit ? -limit : (u > limit ? limit : u);
       const float ga = bf16_round(__fmul_rn(g, alpha));
-      const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-ga))));
+      const float sg = bf16_round(__frcp_rn(__fadd_rn(1.0f, expf(-ga))));
       const float gs = bf16_round(__fmul_rn(g, sg));
       const float u1 = bf16_round(__fadd_rn(u, 1.0f));
       out[i] = __float2bfloat16_rn(__fmul_rn(gs, u1));

@@ -382,3 +382,63 @@ def register_ops() -> None:
                     torch.empty((T, top_k), dtype=torch.int64, device=hidden.device))
 
         _registered = True
+
+
+# ------------------------------------------------------------------ staged forward
+WS_REGIONS = ("sorted_token", "sorted_expert", "sorted_weight", "counts", "offsets", "act_sf_offsets",
+              "inter_sf_offsets", "act_codes", "act_scales", "inter_codes", "inter_scales", "router_idx",
+              "router_weights", "total")
+
+
+class ExpertsWorkspace:
+    """Device workspace of the staged expert forward (route_quant -> gemm1 -> gemm2) with
+    typed views of its regions; the layout comes from gptoss_moe_workspace_layout."""
+
+    def __init__(self, T: int, k: int, E: int, H: int, I: int, device):
+        self.T, self.k, self.E, self.H, self.I = T, k, E, H, I
+        offs = (ctypes.c_int64 * len(WS_REGIONS))()
+        _lib.call("gptoss_moe_workspace_layout", T, k, E, H, I, ctypes.addressof(offs))
+        self.offsets = dict(zip(WS_REGIONS, list(offs)))
+        self.nbytes = int(self.offsets["total"])
+        self.buf = torch.empty(max(self.nbytes, 256), dtype=torch.uint8, device=device)
+        A = T * k
+        o = self.offsets
+
+        def view(name, dtype, n):
+            nb = n * torch.empty((), dtype=dtype).element_size()
+            return self.buf[o[name]:o[name] + nb].view(dtype)
+
+        self.sorted_token = view("sorted_token", torch.int64, A)
+        self.sorted_expert = view("sorted_expert", torch.int64, A)
+        self.sorted_weight = view("sorted_weight", torch.float32, A)
+        self.counts = view("counts", torch.int32, E)
+        self.expert_offsets = view("offsets", torch.int32, E)
+        self.act_sf_offsets = view("act_sf_offsets", torch.int32, E)
+        self.inter_sf_offsets = view("inter_sf_offsets", torch.int32, E)
+        self.act_codes = view("act_codes", torch.uint8, A * H).view(A, H)
+        self.act_scales = self.buf[o["act_scales"]:o["inter_codes"]]
+        self.inter_codes = view("inter_codes", torch.uint8, A * I).view(A, I)
+        self.inter_scales = self.buf[o["inter_scales"]:o["router_idx"]]
+
+    @property
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+
+def route_quant(ws: ExpertsWorkspace, hidden, router_indices, routing_weights):
+    _lib.call("gptoss_moe_route_quant", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(),
+              ws.T, ws.k, ws.E, ws.H, ws.I, ws.ptr, ws.buf.numel(), status_tensor(hidden.device).data_ptr(),
+              _stream(hidden.device))
+
+
+def gemm1(ws: ExpertsWorkspace, gu_data, gu_scales, gu_bias, alpha: float = 1.702, limit: float = 7.0,
+          gemm_mode: int = GEMM_AUTO):
+    _lib.call("gptoss_moe_gemm1", ws.T, ws.k, ws.E, ws.H, ws.I, gu_data.data_ptr(), gu_scales.data_ptr(),
+              gu_scales.numel() // ws.E, gu_bias.data_ptr(), float(alpha), float(limit), ws.ptr, ws.buf.numel(),
+              int(gemm_mode), status_tensor(gu_data.device).data_ptr(), _stream(gu_data.device))
+
+
+def gemm2(ws: ExpertsWorkspace, dn_data, dn_scales, dn_bias, out, gemm_mode: int = GEMM_AUTO):
+    _lib.call("gptoss_moe_gemm2", ws.T, ws.k, ws.E, ws.H, ws.I, dn_data.data_ptr(), dn_scales.data_ptr(),
+              dn_scales.numel() // ws.E, dn_bias.data_ptr(), out.data_ptr(), ws.ptr, ws.buf.numel(), int(gemm_mode),
+              status_tensor(dn_data.device).data_ptr(), _stream(dn_data.device))

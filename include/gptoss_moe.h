@@ -169,6 +169,51 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight,
                              void* router_scores_out, void* workspace, size_t workspace_bytes,
                              int gemm_mode, int32_t* status_dev, void* stream);
 
+/* ---- The expert forward as three stages on a shared workspace (same kernels as
+ * gptoss_moe_experts_forward; used for per-stage timing and by expert parallelism,
+ * which exchanges rows between the stages). */
+
+/* Byte offsets of the workspace regions, in this order (GPTOSS_WS_* indices):
+ * sorted_token i64[A], sorted_expert i64[A], sorted_weight f32[A], counts i32[E],
+ * offsets i32[E], act_sf_offsets i32[E], inter_sf_offsets i32[E], act_codes u8[A,H],
+ * act_scales (blocked), inter_codes u8[A,I], inter_scales (blocked), router_idx i64[A],
+ * router_weights f32[A], total bytes. Host only. */
+enum {
+  GPTOSS_WS_SORTED_TOKEN = 0, GPTOSS_WS_SORTED_EXPERT, GPTOSS_WS_SORTED_WEIGHT, GPTOSS_WS_COUNTS,
+  GPTOSS_WS_OFFSETS, GPTOSS_WS_ACT_SF_OFFSETS, GPTOSS_WS_INTER_SF_OFFSETS, GPTOSS_WS_ACT_CODES,
+  GPTOSS_WS_ACT_SCALES, GPTOSS_WS_INTER_CODES, GPTOSS_WS_INTER_SCALES, GPTOSS_WS_ROUTER_IDX,
+  GPTOSS_WS_ROUTER_WEIGHTS, GPTOSS_WS_TOTAL, GPTOSS_WS_NUM_REGIONS
+};
+int gptoss_moe_workspace_layout(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                                int64_t intermediate_size, int64_t* offsets_out /* host [14] */);
+
+/* Stage 1 (fused_moe_routing + hidden[sorted_token] + quantize_activations_to_fp8 +
+ * batch_convert_a_scales_for_w4a8_gpu, kernels/cutlass_experts.py:399-408 and
+ * kernels/matmul_mxfp4_cutlass.cu:912-1004): fills the routing, act_codes and
+ * act_scales regions and zeroes the padding of both blocked scale regions. */
+int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices,
+                           const float* routing_weights, int64_t num_tokens, int top_k,
+                           int num_experts, int64_t hidden_size, int64_t intermediate_size,
+                           void* workspace, size_t workspace_bytes, int32_t* status_dev,
+                           void* stream);
+
+/* Stage 2 (GEMM1 + bias + SwiGLU + requantisation, kernels/cutlass_experts.py:410-427):
+ * reads act_codes/act_scales, writes inter_codes/inter_scales. */
+int gptoss_moe_gemm1(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                     int64_t intermediate_size, const uint8_t* gate_up_data,
+                     const uint8_t* gate_up_scales, int64_t ldb_gate_up, const float* gate_up_bias,
+                     float swiglu_alpha, float swiglu_limit, void* workspace,
+                     size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream);
+
+/* Stage 3 (GEMM2 + bias, x routing weight, scatter-add, kernels/cutlass_experts.py:429-450):
+ * ADDS into out [T,H] bf16 (zero it first for the reference's semantics, or pass a
+ * residual to fuse the residual add). */
+int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                     int64_t intermediate_size, const uint8_t* down_data,
+                     const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                     void* out, void* workspace, size_t workspace_bytes, int gemm_mode,
+                     int32_t* status_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -327,3 +327,43 @@ def numpy_weights(d: dict) -> dict:
 
 __all__.append("numpy_weights")
 _ = math
+
+
+class DequantCPULayer:
+    """The reference's dequantised PyTorch expert path on the CPU, used as the timed CPU
+    baseline: weights are dequantised to bf16 once at construction (not timed); a call
+    runs the router (HF semantics) and the per-expert formulation of
+    kernels/test_cutlass_experts.py:422-455 (bf16 matmuls, fp32 bias, SwiGLU, bf16
+    accumulation over the top-k)."""
+
+    def __init__(self, d: dict, top_k: int = 4, alpha: float = 1.702, limit: float = 7.0):
+        self.top_k, self.alpha, self.limit = top_k, alpha, limit
+        self.router_w, self.router_b = d["router_w"], d["router_b"]
+        E = d["gu_blocks"].shape[0]
+        self.gu = [torch.from_numpy(mxfp4_dequant(d["gu_blocks"][e].numpy(), d["gu_scales"][e].numpy()))
+                   .to(torch.bfloat16) for e in range(E)]
+        self.dn = [torch.from_numpy(mxfp4_dequant(d["dn_blocks"][e].numpy(), d["dn_scales"][e].numpy()))
+                   .to(torch.bfloat16) for e in range(E)]
+        self.gu_bias, self.dn_bias = d["gu_bias"].float(), d["dn_bias"].float()
+
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        T, H = hidden.shape
+        _, scores, idx = router_topk_hf(hidden, self.router_w, self.router_b, self.top_k)
+        w = scores.float()
+        contrib = torch.zeros((T, self.top_k, H), dtype=torch.bfloat16)
+        for e in torch.unique(idx).tolist():
+            tok, kk = torch.nonzero(idx == e, as_tuple=True)
+            x = hidden[tok]
+            gate_up = (x @ self.gu[e].T) + self.gu_bias[e]
+            gate = gate_up[:, ::2].clamp(max=self.limit)
+            up = gate_up[:, 1::2].clamp(min=-self.limit, max=self.limit)
+            inter = (gate * torch.sigmoid(gate * self.alpha) * (up + 1)).to(torch.bfloat16)
+            down = (inter @ self.dn[e].T) + self.dn_bias[e]
+            contrib[tok, kk] = (w[tok, kk].unsqueeze(-1) * down).to(torch.bfloat16)
+        out = torch.zeros((T, H), dtype=torch.bfloat16)
+        for j in range(self.top_k):
+            out += contrib[:, j]
+        return out
+
+
+__all__.append("DequantCPULayer")
