@@ -37,7 +37,7 @@ CONFIGS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from
 # the ncu capture summarised in profiles/ (None until captured for this kernel/config).
-NCU_TRAFFIC_BYTES = {"decode": None, "prefill": None}
+NCU_TRAFFIC_BYTES = {"decode": 294_423_808, "prefill": None}   # profiles/moe_gemm_swap_decode_T32.md
 
 KERNELS_PER_STEP = 5   # router, route_sort, gather_quant, gemm1, gemm2
 
@@ -253,6 +253,9 @@ def run_ours(args):
     Ks = min(K, 500)
     g1_ms, g2_ms, pre_ms = [], [], []
     for i in range(Ks + 3):
+        # hold the stream so every launch of this step is queued before the GPU reaches
+        # it (the staged calls go through Python; no host gap may land inside an event pair)
+        torch.cuda._sleep(2_000_000)
         flush.zero_()
         e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
         e0.record(stream)
@@ -280,7 +283,7 @@ def run_ours(args):
     flops = 2 * T * k * (H * 2 * I + I * H)
 
     # ---------------------------------------------------------------- end to end
-    xh = d_host = x.cpu().pin_memory()
+    xh = x.cpu().pin_memory()
     oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     xd = torch.empty_like(x)
     Ke = min(K, 500)
@@ -302,7 +305,6 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     assert pkg.ops.read_status(dev) == 0
-    del d_host
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -188,9 +188,9 @@ struct GemmJob {
   GemmParams p;
 };
 
-template <bool SWAP, int EPI>
+template <bool SWAP, bool SPREAD, int EPI>
 int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t st) {
-  using C = GemmConfig<SWAP>;
+  using C = GemmConfig<SWAP, SPREAD>;
   if (job.act_rows <= 0) return GPTOSS_OK;
   CUtensorMap ta, ta32, ta16, tw;
   GPTOSS_TRY(make_act_map(&ta, job.act, job.act_rows, job.lda, C::kActRows));
@@ -207,7 +207,7 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(attr_done & (1ull << dev))) {
-      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, SPREAD, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(C::kSmemBytes)));
       attr_done |= (1ull << dev);
     }
@@ -217,17 +217,23 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
   const int64_t tiles_ub = (job.act_rows / C::kActRows + p.num_experts) * static_cast<int64_t>(p.n_tiles);
   const int grid = static_cast<int>(std::min<int64_t>(di.sms, tiles_ub));
   if (grid <= 0) return GPTOSS_OK;
-  return launch_pdl(moe_gemm_kernel<SWAP, EPI>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ta, ta32, ta16,
-                    tw, p);
+  return launch_pdl(moe_gemm_kernel<SWAP, SPREAD, EPI>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ta, ta32,
+                    ta16, tw, p);
+}
+
+// GEMM orientation of one call. The fused pipeline switches to weights-on-M with 16-row
+// activation chunks (and SPREAD activation scales) when the average expert holds at
+// most 16 rows; the reference-layout op uses 64-row chunks up to 48 rows per expert.
+bool pick_swap(int mode, int64_t rows, int experts, int64_t max_avg) {
+  if (mode == GPTOSS_GEMM_SWAP) return true;
+  if (mode == GPTOSS_GEMM_TOKENS_M) return false;
+  return rows <= max_avg * experts;
 }
 
 template <int EPI>
-int run_gemm(const GemmJob& job, int mode, const DeviceInfo& di, int dev, cudaStream_t st) {
-  bool swap;
-  if (mode == GPTOSS_GEMM_SWAP) swap = true;
-  else if (mode == GPTOSS_GEMM_TOKENS_M) swap = false;
-  else swap = job.act_rows <= 48LL * job.p.num_experts;
-  return swap ? launch_gemm<true, EPI>(job, di, dev, st) : launch_gemm<false, EPI>(job, di, dev, st);
+int run_gemm(const GemmJob& job, bool swap, bool spread, const DeviceInfo& di, int dev, cudaStream_t st) {
+  if (!swap) return launch_gemm<false, false, EPI>(job, di, dev, st);
+  return spread ? launch_gemm<true, true, EPI>(job, di, dev, st) : launch_gemm<true, false, EPI>(job, di, dev, st);
 }
 
 // ---------------------------------------------------------------- workspace layout
@@ -242,7 +248,9 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 Workspace plan_workspace(int64_t T, int k, int E, int64_t H, int64_t I) {
   Workspace w{};
   const int64_t A = T * k;
-  const int64_t blocks = (A + 127) / 128 + E;   // upper bound of sum_e ceil(m_e / 128)
+  // upper bound of the 128-row scale blocks of all experts, either scale row layout
+  // (reference: sum ceil(m/128) <= A/128 + E; SPREAD: sum ceil(64 ceil(m/16) / 128) <= A/32 + E)
+  const int64_t blocks = (A + 31) / 32 + E;
   w.act_sf_cap = blocks * (pad128(H) / 128) * 512;
   w.inter_sf_cap = blocks * (pad128(I) / 128) * 512;
   size_t o = 0;
@@ -271,7 +279,7 @@ int router_launch(const void* hidden, const void* weight, const void* bias, int6
   const size_t smem = sizeof(__nv_bfloat16) * tb * H + sizeof(float) * tb * E;
   GPTOSS_CHECK(smem <= 200 * 1024, "router: hidden size %lld too large", (long long)H);
   const int grid = static_cast<int>((T + tb - 1) / tb);
-  const int threads = 32 * std::min(16, E);
+  const int threads = 32 * std::min(tb == 1 ? 32 : 16, E);
   auto go = [&](auto kern) -> int {
     GPTOSS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     return launch_pdl(kern, dim3(grid), dim3(threads), smem, st, static_cast<const __nv_bfloat16*>(hidden),
@@ -329,7 +337,7 @@ WsPtrs ws_ptrs(uint8_t* ws, const Workspace& L) {
 
 // Stage 1: stable counting sort + gather + FP8 quantisation (blocked scales).
 int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E, int64_t H,
-                      int64_t I, const WsPtrs& w, int* status, cudaStream_t st) {
+                      int64_t I, const WsPtrs& w, bool spread, int* status, cudaStream_t st) {
   const int64_t A = T * k;
   const int64_t Kh = pad128(H), Ki = pad128(I);
   RouteSortParams rp{};
@@ -339,6 +347,7 @@ int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, 
   rp.counts = w.counts; rp.offsets = w.offsets;
   rp.sf_offsets_a = w.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = static_cast<int>(H / 32); rp.sf_a = w.act_sf;
   rp.sf_offsets_b = w.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128); rp.groups_b = static_cast<int>(I / 32); rp.sf_b = w.inter_sf;
+  rp.spread = spread ? 1 : 0;
   rp.err = status;
   GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(E), dim3(1024), 0, st, rp));
   const int tpr = quant_threads_per_row(static_cast<int>(H));
@@ -348,12 +357,12 @@ int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, 
                     static_cast<const __nv_bfloat16*>(hidden), A, static_cast<int>(H), tpr,
                     static_cast<const int64_t*>(w.sorted_token), static_cast<const int64_t*>(w.sorted_expert),
                     static_cast<const int32_t*>(w.offsets), static_cast<const int32_t*>(w.sfoff_a),
-                    static_cast<int>(Kh / 128), w.act_codes, w.act_sf, static_cast<uint8_t*>(nullptr));
+                    static_cast<int>(Kh / 128), spread ? 1 : 0, w.act_codes, w.act_sf, static_cast<uint8_t*>(nullptr));
 }
 
 // Stage 2: GEMM1 + bias + SwiGLU + FP8 requantisation.
 int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit,
-                const WsPtrs& w, int mode, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+                const WsPtrs& w, bool swap, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
   const int64_t Kh = pad128(H), Ki = pad128(I);
   GemmJob g1{};
   g1.act = w.act_codes; g1.act_rows = A; g1.lda = H; g1.wgt = wt.gu_data;
@@ -363,12 +372,12 @@ int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g1.p.out = w.inter_codes; g1.p.ld_out = I; g1.p.bias = wt.gu_bias; g1.p.out_sf = w.inter_sf;
   g1.p.out_sf_offsets = w.sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
   g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
-  return run_gemm<kEpiGemm1>(g1, mode, di, dev, st);
+  return run_gemm<kEpiGemm1>(g1, swap, swap, di, dev, st);
 }
 
 // Stage 3: GEMM2 + bias, x routing weight, bf16 scatter-add into out (accumulates).
 int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, void* out, const WsPtrs& w,
-                int mode, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+                bool swap, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
   const int64_t Ki = pad128(I);
   GemmJob g2{};
   g2.act = w.inter_codes; g2.act_rows = A; g2.lda = I; g2.wgt = wt.dn_data;
@@ -376,7 +385,7 @@ int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g2.p.m_sizes = w.counts; g2.p.m_stride = 1; g2.p.row_offsets = w.offsets; g2.p.sfa_offsets = w.sfoff_b;
   g2.p.sfa = w.inter_sf; g2.p.sfb = wt.dn_scales; g2.p.sfb_stride = wt.ldb_dn; g2.p.err = status;
   g2.p.out = out; g2.p.ld_out = H; g2.p.bias = wt.dn_bias; g2.p.token_idx = w.sorted_token; g2.p.row_weights = w.sorted_weight;
-  return run_gemm<kEpiGemm2>(g2, mode, di, dev, st);
+  return run_gemm<kEpiGemm2>(g2, swap, swap, di, dev, st);
 }
 
 // route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch.
@@ -385,10 +394,11 @@ int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, i
                      uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
                      cudaStream_t st, bool out_zeroed) {
   const WsPtrs w = ws_ptrs(ws, L);
-  GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, status, st));
+  const bool swap = pick_swap(mode, T * k, E, 16);
+  GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, swap, status, st));
   if (!out_zeroed) GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
-  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, mode, status, di, dev, st));
-  return stage_gemm2(T * k, E, H, I, wt, out, w, mode, status, di, dev, st);
+  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, swap, status, di, dev, st));
+  return stage_gemm2(T * k, E, H, I, wt, out, w, swap, status, di, dev, st);
 }
 
 int check_dims(int64_t T, int k, int E, int64_t H, int64_t I) {
@@ -481,9 +491,9 @@ int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, ui
   if (dtype == GPTOSS_DTYPE_BF16)
     return launch_pdl(gather_quant_kernel<__nv_bfloat16>, dim3(blocks), dim3(tpr * rpb), 0, st,
                       static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(cols), tpr, no_i64, no_i64, no_i32,
-                      no_i32, 0, codes, no_u8, scales);
+                      no_i32, 0, 0, codes, no_u8, scales);
   return launch_pdl(gather_quant_kernel<float>, dim3(blocks), dim3(tpr * rpb), 0, st, static_cast<const float*>(x), rows,
-                    static_cast<int>(cols), tpr, no_i64, no_i64, no_i32, no_i32, 0, codes, no_u8, scales);
+                    static_cast<int>(cols), tpr, no_i64, no_i64, no_i32, no_i32, 0, 0, codes, no_u8, scales);
 }
 
 int gptoss_swiglu(const void* x, int dtype, int64_t rows, int64_t cols, void* out, float alpha, float limit,
@@ -587,7 +597,8 @@ int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t ld
   job.p.sfb = b_blockscales; job.p.sfb_stride = ldb_blockscale;
   job.p.err = status_dev ? status_dev : di.status_sink;
   job.p.out = out; job.p.ld_out = n; job.p.alphas = alphas;
-  return run_gemm<kEpiPlain>(job, gemm_mode, di, dev, static_cast<cudaStream_t>(stream));
+  return run_gemm<kEpiPlain>(job, pick_swap(gemm_mode, m_total, num_experts, 48), false, di, dev,
+                             static_cast<cudaStream_t>(stream));
 }
 
 size_t gptoss_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
@@ -675,8 +686,8 @@ int gptoss_moe_workspace_layout(int64_t num_tokens, int top_k, int num_experts, 
 
 int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices, const float* routing_weights,
                            int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
-                           int64_t intermediate_size, void* workspace, size_t workspace_bytes, int32_t* status_dev,
-                           void* stream) {
+                           int64_t intermediate_size, void* workspace, size_t workspace_bytes, int gemm_mode,
+                           int32_t* status_dev, void* stream) {
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   DeviceInfo di;
   GPTOSS_TRY(bind_device(workspace, "workspace", &di));
@@ -687,6 +698,7 @@ int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices, co
   if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
   return stage_route_quant(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
                            intermediate_size, ws_ptrs(static_cast<uint8_t*>(workspace), L),
+                           pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
                            status_dev ? status_dev : di.status_sink, static_cast<cudaStream_t>(stream));
 }
 
@@ -710,8 +722,9 @@ int gptoss_moe_gemm1(int64_t num_tokens, int top_k, int num_experts, int64_t hid
   GPTOSS_CUDA(cudaGetDevice(&dev));
   ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias, nullptr, nullptr, 0, nullptr};
   return stage_gemm1(num_tokens * top_k, num_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit,
-                     ws_ptrs(static_cast<uint8_t*>(workspace), L), gemm_mode, status_dev ? status_dev : di.status_sink,
-                     di, dev, static_cast<cudaStream_t>(stream));
+                     ws_ptrs(static_cast<uint8_t*>(workspace), L),
+                     pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
+                     status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream));
 }
 
 int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size, int64_t intermediate_size,
@@ -733,8 +746,9 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
   GPTOSS_CUDA(cudaGetDevice(&dev));
   ExpertWeights w{nullptr, nullptr, 0, nullptr, down_data, down_scales, ldb_down, down_bias};
   return stage_gemm2(num_tokens * top_k, num_experts, hidden_size, intermediate_size, w, out,
-                     ws_ptrs(static_cast<uint8_t*>(workspace), L), gemm_mode, status_dev ? status_dev : di.status_sink,
-                     di, dev, static_cast<cudaStream_t>(stream));
+                     ws_ptrs(static_cast<uint8_t*>(workspace), L),
+                     pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
+                     status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -62,16 +62,18 @@ struct GemmParams {
   float swiglu_alpha, swiglu_limit;
 };
 
-template <bool SWAP>
+template <bool SWAP, bool SPREAD = false>
 struct GemmConfig {
+  static_assert(SWAP || !SPREAD, "spread activation scales are a SWAP-mode layout");
   static constexpr int kWgtRows = SWAP ? 128 : 192;   // weight rows per tile
-  // Activation rows per tile. In SWAP mode a chunk starts 0 or 64 rows into its 128-row
-  // scale block, so the scale TMEM address moves by 0 or 2 columns (the same even
-  // offsets CUTLASS uses for its N=64 / N=192 tiles).
-  static constexpr int kActRows = SWAP ? 64 : 128;
+  // Activation rows per tile. SWAP with reference-layout scales uses 64-row chunks that
+  // start 0 or 64 rows into a 128-row scale block (TMEM column offset 0 or 2); SPREAD
+  // uses 16-row chunks (a 2 KB activation slot, so the ring holds 11 stages).
+  static constexpr int kActRows = SWAP ? (SPREAD ? 16 : 64) : 128;
+  static constexpr int kColChunks = (kActRows + 31) / 32;   // 32-column TMEM loads per tile
   static constexpr int kMmaM = 128;
   static constexpr int kMmaN = SWAP ? kActRows : kWgtRows;
-  static constexpr int kStages = SWAP ? 8 : 5;
+  static constexpr int kStages = SWAP ? (SPREAD ? 11 : 8) : 5;
   static constexpr int kAccBufs = SWAP ? 4 : 2;
   static constexpr int kAccCols = kMmaN;              // fp32 columns per accumulator
   static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
@@ -93,13 +95,13 @@ struct GemmConfig {
 
 constexpr int kMaxExpertsGemm = 256;
 
-template <bool SWAP, int EPI>
+template <bool SWAP, bool SPREAD, int EPI>
 __global__ void __launch_bounds__(192, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,
                     const __grid_constant__ CUtensorMap tm_act32,
                     const __grid_constant__ CUtensorMap tm_act16,
                     const __grid_constant__ CUtensorMap tm_wgt, const GemmParams p) {
-  using C = GemmConfig<SWAP>;
+  using C = GemmConfig<SWAP, SPREAD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ int s_chunk_prefix[kMaxExpertsGemm + 1];
   __shared__ int s_chunks[kMaxExpertsGemm];
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(192, 1)
   // the chunk holds that few (the MMA N follows); the chunk still starts on a 64-row
   // boundary, so the scale TMEM shift stays 0 or 2 columns.
   auto act_rows_of = [&](int e, int ch) -> int {
-    if constexpr (!SWAP) {
+    if constexpr (!SWAP || SPREAD) {
       return C::kActRows;
     } else {
       const int left = p.m_sizes[e * p.m_stride] - ch * C::kActRows;
@@ -196,7 +198,7 @@ __global__ void __launch_bounds__(192, 1)
         decode(t, e, nt, ch);
         const int act_row0 = p.row_offsets[e] + ch * C::kActRows;
         const int wgt_row0 = nt * C::kWgtRows;
-        const int act_blk = (ch * C::kActRows) >> 7;
+        const int act_blk = static_cast<int>(act_sf_row<SPREAD>(static_cast<int64_t>(ch) * C::kActRows) >> 7);
         const uint8_t* sfa_src = p.sfa + p.sfa_offsets[e] + static_cast<int64_t>(act_blk) * p.num_kb * 512;
         const int wblk0 = wgt_row0 >> 7;
         const int nwblk_total = (p.N + 127) >> 7;
@@ -246,7 +248,8 @@ __global__ void __launch_bounds__(192, 1)
         // Column shift selecting the 32-row groups this tile starts at inside the
         // copied 128-row scale blocks.
         const uint32_t wshift = SWAP ? 0u : static_cast<uint32_t>(((nt * C::kWgtRows) & 127) >> 5);
-        const uint32_t ashift = SWAP ? static_cast<uint32_t>(((ch * C::kActRows) & 127) >> 5) : 0u;
+        const uint32_t ashift =
+            SWAP ? static_cast<uint32_t>((act_sf_row<SPREAD>(static_cast<int64_t>(ch) * C::kActRows) & 127) >> 5) : 0u;
         const uint32_t t_sfa = tmem_base + C::kSfActCol;
         const uint32_t t_sfw = tmem_base + C::kSfWgtCol;
         const uint32_t mma_n = SWAP ? static_cast<uint32_t>(act_rows_of(e, ch)) : static_cast<uint32_t>(C::kMmaN);
@@ -299,7 +302,7 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) ok = mbar_wait(accf_bar(b), acc_phase, p.err, kDevTimeoutEpilogue);
       if (!ok) {
         if constexpr (SWAP && EPI == kEpiGemm1) {
-          for (int c = 0; c < 2 * (C::kActRows / 32); ++c) asm volatile("bar.sync 1, 128;" ::: "memory");
+          for (int c = 0; c < 2 * C::kColChunks; ++c) asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         continue;
       }
@@ -415,9 +418,10 @@ __global__ void __launch_bounds__(192, 1)
         const bool vcol = wrow_i < p.N;
         const float bsv = (EPI != kEpiPlain && vcol) ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < C::kActRows / 32; ++c) {
+        for (int c = 0; c < C::kColChunks; ++c) {
           const int a0 = ch * C::kActRows + c * 32;             // first row inside expert
-          const bool live = a0 < m_e;                           // uniform over the CTA
+          const int a_end = min(m_e, ch * C::kActRows + C::kActRows);
+          const bool live = a0 < a_end;                         // uniform over the CTA
           uint32_t r[32];
           if (live) {
             __syncwarp();
@@ -430,7 +434,7 @@ __global__ void __launch_bounds__(192, 1)
               __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                if (vcol && a0 + j < m_e)
+                if (vcol && a0 + j < a_end)
                   o[(static_cast<int64_t>(row0) + a0 + j) * p.ld_out + wrow_i] =
                       __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
               }
@@ -440,7 +444,7 @@ __global__ void __launch_bounds__(192, 1)
               __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 4
               for (int j = 0; j < 32; ++j) {
-                if (a0 + j >= m_e) break;                       // warp-uniform
+                if (a0 + j >= a_end) break;                     // warp-uniform
                 const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
                 const int64_t tok = p.token_idx[grow];
                 const float wr = p.row_weights[grow];
@@ -457,7 +461,7 @@ __global__ void __launch_bounds__(192, 1)
             const int f = wrow_i >> 1;                          // intermediate feature
             const int grp = f >> 5;                             // quant group (2 warps)
             float hv[32];
-            const int nv = min(32, m_e - a0);                   // valid rows, warp-uniform
+            const int nv = min(32, a_end - a0);                 // valid rows, warp-uniform
             if (live) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -497,7 +501,7 @@ __global__ void __launch_bounds__(192, 1)
                 if ((lane & 1) == 0 && vcol && f < p.out_features)
                   codes_out[grow * p.ld_out + f] = static_cast<uint8_t>(c2 & 0xFFu);
                 if (lane == 0 && (q & 1) == 0 && f < p.out_features)
-                  p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(a0 + j, grp, p.out_g4)] =
+                  p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(act_sf_row<SPREAD>(a0 + j), grp, p.out_g4)] =
                       static_cast<uint8_t>((rb >> 23) & 0xFFu);
               }
             }

@@ -32,6 +32,26 @@ __host__ __device__ __forceinline__ int64_t blocked_sf_cosize(int64_t rows, int 
   return ((rows + 127) / 128) * static_cast<int64_t>((groups + 3) / 4) * 512;
 }
 
+// Activation scale rows. SPREAD places real row r at scale row 64*(r/16) + r%16, so every
+// 16-row chunk starts at scale row 0 or 64 of a 128-row block: its scales sit at a TMEM
+// column offset of 0 or 2 (the even offsets CUTLASS uses for N=64 / N=192 tiles).
+template <bool SPREAD>
+__host__ __device__ __forceinline__ int64_t act_sf_row(int64_t r) {
+  if constexpr (SPREAD) return ((r >> 4) << 6) + (r & 15);
+  else return r;
+}
+
+// Scale rows (padded to 128) one expert of m rows occupies.
+__host__ __device__ __forceinline__ int64_t act_sf_rows(int64_t m, bool spread) {
+  const int64_t rows = spread ? ((m + 15) / 16) * 64 : m;
+  return (rows + 127) / 128 * 128;
+}
+
+// Bytes of one expert's activation scale region for m rows.
+__host__ __device__ __forceinline__ int64_t act_sf_cosize(int64_t m, int groups, bool spread) {
+  return m > 0 ? act_sf_rows(m, spread) / 128 * static_cast<int64_t>((groups + 3) / 4) * 512 : 0;
+}
+
 __device__ __forceinline__ float torch_max_abs(float m, float x) {
   // torch.max propagates NaN; fmaxf would drop it.
   const float a = fabsf(x);

@@ -32,7 +32,7 @@ constexpr int kMaxTopK = 8;
 constexpr int kRouterVecChunk = 12;   // 8-element slices per lane per pass (H <= 3072 in one pass)
 
 template <int TB>
-__global__ void __launch_bounds__(512) router_topk_kernel(
+__global__ void __launch_bounds__(TB == 1 ? 1024 : 512) router_topk_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ bias, int T, int H, int E, int K,
     int64_t* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_scores,
@@ -110,38 +110,56 @@ __global__ void __launch_bounds__(512) router_topk_kernel(
   }
   __syncthreads();
 
-  // Top-k (ties -> lower expert index first) and softmax over the selected logits.
-  if (threadIdx.x < ntok) {
-    const int t = threadIdx.x;
+  // Top-k (ties -> lower expert index first) and softmax over the selected logits; one
+  // warp per token, each lane holding experts lane, lane + 32, ...
+  for (int t = warp; t < ntok; t += nwarps) {
     const float* lg = logits + t * E;
+    float lv[kMaxExperts / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      const int e = lane + 32 * i;
+      lv[i] = e < E ? lg[e] : -INFINITY;
+    }
     int sel[kMaxTopK];
     float val[kMaxTopK];
     for (int j = 0; j < K; ++j) {
-      int best = -1;
-      float bv = 0.0f;
-      for (int e = 0; e < E; ++e) {
-        bool taken = false;
-        for (int q = 0; q < j; ++q) taken |= (sel[q] == e);
-        if (taken) continue;
-        const float v = lg[e];
-        if (best < 0 || v > bv || (v != v && bv == bv)) { best = e; bv = v; }
+      // lane-local best (NaN counts as largest, like torch.topk), then a warp argmax
+      float bv = -INFINITY;
+      int be = 0x7fffffff;                 // no candidate yet
+#pragma unroll
+      for (int i = 0; i < kMaxExperts / 32; ++i) {
+        const int e = lane + 32 * i;       // ascending, so a tie keeps the lower id
+        const bool better = lv[i] > bv || (lv[i] != lv[i] && bv == bv);
+        if (e < E && (be == 0x7fffffff || better)) { bv = lv[i]; be = e; }
       }
-      sel[j] = best;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        const bool better = (ov > bv) || (ov != ov && bv == bv) || ((ov == bv || (ov != ov && bv != bv)) && oe < be);
+        if (better) { bv = ov; be = oe; }
+      }
+      sel[j] = be;
       val[j] = bv;
+#pragma unroll
+      for (int i = 0; i < kMaxExperts / 32; ++i)
+        if (lane + 32 * i == be) lv[i] = -INFINITY;   // selected
     }
-    const float m = val[0];
-    float ex[kMaxTopK], s = 0.0f;
-    for (int j = 0; j < K; ++j) { ex[j] = expf(__fsub_rn(val[j], m)); s = __fadd_rn(s, ex[j]); }
-    const float inv = __frcp_rn(s);
-    const int64_t tg = t0 + t;
-    for (int j = 0; j < K; ++j) {
-      const __nv_bfloat16 pr = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
-      out_idx[tg * K + j] = sel[j];
-      if (out_scores) out_scores[tg * K + j] = pr;
-      if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(pr);
+    if (lane == 0) {
+      const float m = val[0];
+      float ex[kMaxTopK], s = 0.0f;
+      for (int j = 0; j < K; ++j) { ex[j] = expf(__fsub_rn(val[j], m)); s = __fadd_rn(s, ex[j]); }
+      const float inv = __frcp_rn(s);
+      const int64_t tg = t0 + t;
+      for (int j = 0; j < K; ++j) {
+        const __nv_bfloat16 pr = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
+        out_idx[tg * K + j] = sel[j];
+        if (out_scores) out_scores[tg * K + j] = pr;
+        if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(pr);
+      }
     }
     if (out_logits)
-      for (int e = 0; e < E; ++e) out_logits[tg * E + e] = __float2bfloat16_rn(lg[e]);
+      for (int e = lane; e < E; e += 32) out_logits[(t0 + t) * static_cast<int64_t>(E) + e] = __float2bfloat16_rn(lg[e]);
   }
 }
 
@@ -163,6 +181,7 @@ struct RouteSortParams {
   int32_t* sf_offsets_b;           // [E] bytes, intermediate layout
   int g4_b, groups_b;
   uint8_t* sf_b;
+  int spread;                      // activation scales in the SPREAD row layout
   int* err;                        // set if an index is outside [0, E)
 };
 
@@ -186,25 +205,54 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
     atomicAdd(&hist[ex], 1);
   }
   __syncthreads();
-  int off = 0;
-  for (int q = 0; q < e; ++q) off += hist[q];
+  // Exclusive prefixes of the counts and of both scale-region sizes, once, by warp 0
+  // (E <= 256: eight values per lane, then a warp scan).
+  __shared__ int s_off[kMaxExperts];
+  __shared__ int64_t s_sfa[kMaxExperts], s_sfb[kMaxExperts];
+  if (warp == 0) {
+    int c_run = 0;
+    int64_t a_run = 0, b_run = 0;
+    const int per = (p.E + 31) / 32;
+    const int q0 = lane * per;
+    int cl[8];
+    int64_t al[8], bl[8];
+    for (int i = 0; i < per; ++i) {
+      const int q = q0 + i;
+      const int c = q < p.E ? hist[q] : 0;
+      cl[i] = c;
+      al[i] = (q < p.E && p.sf_offsets_a) ? act_sf_cosize(c, p.g4_a * 4, p.spread != 0) : 0;
+      bl[i] = (q < p.E && p.sf_offsets_a) ? act_sf_cosize(c, p.g4_b * 4, p.spread != 0) : 0;
+      c_run += c; a_run += al[i]; b_run += bl[i];
+    }
+    int c_inc = c_run;
+    int64_t a_inc = a_run, b_inc = b_run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int c2 = __shfl_up_sync(0xffffffffu, c_inc, o);
+      const int64_t a2 = __shfl_up_sync(0xffffffffu, a_inc, o);
+      const int64_t b2 = __shfl_up_sync(0xffffffffu, b_inc, o);
+      if (lane >= o) { c_inc += c2; a_inc += a2; b_inc += b2; }
+    }
+    int c_ex = c_inc - c_run;
+    int64_t a_ex = a_inc - a_run, b_ex = b_inc - b_run;
+    for (int i = 0; i < per; ++i) {
+      const int q = q0 + i;
+      if (q < p.E) { s_off[q] = c_ex; s_sfa[q] = a_ex; s_sfb[q] = b_ex; }
+      c_ex += cl[i]; a_ex += al[i]; b_ex += bl[i];
+    }
+  }
+  __syncthreads();
+  const int off = s_off[e];
   const int cnt = hist[e];
   if (tid == 0) {
     p.counts[e] = cnt;
     p.offsets[e] = off;
     s_base = 0;
-  }
-  if (p.sf_offsets_a != nullptr && tid == 0) {
-    int64_t sa = 0, sb = 0;
-    for (int q = 0; q < e; ++q) {
-      sa += blocked_sf_cosize(hist[q], p.g4_a * 4);
-      sb += blocked_sf_cosize(hist[q], p.g4_b * 4);
+    if (p.sf_offsets_a != nullptr) {
+      p.sf_offsets_a[e] = static_cast<int32_t>(s_sfa[e]);
+      p.sf_offsets_b[e] = static_cast<int32_t>(s_sfb[e]);
     }
-    p.sf_offsets_a[e] = static_cast<int32_t>(sa);
-    p.sf_offsets_b[e] = static_cast<int32_t>(sb);
-    s_base = 0;
   }
-  __syncthreads();
   // Zero this expert's blocked scale regions (16-byte stores); the quantisers that run
   // after this kernel overwrite the valid entries, so the padding ends up zero.
   if (p.sf_offsets_a != nullptr) {
@@ -212,14 +260,13 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
       uint8_t* buf = pass == 0 ? p.sf_a : p.sf_b;
       const int gp = (pass == 0 ? p.g4_a : p.g4_b) * 4;
       if (buf == nullptr) continue;
-      int64_t base = 0;
-      for (int q = 0; q < e; ++q) base += blocked_sf_cosize(hist[q], gp);
-      uint4* dst = reinterpret_cast<uint4*>(buf + base);     // base is a multiple of 512
-      const int64_t n16 = blocked_sf_cosize(cnt, gp) >> 4;
+      uint4* dst = reinterpret_cast<uint4*>(buf + (pass == 0 ? s_sfa[e] : s_sfb[e]));   // multiple of 512
+      const int64_t n16 = act_sf_cosize(cnt, gp, p.spread != 0) >> 4;
       const uint4 z = make_uint4(0, 0, 0, 0);
       for (int64_t i = tid; i < n16; i += blockDim.x) dst[i] = z;
     }
   }
+  __syncthreads();
   // Pass 2: stable compaction of this expert's assignments, 1024 at a time.
   for (int c0 = 0; c0 < p.A; c0 += blockDim.x) {
     const int i = c0 + tid;
@@ -254,7 +301,7 @@ template <typename InT>
 __global__ void __launch_bounds__(256) gather_quant_kernel(
     const InT* __restrict__ src, int64_t rows, int H, int tpr, const int64_t* __restrict__ sorted_token,
     const int64_t* __restrict__ sorted_expert, const int32_t* __restrict__ offsets,
-    const int32_t* __restrict__ sf_offsets, int g4, uint8_t* __restrict__ out_codes,
+    const int32_t* __restrict__ sf_offsets, int g4, int spread, uint8_t* __restrict__ out_codes,
     uint8_t* __restrict__ sf_blocked, uint8_t* __restrict__ sf_rowmajor) {
   pdl_trigger();
   pdl_wait();
@@ -269,6 +316,7 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
     src_row = sorted_token[row];
     const int ex = static_cast<int>(sorted_expert[row]);
     r_in = row - offsets[ex];
+    if (spread) r_in = act_sf_row<true>(r_in);
     sf_base = sf_offsets[ex];
   }
   const InT* xr = src + src_row * H;

@@ -425,10 +425,10 @@ class ExpertsWorkspace:
         return self.buf.data_ptr()
 
 
-def route_quant(ws: ExpertsWorkspace, hidden, router_indices, routing_weights):
+def route_quant(ws: ExpertsWorkspace, hidden, router_indices, routing_weights, gemm_mode: int = GEMM_AUTO):
     _lib.call("gptoss_moe_route_quant", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(),
-              ws.T, ws.k, ws.E, ws.H, ws.I, ws.ptr, ws.buf.numel(), status_tensor(hidden.device).data_ptr(),
-              _stream(hidden.device))
+              ws.T, ws.k, ws.E, ws.H, ws.I, ws.ptr, ws.buf.numel(), int(gemm_mode),
+              status_tensor(hidden.device).data_ptr(), _stream(hidden.device))
 
 
 def gemm1(ws: ExpertsWorkspace, gu_data, gu_scales, gu_bias, alpha: float = 1.702, limit: float = 7.0,

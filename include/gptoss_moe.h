@@ -41,7 +41,10 @@ enum {
 enum { GPTOSS_DTYPE_BF16 = 0, GPTOSS_DTYPE_F32 = 1 };
 
 /* GEMM orientation: AUTO picks SWAP (weights on the MMA M side) when the average
- * expert holds <= 48 rows, else TOKENS_M. Results agree to fp32 accumulation order. */
+ * expert holds few rows (<= 16 in the fused expert forward and its stages, <= 48 in
+ * gptoss_fp4_group_mm), else TOKENS_M. Results agree to fp32 accumulation order. The
+ * stages of one forward (route_quant, gemm1, gemm2) must be called with the same mode:
+ * it also selects the row layout of the activation scales in the workspace. */
 enum { GPTOSS_GEMM_AUTO = 0, GPTOSS_GEMM_TOKENS_M = 1, GPTOSS_GEMM_SWAP = 2 };
 
 /* Message for the last failing call on this thread ("" if none). */
@@ -194,8 +197,8 @@ int gptoss_moe_workspace_layout(int64_t num_tokens, int top_k, int num_experts, 
 int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices,
                            const float* routing_weights, int64_t num_tokens, int top_k,
                            int num_experts, int64_t hidden_size, int64_t intermediate_size,
-                           void* workspace, size_t workspace_bytes, int32_t* status_dev,
-                           void* stream);
+                           void* workspace, size_t workspace_bytes, int gemm_mode,
+                           int32_t* status_dev, void* stream);
 
 /* Stage 2 (GEMM1 + bias + SwiGLU + requantisation, kernels/cutlass_experts.py:410-427):
  * reads act_codes/act_scales, writes inter_codes/inter_scales. */

@@ -169,3 +169,35 @@ def test_empty_batch(pkg, dev):
 
 def test_cfg_roundtrip():
     assert Cfg(4, 8, 8).num_local_experts == 4
+
+
+@pytest.mark.parametrize("mode", ["tokens_m", "swap"])
+def test_fused_route_quant_stage_bit_exact(pkg, dev, mode):
+    # The fused path's first stage (counting sort + gather + FP8 quantisation straight into
+    # the blocked scale layout) reproduces the reference's GEMM1 inputs byte for byte.
+    import hashlib
+    for name in ("small", "decode", "cpu_ref"):
+        seed, E, H, I, T, k = MG.LAYERS[name]
+        g = golden(f"layer_{name}.npz")
+        d, idx, w = MG.layer_inputs(name)
+        ws = pkg.ops.ExpertsWorkspace(T, k, E, H, I, dev)
+        pkg.ops.route_quant(ws, d["hidden"].to(dev), idx.to(dev), w.to(dev), MODES[mode])
+        torch.cuda.synchronize()
+        st, se, sw, counts, offsets = O.route_stable(idx.numpy(), w.numpy(), E)
+        assert np.array_equal(ws.sorted_token.cpu().numpy(), st)
+        assert np.array_equal(ws.counts.cpu().numpy(), counts)
+        codes = ws.act_codes.cpu().numpy()
+        assert hashlib.sha256(codes.tobytes()).hexdigest() == bytes(g["act_codes_sha"]).decode()
+        # decode the blocked scales back to row-major
+        spread = mode == "swap"
+        blob = ws.act_scales.cpu().numpy()
+        sfo = ws.act_sf_offsets.cpu().numpy()
+        G, g4 = H // 32, (O.pad_k_to_tile(H) // 32 + 3) // 4
+        rows = np.zeros((T * k, G), dtype=np.uint8)
+        for e in range(E):
+            m, o = int(counts[e]), int(offsets[e])
+            r = np.arange(m)
+            srow = ((r // 16) * 64 + r % 16) if spread else r
+            for gg in range(G):
+                rows[o:o + m, gg] = blob[sfo[e] + O.blocked_sf_offset(srow, gg, g4)]
+        assert hashlib.sha256(rows.tobytes()).hexdigest() == bytes(g["act_scales_sha"]).decode()
