@@ -40,6 +40,9 @@ _SIGNATURES = {
     "gptoss_moe_layer_forward": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64,
                                       _vp, _vp, _c_int64, _vp, _vp, _vp, _c_int64, _vp,
                                       _f, _f, _vp, _vp, _vp, _vp, _sz, _i, _vp, _vp]),
+    "gptoss_moe_experts_forward_noalloc": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64,
+                                                _vp, _vp, _c_int64, _vp, _vp, _vp, _c_int64, _vp,
+                                                _f, _f, _vp, _i, _vp, _vp]),
     "gptoss_moe_workspace_layout": (_i, [_c_int64, _i, _i, _c_int64, _c_int64, _vp]),
     "gptoss_moe_route_quant": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64, _vp, _sz, _i, _vp, _vp]),
     "gptoss_moe_gemm1": (_i, [_c_int64, _i, _i, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _sz,

@@ -411,6 +411,30 @@ int check_dims(int64_t T, int k, int E, int64_t H, int64_t I) {
   return GPTOSS_OK;
 }
 
+// ---------------------------------------------------------------- no-allocation forward
+// Scratch of gptoss_moe_experts_forward_noalloc. It is a module global, so every GPU
+// that loads this library holds GPTOSS_NOALLOC_SCRATCH_BYTES of it until the process
+// exits. Host code cannot use the symbol as a device address: the address is looked up
+// once per device with cudaGetSymbolAddress while that device is current.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[GPTOSS_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(int dev, uint8_t** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(GPTOSS_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return GPTOSS_OK;
+}
+
 }  // namespace
 
 // ======================================================================= C ABI
@@ -749,6 +773,40 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
                      ws_ptrs(static_cast<uint8_t*>(workspace), L),
                      pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
                      status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream));
+}
+
+int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router_indices,
+                                       const float* routing_weights, int64_t num_tokens, int top_k, int num_experts,
+                                       int64_t hidden_size, int64_t intermediate_size, const uint8_t* gate_up_data,
+                                       const uint8_t* gate_up_scales, int64_t ldb_gate_up, const float* gate_up_bias,
+                                       const uint8_t* down_data, const uint8_t* down_scales, int64_t ldb_down,
+                                       const float* down_bias, float swiglu_alpha, float swiglu_limit, void* out,
+                                       int gemm_mode, int32_t* status_dev, void* stream) {
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                  down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(w, hidden_size, intermediate_size, num_experts));
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (L.total > static_cast<size_t>(GPTOSS_NOALLOC_SCRATCH_BYTES))
+    return fail(GPTOSS_ERR_INVALID_ARGUMENT,
+                "experts_forward_noalloc: this batch needs %zu bytes of scratch but the library's static "
+                "scratch holds %zu (GPTOSS_NOALLOC_SCRATCH_BYTES); use gptoss_moe_experts_forward with a "
+                "caller workspace or fewer tokens",
+                L.total, static_cast<size_t>(GPTOSS_NOALLOC_SCRATCH_BYTES));
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(hidden && router_indices && routing_weights && out, "experts_forward_noalloc: null pointer");
+  GPTOSS_CHECK(aligned(hidden, 16) && aligned(out, 16), "experts_forward_noalloc: misaligned pointer");
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  uint8_t* ws = nullptr;
+  GPTOSS_TRY(noalloc_scratch(dev, &ws));
+  return experts_pipeline(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
+                          intermediate_size, w, swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode,
+                          status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream),
+                          false);
 }
 
 }  // extern "C"

@@ -217,6 +217,37 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
                      void* out, void* workspace, size_t workspace_bytes, int gemm_mode,
                      int32_t* status_dev, void* stream);
 
+/* ---- Expert forward without any device allocation.
+ *
+ * No counterpart in the reference. Some callers cannot hand this library a workspace or let
+ * it allocate one: runtimes that reserve all device memory up front behind their own pool
+ * (an out-of-band cudaMalloc fails there), hosts that bind the C ABI through an FFI and have
+ * no device allocator to call, and latency-critical loops that cannot pay for cudaMalloc /
+ * cudaFree, which synchronise the device. For them this entry point runs the same five kernels
+ * as gptoss_moe_experts_forward with the workspace in a static device array of
+ * GPTOSS_NOALLOC_SCRATCH_BYTES inside this library (every GPU that loads the library holds it
+ * until the process exits). Batches whose workspace (gptoss_moe_workspace_bytes) exceeds that
+ * size are rejected with GPTOSS_ERR_INVALID_ARGUMENT — at H = I = 2880 and 32 experts that
+ * is about 2,400 token-expert assignments (600 tokens at top-4). The first call on a device
+ * does a one-time set-up: it looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current) and caches it; make that first call before any stream capture
+ * begins. All calls share the one
+ * array and it keeps the previous call's contents; every region is rewritten before it is
+ * read, so nothing needs clearing, but calls that overlap on the GPU (other streams, other
+ * threads) race on it. Inputs, outputs and the status word are the caller's, exactly as in
+ * gptoss_moe_experts_forward; no cudaMalloc, cudaFree or allocating library routine is called. */
+#define GPTOSS_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router_indices,
+                                       const float* routing_weights, int64_t num_tokens,
+                                       int top_k, int num_experts, int64_t hidden_size,
+                                       int64_t intermediate_size, const uint8_t* gate_up_data,
+                                       const uint8_t* gate_up_scales, int64_t ldb_gate_up,
+                                       const float* gate_up_bias, const uint8_t* down_data,
+                                       const uint8_t* down_scales, int64_t ldb_down,
+                                       const float* down_bias, float swiglu_alpha,
+                                       float swiglu_limit, void* out, int gemm_mode,
+                                       int32_t* status_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
