@@ -26,3 +26,4 @@ from .cutlass_experts import (  # noqa: F401
     swiglu,
 )
 from .layer import GptOssMoELayer  # noqa: F401
+from . import ep  # noqa: F401,E402

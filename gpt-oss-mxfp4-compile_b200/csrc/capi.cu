@@ -809,4 +809,135 @@ int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router
                           false);
 }
 
+// ---------------------------------------------------------------- expert parallelism
+int64_t gptoss_ep_row_bytes(int64_t hidden_size) {
+  if (hidden_size <= 0 || hidden_size % 32 != 0) return 0;
+  return ep_row_bytes(static_cast<int>(hidden_size));
+}
+
+size_t gptoss_ep_dispatch_workspace_bytes(int64_t num_tokens, int top_k, int world_size) {
+  if (num_tokens < 0 || top_k < 1 || world_size < 1) return 0;
+  const size_t A = static_cast<size_t>(num_tokens) * top_k;
+  return align256(sizeof(int64_t) * A) * 2 + align256(sizeof(float) * A) + align256(sizeof(int32_t) * A) +
+         align256(sizeof(int32_t) * world_size);
+}
+
+int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
+                       int64_t num_tokens, int top_k, int num_experts, int world_size, int64_t hidden_size,
+                       uint8_t* send_rows, int32_t* send_counts, int32_t* pos_of, void* workspace,
+                       size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  GPTOSS_CHECK(world_size >= 1 && world_size <= kMaxExperts, "ep_dispatch: world_size must be in [1, %d]", kMaxExperts);
+  GPTOSS_CHECK(num_experts >= world_size && num_experts % world_size == 0,
+               "ep_dispatch: num_experts (%d) must be a multiple of world_size (%d)", num_experts, world_size);
+  GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK && top_k <= num_experts,
+               "ep_dispatch: bad sizes (T=%lld k=%d)", (long long)num_tokens, top_k);
+  GPTOSS_CHECK(hidden_size > 0 && hidden_size % 32 == 0, "ep_dispatch: hidden size must be a multiple of 32");
+  GPTOSS_CHECK(num_tokens * top_k < (1LL << 31), "ep_dispatch: too many assignments");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(send_counts, "send_counts", &di));
+  const size_t need = gptoss_ep_dispatch_workspace_bytes(num_tokens, top_k, world_size);
+  if (workspace_bytes < need) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t A = num_tokens * top_k;
+  if (A == 0) {
+    GPTOSS_CUDA(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world_size, st));
+    return GPTOSS_OK;
+  }
+  GPTOSS_CHECK(hidden && router_indices && routing_weights && send_rows && pos_of && workspace,
+               "ep_dispatch: null pointer");
+  GPTOSS_CHECK(aligned(hidden, 16) && aligned(send_rows, 16) && aligned(workspace, 256),
+               "ep_dispatch: misaligned pointer");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  size_t o = 0;
+  auto take = [&](size_t bytes) { uint8_t* r = ws + o; o += align256(bytes); return r; };
+  RouteSortParams rp{};
+  rp.router_indices = router_indices; rp.routing_weights = routing_weights;
+  rp.A = static_cast<int>(A); rp.K = top_k; rp.E = world_size;
+  rp.sorted_token = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * A));
+  rp.sorted_expert = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * A));
+  rp.sorted_weight = reinterpret_cast<float*>(take(sizeof(float) * A));
+  rp.sorted_src = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * A));
+  rp.offsets = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * world_size));
+  rp.counts = send_counts;
+  rp.divisor = num_experts / world_size;
+  rp.err = status_dev ? status_dev : di.status_sink;
+  GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(world_size), dim3(1024), 0, st, rp));
+  const int tpr = quant_threads_per_row(static_cast<int>(hidden_size));
+  const int rpb = 256 / tpr;
+  return launch_pdl(ep_pack_kernel, dim3(static_cast<unsigned>((A + rpb - 1) / rpb)), dim3(tpr * rpb), 0, st,
+                    static_cast<const __nv_bfloat16*>(hidden), static_cast<int>(hidden_size), top_k,
+                    num_experts / world_size, A, router_indices, routing_weights,
+                    static_cast<const int32_t*>(rp.sorted_src), tpr, send_rows, pos_of);
+}
+
+int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num_local_experts, int64_t hidden_size,
+                             int64_t intermediate_size, const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                             int64_t ldb_gate_up, const float* gate_up_bias, const uint8_t* down_data,
+                             const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                             float swiglu_alpha, float swiglu_limit, void* back_rows, void* workspace,
+                             size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
+  GPTOSS_TRY(check_dims(num_rows, 1, num_local_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                  down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(w, hidden_size, intermediate_size, num_local_experts));
+  if (num_rows == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(recv_rows && back_rows && workspace, "ep_expert_forward: null pointer");
+  GPTOSS_CHECK(aligned(recv_rows, 16) && aligned(back_rows, 16) && aligned(workspace, 256),
+               "ep_expert_forward: misaligned pointer");
+  const Workspace L = plan_workspace(num_rows, 1, num_local_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const WsPtrs p = ws_ptrs(ws, L);
+  int* status = status_dev ? status_dev : di.status_sink;
+  int64_t* lexp = reinterpret_cast<int64_t*>(ws + L.router_idx);
+  float* lw = reinterpret_cast<float*>(ws + L.router_w);
+  const bool swap = pick_swap(gemm_mode, num_rows, num_local_experts, 16);
+  const int H = static_cast<int>(hidden_size);
+  const int64_t Kh = pad128(hidden_size), Ki = pad128(intermediate_size);
+  const int ublocks = static_cast<int>(std::min<int64_t>((num_rows + 255) / 256, 4 * di.sms));
+  GPTOSS_TRY(launch_pdl(ep_unpack_meta_kernel, dim3(ublocks), dim3(256), 0, st, recv_rows, num_rows, H, lexp, lw));
+  RouteSortParams rp{};
+  rp.router_indices = lexp; rp.routing_weights = lw;
+  rp.A = static_cast<int>(num_rows); rp.K = 1; rp.E = num_local_experts;
+  rp.sorted_token = p.sorted_token; rp.sorted_expert = p.sorted_expert; rp.sorted_weight = p.sorted_weight;
+  rp.counts = p.counts; rp.offsets = p.offsets;
+  rp.sf_offsets_a = p.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = H / 32; rp.sf_a = p.act_sf;
+  rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
+  rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
+  rp.spread = swap ? 1 : 0;
+  rp.err = status;
+  GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
+  GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(num_rows)), dim3(256), 0, st, recv_rows,
+                        num_rows, H, static_cast<const int64_t*>(p.sorted_token),
+                        static_cast<const int64_t*>(p.sorted_expert), static_cast<const int32_t*>(p.offsets),
+                        static_cast<const int32_t*>(p.sfoff_a), static_cast<int>(Kh / 128), swap ? 1 : 0,
+                        p.act_codes, p.act_sf));
+  GPTOSS_CUDA(cudaMemsetAsync(back_rows, 0, static_cast<size_t>(num_rows * hidden_size) * sizeof(__nv_bfloat16), st));
+  GPTOSS_TRY(stage_gemm1(num_rows, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p,
+                         swap, status, di, dev, st));
+  return stage_gemm2(num_rows, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, swap, status, di,
+                     dev, st);
+}
+
+int gptoss_ep_combine(const void* back_rows, const int32_t* pos_of, const int64_t* router_indices, int64_t num_tokens,
+                      int top_k, int64_t hidden_size, void* out, void* stream) {
+  GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK, "ep_combine: bad sizes");
+  GPTOSS_CHECK(hidden_size > 0 && hidden_size % 2 == 0, "ep_combine: hidden size must be even");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(out, "out", &di));
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(back_rows && pos_of && router_indices, "ep_combine: null pointer");
+  GPTOSS_CHECK(aligned(back_rows, 4) && aligned(out, 4), "ep_combine: misaligned pointer");
+  return launch_pdl(ep_combine_kernel, dim3(static_cast<unsigned>(num_tokens)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(back_rows), pos_of,
+                    router_indices, num_tokens, top_k, static_cast<int>(hidden_size),
+                    static_cast<__nv_bfloat16*>(out));
+}
+
 }  // extern "C"

@@ -1,5 +1,5 @@
 // Thin inline-PTX layer for sm_100a: mbarriers with bounded waits, TMA (tensor and
-// bulk, no multicast anywhere), tcgen05 (alloc / mma / cp / ld / commit / fences) and
+// bulk; every load targets this CTA only), tcgen05 (alloc / mma / cp / ld / commit / fences) and
 // the shared-memory and instruction descriptors the block-scaled MMA consumes.
 //
 // Descriptor bit layouts follow the PTX ISA "tcgen05 matrix descriptors" and

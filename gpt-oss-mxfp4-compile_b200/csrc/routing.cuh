@@ -182,6 +182,8 @@ struct RouteSortParams {
   int g4_b, groups_b;
   uint8_t* sf_b;
   int spread;                      // activation scales in the SPREAD row layout
+  int divisor;                     // bucket of assignment i = router_indices[i] / divisor (0, 1: expert)
+  int32_t* sorted_src;             // optional [A]: assignment index i of each sorted entry
   int* err;                        // set if an index is outside [0, E)
 };
 
@@ -193,12 +195,13 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
   pdl_wait();
   const int e = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t dv = p.divisor > 1 ? p.divisor : 1;
   for (int i = tid; i < p.E; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   // Pass 1: full histogram (every CTA builds it; A is small next to the GEMMs).
   for (int i = tid; i < p.A; i += blockDim.x) {
-    const int64_t ex = p.router_indices[i];
-    if (ex < 0 || ex >= p.E) {
+    const int64_t ex = p.router_indices[i] / dv;
+    if (p.router_indices[i] < 0 || ex >= p.E) {
       if (p.err) atomicCAS(p.err, 0, 0x201);
       continue;
     }
@@ -266,11 +269,21 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
       for (int64_t i = tid; i < n16; i += blockDim.x) dst[i] = z;
     }
   }
+  // Entries past the last valid one (only when some index was out of range) get the
+  // sentinel -1, which every consumer of the sorted arrays skips.
+  if (e == p.E - 1) {
+    for (int i = off + cnt + tid; i < p.A; i += blockDim.x) {
+      p.sorted_token[i] = -1;
+      p.sorted_expert[i] = -1;
+      p.sorted_weight[i] = 0.0f;
+      if (p.sorted_src) p.sorted_src[i] = -1;
+    }
+  }
   __syncthreads();
   // Pass 2: stable compaction of this expert's assignments, 1024 at a time.
   for (int c0 = 0; c0 < p.A; c0 += blockDim.x) {
     const int i = c0 + tid;
-    const bool mine = (i < p.A) && (p.router_indices[i] == e);
+    const bool mine = (i < p.A) && (p.router_indices[i] >= 0) && (p.router_indices[i] / dv == e);
     const unsigned bal = __ballot_sync(0xffffffffu, mine);
     if (lane == 0) warp_cnt[warp] = __popc(bal);
     __syncthreads();
@@ -283,6 +296,7 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
       const int pos = off + s_base + before + __popc(bal & ((1u << lane) - 1u));
       p.sorted_token[pos] = i / p.K;
       p.sorted_expert[pos] = e;
+      if (p.sorted_src) p.sorted_src[pos] = i;
       p.sorted_weight[pos] = p.routing_weights[i];
     }
     __syncthreads();
@@ -314,6 +328,7 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
   int64_t sf_base = 0, r_in = 0;
   if (sorted_token != nullptr) {
     src_row = sorted_token[row];
+    if (src_row < 0) return;   // sentinel of an out-of-range router index
     const int ex = static_cast<int>(sorted_expert[row]);
     r_in = row - offsets[ex];
     if (spread) r_in = act_sf_row<true>(r_in);
@@ -425,6 +440,136 @@ __global__ void swiglu_kernel(const T* __restrict__ in, int64_t rows, int64_t n,
       const float u1 = bf16_round(__fadd_rn(u, 1.0f));
       out[i] = __float2bfloat16_rn(__fmul_rn(gs, u1));
     }
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Expert parallelism. A dispatched row carries everything the receiving rank needs:
+//   [FP8 codes H | UE8M0 scales H/32 | pad | local expert int32 | routing weight f32]
+// padded to a multiple of 16 bytes (H = 2880: 2992 bytes). Rows are quantised before they
+// are sent (quantisation is per row, so the codes equal the single-GPU ones).
+__host__ __device__ __forceinline__ int64_t ep_row_bytes(int H) {
+  return ((static_cast<int64_t>(H) + H / 32 + 8 + 15) / 16) * 16;
+}
+
+// Pack: entry p of the destination-sorted order (route_sort_kernel with divisor =
+// experts per rank) -> quantised row p of the send buffer; pos_of[i] = p remembers where
+// assignment i went so the combine can find its returned row.
+__global__ void __launch_bounds__(256) ep_pack_kernel(
+    const __nv_bfloat16* __restrict__ hidden, int H, int K, int experts_per_rank, int64_t A,
+    const int64_t* __restrict__ router_indices, const float* __restrict__ routing_weights,
+    const int32_t* __restrict__ sorted_src, int tpr, uint8_t* __restrict__ send_rows,
+    int32_t* __restrict__ pos_of) {
+  pdl_trigger();
+  pdl_wait();
+  const int rows_per_block = blockDim.x / tpr;
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * rows_per_block + threadIdx.x / tpr;
+  if (p >= A) return;
+  const int sub = threadIdx.x % tpr;
+  const int G = H >> 5;
+  const int i = sorted_src[p];
+  if (i < 0) return;   // sentinel of an out-of-range router index
+  const int64_t t = i / K;
+  const int64_t rb = ep_row_bytes(H);
+  uint8_t* row = send_rows + p * rb;
+  const __nv_bfloat16* xr = hidden + t * H;
+  for (int g = sub; g < G; g += tpr) {
+    const uint4* pp = reinterpret_cast<const uint4*>(xr + g * 32);
+    uint4 u[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) u[q] = __ldg(pp + q);
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t w4[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[q * 8 + 2 * j] = bf16_bits_lo(w4[j]);
+        v[q * 8 + 2 * j + 1] = bf16_bits_hi(w4[j]);
+      }
+    }
+    uint32_t codes[8];
+    const uint8_t sc = quantize_group32(v, codes);
+    uint4* o = reinterpret_cast<uint4*>(row + g * 32);
+    o[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+    o[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+    row[H + g] = sc;
+  }
+  if (sub == 0) {
+    for (int64_t b = H + G; b < rb - 8; ++b) row[b] = 0;   // padding travels as zeros
+    int32_t* meta = reinterpret_cast<int32_t*>(row + rb - 8);
+    meta[0] = static_cast<int32_t>(router_indices[i] % experts_per_rank);
+    meta[1] = __float_as_int(routing_weights[i]);
+    pos_of[i] = static_cast<int32_t>(p);
+  }
+}
+
+// Receiving rank: row r's (local expert, weight) -> arrays route_sort_kernel reads.
+__global__ void ep_unpack_meta_kernel(const uint8_t* __restrict__ recv_rows, int64_t R, int H,
+                                      int64_t* __restrict__ expert, float* __restrict__ weight) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t rb = ep_row_bytes(H);
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < R;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t* meta = reinterpret_cast<const int32_t*>(recv_rows + r * rb + rb - 8);
+    expert[r] = meta[0];
+    weight[r] = __int_as_float(meta[1]);
+  }
+}
+
+// Expert-sorted position p <- received row sorted_token[p]: copy its codes into the
+// GEMM's activation rows and scatter its scales into the blocked layout.
+__global__ void __launch_bounds__(256) ep_gather_kernel(
+    const uint8_t* __restrict__ recv_rows, int64_t R, int H, const int64_t* __restrict__ sorted_row,
+    const int64_t* __restrict__ sorted_expert, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ sf_offsets, int g4, int spread, uint8_t* __restrict__ act_codes,
+    uint8_t* __restrict__ act_sf) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t p = blockIdx.x;
+  if (p >= R) return;
+  const int64_t rb = ep_row_bytes(H);
+  if (sorted_row[p] < 0) return;   // sentinel of an out-of-range local expert id
+  const uint8_t* src = recv_rows + sorted_row[p] * rb;
+  const int ex = static_cast<int>(sorted_expert[p]);
+  int64_t r_in = p - offsets[ex];
+  if (spread) r_in = act_sf_row<true>(r_in);
+  const int64_t base = sf_offsets[ex];
+  for (int v = threadIdx.x; v < H / 16; v += blockDim.x)
+    reinterpret_cast<uint4*>(act_codes + p * H)[v] = reinterpret_cast<const uint4*>(src)[v];
+  for (int g = threadIdx.x; g < H / 32; g += blockDim.x)
+    act_sf[base + blocked_sf_offset(r_in, g, g4)] = src[H + g];
+}
+
+// Combine: out[t] = bf16 of the fp32 sum of the token's k returned rows, added in ascending
+// expert order -- what the reference's scatter_add_ of expert-sorted bf16 rows into a zero
+// bf16 tensor gives on the CPU (cutlass_experts.py:445-450; fp32 accumulation, one
+// rounding).
+__global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __restrict__ back_rows,
+                                                         const int32_t* __restrict__ pos_of,
+                                                         const int64_t* __restrict__ router_indices, int64_t T,
+                                                         int K, int H, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t t = blockIdx.x;
+  if (t >= T) return;
+  int order[kMaxTopK];
+  for (int j = 0; j < K; ++j) order[j] = j;
+  for (int a = 1; a < K; ++a)                      // insertion sort by expert id
+    for (int b = a; b > 0 && router_indices[t * K + order[b]] < router_indices[t * K + order[b - 1]]; --b) {
+      const int tmp = order[b]; order[b] = order[b - 1]; order[b - 1] = tmp;
+    }
+  for (int h2 = threadIdx.x; h2 < H / 2; h2 += blockDim.x) {
+    float a0 = 0.0f, a1 = 0.0f;
+    for (int j = 0; j < K; ++j) {
+      const int64_t pr = pos_of[t * K + order[j]];
+      if (pr < 0 || pr >= T * K) continue;   // assignment with an out-of-range expert id
+      const __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(back_rows + pr * H)[h2];
+      a0 += __bfloat162float(v.x);
+      a1 += __bfloat162float(v.y);
+    }
+    reinterpret_cast<__nv_bfloat162*>(out + t * H)[h2] = __floats2bfloat162_rn(a0, a1);
   }
 }
 

@@ -1,0 +1,142 @@
+"""Expert parallelism: one process per GPU, the experts sharded by contiguous ranges.
+
+The reference runs on one GPU only ("Expert parallelism not implemented",
+kernels/cutlass_matmul_investigations.md:231). Here rank r of W owns experts
+[r*E/W, (r+1)*E/W); tokens stay data parallel (each rank routes its own tokens). One
+forward is
+
+  1. dispatch kernels: stable sort of the T*k assignments by destination rank and FP8
+     quantisation of each assignment's hidden row into a packed send row
+     [codes H | UE8M0 scales H/32 | pad | local expert i32 | weight f32];
+  2. all_to_all_single of the per-rank counts, one device->host read of the splits,
+     all_to_all_single of the rows (NCCL over NVLink / NVSwitch);
+  3. the local expert forward on the received rows (route sort by local expert, scales
+     gathered into the blocked layout, GEMM1 + SwiGLU + requant, GEMM2 + bias x weight),
+     one weighted bf16 row back per received row;
+  4. all_to_all_single of those rows with the splits reversed;
+  5. combine: each token's k rows summed in fp32 in ascending expert order and rounded
+     to bf16 once, what the single-device scatter_add_ of bf16 rows gives on the CPU
+     (kernels/cutlass_experts.py:445-450).
+
+Quantisation is per row, so the FP8 codes and scales equal the single-GPU ones bit for
+bit; rows are independent through both GEMMs.
+
+The split sizes are read on the host once per forward (step 2), so a forward is not
+CUDA-graph capturable. The kernels sit behind :class:`CudaKernels`; a different object
+with the same three methods can stand in for it (the CPU tests use the oracle's
+restatement with the gloo backend).
+"""
+from __future__ import annotations
+
+import types
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import ops as _ops
+from .cutlass_experts import CutlassGptOssExperts
+
+
+class CudaKernels:
+    """The sm_100a kernels of the three local steps."""
+
+    @staticmethod
+    def dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int):
+        return _ops.ep_dispatch(hidden, router_indices, routing_weights, num_experts, world_size)
+
+    @staticmethod
+    def expert_forward(recv_rows, experts: CutlassGptOssExperts):
+        return _ops.ep_expert_forward(recv_rows, experts.gate_up_proj_data, experts.gate_up_proj_scales,
+                                      experts.gate_up_proj_bias.data, experts.down_proj_data,
+                                      experts.down_proj_scales, experts.down_proj_bias.data, float(experts.alpha),
+                                      float(experts.limit), int(experts.gemm_mode))
+
+    @staticmethod
+    def combine(back_rows, pos_of, router_indices):
+        return _ops.ep_combine(back_rows, pos_of, router_indices)
+
+
+def shard_experts(experts: CutlassGptOssExperts, rank: int, world_size: int) -> CutlassGptOssExperts:
+    """A CutlassGptOssExperts holding experts [rank*E/W, (rank+1)*E/W) of `experts`
+    (views of its buffers, no copy)."""
+    E = experts.num_experts
+    if E % world_size != 0:
+        raise ValueError(f"num_experts {E} is not a multiple of world_size {world_size}")
+    e_loc = E // world_size
+    lo, hi = rank * e_loc, (rank + 1) * e_loc
+    cfg = types.SimpleNamespace(num_local_experts=e_loc, intermediate_size=experts.intermediate_size,
+                                hidden_size=experts.hidden_size, swiglu_limit=experts.limit)
+    loc = CutlassGptOssExperts(cfg).to(experts.gate_up_proj_bias.device)
+    loc.alpha, loc.limit, loc.gemm_mode = experts.alpha, experts.limit, experts.gemm_mode
+    loc.gate_up_proj_bias.data = experts.gate_up_proj_bias.data[lo:hi]
+    loc.down_proj_bias.data = experts.down_proj_bias.data[lo:hi]
+    for name in ("gate_up_proj_data", "gate_up_proj_scales", "down_proj_data", "down_proj_scales"):
+        setattr(loc, name, getattr(experts, name)[lo:hi])
+    return loc
+
+
+class ExpertParallelExperts(nn.Module):
+    """Drop-in for CutlassGptOssExperts.forward across a process group: same
+    (hidden_states, router_indices, routing_weights) -> out contract, router_indices
+    holding GLOBAL expert ids; `local_experts` holds this rank's E/W experts."""
+
+    def __init__(self, local_experts: CutlassGptOssExperts, num_experts: int, group=None, kernels=None):
+        super().__init__()
+        self.group = group
+        self.world_size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if local_experts.num_experts * self.world_size != num_experts:
+            raise ValueError(f"{local_experts.num_experts} local experts x {self.world_size} ranks != {num_experts}")
+        self.experts = local_experts
+        self.num_experts = num_experts
+        self.hidden_size = local_experts.hidden_size
+        self.kernels = kernels if kernels is not None else CudaKernels()
+        self.last_splits = None   # (send, recv) rows per peer of the last forward
+
+    def forward(self, hidden_states: torch.Tensor, router_indices: torch.Tensor,
+                routing_weights: torch.Tensor) -> torch.Tensor:
+        shape = hidden_states.shape
+        H = self.hidden_size
+        h = hidden_states.reshape(-1, H).contiguous()
+        idx = router_indices.reshape(h.shape[0], router_indices.shape[-1]).contiguous()
+        w = routing_weights.reshape(idx.shape).to(torch.float32).contiguous()
+        k, g = self.kernels, self.group
+        send_rows, send_counts, pos_of = k.dispatch(h, idx, w, self.num_experts, self.world_size)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=g)
+        splits = torch.stack([send_counts, recv_counts]).cpu()       # the one device -> host read
+        s_send, s_recv = splits[0].tolist(), splits[1].tolist()
+        self.last_splits = (s_send, s_recv)
+        recv_rows = send_rows.new_empty((sum(s_recv), send_rows.shape[1]))
+        dist.all_to_all_single(recv_rows, send_rows, output_split_sizes=s_recv, input_split_sizes=s_send, group=g)
+        back = k.expert_forward(recv_rows, self.experts)
+        ret = back.new_empty((send_rows.shape[0], H))
+        dist.all_to_all_single(ret, back, output_split_sizes=s_send, input_split_sizes=s_recv, group=g)
+        out = k.combine(ret, pos_of, idx)
+        return out.view(shape)
+
+
+class ExpertParallelMoELayer(nn.Module):
+    """Router (local tokens) + expert-parallel experts: the GptOssMLP shape of the block
+    with the experts sharded. `router_weight` [E, H] / `router_bias` [E] bf16 are
+    replicated on every rank."""
+
+    def __init__(self, router_weight: torch.Tensor, router_bias: torch.Tensor, top_k: int,
+                 experts: ExpertParallelExperts):
+        super().__init__()
+        self.router_weight = nn.Parameter(router_weight, requires_grad=False)
+        self.router_bias = nn.Parameter(router_bias, requires_grad=False)
+        self.top_k = top_k
+        self.experts = experts
+
+    def forward(self, hidden_states: torch.Tensor):
+        _ops.register_ops()
+        h = hidden_states.reshape(-1, self.experts.hidden_size).contiguous()
+        _, scores, idx = torch.ops.gptoss.router_topk(h, self.router_weight.data, self.router_bias.data,
+                                                      int(self.top_k))
+        out = self.experts(h, idx, scores.float())
+        return out.view(hidden_states.shape), scores, idx
+
+
+__all__ = ["CudaKernels", "ExpertParallelExperts", "ExpertParallelMoELayer", "shard_experts"]

@@ -442,3 +442,80 @@ def gemm2(ws: ExpertsWorkspace, dn_data, dn_scales, dn_bias, out, gemm_mode: int
     _lib.call("gptoss_moe_gemm2", ws.T, ws.k, ws.E, ws.H, ws.I, dn_data.data_ptr(), dn_scales.data_ptr(),
               dn_scales.numel() // ws.E, dn_bias.data_ptr(), out.data_ptr(), ws.ptr, ws.buf.numel(), int(gemm_mode),
               status_tensor(dn_data.device).data_ptr(), _stream(dn_data.device))
+
+
+# ------------------------------------------------------------------ expert parallelism
+def ep_row_bytes(hidden_size: int) -> int:
+    """Bytes of one dispatched row: FP8 codes, UE8M0 scales, padding, int32 local expert,
+    f32 routing weight (16-byte multiple)."""
+    rb = int(_lib.query("gptoss_ep_row_bytes", int(hidden_size)))
+    if rb <= 0:
+        raise RuntimeError(f"ep_row_bytes: hidden size {hidden_size} must be a positive multiple of 32")
+    return rb
+
+
+def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int):
+    """Sorts the T*k assignments by destination rank (experts [r*E/W, (r+1)*E/W) live on
+    rank r) and quantises each assignment's hidden row into a packed send row.
+    Returns (send_rows u8 [T*k, row_bytes], send_counts i32 [W], pos_of i32 [T*k])."""
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _cuda(router_indices, "router_indices")
+    _dtype(router_indices, (torch.int64,), "router_indices")
+    _cuda(routing_weights, "routing_weights")
+    _dtype(routing_weights, (torch.float32,), "routing_weights")
+    T, H = hidden.shape
+    k = router_indices.shape[1]
+    dev = hidden.device
+    A = T * k
+    send_rows = torch.empty((A, ep_row_bytes(H)), dtype=torch.uint8, device=dev)
+    send_counts = torch.empty(world_size, dtype=torch.int32, device=dev)
+    pos_of = torch.empty(A, dtype=torch.int32, device=dev)
+    nbytes = int(_lib.query("gptoss_ep_dispatch_workspace_bytes", T, k, world_size))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    _lib.call("gptoss_ep_dispatch", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(), T, k,
+              int(num_experts), int(world_size), H, send_rows.data_ptr(), send_counts.data_ptr(), pos_of.data_ptr(),
+              ws.data_ptr(), ws.numel(), status_tensor(dev).data_ptr(), _stream(dev))
+    return send_rows, send_counts, pos_of
+
+
+def ep_expert_forward(recv_rows, gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias, alpha: float = 1.702,
+                      limit: float = 7.0, gemm_mode: int = GEMM_AUTO):
+    """Received rows [R, row_bytes] -> routing-weighted expert outputs [R, H] bf16 on this
+    rank's local experts (the weights' leading dimension)."""
+    _cuda(recv_rows, "recv_rows")
+    _dtype(recv_rows, (torch.uint8,), "recv_rows")
+    _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias)
+    E_loc = gu_data.shape[0]
+    I = gu_data.shape[1] // 2
+    H = dn_data.shape[1]
+    R = recv_rows.shape[0]
+    if recv_rows.dim() != 2 or (R and recv_rows.shape[1] != ep_row_bytes(H)):
+        raise RuntimeError(f"recv_rows: expected [R, {ep_row_bytes(H)}], got {tuple(recv_rows.shape)}")
+    dev = gu_data.device
+    back = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(max(workspace_bytes(R, 1, E_loc, H, I) if R else 0, 256), dtype=torch.uint8, device=dev)
+    _lib.call("gptoss_ep_expert_forward", recv_rows.data_ptr() if R else None, R, E_loc, H, I, gu_data.data_ptr(),
+              gu_scales.data_ptr(), gu_scales.numel() // E_loc, gu_bias.data_ptr(), dn_data.data_ptr(),
+              dn_scales.data_ptr(), dn_scales.numel() // E_loc, dn_bias.data_ptr(), float(alpha), float(limit),
+              back.data_ptr() if R else None, ws.data_ptr(), ws.numel(), int(gemm_mode),
+              status_tensor(dev).data_ptr(), _stream(dev))
+    return back
+
+
+def ep_combine(back_rows, pos_of, router_indices):
+    """Returned rows [T*k, H] -> out [T, H]: each token's k rows summed in fp32 in
+    ascending expert order, rounded to bf16 once."""
+    _cuda(back_rows, "back_rows")
+    _dtype(back_rows, (torch.bfloat16,), "back_rows")
+    _cuda(pos_of, "pos_of")
+    _cuda(router_indices, "router_indices")
+    T, k = router_indices.shape
+    H = back_rows.shape[1]
+    dev = back_rows.device
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    if T == 0:
+        return out
+    _lib.call("gptoss_ep_combine", back_rows.data_ptr(), pos_of.data_ptr(), router_indices.data_ptr(), T, k, H,
+              out.data_ptr(), _stream(dev))
+    return out

@@ -248,6 +248,50 @@ int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router
                                        float swiglu_limit, void* out, int gemm_mode,
                                        int32_t* status_dev, void* stream);
 
+/* ---- Expert parallelism (one process per GPU, experts sharded by contiguous ranges).
+ *
+ * No counterpart in the reference, which runs on one GPU ("Expert parallelism not
+ * implemented", kernels/cutlass_matmul_investigations.md:231). Rank r of W owns experts
+ * [r*E/W, (r+1)*E/W). One layer is
+ *   gptoss_ep_dispatch   -> send_counts, send_rows (quantised, ordered by destination rank)
+ *   all-to-all of the counts, then of the rows (the caller's collective, e.g. NCCL)
+ *   gptoss_ep_expert_forward on the received rows -> back_rows (weighted bf16, same order)
+ *   all-to-all of back_rows with the splits reversed
+ *   gptoss_ep_combine    -> out[t] = fp32 sum of token t's k rows (ascending expert), to bf16.
+ * A row is gptoss_ep_row_bytes(H) bytes: FP8 codes [H], UE8M0 scales [H/32], padding, then
+ * the local expert id (int32) and routing weight (f32) in its last 8 bytes. The codes and
+ * scales are those gptoss_quantize_fp8 gives for the token's hidden row. */
+int64_t gptoss_ep_row_bytes(int64_t hidden_size);
+size_t gptoss_ep_dispatch_workspace_bytes(int64_t num_tokens, int top_k, int world_size);
+/* router_indices hold GLOBAL expert ids. send_rows: [T*k, row_bytes]; send_counts: [W]
+ * int32 rows per destination rank; pos_of: [T*k] int32, row of send_rows that assignment
+ * i = t*k + j went to (the same row of the returned back_rows). */
+int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
+                       int64_t num_tokens, int top_k, int num_experts, int world_size,
+                       int64_t hidden_size, uint8_t* send_rows, int32_t* send_counts,
+                       int32_t* pos_of, void* workspace, size_t workspace_bytes,
+                       int32_t* status_dev, void* stream);
+/* Received rows -> back_rows [num_rows, H] bf16, row r = routing weight x expert output of
+ * row r (route sort by local expert, blocked-scale gather, GEMM1 + SwiGLU + requant,
+ * GEMM2 + bias). Weights are this rank's [E/W, ...] slices; workspace =
+ * gptoss_moe_workspace_bytes(num_rows, 1, E/W, H, I). A local expert id outside [0, E/W)
+ * sets *status_dev. */
+int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num_local_experts,
+                             int64_t hidden_size, int64_t intermediate_size,
+                             const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                             int64_t ldb_gate_up, const float* gate_up_bias,
+                             const uint8_t* down_data, const uint8_t* down_scales,
+                             int64_t ldb_down, const float* down_bias, float swiglu_alpha,
+                             float swiglu_limit, void* back_rows, void* workspace,
+                             size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
+                             void* stream);
+/* out [T, H] bf16 (overwritten): the k returned rows of each token summed in fp32 in
+ * ascending global expert order and rounded to bf16 once -- the result of the reference's
+ * scatter_add_ of expert-sorted bf16 rows into a zero bf16 tensor on the CPU
+ * (kernels/cutlass_experts.py:445-450). */
+int gptoss_ep_combine(const void* back_rows, const int32_t* pos_of, const int64_t* router_indices,
+                      int64_t num_tokens, int top_k, int64_t hidden_size, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

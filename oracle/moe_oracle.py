@@ -18,6 +18,7 @@ __all__ = [
     "route_stable", "router_topk_hf", "router_logits_fp32",
     "mxfp4_dequant", "fp8_dequant", "group_mm_bf16", "swiglu_fp32",
     "w4a8_experts_forward", "dequant_fp32_reference", "synth_layer", "synth_router_bias",
+    "ep_row_bytes", "ep_dispatch", "ep_expert_rows", "ep_combine", "slice_experts",
 ]
 
 MXFP_BLOCK = 32
@@ -367,3 +368,86 @@ class DequantCPULayer:
 
 
 __all__.append("DequantCPULayer")
+
+
+# ---------------------------------------------------------------------------------------
+# Expert parallelism. The reference has none (kernels/cutlass_matmul_investigations.md:231);
+# these restate the sharded path so that, chained with all-to-alls, it reproduces
+# w4a8_experts_forward exactly: quantisation is per row (position-invariant), each row's
+# GEMMs are independent of the other rows, and ep_combine adds a token's rows the way
+# scatter_add_ does in w4a8_experts_forward on the CPU (fp32 accumulation in ascending
+# expert order, one bf16 rounding).
+def ep_row_bytes(H: int) -> int:
+    """[codes H | scales H/32 | pad | local expert i32 | weight f32], 16-byte multiple."""
+    return (H + H // 32 + 8 + 15) // 16 * 16
+
+
+def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int):
+    """Assignments stably sorted by destination rank (expert // (E/W)); row p = quantised
+    hidden row of its token + (local expert, weight). Returns numpy
+    (send_rows u8 [A, row_bytes], send_counts i32 [W], pos_of i32 [A])."""
+    h = hidden.float().numpy() if isinstance(hidden, torch.Tensor) else np.asarray(hidden, np.float32)
+    idx = np.asarray(router_indices, dtype=np.int64)
+    w = np.asarray(routing_weights, dtype=np.float32).reshape(-1)
+    T, k = idx.shape
+    H = h.shape[1]
+    e_loc = num_experts // world_size
+    flat = idx.reshape(-1)
+    dest = flat // e_loc
+    order = np.argsort(dest, kind="stable")
+    counts = np.bincount(dest, minlength=world_size).astype(np.int32)
+    rb = ep_row_bytes(H)
+    rows = np.zeros((T * k, rb), dtype=np.uint8)
+    if T * k:
+        codes, sf = quantize_fp8_ue8m0(h[order // k])
+        rows[:, :H] = codes
+        rows[:, H:H + H // 32] = sf
+        rows[:, rb - 8:rb - 4] = (flat[order] % e_loc).astype(np.int32).view(np.uint8).reshape(-1, 4)
+        rows[:, rb - 4:] = w[order].astype(np.float32).view(np.uint8).reshape(-1, 4)
+    pos_of = np.empty(T * k, dtype=np.int32)
+    pos_of[order] = np.arange(T * k, dtype=np.int32)
+    return rows, counts, pos_of
+
+
+def ep_expert_rows(recv_rows: np.ndarray, H: int, w_local: dict, alpha: float = 1.702, limit: float = 7.0):
+    """Received rows -> bf16 [R, H]: row r = bf16((down(swiglu(gate_up(row r))) + b) x w_r)
+    on the local experts, the per-row part of w4a8_experts_forward (cutlass_experts.py:414-449)."""
+    rows = np.asarray(recv_rows, dtype=np.uint8)
+    R = rows.shape[0]
+    out = torch.zeros((R, H), dtype=torch.bfloat16)
+    if R == 0:
+        return out
+    rb = rows.shape[1]
+    e_loc = w_local["gu_blocks"].shape[0]
+    lexp = np.ascontiguousarray(rows[:, rb - 8:rb - 4]).view(np.int32).reshape(-1).astype(np.int64)
+    wt = np.ascontiguousarray(rows[:, rb - 4:]).view(np.float32).reshape(-1)
+    st, se, sw, counts, offsets = route_stable(lexp[:, None], wt[:, None], e_loc)
+    a_codes = rows[st, :H]
+    a_sf = rows[st, H:H + H // 32]
+    gu = group_mm_bf16(a_codes, a_sf, w_local["gu_blocks"], w_local["gu_scales"], counts, offsets)
+    gu32 = gu + torch.as_tensor(w_local["gu_bias"]).float()[torch.from_numpy(se)]
+    inter = swiglu_fp32(gu32, alpha, limit)
+    i_codes, i_sf = quantize_fp8_ue8m0(inter)
+    dn = group_mm_bf16(i_codes, i_sf, w_local["dn_blocks"], w_local["dn_scales"], counts, offsets)
+    dn32 = (dn + torch.as_tensor(w_local["dn_bias"]).float()[torch.from_numpy(se)]) * torch.from_numpy(sw)[:, None]
+    out[torch.from_numpy(st)] = dn32.to(torch.bfloat16)
+    return out
+
+
+def ep_combine(back_rows: torch.Tensor, pos_of, router_indices) -> torch.Tensor:
+    """out[t] = bf16(fp32 sum of token t's k rows in ascending expert order)."""
+    idx = np.asarray(router_indices, dtype=np.int64)
+    pos = np.asarray(pos_of, dtype=np.int64)
+    T, k = idx.shape
+    acc = torch.zeros((T, back_rows.shape[1]), dtype=torch.float32)
+    order = np.argsort(idx, axis=1, kind="stable")
+    for j in range(k):
+        src = pos[np.arange(T) * k + order[:, j]]
+        acc = acc + back_rows[torch.from_numpy(src)].float()
+    return acc.to(torch.bfloat16)
+
+
+def slice_experts(w: dict, lo: int, hi: int) -> dict:
+    """Row-major weights of experts [lo, hi)."""
+    keys = ("gu_blocks", "gu_scales", "gu_bias", "dn_blocks", "dn_scales", "dn_bias")
+    return {key: w[key][lo:hi] for key in keys}

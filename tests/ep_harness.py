@@ -1,0 +1,165 @@
+"""Expert-parallel test harness (not part of the product): the oracle's restatement of
+the three local EP steps behind the kernel interface of ExpertParallelExperts, the
+routing cases, and a per-rank worker used by the gloo (CPU) and NCCL (GPU) tests."""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+import oracle as O
+from helpers import Cfg
+
+E, H, I, K = 8, 256, 256, 4
+SEED = 11
+
+
+class OracleKernels:
+    """dispatch / expert_forward / combine on the CPU with the oracle."""
+
+    def __init__(self, w_local: dict, hidden_size: int):
+        self.w_local = w_local
+        self.H = hidden_size
+
+    def dispatch(self, hidden, router_indices, routing_weights, num_experts, world_size):
+        rows, counts, pos = O.ep_dispatch(hidden, router_indices.numpy(), routing_weights.numpy(), num_experts,
+                                          world_size)
+        return torch.from_numpy(rows), torch.from_numpy(counts), torch.from_numpy(pos)
+
+    def expert_forward(self, recv_rows, experts):
+        return O.ep_expert_rows(recv_rows.numpy(), self.H, self.w_local)
+
+    def combine(self, back_rows, pos_of, router_indices):
+        return O.ep_combine(back_rows, pos_of.numpy(), router_indices.numpy())
+
+
+def routing_case(case: str, rank: int, world: int, T: int, num_experts: int = E, k: int = K):
+    """(hidden bf16 [T, H], router_indices i64 [T, k], routing_weights f32 [T, k]) of a
+    rank: 'random' top-k of random logits, 'rank0' every assignment on rank 0's experts,
+    'empty' rank 1 holds no tokens."""
+    g = torch.Generator().manual_seed(1000 + 17 * rank + 101 * ("random", "rank0", "empty").index(case))
+    if case == "empty" and rank == 1:
+        T = 0
+    h = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, num_experts, generator=g)
+    if case == "rank0":
+        logits[:, num_experts // world:] -= 100.0
+    wv, ix = torch.topk(logits, k, dim=-1)
+    return h, ix, torch.softmax(wv, dim=-1).float()
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def cpu_worker(rank: int, world: int, port: int, cases, q):
+    """One gloo rank: ExpertParallelExperts with OracleKernels vs the single-process oracle."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import __graft_entry__ as ge
+
+        pkg = ge.load_package()
+        from gpt_oss_mxfp4_compile_b200 import ep as EP
+
+        d = O.synth_layer(SEED, E=E, H=H, I=I, T=1)
+        wn = O.numpy_weights(d)
+        e_loc = E // world
+        local = pkg.CutlassGptOssExperts(Cfg(e_loc, H, I))
+        mod = EP.ExpertParallelExperts(local, E, kernels=OracleKernels(O.slice_experts(wn, rank * e_loc,
+                                                                                     (rank + 1) * e_loc), H))
+        results = []
+        for case in cases:
+            h, ix, wv = routing_case(case, rank, world, 16)
+            out = mod(h, ix, wv)
+            ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
+            results.append((case, tuple(out.shape), bool(torch.equal(out, ref)), mod.last_splits))
+        q.put((rank, results, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def run_ranks(target, world: int, *args, timeout: float = 240.0):
+    """Runs `target(rank, world, port, *args, q)` in `world` spawned processes; returns
+    the per-rank results in rank order."""
+    ctx = torch.multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            rank, res, err = q.get(timeout=timeout)
+            got[rank] = (res, err)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    return [got[r] for r in range(world)]
+
+
+_ = np
+
+
+def nccl_worker(rank: int, world: int, port: int, shapes, q):
+    """One NCCL rank on cuda:rank: ExpertParallelExperts (CUDA kernels, NCCL all-to-alls)
+    vs the oracle on this rank's tokens and vs the single-GPU forward; then the layer
+    (router + EP experts) vs the single-GPU GptOssMoELayer."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        import __graft_entry__ as ge
+        from helpers import build_experts, build_layer, max_abs_over_rms, rel_l2
+
+        pkg = ge.load_package()
+        pkg.ensure_custom_op_registered()
+        EP = pkg.ep
+        results = []
+        for (e_tot, hs, isz, T) in shapes:
+            d = O.synth_layer(SEED, E=e_tot, H=hs, I=isz, T=1)
+            wn = O.numpy_weights(d)
+            full = build_experts(pkg, d, dev, e_tot, hs, isz)
+            mod = EP.ExpertParallelExperts(EP.shard_experts(full, rank, world), e_tot)
+            g = torch.Generator().manual_seed(500 + rank)
+            h = torch.randn(T + 8 * rank, hs, generator=g).to(torch.bfloat16)
+            wv, ix = torch.topk(torch.randn(h.shape[0], e_tot, generator=g), K, dim=-1)
+            wv = torch.softmax(wv, -1).float()
+            out = mod(h.to(dev), ix.to(dev), wv.to(dev))
+            torch.cuda.synchronize()
+            st = pkg.ops.read_status(dev)
+            ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
+            single = full(h.to(dev), ix.to(dev), wv.to(dev))
+            results.append(("experts", e_tot, hs, st, rel_l2(out.cpu(), ref), max_abs_over_rms(out.cpu(), ref),
+                            (out.float() - single.float()).abs().max().item() / single.float().abs().max().item(),
+                            mod.last_splits))
+            # the layer: router on local tokens + EP experts vs the single-GPU layer
+            single_layer = build_layer(pkg, d, dev, e_tot, hs, isz, K)
+            ep_layer = EP.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), K, mod)
+            o1, s1, i1 = ep_layer(h.to(dev))
+            o2, s2, i2 = single_layer(h.to(dev))
+            torch.cuda.synchronize()
+            results.append(("layer", e_tot, hs, pkg.ops.read_status(dev), bool(torch.equal(i1, i2)),
+                            bool(torch.equal(s1, s2)), rel_l2(o1.cpu(), o2.cpu()), None))
+        q.put((rank, results, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        import traceback
+
+        q.put((rank, None, repr(e) + traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()

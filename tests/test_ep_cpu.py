@@ -1,0 +1,66 @@
+"""Expert parallelism without a GPU: the oracle's EP restatement and the host logic of
+ExpertParallelExperts (count exchange, split bookkeeping, all-to-alls in both directions,
+return positions) on world_size-2 gloo ranks."""
+import numpy as np
+import torch
+
+import oracle as O
+from ep_harness import E, H, I, K, SEED, cpu_worker, routing_case, run_ranks
+
+
+def test_oracle_ep_chain_equals_single_device_forward():
+    # dispatch -> (identity all-to-all, one rank) -> expert rows -> combine reproduces
+    # w4a8_experts_forward bit for bit, also when the experts are split in two halves
+    # whose rows are exchanged by hand.
+    d = O.synth_layer(SEED, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    h, ix, wv = routing_case("random", 0, 2, 24)
+    ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
+    rows, counts, pos = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, 1)
+    back = O.ep_expert_rows(rows, H, O.slice_experts(wn, 0, E))
+    assert torch.equal(O.ep_combine(back, pos, ix.numpy()), ref)
+    rows, counts, pos = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, 2)
+    assert counts.sum() == rows.shape[0] == 24 * K
+    c0 = int(counts[0])
+    b0 = O.ep_expert_rows(rows[:c0], H, O.slice_experts(wn, 0, E // 2))
+    b1 = O.ep_expert_rows(rows[c0:], H, O.slice_experts(wn, E // 2, E))
+    assert torch.equal(O.ep_combine(torch.cat([b0, b1]), pos, ix.numpy()), ref)
+
+
+def test_oracle_ep_rows_carry_single_device_codes():
+    # the dispatched codes and scales equal the single-device quantiser's for the token row
+    h, ix, wv = routing_case("random", 0, 2, 8)
+    rows, counts, pos = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, 4)
+    codes, sf = O.quantize_fp8_ue8m0(h)
+    rb = O.ep_row_bytes(H)
+    assert rows.shape == (8 * K, rb) and rb % 16 == 0
+    for i in range(8 * K):
+        t, p = i // K, pos[i]
+        assert np.array_equal(rows[p, :H], codes[t]) and np.array_equal(rows[p, H:H + H // 32], sf[t])
+        assert rows[p, rb - 8:rb - 4].view(np.int32)[0] == ix.numpy().reshape(-1)[i] % (E // 4)
+        assert rows[p, rb - 4:].view(np.float32)[0] == wv.numpy().reshape(-1)[i]
+    # destination-rank order, stable
+    dest = ix.numpy().reshape(-1) // (E // 4)
+    assert np.array_equal(np.argsort(pos), np.argsort(dest, kind="stable"))
+    assert np.array_equal(counts, np.bincount(dest, minlength=4))
+
+
+def test_gloo_two_ranks_match_single_device_oracle():
+    res = run_ranks(cpu_worker, 2, ["random", "rank0", "empty"])
+    for rank, (out, err) in enumerate(res):
+        assert err is None, f"rank {rank}: {err}"
+        by_case = {c: (shape, eq, splits) for c, shape, eq, splits in out}
+        for case, (shape, eq, splits) in by_case.items():
+            assert eq, f"rank {rank} case {case}: output differs from the oracle"
+        # every assignment of 'rank0' goes to rank 0; rank 1 receives nothing
+        s_send, s_recv = by_case["rank0"][2]
+        assert s_send[1] == 0 and (rank == 0 or sum(s_recv) == 0)
+        # 'empty': rank 1 has no tokens, sends nothing and still serves rank 0's rows
+        shape, _, (s_send, s_recv) = by_case["empty"]
+        if rank == 1:
+            assert shape == (0, H) and sum(s_send) == 0
+    # the splits agree across ranks: what r sends to q is what q receives from r
+    for case_i in range(3):
+        s0 = res[0][0][case_i][3]
+        s1 = res[1][0][case_i][3]
+        assert s0[0][1] == s1[1][0] and s1[0][0] == s0[1][1]

@@ -1,0 +1,105 @@
+"""Expert-parallel kernels on one GPU: dispatch rows bit-exact with the oracle, the local
+expert forward within the output tolerance, the combine bit-exact, and a W-rank chain
+emulated on one device (the all-to-alls done by slicing) against the oracle and the
+single-GPU forward."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from helpers import assert_output_tolerance, build_experts
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(seed, T, E, H, k=4):
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    wv, ix = torch.topk(torch.randn(T, E, generator=g), k, dim=-1)
+    return h, ix, torch.softmax(wv, dim=-1).float()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("H", [512, 2880])
+def test_dispatch_rows_bit_exact(pkg, dev, world, H):
+    E = 32
+    h, ix, wv = _inputs(world + H, 37, E, H)
+    rows, counts, pos = pkg.ops.ep_dispatch(h.to(dev), ix.to(dev), wv.to(dev), E, world)
+    torch.cuda.synchronize()
+    assert pkg.ops.read_status(dev) == 0
+    r_o, c_o, p_o = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, world)
+    assert rows.shape == r_o.shape and rows.shape[1] == pkg.ops.ep_row_bytes(H) == O.ep_row_bytes(H)
+    assert np.array_equal(counts.cpu().numpy(), c_o)
+    assert np.array_equal(pos.cpu().numpy(), p_o)
+    assert np.array_equal(rows.cpu().numpy(), r_o)
+
+
+def test_dispatch_empty_and_bad_index(pkg, dev):
+    H, E = 512, 8
+    rows, counts, pos = pkg.ops.ep_dispatch(torch.empty(0, H, dtype=torch.bfloat16, device=dev),
+                                            torch.empty(0, 4, dtype=torch.int64, device=dev),
+                                            torch.empty(0, 4, device=dev), E, 2)
+    assert rows.shape == (0, pkg.ops.ep_row_bytes(H)) and counts.tolist() == [0, 0]
+    # an expert id outside [0, E) sets the status word; the other rows are still packed
+    h, ix, wv = _inputs(3, 8, E, H)
+    ix[2, 1] = E + 5
+    rows, counts, pos = pkg.ops.ep_dispatch(h.to(dev), ix.to(dev), wv.to(dev), E, 2)
+    torch.cuda.synchronize()
+    assert pkg.ops.read_status(dev) == 0x201
+    assert int(counts.sum()) == 8 * 4 - 1
+
+
+def test_expert_rows_and_combine(pkg, dev):
+    E, H, I = 8, 512, 512
+    d = O.synth_layer(21, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    m = build_experts(pkg, d, dev, E, H, I)
+    h, ix, wv = _inputs(4, 48, E, H)
+    rows, counts, pos = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, 2)
+    c0 = int(counts[0])
+    for q, (lo, hi) in enumerate(((0, c0), (c0, rows.shape[0]))):
+        loc = pkg.ep.shard_experts(m, q, 2)
+        for mode in (1, 2):
+            loc.gemm_mode = mode
+            back = pkg.ep.CudaKernels.expert_forward(torch.from_numpy(rows[lo:hi]).to(dev), loc)
+            torch.cuda.synchronize()
+            assert pkg.ops.read_status(dev) == 0
+            ref = O.ep_expert_rows(rows[lo:hi], H, O.slice_experts(wn, q * E // 2, (q + 1) * E // 2))
+            assert_output_tolerance(back.cpu(), ref, f"expert rows rank {q} mode {mode}")
+    # combine is bit-exact for the same returned rows
+    back = torch.randn(48 * 4, H).to(torch.bfloat16)
+    out = pkg.ops.ep_combine(back.to(dev), torch.from_numpy(pos).to(dev), ix.to(dev))
+    assert torch.equal(out.cpu(), O.ep_combine(back, pos, ix.numpy()))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_emulated_ranks_chain(pkg, dev, world):
+    # dispatch on every "rank", all-to-all by slicing, local experts, all-to-all back,
+    # combine: equals the oracle within tolerance and the single-GPU forward closely.
+    E, H, I = 8, 512, 512
+    d = O.synth_layer(5, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    m = build_experts(pkg, d, dev, E, H, I)
+    ins = [_inputs(100 + r, 24 + 8 * r, E, H) for r in range(world)]
+    disp = [pkg.ops.ep_dispatch(h.to(dev), ix.to(dev), wv.to(dev), E, world) for h, ix, wv in ins]
+    seg = []  # seg[r][q] = rows of rank r for rank q
+    for rows, counts, pos in disp:
+        c = counts.cpu().tolist()
+        o = np.concatenate([[0], np.cumsum(c)]).tolist()
+        seg.append([rows[o[q]:o[q + 1]] for q in range(world)])
+    backs = []
+    for q in range(world):
+        recv = torch.cat([seg[r][q] for r in range(world)])
+        back = pkg.ep.CudaKernels.expert_forward(recv, pkg.ep.shard_experts(m, q, world))
+        sizes = [seg[r][q].shape[0] for r in range(world)]
+        backs.append(list(torch.split(back, sizes)))
+    for r, (h, ix, wv) in enumerate(ins):
+        ret = torch.cat([backs[q][r] for q in range(world)])
+        out = pkg.ops.ep_combine(ret, disp[r][2], ix.to(dev))
+        torch.cuda.synchronize()
+        assert pkg.ops.read_status(dev) == 0
+        ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
+        assert_output_tolerance(out.cpu(), ref, f"rank {r}")
+        single = m(h.to(dev), ix.to(dev), wv.to(dev))
+        diff = (out.float() - single.float()).abs().max().item()
+        assert diff <= 2 ** -7 * single.float().abs().max().item(), diff
