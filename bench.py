@@ -6,8 +6,9 @@ forward over one batch of synthetic tokens).
   python bench.py --impl reference ...     CPU baseline arm (rank 0 only)
 
 Workload at N=1 is BASELINE config 1 (decode, T=32 tokens, E=32, H=I=2880, top-4,
-seeded synthetic weights/inputs). Under torchrun every rank runs its own batch of T
-tokens on its own GPU (weak scaling); the reported value is the whole-job tokens/s
+seeded synthetic weights/inputs). Under torchrun (N>1) the layer runs expert-parallel:
+rank r holds experts [r*E/N, (r+1)*E/N) and its own batch of T tokens (weak scaling);
+dispatch and combine are NCCL all-to-alls. The reported value is the whole-job tokens/s
 over the max-over-ranks device time.
 
 Timing: W warm-up steps, then exactly K steps, each bracketed by CUDA events on the
@@ -40,6 +41,8 @@ CONFIGS = {
 NCU_TRAFFIC_BYTES = {"decode": 294_423_808, "prefill": None}   # profiles/moe_gemm_swap_decode_T32.md
 
 KERNELS_PER_STEP = 5   # router, route_sort, gather_quant, gemm1, gemm2
+# router; dispatch: route_sort + pack; local: unpack, route_sort, gather, gemm1, gemm2; combine
+KERNELS_PER_STEP_EP = 9
 
 
 def parse_args():
@@ -51,6 +54,9 @@ def parse_args():
     ap.add_argument("--config", choices=list(CONFIGS), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=45.0)
+    ap.add_argument("--ep-layout", choices=["auto", "capacity", "exact"], default="auto",
+                    help="N>1 exchange layout: fixed-capacity segments (no host sync) or exact splits; "
+                         "auto = capacity when W*T*k <= 8192 rows")
     return ap.parse_args()
 
 
@@ -200,15 +206,38 @@ def run_ours(args):
         num_experts_per_tok = k
         swiglu_limit = 7.0
 
-    d = O.synth_layer(rank, E=E, H=H, I=I, T=T, skew=skew)
-    layer = pkg.GptOssMoELayer(Cfg()).to(dev)
-    layer.router_weight.data.copy_(d["router_w"])
-    layer.router_bias.data.copy_(d["router_b"])
-    ex = layer.experts
-    ex.gate_up_proj_bias.data.copy_(d["gu_bias"])
-    ex.down_proj_bias.data.copy_(d["dn_bias"])
-    pkg.load_cutlass_weights(ex, d["gu_blocks"], d["gu_scales"], d["dn_blocks"], d["dn_scales"], dev)
-    x = d["hidden"].to(dev)
+    if world == 1:
+        d = O.synth_layer(rank, E=E, H=H, I=I, T=T, skew=skew)
+        layer = pkg.GptOssMoELayer(Cfg()).to(dev)
+        layer.router_weight.data.copy_(d["router_w"])
+        layer.router_bias.data.copy_(d["router_b"])
+        ex = layer.experts
+        ex.gate_up_proj_bias.data.copy_(d["gu_bias"])
+        ex.down_proj_bias.data.copy_(d["dn_bias"])
+        pkg.load_cutlass_weights(ex, d["gu_blocks"], d["gu_scales"], d["dn_blocks"], d["dn_scales"], dev)
+        x = d["hidden"].to(dev)
+    else:
+        # one layer's weights, identical on every rank (seed 0); each rank keeps its
+        # E/N experts and routes its own tokens
+        d = O.synth_layer(0, E=E, H=H, I=I, T=T, skew=skew, with_hidden=False)
+        e_loc = E // world
+        lo, hi = rank * e_loc, (rank + 1) * e_loc
+
+        class LocalCfg(Cfg):
+            num_local_experts = e_loc
+
+        ex = pkg.CutlassGptOssExperts(LocalCfg()).to(dev)
+        ex.gate_up_proj_bias.data.copy_(d["gu_bias"][lo:hi])
+        ex.down_proj_bias.data.copy_(d["dn_bias"][lo:hi])
+        pkg.load_cutlass_weights(ex, d["gu_blocks"][lo:hi], d["gu_scales"][lo:hi], d["dn_blocks"][lo:hi],
+                                 d["dn_scales"][lo:hi], dev)
+        layout = args.ep_layout
+        if layout == "auto":
+            layout = "capacity" if world * T * k <= 8192 else "exact"
+        ep_experts = pkg.ep.ExpertParallelExperts(ex, E, capacity_tokens=T if layout == "capacity" else None)
+        layer = pkg.ep.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), k, ep_experts)
+        g = torch.Generator().manual_seed(1000 + rank)
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
     del d
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -248,6 +277,93 @@ def run_ours(args):
     value = T * world / (ms / 1e3)
 
     # ---------------------------------------------------------------- per-stage (roofline)
+    stages = (stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, args.config)
+              if world == 1 else None)
+
+    # ---------------------------------------------------------------- end to end
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    Ke = min(K, 500)
+    e2e_t = []
+    barrier()
+    for i in range(Ke + 3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        flush.zero_()
+        a.record(stream)
+        xd.copy_(xh, non_blocking=True)
+        y, _, _ = layer(xd)
+        oh.copy_(y, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if i >= 3:
+            e2e_t.append(a.elapsed_time(b))
+    e2e_ms = statistics.mean(e2e_t)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    assert pkg.ops.read_status(dev) == 0
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(args.config, 1000, args.cpu_budget_s)
+        cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
+
+    ep_info = None
+    if world > 1:
+        rb = pkg.ops.ep_row_bytes(H)
+        epx = layer.experts
+        if epx.capacity_tokens:
+            cap = epx.capacity_tokens * k
+            sent = epx.last_send_counts.cpu().tolist()
+            ep_info = {"layout": "fixed capacity", "capacity_rows_per_peer": cap, "rank0_rows_used": sent,
+                       "rank0_nvlink_bytes_per_step": (world - 1) * cap * (rb + 2 * H), "host_syncs_per_step": 0}
+        else:
+            s_send, s_recv = epx.last_splits
+            ep_info = {"layout": "exact splits", "rank0_rows_sent": s_send, "rank0_rows_received": s_recv,
+                       "rank0_nvlink_bytes_per_step": (sum(s_send) - s_send[rank] + sum(s_recv) - s_recv[rank])
+                       * (rb + 2 * H), "host_syncs_per_step": 1}
+        ep_info.update({"experts_per_rank": E // world, "row_bytes_dispatch": rb, "row_bytes_combine": H * 2})
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8 e4m3 x fp4 e2m1 (UE8M0 1x32 scales), fp32 accumulate",
+            "data": "synthetic (seeded: random MXFP4 weights, N(0,1) bf16 hidden)",
+            "config": {"workload": desc, "T": T, "T_per_rank": T, "E": E, "hidden": H, "intermediate": I,
+                       "top_k": k,
+                       "parallelism": f"ep{world} (E/{world} experts per GPU, NCCL all-to-all)" if world > 1
+                       else "single GPU",
+                       "l2": "256 MiB written before every timed step (outside the events); weights 424 MB > L2"},
+            "roofline": stages["roofline"] if stages else None,
+            "clocks": clocks,
+            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2 + (2 * world * 4 if ep_info and ep_info["host_syncs_per_step"]
+                                                       else 0)},
+            "gpu_launches": K * (KERNELS_PER_STEP if world == 1 else KERNELS_PER_STEP_EP),
+            "cpu_baseline": cpu,
+        }
+        if stages:
+            line["config"]["experts_touched"] = stages["touched"]
+            line["layer_hbm"] = stages["layer_hbm"]
+            line["mma"] = stages["mma"]
+        if ep_info:
+            line["ep"] = ep_info
+            line["roofline_note"] = "per-kernel roofline is reported by the N=1 run"
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, cfg_name):
+    """Times router+route+quant, GEMM1 and GEMM2 separately (single GPU) and returns the
+    roofline of the dominant kernel (GEMM1) plus layer-level HBM and MMA figures."""
+    import torch
     ws = pkg.ops.ExpertsWorkspace(T, k, E, H, I, dev)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     Ks = min(K, 500)
@@ -281,66 +397,18 @@ def run_ours(args):
     g1_gbs = b_g1 / (t_g1 / 1e3) / 1e9
     layer_gbs = b_layer / (ms / 1e3) / 1e9
     flops = 2 * T * k * (H * 2 * I + I * H)
-
-    # ---------------------------------------------------------------- end to end
-    xh = x.cpu().pin_memory()
-    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
-    Ke = min(K, 500)
-    e2e_t = []
-    for i in range(Ke + 3):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        flush.zero_()
-        a.record(stream)
-        xd.copy_(xh, non_blocking=True)
-        y, _, _ = layer(xd)
-        oh.copy_(y, non_blocking=True)
-        b.record(stream)
-        b.synchronize()
-        if i >= 3:
-            e2e_t.append(a.elapsed_time(b))
-    e2e_ms = statistics.mean(e2e_t)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    assert pkg.ops.read_status(dev) == 0
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline(args.config, 1000, args.cpu_budget_s)
-        cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
-
-    if rank == 0:
-        traffic = NCU_TRAFFIC_BYTES.get(args.config)
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp8 e4m3 x fp4 e2m1 (UE8M0 1x32 scales), fp32 accumulate",
-            "data": "synthetic (seeded: random MXFP4 weights, N(0,1) bf16 hidden)",
-            "config": {"workload": desc, "T": T, "E": E, "hidden": H, "intermediate": I, "top_k": k,
-                       "parallelism": f"replica x{world}" if world > 1 else "single GPU",
-                       "l2": "256 MiB written before every timed step (outside the events); weights 424 MB > L2",
-                       "experts_touched": touched},
-            "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel (GEMM1 gate_up + SwiGLU + requant)",
-                         "achieved": g1_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": g1_gbs / hbm_peak,
-                         "traffic": traffic, "peak_kind": peak_kind, "alg_bytes_per_launch": b_g1,
-                         "ms_per_launch": t_g1},
-            "layer_hbm": {"alg_bytes": b_layer, "achieved_gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
-                          "stage_ms": {"router+route+quant": t_pre, "gemm1": t_g1, "gemm2": t_g2},
-                          "gemm2_gbs": b_g2 / (t_g2 / 1e3) / 1e9},
-            "mma": {"flops_per_step": flops, "tflops": flops / (ms / 1e3) / 1e12},
-            "clocks": clocks,
-            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2},
-            "gpu_launches": K * KERNELS_PER_STEP,
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return {
+        "touched": touched,
+        "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel (GEMM1 gate_up + SwiGLU + requant)",
+                     "achieved": g1_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": g1_gbs / hbm_peak,
+                     "traffic": NCU_TRAFFIC_BYTES.get(cfg_name), "peak_kind": peak_kind, "alg_bytes_per_launch": b_g1,
+                     "ms_per_launch": t_g1},
+        "layer_hbm": {"alg_bytes": b_layer, "achieved_gbs": layer_gbs, "frac": layer_gbs / hbm_peak,
+                      "stage_ms": {"router+route+quant": t_pre, "gemm1": t_g1, "gemm2": t_g2},
+                      "gemm2_gbs": b_g2 / (t_g2 / 1e3) / 1e9},
+        "mma": {"flops_per_step": flops, "tflops": flops / (ms / 1e3) / 1e12,
+                "frac_of_bf16_dense": flops / (ms / 1e3) / 1e12 / bf16_peak if bf16_peak else None},
+    }
 
 
 def main():

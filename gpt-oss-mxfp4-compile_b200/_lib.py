@@ -46,10 +46,11 @@ _SIGNATURES = {
     "gptoss_moe_workspace_layout": (_i, [_c_int64, _i, _i, _c_int64, _c_int64, _vp]),
     "gptoss_ep_row_bytes": (_c_int64, [_c_int64]),
     "gptoss_ep_dispatch_workspace_bytes": (_sz, [_c_int64, _i, _i]),
-    "gptoss_ep_dispatch": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _i, _c_int64, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "gptoss_ep_dispatch": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _i, _c_int64, _c_int64, _vp, _vp, _vp, _vp, _sz,
+                                _vp, _vp]),
     "gptoss_ep_expert_forward": (_i, [_vp, _c_int64, _i, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, _vp,
                                       _c_int64, _vp, _f, _f, _vp, _vp, _sz, _i, _vp, _vp]),
-    "gptoss_ep_combine": (_i, [_vp, _vp, _vp, _c_int64, _i, _c_int64, _vp, _vp]),
+    "gptoss_ep_combine": (_i, [_vp, _c_int64, _vp, _vp, _c_int64, _i, _c_int64, _vp, _vp]),
     "gptoss_moe_route_quant": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64, _vp, _sz, _i, _vp, _vp]),
     "gptoss_moe_gemm1": (_i, [_c_int64, _i, _i, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _sz,
                               _i, _vp, _vp]),

@@ -824,8 +824,8 @@ size_t gptoss_ep_dispatch_workspace_bytes(int64_t num_tokens, int top_k, int wor
 
 int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
                        int64_t num_tokens, int top_k, int num_experts, int world_size, int64_t hidden_size,
-                       uint8_t* send_rows, int32_t* send_counts, int32_t* pos_of, void* workspace,
-                       size_t workspace_bytes, int32_t* status_dev, void* stream) {
+                       int64_t capacity, uint8_t* send_rows, int32_t* send_counts, int32_t* pos_of,
+                       void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream) {
   GPTOSS_CHECK(world_size >= 1 && world_size <= kMaxExperts, "ep_dispatch: world_size must be in [1, %d]", kMaxExperts);
   GPTOSS_CHECK(num_experts >= world_size && num_experts % world_size == 0,
                "ep_dispatch: num_experts (%d) must be a multiple of world_size (%d)", num_experts, world_size);
@@ -833,17 +833,21 @@ int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const 
                "ep_dispatch: bad sizes (T=%lld k=%d)", (long long)num_tokens, top_k);
   GPTOSS_CHECK(hidden_size > 0 && hidden_size % 32 == 0, "ep_dispatch: hidden size must be a multiple of 32");
   GPTOSS_CHECK(num_tokens * top_k < (1LL << 31), "ep_dispatch: too many assignments");
+  GPTOSS_CHECK(capacity == 0 || capacity >= num_tokens * top_k,
+               "ep_dispatch: capacity %lld must be 0 (compact rows) or >= num_tokens * top_k (%lld)",
+               (long long)capacity, (long long)(num_tokens * top_k));
+  GPTOSS_CHECK(capacity * world_size < (1LL << 31), "ep_dispatch: capacity * world_size too large");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(send_counts, "send_counts", &di));
   const size_t need = gptoss_ep_dispatch_workspace_bytes(num_tokens, top_k, world_size);
   if (workspace_bytes < need) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t A = num_tokens * top_k;
-  if (A == 0) {
+  if (A == 0 && capacity == 0) {
     GPTOSS_CUDA(cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world_size, st));
     return GPTOSS_OK;
   }
-  GPTOSS_CHECK(hidden && router_indices && routing_weights && send_rows && pos_of && workspace,
+  GPTOSS_CHECK(send_rows && workspace && (A == 0 || (hidden && router_indices && routing_weights && pos_of)),
                "ep_dispatch: null pointer");
   GPTOSS_CHECK(aligned(hidden, 16) && aligned(send_rows, 16) && aligned(workspace, 256),
                "ep_dispatch: misaligned pointer");
@@ -864,10 +868,13 @@ int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const 
   GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(world_size), dim3(1024), 0, st, rp));
   const int tpr = quant_threads_per_row(static_cast<int>(hidden_size));
   const int rpb = 256 / tpr;
-  return launch_pdl(ep_pack_kernel, dim3(static_cast<unsigned>((A + rpb - 1) / rpb)), dim3(tpr * rpb), 0, st,
+  const int64_t rows = capacity > 0 ? capacity * world_size : A;
+  return launch_pdl(ep_pack_kernel, dim3(static_cast<unsigned>((rows + rpb - 1) / rpb)), dim3(tpr * rpb), 0, st,
                     static_cast<const __nv_bfloat16*>(hidden), static_cast<int>(hidden_size), top_k,
                     num_experts / world_size, A, router_indices, routing_weights,
-                    static_cast<const int32_t*>(rp.sorted_src), tpr, send_rows, pos_of);
+                    static_cast<const int32_t*>(rp.sorted_src), capacity, world_size,
+                    static_cast<const int32_t*>(send_counts), static_cast<const int32_t*>(rp.offsets), tpr,
+                    send_rows, pos_of);
 }
 
 int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num_local_experts, int64_t hidden_size,
@@ -911,6 +918,7 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
   rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
   rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
   rp.spread = swap ? 1 : 0;
+  rp.allow_empty = 1;
   rp.err = status;
   GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
   GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(num_rows)), dim3(256), 0, st, recv_rows,
@@ -925,8 +933,9 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
                      dev, st);
 }
 
-int gptoss_ep_combine(const void* back_rows, const int32_t* pos_of, const int64_t* router_indices, int64_t num_tokens,
-                      int top_k, int64_t hidden_size, void* out, void* stream) {
+int gptoss_ep_combine(const void* back_rows, int64_t num_back_rows, const int32_t* pos_of,
+                      const int64_t* router_indices, int64_t num_tokens, int top_k, int64_t hidden_size, void* out,
+                      void* stream) {
   GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK, "ep_combine: bad sizes");
   GPTOSS_CHECK(hidden_size > 0 && hidden_size % 2 == 0, "ep_combine: hidden size must be even");
   DeviceInfo di;
@@ -936,7 +945,7 @@ int gptoss_ep_combine(const void* back_rows, const int32_t* pos_of, const int64_
   GPTOSS_CHECK(aligned(back_rows, 4) && aligned(out, 4), "ep_combine: misaligned pointer");
   return launch_pdl(ep_combine_kernel, dim3(static_cast<unsigned>(num_tokens)), dim3(256), 0,
                     static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(back_rows), pos_of,
-                    router_indices, num_tokens, top_k, static_cast<int>(hidden_size),
+                    router_indices, num_tokens, top_k, static_cast<int>(hidden_size), num_back_rows,
                     static_cast<__nv_bfloat16*>(out));
 }
 

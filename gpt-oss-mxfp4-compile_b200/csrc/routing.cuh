@@ -184,6 +184,7 @@ struct RouteSortParams {
   int spread;                      // activation scales in the SPREAD row layout
   int divisor;                     // bucket of assignment i = router_indices[i] / divisor (0, 1: expert)
   int32_t* sorted_src;             // optional [A]: assignment index i of each sorted entry
+  int allow_empty;                 // index -1 marks an empty slot: skipped without an error
   int* err;                        // set if an index is outside [0, E)
 };
 
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
   // Pass 1: full histogram (every CTA builds it; A is small next to the GEMMs).
   for (int i = tid; i < p.A; i += blockDim.x) {
     const int64_t ex = p.router_indices[i] / dv;
+    if (p.allow_empty && p.router_indices[i] == -1) continue;
     if (p.router_indices[i] < 0 || ex >= p.E) {
       if (p.err) atomicCAS(p.err, 0, 0x201);
       continue;
@@ -453,25 +455,45 @@ __host__ __device__ __forceinline__ int64_t ep_row_bytes(int H) {
 }
 
 // Pack: entry p of the destination-sorted order (route_sort_kernel with divisor =
-// experts per rank) -> quantised row p of the send buffer; pos_of[i] = p remembers where
-// assignment i went so the combine can find its returned row.
+// experts per rank) -> quantised send row; pos_of[i] remembers which row assignment i
+// went to so the combine can find its returned row.
+//   cap == 0: compact rows, row p (per-destination splits are variable);
+//   cap > 0:  W fixed segments of cap rows, entry j of destination q in row q*cap + j;
+//             unused rows carry local expert -1 (an empty slot the receiver skips), so the
+//             exchange has equal splits and needs no host-visible counts.
 __global__ void __launch_bounds__(256) ep_pack_kernel(
     const __nv_bfloat16* __restrict__ hidden, int H, int K, int experts_per_rank, int64_t A,
     const int64_t* __restrict__ router_indices, const float* __restrict__ routing_weights,
-    const int32_t* __restrict__ sorted_src, int tpr, uint8_t* __restrict__ send_rows,
+    const int32_t* __restrict__ sorted_src, int64_t cap, int world, const int32_t* __restrict__ dest_counts,
+    const int32_t* __restrict__ dest_offsets, int tpr, uint8_t* __restrict__ send_rows,
     int32_t* __restrict__ pos_of) {
   pdl_trigger();
   pdl_wait();
   const int rows_per_block = blockDim.x / tpr;
-  const int64_t p = static_cast<int64_t>(blockIdx.x) * rows_per_block + threadIdx.x / tpr;
-  if (p >= A) return;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * rows_per_block + threadIdx.x / tpr;
+  const int64_t rows_total = cap > 0 ? cap * world : A;
+  if (r >= rows_total) return;
   const int sub = threadIdx.x % tpr;
   const int G = H >> 5;
+  const int64_t rb = ep_row_bytes(H);
+  uint8_t* row = send_rows + r * rb;
+  int64_t p = r;
+  if (cap > 0) {
+    const int q = static_cast<int>(r / cap);
+    const int64_t j = r - static_cast<int64_t>(q) * cap;
+    if (j >= dest_counts[q]) {
+      if (sub == 0) {
+        int32_t* meta = reinterpret_cast<int32_t*>(row + rb - 8);
+        meta[0] = -1;
+        meta[1] = 0;
+      }
+      return;
+    }
+    p = dest_offsets[q] + j;
+  }
   const int i = sorted_src[p];
   if (i < 0) return;   // sentinel of an out-of-range router index
   const int64_t t = i / K;
-  const int64_t rb = ep_row_bytes(H);
-  uint8_t* row = send_rows + p * rb;
   const __nv_bfloat16* xr = hidden + t * H;
   for (int g = sub; g < G; g += tpr) {
     const uint4* pp = reinterpret_cast<const uint4*>(xr + g * 32);
@@ -500,7 +522,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(
     int32_t* meta = reinterpret_cast<int32_t*>(row + rb - 8);
     meta[0] = static_cast<int32_t>(router_indices[i] % experts_per_rank);
     meta[1] = __float_as_int(routing_weights[i]);
-    pos_of[i] = static_cast<int32_t>(p);
+    pos_of[i] = static_cast<int32_t>(r);
   }
 }
 
@@ -549,7 +571,8 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(
 __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __restrict__ back_rows,
                                                          const int32_t* __restrict__ pos_of,
                                                          const int64_t* __restrict__ router_indices, int64_t T,
-                                                         int K, int H, __nv_bfloat16* __restrict__ out) {
+                                                         int K, int H, int64_t rows,
+                                                         __nv_bfloat16* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
   const int64_t t = blockIdx.x;
@@ -564,7 +587,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __
     float a0 = 0.0f, a1 = 0.0f;
     for (int j = 0; j < K; ++j) {
       const int64_t pr = pos_of[t * K + order[j]];
-      if (pr < 0 || pr >= T * K) continue;   // assignment with an out-of-range expert id
+      if (pr < 0 || pr >= rows) continue;   // assignment with an out-of-range expert id
       const __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(back_rows + pr * H)[h2];
       a0 += __bfloat162float(v.x);
       a1 += __bfloat162float(v.y);

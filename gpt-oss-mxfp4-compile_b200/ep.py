@@ -21,10 +21,17 @@ forward is
 Quantisation is per row, so the FP8 codes and scales equal the single-GPU ones bit for
 bit; rows are independent through both GEMMs.
 
-The split sizes are read on the host once per forward (step 2), so a forward is not
-CUDA-graph capturable. The kernels sit behind :class:`CudaKernels`; a different object
-with the same three methods can stand in for it (the CPU tests use the oracle's
-restatement with the gloo backend).
+Two exchange layouts:
+  * exact splits (default): rows are compact; the split sizes are read on the host once
+    per forward (step 2), so the forward is not CUDA-graph capturable;
+  * fixed capacity (`capacity_tokens` set, the same on every rank): every rank sends W
+    segments of capacity_tokens*k rows, unused rows marked empty, so both all-to-alls
+    have equal splits, nothing is read on the host and the forward can be captured in a
+    CUDA graph. It moves W*capacity_tokens*k rows per rank and direction, which pays at
+    decode-sized batches where a host round trip costs more than the padding.
+The kernels sit behind :class:`CudaKernels`; a different object with the same three
+methods can stand in for it (the CPU tests use the oracle's restatement with the gloo
+backend).
 """
 from __future__ import annotations
 
@@ -42,8 +49,8 @@ class CudaKernels:
     """The sm_100a kernels of the three local steps."""
 
     @staticmethod
-    def dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int):
-        return _ops.ep_dispatch(hidden, router_indices, routing_weights, num_experts, world_size)
+    def dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, capacity: int = 0):
+        return _ops.ep_dispatch(hidden, router_indices, routing_weights, num_experts, world_size, capacity)
 
     @staticmethod
     def expert_forward(recv_rows, experts: CutlassGptOssExperts):
@@ -81,8 +88,10 @@ class ExpertParallelExperts(nn.Module):
     (hidden_states, router_indices, routing_weights) -> out contract, router_indices
     holding GLOBAL expert ids; `local_experts` holds this rank's E/W experts."""
 
-    def __init__(self, local_experts: CutlassGptOssExperts, num_experts: int, group=None, kernels=None):
+    def __init__(self, local_experts: CutlassGptOssExperts, num_experts: int, group=None, kernels=None,
+                 capacity_tokens: int | None = None):
         super().__init__()
+        self.capacity_tokens = capacity_tokens
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -92,7 +101,8 @@ class ExpertParallelExperts(nn.Module):
         self.num_experts = num_experts
         self.hidden_size = local_experts.hidden_size
         self.kernels = kernels if kernels is not None else CudaKernels()
-        self.last_splits = None   # (send, recv) rows per peer of the last forward
+        self.last_splits = None        # exact splits: (send, recv) rows per peer of the last forward
+        self.last_send_counts = None   # fixed capacity: device tensor of rows per destination
 
     def forward(self, hidden_states: torch.Tensor, router_indices: torch.Tensor,
                 routing_weights: torch.Tensor) -> torch.Tensor:
@@ -102,6 +112,18 @@ class ExpertParallelExperts(nn.Module):
         idx = router_indices.reshape(h.shape[0], router_indices.shape[-1]).contiguous()
         w = routing_weights.reshape(idx.shape).to(torch.float32).contiguous()
         k, g = self.kernels, self.group
+        if self.capacity_tokens:
+            if h.shape[0] > self.capacity_tokens:
+                raise RuntimeError(f"{h.shape[0]} tokens exceed capacity_tokens={self.capacity_tokens}")
+            cap = self.capacity_tokens * idx.shape[1]
+            send_rows, send_counts, pos_of = k.dispatch(h, idx, w, self.num_experts, self.world_size, cap)
+            recv_rows = torch.empty_like(send_rows)
+            dist.all_to_all_single(recv_rows, send_rows, group=g)
+            back = k.expert_forward(recv_rows, self.experts)
+            ret = torch.empty_like(back)
+            dist.all_to_all_single(ret, back, group=g)
+            self.last_send_counts = send_counts
+            return k.combine(ret, pos_of, idx).view(shape)
         send_rows, send_counts, pos_of = k.dispatch(h, idx, w, self.num_experts, self.world_size)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=g)

@@ -454,10 +454,11 @@ def ep_row_bytes(hidden_size: int) -> int:
     return rb
 
 
-def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int):
+def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, capacity: int = 0):
     """Sorts the T*k assignments by destination rank (experts [r*E/W, (r+1)*E/W) live on
     rank r) and quantises each assignment's hidden row into a packed send row.
-    Returns (send_rows u8 [T*k, row_bytes], send_counts i32 [W], pos_of i32 [T*k])."""
+    Returns (send_rows u8 [rows, row_bytes], send_counts i32 [W], pos_of i32 [T*k]) with
+    rows = T*k (capacity 0: compact) or W*capacity (fixed segments, empty rows marked)."""
     _cuda(hidden, "hidden_states")
     _dtype(hidden, (torch.bfloat16,), "hidden_states")
     _cuda(router_indices, "router_indices")
@@ -468,13 +469,17 @@ def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world
     k = router_indices.shape[1]
     dev = hidden.device
     A = T * k
-    send_rows = torch.empty((A, ep_row_bytes(H)), dtype=torch.uint8, device=dev)
+    if capacity and capacity < A:
+        raise RuntimeError(f"ep_dispatch: capacity {capacity} < T*k = {A}")
+    send_rows = torch.empty((world_size * capacity if capacity else A, ep_row_bytes(H)), dtype=torch.uint8,
+                            device=dev)
     send_counts = torch.empty(world_size, dtype=torch.int32, device=dev)
     pos_of = torch.empty(A, dtype=torch.int32, device=dev)
     nbytes = int(_lib.query("gptoss_ep_dispatch_workspace_bytes", T, k, world_size))
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     _lib.call("gptoss_ep_dispatch", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(), T, k,
-              int(num_experts), int(world_size), H, send_rows.data_ptr(), send_counts.data_ptr(), pos_of.data_ptr(),
+              int(num_experts), int(world_size), H, int(capacity), send_rows.data_ptr(), send_counts.data_ptr(),
+              pos_of.data_ptr(),
               ws.data_ptr(), ws.numel(), status_tensor(dev).data_ptr(), _stream(dev))
     return send_rows, send_counts, pos_of
 
@@ -516,6 +521,6 @@ def ep_combine(back_rows, pos_of, router_indices):
     out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     if T == 0:
         return out
-    _lib.call("gptoss_ep_combine", back_rows.data_ptr(), pos_of.data_ptr(), router_indices.data_ptr(), T, k, H,
-              out.data_ptr(), _stream(dev))
+    _lib.call("gptoss_ep_combine", back_rows.data_ptr(), back_rows.shape[0], pos_of.data_ptr(),
+              router_indices.data_ptr(), T, k, H, out.data_ptr(), _stream(dev))
     return out

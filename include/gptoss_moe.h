@@ -263,19 +263,24 @@ int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router
  * scales are those gptoss_quantize_fp8 gives for the token's hidden row. */
 int64_t gptoss_ep_row_bytes(int64_t hidden_size);
 size_t gptoss_ep_dispatch_workspace_bytes(int64_t num_tokens, int top_k, int world_size);
-/* router_indices hold GLOBAL expert ids. send_rows: [T*k, row_bytes]; send_counts: [W]
- * int32 rows per destination rank; pos_of: [T*k] int32, row of send_rows that assignment
- * i = t*k + j went to (the same row of the returned back_rows). */
+/* router_indices hold GLOBAL expert ids; send_counts: [W] int32 rows per destination rank;
+ * pos_of: [T*k] int32, row of send_rows that assignment i = t*k + j went to (the same row
+ * of the returned back_rows).
+ * capacity == 0: send_rows [T*k, row_bytes], compact, destination-major; the exchange
+ *   needs send_counts on the host for its splits.
+ * capacity >= T*k: send_rows [W*capacity, row_bytes], destination q's rows at
+ *   [q*capacity, q*capacity + send_counts[q]), the rest marked empty (local expert -1);
+ *   the exchange uses equal splits of capacity rows and no host-visible counts. */
 int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
                        int64_t num_tokens, int top_k, int num_experts, int world_size,
-                       int64_t hidden_size, uint8_t* send_rows, int32_t* send_counts,
-                       int32_t* pos_of, void* workspace, size_t workspace_bytes,
-                       int32_t* status_dev, void* stream);
+                       int64_t hidden_size, int64_t capacity, uint8_t* send_rows,
+                       int32_t* send_counts, int32_t* pos_of, void* workspace,
+                       size_t workspace_bytes, int32_t* status_dev, void* stream);
 /* Received rows -> back_rows [num_rows, H] bf16, row r = routing weight x expert output of
  * row r (route sort by local expert, blocked-scale gather, GEMM1 + SwiGLU + requant,
- * GEMM2 + bias). Weights are this rank's [E/W, ...] slices; workspace =
- * gptoss_moe_workspace_bytes(num_rows, 1, E/W, H, I). A local expert id outside [0, E/W)
- * sets *status_dev. */
+ * GEMM2 + bias); empty rows (local expert -1) are skipped and come back as zeros. Weights
+ * are this rank's [E/W, ...] slices; workspace = gptoss_moe_workspace_bytes(num_rows, 1,
+ * E/W, H, I). Any other local expert id outside [0, E/W) sets *status_dev. */
 int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num_local_experts,
                              int64_t hidden_size, int64_t intermediate_size,
                              const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
@@ -289,8 +294,9 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
  * ascending global expert order and rounded to bf16 once -- the result of the reference's
  * scatter_add_ of expert-sorted bf16 rows into a zero bf16 tensor on the CPU
  * (kernels/cutlass_experts.py:445-450). */
-int gptoss_ep_combine(const void* back_rows, const int32_t* pos_of, const int64_t* router_indices,
-                      int64_t num_tokens, int top_k, int64_t hidden_size, void* out, void* stream);
+int gptoss_ep_combine(const void* back_rows, int64_t num_back_rows, const int32_t* pos_of,
+                      const int64_t* router_indices, int64_t num_tokens, int top_k,
+                      int64_t hidden_size, void* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -382,10 +382,13 @@ def ep_row_bytes(H: int) -> int:
     return (H + H // 32 + 8 + 15) // 16 * 16
 
 
-def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int):
+def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, capacity: int = 0):
     """Assignments stably sorted by destination rank (expert // (E/W)); row p = quantised
     hidden row of its token + (local expert, weight). Returns numpy
-    (send_rows u8 [A, row_bytes], send_counts i32 [W], pos_of i32 [A])."""
+    (send_rows u8 [rows, row_bytes], send_counts i32 [W], pos_of i32 [A]); rows = A when
+    capacity is 0, else W * capacity with destination q's rows starting at q * capacity and
+    the unused rows marked empty (local expert -1, weight 0; their other bytes are
+    unspecified and zero here)."""
     h = hidden.float().numpy() if isinstance(hidden, torch.Tensor) else np.asarray(hidden, np.float32)
     idx = np.asarray(router_indices, dtype=np.int64)
     w = np.asarray(routing_weights, dtype=np.float32).reshape(-1)
@@ -406,6 +409,16 @@ def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world
         rows[:, rb - 4:] = w[order].astype(np.float32).view(np.uint8).reshape(-1, 4)
     pos_of = np.empty(T * k, dtype=np.int32)
     pos_of[order] = np.arange(T * k, dtype=np.int32)
+    if capacity:
+        assert capacity >= T * k
+        offs = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
+        padded = np.zeros((world_size * capacity, rb), dtype=np.uint8)
+        padded[:, rb - 8:rb - 4] = np.full((world_size * capacity, 1), -1, dtype=np.int32).view(np.uint8)
+        for q in range(world_size):
+            c = int(counts[q])
+            padded[q * capacity:q * capacity + c] = rows[offs[q]:offs[q] + c]
+        pos_of = (dest * capacity + (pos_of - offs[dest])).astype(np.int32)
+        rows = padded
     return rows, counts, pos_of
 
 
@@ -421,7 +434,9 @@ def ep_expert_rows(recv_rows: np.ndarray, H: int, w_local: dict, alpha: float = 
     e_loc = w_local["gu_blocks"].shape[0]
     lexp = np.ascontiguousarray(rows[:, rb - 8:rb - 4]).view(np.int32).reshape(-1).astype(np.int64)
     wt = np.ascontiguousarray(rows[:, rb - 4:]).view(np.float32).reshape(-1)
-    st, se, sw, counts, offsets = route_stable(lexp[:, None], wt[:, None], e_loc)
+    keep = np.nonzero(lexp != -1)[0]                       # rows marked empty are skipped
+    st, se, sw, counts, offsets = route_stable(lexp[keep, None], wt[keep, None], e_loc)
+    st = keep[st]
     a_codes = rows[st, :H]
     a_sf = rows[st, H:H + H // 32]
     gu = group_mm_bf16(a_codes, a_sf, w_local["gu_blocks"], w_local["gu_scales"], counts, offsets)

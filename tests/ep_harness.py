@@ -25,9 +25,9 @@ class OracleKernels:
         self.w_local = w_local
         self.H = hidden_size
 
-    def dispatch(self, hidden, router_indices, routing_weights, num_experts, world_size):
+    def dispatch(self, hidden, router_indices, routing_weights, num_experts, world_size, capacity=0):
         rows, counts, pos = O.ep_dispatch(hidden, router_indices.numpy(), routing_weights.numpy(), num_experts,
-                                          world_size)
+                                          world_size, capacity)
         return torch.from_numpy(rows), torch.from_numpy(counts), torch.from_numpy(pos)
 
     def expert_forward(self, recv_rows, experts):
@@ -73,14 +73,17 @@ def cpu_worker(rank: int, world: int, port: int, cases, q):
         wn = O.numpy_weights(d)
         e_loc = E // world
         local = pkg.CutlassGptOssExperts(Cfg(e_loc, H, I))
-        mod = EP.ExpertParallelExperts(local, E, kernels=OracleKernels(O.slice_experts(wn, rank * e_loc,
-                                                                                     (rank + 1) * e_loc), H))
+        kern = OracleKernels(O.slice_experts(wn, rank * e_loc, (rank + 1) * e_loc), H)
+        mod = EP.ExpertParallelExperts(local, E, kernels=kern)
+        fixed = EP.ExpertParallelExperts(local, E, kernels=kern, capacity_tokens=16)
         results = []
         for case in cases:
             h, ix, wv = routing_case(case, rank, world, 16)
             out = mod(h, ix, wv)
+            out_fixed = fixed(h, ix, wv)
             ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
-            results.append((case, tuple(out.shape), bool(torch.equal(out, ref)), mod.last_splits))
+            results.append((case, tuple(out.shape), bool(torch.equal(out, ref) and torch.equal(out_fixed, ref)),
+                            mod.last_splits))
         q.put((rank, results, None))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, None, repr(e)))
@@ -135,19 +138,23 @@ def nccl_worker(rank: int, world: int, port: int, shapes, q):
             d = O.synth_layer(SEED, E=e_tot, H=hs, I=isz, T=1)
             wn = O.numpy_weights(d)
             full = build_experts(pkg, d, dev, e_tot, hs, isz)
-            mod = EP.ExpertParallelExperts(EP.shard_experts(full, rank, world), e_tot)
+            local = EP.shard_experts(full, rank, world)
+            mod = EP.ExpertParallelExperts(local, e_tot)
+            fixed = EP.ExpertParallelExperts(local, e_tot, capacity_tokens=T + 8 * world)
             g = torch.Generator().manual_seed(500 + rank)
             h = torch.randn(T + 8 * rank, hs, generator=g).to(torch.bfloat16)
             wv, ix = torch.topk(torch.randn(h.shape[0], e_tot, generator=g), K, dim=-1)
             wv = torch.softmax(wv, -1).float()
             out = mod(h.to(dev), ix.to(dev), wv.to(dev))
+            out_fixed = fixed(h.to(dev), ix.to(dev), wv.to(dev))
             torch.cuda.synchronize()
             st = pkg.ops.read_status(dev)
             ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
             single = full(h.to(dev), ix.to(dev), wv.to(dev))
-            results.append(("experts", e_tot, hs, st, rel_l2(out.cpu(), ref), max_abs_over_rms(out.cpu(), ref),
-                            (out.float() - single.float()).abs().max().item() / single.float().abs().max().item(),
-                            mod.last_splits))
+            for o in (out, out_fixed):
+                results.append(("experts", e_tot, hs, st, rel_l2(o.cpu(), ref), max_abs_over_rms(o.cpu(), ref),
+                                (o.float() - single.float()).abs().max().item() / single.float().abs().max().item(),
+                                mod.last_splits))
             # the layer: router on local tokens + EP experts vs the single-GPU layer
             single_layer = build_layer(pkg, d, dev, e_tot, hs, isz, K)
             ep_layer = EP.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), K, mod)

@@ -64,3 +64,25 @@ def test_gloo_two_ranks_match_single_device_oracle():
         s0 = res[0][0][case_i][3]
         s1 = res[1][0][case_i][3]
         assert s0[0][1] == s1[1][0] and s1[0][0] == s0[1][1]
+
+
+def test_oracle_capacity_layout():
+    # fixed-capacity segments: same rows as the compact layout, moved to q*cap, the rest
+    # marked empty; the chain through them still equals the single-device forward.
+    d = O.synth_layer(SEED, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    h, ix, wv = routing_case("random", 1, 2, 12)
+    ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
+    rows_c, counts, pos_c = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, 2)
+    cap = 12 * K
+    rows, counts2, pos = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, 2, cap)
+    rb = O.ep_row_bytes(H)
+    assert rows.shape == (2 * cap, rb) and np.array_equal(counts, counts2)
+    c0, c1 = int(counts[0]), int(counts[1])
+    assert np.array_equal(rows[:c0], rows_c[:c0]) and np.array_equal(rows[cap:cap + c1], rows_c[c0:])
+    empty = np.concatenate([np.arange(c0, cap), np.arange(cap + c1, 2 * cap)])
+    assert (rows[empty, rb - 8:rb - 4].view(np.int32) == -1).all()
+    assert np.array_equal(rows[pos], rows_c[pos_c])
+    b0 = O.ep_expert_rows(rows[:cap], H, O.slice_experts(wn, 0, E // 2))
+    b1 = O.ep_expert_rows(rows[cap:], H, O.slice_experts(wn, E // 2, E))
+    assert torch.equal(O.ep_combine(torch.cat([b0, b1]), pos, ix.numpy()), ref)

@@ -103,3 +103,44 @@ def test_emulated_ranks_chain(pkg, dev, world):
         single = m(h.to(dev), ix.to(dev), wv.to(dev))
         diff = (out.float() - single.float()).abs().max().item()
         assert diff <= 2 ** -7 * single.float().abs().max().item(), diff
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_dispatch_capacity_layout_bit_exact(pkg, dev, world):
+    E, H, T = 32, 2880, 19
+    h, ix, wv = _inputs(77 + world, T, E, H)
+    cap = T * 4 + 3
+    rows, counts, pos = pkg.ops.ep_dispatch(h.to(dev), ix.to(dev), wv.to(dev), E, world, cap)
+    torch.cuda.synchronize()
+    assert pkg.ops.read_status(dev) == 0
+    r_o, c_o, p_o = O.ep_dispatch(h, ix.numpy(), wv.numpy(), E, world, cap)
+    rows = rows.cpu().numpy()
+    rb = O.ep_row_bytes(H)
+    assert rows.shape == r_o.shape == (world * cap, rb)
+    assert np.array_equal(counts.cpu().numpy(), c_o) and np.array_equal(pos.cpu().numpy(), p_o)
+    used = np.zeros(world * cap, dtype=bool)
+    used[p_o] = True
+    assert np.array_equal(rows[used], r_o[used])                       # every byte of a used row
+    assert np.array_equal(rows[~used, rb - 8:], r_o[~used, rb - 8:])   # empty marker + zero weight
+
+
+def test_emulated_ranks_chain_capacity(pkg, dev):
+    E, H, I, world = 8, 512, 512, 4
+    d = O.synth_layer(6, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    m = build_experts(pkg, d, dev, E, H, I)
+    cap_tokens = 20
+    cap = cap_tokens * 4
+    ins = [_inputs(200 + r, 12 + 2 * r, E, H) for r in range(world)]
+    disp = [pkg.ops.ep_dispatch(h.to(dev), ix.to(dev), wv.to(dev), E, world, cap) for h, ix, wv in ins]
+    # equal splits: rank q receives segment q of every rank, in rank order
+    backs = []
+    for q in range(world):
+        recv = torch.cat([disp[r][0][q * cap:(q + 1) * cap] for r in range(world)])
+        backs.append(pkg.ep.CudaKernels.expert_forward(recv, pkg.ep.shard_experts(m, q, world)))
+    for r, (h, ix, wv) in enumerate(ins):
+        ret = torch.cat([backs[q][r * cap:(r + 1) * cap] for q in range(world)])
+        out = pkg.ops.ep_combine(ret, disp[r][2], ix.to(dev))
+        torch.cuda.synchronize()
+        assert pkg.ops.read_status(dev) == 0
+        assert_output_tolerance(out.cpu(), O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn), f"rank {r}")
