@@ -2,13 +2,15 @@
 // scales, fp32 accumulation in TMEM via tcgen05.mma kind::mxf8f6f4.block_scale.
 //
 // One persistent CTA per SM walks a ragged tile list built on the device from the
-// per-expert row counts (no host sync). Warp roles (192 threads):
+// per-expert row counts (no host sync). Warp roles:
 //   warp 0     TMA producer: activation tile (2-D map, fp8), weight tile (3-D map,
 //              packed e2m1 expanded to the 8-bit smem container by the TMA unit),
 //              plus the 512-byte blocked scale chunks (plain bulk copies).
 //   warp 1     TMEM allocator + single-thread MMA issuer: tcgen05.cp of the scale chunks
 //              into TMEM, then 4 MMAs (K = 32 each) per 128-deep K block.
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator and one of three fused tails.
+//   warps 2+   epilogue: tcgen05.ld of the accumulator and one of three fused tails;
+//              4 warps (SWAP) or 12 warps, three per TMEM lane quarter, each warpgroup
+//              taking one 64-column slice of the 192-column tile (SWAP = false).
 //
 // Two orientations:
 //   SWAP = false  M = 128 activation rows, N = 192 weight rows (prefill-sized groups).
@@ -90,13 +92,34 @@ struct GemmConfig {
                                         : (kSfWgtCol + 4 * kWgtSfChunks) <= 256 ? 256 : 512;
   static constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + 2 * kAccBufs + 1) + 16;
   static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 2048;
-  static constexpr int kThreads = 192;
+  // Epilogue warps: one warpgroup for weights-on-M tiles (their GEMM1 epilogue reduces
+  // across the warpgroup); tokens-on-M tiles give each warpgroup one 64-column slice, so
+  // three warps share every TMEM lane quarter and hide each other's latency.
+  static constexpr int kEpiWarps = SWAP ? 4 : 4 * (kWgtRows / 64);
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
 
 constexpr int kMaxExpertsGemm = 256;
 
+// 32 consecutive fp32 bias values (16-byte vector loads when all are in range; zero past
+// `valid`). `b` is 16-byte aligned whenever valid >= 32 (N and the column are multiples
+// of 32).
+__device__ __forceinline__ void load_bias32(const float* b, int valid, float (&out)[32]) {
+  if (valid >= 32) {
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = __ldg(b4 + i);
+      out[4 * i] = v.x; out[4 * i + 1] = v.y; out[4 * i + 2] = v.z; out[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) out[i] = i < valid ? b[i] : 0.0f;
+  }
+}
+
 template <bool SWAP, bool SPREAD, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,
                     const __grid_constant__ CUtensorMap tm_act32,
                     const __grid_constant__ CUtensorMap tm_act16,
@@ -132,7 +155,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < C::kAccBufs; ++b) {
       mbar_init(accf_bar(b), 1);
-      mbar_init(acce_bar(b), 4);
+      mbar_init(acce_bar(b), C::kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
@@ -291,6 +314,8 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ================================================================ epilogue
     const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int wg = (warp - 2) >> 2;         // epilogue warpgroup
+    constexpr int kWgs = C::kEpiWarps / 4;
     int local = 0;
     bool ok = true;   // after a timeout keep walking the tiles (named barriers stay
                       // matched across the four warps) but touch no TMEM or memory
@@ -318,21 +343,21 @@ __global__ void __launch_bounds__(192, 1)
         const int n_tile0 = nt * C::kWgtRows;
         if constexpr (EPI == kEpiGemm1) {
 #pragma unroll 1
-          for (int gi = 0; gi < C::kWgtRows / 64; ++gi) {
+          for (int gi = wg; gi < C::kWgtRows / 64; gi += kWgs) {
             float h[32];
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
               uint32_t r[32];
               __syncwarp();
               tmem_ld_32x32b_x32(t_acc + (2 * gi + half) * 32, r);
-              tmem_ld_wait();
               const int nb = n_tile0 + (2 * gi + half) * 32;
-              const float* bs = p.bias + static_cast<int64_t>(e) * p.N + nb;
+              float bsv[32];
+              load_bias32(p.bias + static_cast<int64_t>(e) * p.N + nb, p.N - nb, bsv);
+              tmem_ld_wait();
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const bool in = nb + 2 * j + 1 < p.N;
-                const float g = __fadd_rn(bf16_round(__uint_as_float(r[2 * j])), in ? bs[2 * j] : 0.0f);
-                const float u = __fadd_rn(bf16_round(__uint_as_float(r[2 * j + 1])), in ? bs[2 * j + 1] : 0.0f);
+                const float g = __fadd_rn(bf16_round(__uint_as_float(r[2 * j])), bsv[2 * j]);
+                const float u = __fadd_rn(bf16_round(__uint_as_float(r[2 * j + 1])), bsv[2 * j + 1]);
                 h[half * 16 + j] = swiglu_pair(g, u, p.swiglu_alpha, p.swiglu_limit);
               }
             }
@@ -354,7 +379,7 @@ __global__ void __launch_bounds__(192, 1)
             if (vrow) { tok = p.token_idx[grow]; wrow = p.row_weights[grow]; }
           }
 #pragma unroll 1
-          for (int c = 0; c < C::kWgtRows / 32; ++c) {
+          for (int c = wg; c < C::kWgtRows / 32; c += kWgs) {
             uint32_t r[32];
             __syncwarp();
             tmem_ld_32x32b_x32(t_acc + c * 32, r);
@@ -380,14 +405,14 @@ __global__ void __launch_bounds__(192, 1)
                   o[j] = __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
               }
             } else {  // kEpiGemm2
-              const float* bs = p.bias + static_cast<int64_t>(e) * p.N + nb;
+              float bsv[32];
+              load_bias32(p.bias + static_cast<int64_t>(e) * p.N + nb, p.N - nb, bsv);
               __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + tok * p.ld_out + nb;
               uint32_t pk[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const bool in0 = nb + 2 * j < p.N, in1 = nb + 2 * j + 1 < p.N;
-                const float y0 = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[2 * j])), in0 ? bs[2 * j] : 0.f), wrow);
-                const float y1 = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[2 * j + 1])), in1 ? bs[2 * j + 1] : 0.f), wrow);
+                const float y0 = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[2 * j])), bsv[2 * j]), wrow);
+                const float y1 = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[2 * j + 1])), bsv[2 * j + 1]), wrow);
                 const __nv_bfloat162 v2 = __floats2bfloat162_rn(y0, y1);
                 pk[j] = *reinterpret_cast<const uint32_t*>(&v2);
               }
