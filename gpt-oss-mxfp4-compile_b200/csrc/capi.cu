@@ -18,6 +18,7 @@
 #include "numerics.cuh"
 #include "routing.cuh"
 #include "gemm.cuh"
+#include "prologue.cuh"
 
 using namespace gptoss;
 
@@ -112,19 +113,33 @@ int64_t pad128(int64_t k) { return (k + 127) / 128 * 128; }
 // previous kernel on the stream drains; every kernel of this library waits
 // (griddepcontrol.wait) before touching global memory, so ordering is unchanged.
 template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       dim3 cluster, Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster.x;
+    attr[1].val.clusterDim.y = cluster.y;
+    attr[1].val.clusterDim.z = cluster.z;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   GPTOSS_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
   return GPTOSS_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, st, dim3(1, 1, 1), std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- TMA descriptors
@@ -274,22 +289,38 @@ Workspace plan_workspace(int64_t T, int k, int E, int64_t H, int64_t I) {
 
 int router_launch(const void* hidden, const void* weight, const void* bias, int64_t T, int64_t H, int E,
                   int k, int64_t* idx, void* scores, float* wf32, void* logits, void* zero_rows,
-                  int64_t zero_elems, cudaStream_t st) {
-  int tb = T <= 256 ? 1 : (T <= 4096 ? 4 : 16);
-  const size_t smem = sizeof(__nv_bfloat16) * tb * H + sizeof(float) * tb * E;
-  GPTOSS_CHECK(smem <= 200 * 1024, "router: hidden size %lld too large", (long long)H);
-  const int grid = static_cast<int>((T + tb - 1) / tb);
-  const int threads = 32 * std::min(tb == 1 ? 32 : 16, E);
-  auto go = [&](auto kern) -> int {
-    GPTOSS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    return launch_pdl(kern, dim3(grid), dim3(threads), smem, st, static_cast<const __nv_bfloat16*>(hidden),
-                      static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
-                      static_cast<int>(T), static_cast<int>(H), E, k, idx, static_cast<__nv_bfloat16*>(scores), wf32,
-                      static_cast<__nv_bfloat16*>(logits), static_cast<__nv_bfloat16*>(zero_rows), zero_elems);
+                  int64_t zero_elems, int sms, int dev, cudaStream_t st) {
+  const int64_t nblocks = (T + kRtTok - 1) / kRtTok;
+  GPTOSS_CHECK(nblocks < (1LL << 31), "router: too many tokens");
+  const int nchunks = static_cast<int>((H + kRtKc - 1) / kRtKc);
+  const int tiles = (E + 7) / 8;                 // n-tiles of 8 experts over 4 warps
+  const int nt = tiles <= 4 ? 1 : (tiles <= 8 ? 2 : (tiles <= 16 ? 4 : 8));
+  // Split K over a cluster when the token blocks alone would leave SMs idle.
+  int S = 1;
+  if (nblocks < sms)
+    S = static_cast<int>(std::min<int64_t>({router_max_split(nt), nchunks, (sms + nblocks - 1) / nblocks}));
+  const int cpc = (nchunks + S - 1) / S;
+  const size_t smem = router_smem_bytes(nt);
+  auto go = [&](auto kern, int slot) -> int {
+    static uint64_t attr_done[4] = {0, 0, 0, 0};   // one bit per device and instance
+    static std::mutex mu;
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      if (!(attr_done[slot] & (1ull << dev))) {
+        GPTOSS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        attr_done[slot] |= (1ull << dev);
+      }
+    }
+    return launch_pdl_cluster(kern, dim3(static_cast<unsigned>(nblocks), S), dim3(128), smem, st, dim3(1, S, 1),
+                              static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(weight),
+                              static_cast<const __nv_bfloat16*>(bias), static_cast<int>(T), static_cast<int>(H), E, k,
+                              cpc, idx, static_cast<__nv_bfloat16*>(scores), wf32, static_cast<__nv_bfloat16*>(logits),
+                              static_cast<__nv_bfloat16*>(zero_rows), zero_elems);
   };
-  if (tb == 1) return go(router_topk_kernel<1>);
-  if (tb == 4) return go(router_topk_kernel<4>);
-  return go(router_topk_kernel<16>);
+  if (nt == 1) return go(router_mma_kernel<1>, 0);
+  if (nt == 2) return go(router_mma_kernel<2>, 1);
+  if (nt == 4) return go(router_mma_kernel<4>, 2);
+  return go(router_mma_kernel<8>, 3);
 }
 
 struct ExpertWeights {
@@ -350,14 +381,11 @@ int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, 
   rp.spread = spread ? 1 : 0;
   rp.err = status;
   GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(E), dim3(1024), 0, st, rp));
-  const int tpr = quant_threads_per_row(static_cast<int>(H));
-  const int rpb = 256 / tpr;
-  const int qblocks = static_cast<int>((A + rpb - 1) / rpb);
-  return launch_pdl(gather_quant_kernel<__nv_bfloat16>, dim3(qblocks), dim3(tpr * rpb), 0, st,
-                    static_cast<const __nv_bfloat16*>(hidden), A, static_cast<int>(H), tpr,
+  return launch_pdl(gather_quant_rows_kernel, dim3(static_cast<unsigned>((A + 7) / 8)), dim3(256), 0, st,
+                    static_cast<const __nv_bfloat16*>(hidden), A, static_cast<int>(H),
                     static_cast<const int64_t*>(w.sorted_token), static_cast<const int64_t*>(w.sorted_expert),
                     static_cast<const int32_t*>(w.offsets), static_cast<const int32_t*>(w.sfoff_a),
-                    static_cast<int>(Kh / 128), spread ? 1 : 0, w.act_codes, w.act_sf, static_cast<uint8_t*>(nullptr));
+                    static_cast<int>(Kh / 128), spread ? 1 : 0, w.act_codes, w.act_sf);
 }
 
 // Stage 2: GEMM1 + bias + SwiGLU + FP8 requantisation.
@@ -372,6 +400,7 @@ int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g1.p.out = w.inter_codes; g1.p.ld_out = I; g1.p.bias = wt.gu_bias; g1.p.out_sf = w.inter_sf;
   g1.p.out_sf_offsets = w.sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
   g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
+  g1.p.prefetch_tiles = swap ? 3 : 0;
   return run_gemm<kEpiGemm1>(g1, swap, swap, di, dev, st);
 }
 
@@ -388,15 +417,84 @@ int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   return run_gemm<kEpiGemm2>(g2, swap, swap, di, dev, st);
 }
 
-// route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch.
+// ---------------------------------------------------------------- decode-sized prologue
+// Router (optional) + counting sort + quantisation in one cluster launch
+// (decode_prologue_kernel) for batches of at most kDpMaxTokens tokens.
+struct RouterArgs {
+  const void* weight; const void* bias; int64_t* ridx_out; void* scores_out; float* rw_out;
+};
+
+bool decode_prologue_fits(int64_t T, int k, int E, int64_t H, bool router, size_t* smem, int* slice) {
+  if (T < 1 || T > kDpMaxTokens || T * k > kDpMaxAssign || H % 8 != 0) return false;
+  const int nchunks = static_cast<int>((H + 63) / 64);
+  *slice = (nchunks + kDpCluster - 1) / kDpCluster;
+  *slice += *slice & 1;                       // whole 128-wide k-atoms per rank
+  const DpLayout Ld = dp_layout(static_cast<int>(T), E, k, *slice, router);
+  *smem = Ld.total;
+  return Ld.total <= kDpMaxSmem;
+}
+
+int run_decode_prologue(const void* hidden, const RouterArgs* ra, const int64_t* ridx, const float* rw, int64_t T,
+                        int k, int E, int64_t H, int64_t I, const WsPtrs& w, bool spread, void* zero_out,
+                        int* status, size_t smem, int slice, int dev, cudaStream_t st) {
+  static uint64_t attr_done = 0;   // one bit per device
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_done & (1ull << dev))) {
+      GPTOSS_CUDA(cudaFuncSetAttribute(decode_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kDpMaxSmem)));
+      attr_done |= (1ull << dev);
+    }
+  }
+  DecodePrologueParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(hidden);
+  if (ra != nullptr) {
+    p.w = static_cast<const __nv_bfloat16*>(ra->weight);
+    p.bias = static_cast<const __nv_bfloat16*>(ra->bias);
+    p.ridx_out = ra->ridx_out;
+    p.scores_out = static_cast<__nv_bfloat16*>(ra->scores_out);
+    p.rw_out = ra->rw_out;
+  } else {
+    p.ridx_in = ridx;
+    p.rw_in = rw;
+  }
+  p.T = static_cast<int>(T); p.H = static_cast<int>(H); p.E = E; p.K = k;
+  p.slice_chunks = slice;
+  p.sorted_token = w.sorted_token; p.sorted_expert = w.sorted_expert; p.sorted_weight = w.sorted_weight;
+  p.counts = w.counts; p.offsets = w.offsets; p.sf_offsets_a = w.sfoff_a; p.sf_offsets_b = w.sfoff_b;
+  p.act_codes = w.act_codes; p.act_sf = w.act_sf; p.inter_sf = w.inter_sf;
+  p.g4_a = static_cast<int>(pad128(H) / 128); p.g4_b = static_cast<int>(pad128(I) / 128);
+  p.spread = spread ? 1 : 0;
+  p.zero_out = static_cast<__nv_bfloat16*>(zero_out);
+  p.err = status;
+  return launch_pdl_cluster(decode_prologue_kernel, dim3(kDpCluster), dim3(kDpThreads), smem, st,
+                            dim3(kDpCluster, 1, 1), p);
+}
+
+// route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch. With `ra` the router runs
+// first (inside the decode prologue, or as router_launch, which also zeroes `out`).
 int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E,
                      int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit, void* out,
                      uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
-                     cudaStream_t st, bool out_zeroed) {
+                     cudaStream_t st, const RouterArgs* ra = nullptr) {
   const WsPtrs w = ws_ptrs(ws, L);
   const bool swap = pick_swap(mode, T * k, E, 16);
-  GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, swap, status, st));
-  if (!out_zeroed) GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
+  size_t smem = 0;
+  int slice = 0;
+  if (decode_prologue_fits(T, k, E, H, ra != nullptr, &smem, &slice)) {
+    GPTOSS_TRY(run_decode_prologue(hidden, ra, ridx, rw, T, k, E, H, I, w, swap, out, status, smem, slice, dev, st));
+  } else {
+    if (ra != nullptr) {
+      GPTOSS_TRY(router_launch(hidden, ra->weight, ra->bias, T, H, E, k, ra->ridx_out, ra->scores_out, ra->rw_out,
+                               nullptr, out, H, di.sms, dev, st));
+      ridx = ra->ridx_out;
+      rw = ra->rw_out;
+    }
+    GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, swap, status, st));
+    if (ra == nullptr)
+      GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
+  }
   GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, swap, status, di, dev, st));
   return stage_gemm2(T * k, E, H, I, wt, out, w, swap, status, di, dev, st);
 }
@@ -492,8 +590,11 @@ int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
   GPTOSS_CHECK(bias != nullptr && router_indices != nullptr, "router: null pointer");
   if (num_tokens == 0) return GPTOSS_OK;
   GPTOSS_CHECK(hidden != nullptr && aligned(hidden, 16) && aligned(weight, 16), "router: inputs must be 16-byte aligned");
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
   return router_launch(hidden, weight, bias, num_tokens, hidden_size, num_experts, top_k, router_indices,
-                       router_scores, routing_weights_f32, logits, nullptr, 0, static_cast<cudaStream_t>(stream));
+                       router_scores, routing_weights_f32, logits, nullptr, 0, di.sms, dev,
+                       static_cast<cudaStream_t>(stream));
 }
 
 int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, uint8_t* codes, uint8_t* scales,
@@ -656,7 +757,7 @@ int gptoss_moe_experts_forward(const void* hidden, const int64_t* router_indices
   return experts_pipeline(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
                           intermediate_size, w, swiglu_alpha, swiglu_limit, out, static_cast<uint8_t*>(workspace), L,
                           gemm_mode, status_dev ? status_dev : di.status_sink, di, dev,
-                          static_cast<cudaStream_t>(stream), false);
+                          static_cast<cudaStream_t>(stream));
 }
 
 int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, const void* router_bias,
@@ -688,11 +789,10 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, cons
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int64_t* ridx = router_indices_out ? router_indices_out : reinterpret_cast<int64_t*>(ws + L.router_idx);
   float* rw = reinterpret_cast<float*>(ws + L.router_w);
-  GPTOSS_TRY(router_launch(hidden, router_weight, router_bias, num_tokens, hidden_size, num_experts, top_k, ridx,
-                           router_scores_out, rw, nullptr, out, hidden_size, st));
-  return experts_pipeline(hidden, ridx, rw, num_tokens, top_k, num_experts, hidden_size, intermediate_size, w,
-                          swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode, status_dev ? status_dev : di.status_sink,
-                          di, dev, st, true);
+  const RouterArgs ra{router_weight, router_bias, ridx, router_scores_out, rw};
+  return experts_pipeline(hidden, nullptr, nullptr, num_tokens, top_k, num_experts, hidden_size, intermediate_size,
+                          w, swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode,
+                          status_dev ? status_dev : di.status_sink, di, dev, st, &ra);
 }
 
 
@@ -805,8 +905,7 @@ int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router
   GPTOSS_TRY(noalloc_scratch(dev, &ws));
   return experts_pipeline(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
                           intermediate_size, w, swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode,
-                          status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream),
-                          false);
+                          status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------- expert parallelism

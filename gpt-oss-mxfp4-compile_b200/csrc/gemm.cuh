@@ -62,6 +62,10 @@ struct GemmParams {
   const int64_t* token_idx;     // kEpiGemm2
   const float* row_weights;     // kEpiGemm2
   float swiglu_alpha, swiglu_limit;
+  // Weights-on-M tiles: weight tiles each CTA prefetches into L2 before waiting on the
+  // previous kernel (0: none). The tiles are guessed assuming one activation chunk per
+  // expert -- the decode case; a wrong guess only costs bandwidth.
+  int prefetch_tiles;
 };
 
 template <bool SWAP, bool SPREAD = false>
@@ -163,6 +167,21 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
   if (warp == 1) {
     tmem_alloc(smem_u32(&s_tmem_base), C::kTmemCols);
     tmem_relinquish();
+  }
+  if constexpr (SWAP) {
+    // The weights do not depend on the previous kernel: while it (the routing prologue)
+    // runs, pull the weight tiles this CTA will most likely stream first into L2.
+    if (warp == 0 && p.prefetch_tiles > 0 && elect_one()) {
+      for (int j = 0; j < p.prefetch_tiles; ++j) {
+        const int t = blockIdx.x + j * gridDim.x;
+        const int e = t / p.n_tiles, nt = t - e * p.n_tiles;
+        if (e >= p.num_experts) break;
+        for (int kb = 0; kb < p.num_kb; ++kb) tma_prefetch_3d(&tm_wgt, kb * 128, nt * C::kWgtRows, e);
+        bulk_prefetch_l2(p.sfb + static_cast<int64_t>(e) * p.sfb_stride +
+                             static_cast<int64_t>((nt * C::kWgtRows) >> 7) * p.num_kb * 512,
+                         static_cast<uint32_t>(p.num_kb) * 512u);
+      }
+    }
   }
   pdl_wait();
   // ---- per-CTA tile map from the device-side counts
@@ -368,7 +387,12 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
               uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + grow * p.ld_out + f0);
               o[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
               o[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
-              p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(r_in, f0 >> 5, p.out_g4)] = s;
+              uint8_t* sfb_e = p.out_sf + p.out_sf_offsets[e];
+              sfb_e[blocked_sf_offset(r_in, f0 >> 5, p.out_g4)] = s;
+              // the K padding groups of the row's last k-atom read as zero scales in GEMM2
+              if ((f0 >> 5) == (p.out_features >> 5) - 1)
+                for (int gz = p.out_features >> 5; gz < 4 * p.out_g4; ++gz)
+                  sfb_e[blocked_sf_offset(r_in, gz, p.out_g4)] = 0;
             }
           }
         } else {
@@ -525,9 +549,15 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
                 const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
                 if ((lane & 1) == 0 && vcol && f < p.out_features)
                   codes_out[grow * p.ld_out + f] = static_cast<uint8_t>(c2 & 0xFFu);
-                if (lane == 0 && (q & 1) == 0 && f < p.out_features)
-                  p.out_sf[p.out_sf_offsets[e] + blocked_sf_offset(act_sf_row<SPREAD>(a0 + j), grp, p.out_g4)] =
-                      static_cast<uint8_t>((rb >> 23) & 0xFFu);
+                if (lane == 0 && (q & 1) == 0 && f < p.out_features) {
+                  uint8_t* sfb_e = p.out_sf + p.out_sf_offsets[e];
+                  const int64_t srow_j = act_sf_row<SPREAD>(a0 + j);
+                  sfb_e[blocked_sf_offset(srow_j, grp, p.out_g4)] = static_cast<uint8_t>((rb >> 23) & 0xFFu);
+                  // the K padding groups of the row's last k-atom read as zero scales in GEMM2
+                  if (grp == (p.out_features >> 5) - 1)
+                    for (int gz = p.out_features >> 5; gz < 4 * p.out_g4; ++gz)
+                      sfb_e[blocked_sf_offset(srow_j, gz, p.out_g4)] = 0;
+                }
               }
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");

@@ -73,8 +73,11 @@ __device__ __forceinline__ float scale_from_bits(uint32_t rbits) {
 __device__ __forceinline__ float inv_scale(float scale) { return __frcp_rn(scale); }
 
 __device__ __forceinline__ float clamp_fp8(float v) {
-  // torch.clamp keeps NaN.
-  return v < -kFp8Max ? -kFp8Max : (v > kFp8Max ? kFp8Max : v);
+  // torch.clamp keeps NaN: the .NaN forms of max / min return NaN when an input is NaN.
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(v), "f"(-kFp8Max));
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(r), "f"(kFp8Max));
+  return r;
 }
 
 // Two floats -> two e4m3 bytes, round-to-nearest-even (low byte = lo).

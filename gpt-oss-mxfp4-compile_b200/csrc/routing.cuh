@@ -1,6 +1,6 @@
 // Routing kernels of the MoE expert path.
 //
-//  router_topk_kernel   logits = x W^T + b (bf16 out, fp32 accumulate), top-k, softmax
+//  router_mma_kernel    logits = x W^T + b (bf16 out, fp32 accumulate), top-k, softmax
 //                       over the k selected logits; HF GptOssTopKRouter semantics
 //                       (F.linear -> torch.topk -> softmax(dtype=bf16)).
 //  route_sort_kernel    one CTA per expert: histogram of all assignments, exclusive
@@ -24,143 +24,217 @@ constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
 
 // ----------------------------------------------------------------------------------
-// Router: each CTA owns TB tokens; their rows are staged in shared memory. Warp w
-// handles experts w, w + nwarps, ...; lane l accumulates the 8-element slices
-// l, l + 32, ... of the dot product in a fixed order (deterministic), with the weight
-// slices of a chunk loaded before any arithmetic so their latencies overlap, then a
-// fixed-order warp tree.
-constexpr int kRouterVecChunk = 12;   // 8-element slices per lane per pass (H <= 3072 in one pass)
+// Router. logits = x W^T + b is a [T, H] x [H, E] projection with E <= 256: it moves x
+// once and does ~2*E flops per byte, so it runs on warp-level bf16 MMAs (m16n8k16,
+// fp32 accumulate) fed by cp.async -- the tensor pipe is not its bound, HBM is.
+// A CTA owns 16 tokens; its 4 warps split the experts (NT n-tiles of 8 each). When there
+// are too few token blocks to cover the SMs the K dimension is split over the CTAs of a
+// thread-block cluster and the fp32 partial logits are summed by the cluster's rank 0
+// through distributed shared memory, in rank order (deterministic).
+// Then: bias add and one bf16 rounding (F.linear), top-k with the lower expert id first
+// on ties, softmax over the k selected logits (HF GptOssTopKRouter).
+constexpr int kRtTok = 16;            // tokens per CTA
+constexpr int kRtKc = 128;            // K elements per shared-memory chunk
+constexpr int kRtLd = kRtKc + 8;      // padded row: conflict-free 4-byte fragment loads
+// Ring depth: 4 chunks (three in flight, ~39 KB at E <= 32); 2 for E > 64 so the ring
+// of a 256-expert W slice still fits in shared memory.
+__host__ __device__ constexpr int router_stages(int nt) { return nt <= 2 ? 4 : 2; }
 
-template <int TB>
-__global__ void __launch_bounds__(TB == 1 ? 1024 : 512) router_topk_kernel(
-    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-    const __nv_bfloat16* __restrict__ bias, int T, int H, int E, int K,
-    int64_t* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_scores,
-    float* __restrict__ out_weights_f32, __nv_bfloat16* __restrict__ out_logits,
-    __nv_bfloat16* __restrict__ zero_rows, int64_t zero_row_elems) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);      // [TB][H]
-  float* logits = reinterpret_cast<float*>(smem_raw + sizeof(__nv_bfloat16) * TB * H);  // [TB][E]
-  pdl_trigger();
-  pdl_wait();
+// K-split ranks of a cluster: at most 8, and at most 8 / nt so the leader's buffer of
+// the ranks' partial logits stays at 16 KB.
+__host__ __device__ constexpr int router_max_split(int nt) { return 8 / nt; }
 
-  const int t0 = blockIdx.x * TB;
-  const int ntok = min(TB, T - t0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
+__host__ __device__ constexpr size_t router_smem_bytes(int nt) {
+  // x ring, W ring, fp32 partial logits [max split][16][32*nt]
+  return static_cast<size_t>(router_stages(nt)) * (kRtTok + 32 * nt) * kRtLd * 2 +
+         sizeof(float) * router_max_split(nt) * kRtTok * 32 * nt;
+}
 
-  const int vec_per_row = H >> 3;     // H % 8 == 0 (host check)
-  for (int i = threadIdx.x; i < ntok * vec_per_row; i += blockDim.x) {
-    const int t = i / vec_per_row, v = i - t * vec_per_row;
-    reinterpret_cast<uint4*>(xs + t * H)[v] =
-        reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t0 + t) * H)[v];
-  }
-  if (zero_rows != nullptr) {          // the combine adds into these rows
-    const int64_t vz = zero_row_elems >> 3;
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int64_t i = threadIdx.x; i < ntok * vz; i += blockDim.x)
-      reinterpret_cast<uint4*>(zero_rows + static_cast<int64_t>(t0) * zero_row_elems)[i] = z;
-  }
-  __syncthreads();
-
-  for (int e = warp; e < E; e += nwarps) {
-    float acc[TB];
+// One token's top-k + softmax by one thread: an insertion pass over the bf16-rounded
+// logits `lg` keeps the k largest in descending order, equal values by ascending expert
+// id, NaN above every number (torch.topk's NaN order).
+__device__ __forceinline__ void router_topk_token(const float* lg, int E, int K, int64_t tg,
+                                                  int64_t* __restrict__ out_idx,
+                                                  __nv_bfloat16* __restrict__ out_scores,
+                                                  float* __restrict__ out_weights_f32) {
+  float bv[kMaxTopK];
+  int be[kMaxTopK];
 #pragma unroll
-    for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
-    const uint4* wr = reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * H);
-    for (int v0 = 0; v0 < vec_per_row; v0 += 32 * kRouterVecChunk) {
-      uint4 wv[kRouterVecChunk];
+  for (int j = 0; j < kMaxTopK; ++j) { bv[j] = -INFINITY; be[j] = -1; }
+  for (int e = 0; e < E; ++e) {
+    float cv = lg[e];
+    int ce = e;
 #pragma unroll
-      for (int i = 0; i < kRouterVecChunk; ++i) {
-        const int v = v0 + lane + 32 * i;
-        wv[i] = v < vec_per_row ? __ldg(wr + v) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int i = 0; i < kRouterVecChunk; ++i) {
-        const int v = v0 + lane + 32 * i;
-        if (v < vec_per_row) {
-          const uint32_t wq[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
-#pragma unroll
-          for (int t = 0; t < TB; ++t) {
-            if (t < ntok) {
-              const uint4 xv = reinterpret_cast<const uint4*>(xs + t * H)[v];
-              const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
-              float a = acc[t];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                a = fmaf(bf16_bits_lo(xq[j]), bf16_bits_lo(wq[j]), a);
-                a = fmaf(bf16_bits_hi(xq[j]), bf16_bits_hi(wq[j]), a);
-              }
-              acc[t] = a;
-            }
-          }
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j < K) {
+        // larger, or NaN over a number, or equal (both NaN counts) with the lower id --
+        // the last case only arises for an entry displaced further down the list
+        const bool cnan = cv != cv, bnan = bv[j] != bv[j];
+        const bool better = be[j] < 0 || cv > bv[j] || (cnan && !bnan) ||
+                            ((cv == bv[j] || (cnan && bnan)) && ce < be[j]);
+        if (better) {
+          const float tv = bv[j]; bv[j] = cv; cv = tv;
+          const int te = be[j]; be[j] = ce; ce = te;
         }
       }
     }
+  }
+  const float m = bv[0];
+  float ex[kMaxTopK], s = 0.0f;
 #pragma unroll
-    for (int t = 0; t < TB; ++t) {
-      float a = acc[t];
+  for (int j = 0; j < kMaxTopK; ++j)
+    if (j < K) { ex[j] = expf(__fsub_rn(bv[j], m)); s = __fadd_rn(s, ex[j]); }
+  const float inv = __frcp_rn(s);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0 && t < ntok) {
-        // F.linear in bf16: fp32 accumulate, add the bias, round once to bf16.
-        logits[t * E + e] = bf16_round(a + __bfloat162float(bias[e]));
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (j < K) {
+      const __nv_bfloat16 pr = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
+      out_idx[tg * K + j] = be[j];
+      if (out_scores) out_scores[tg * K + j] = pr;
+      if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(pr);
+    }
+  }
+}
+
+// grid = (ceil(T / 16), S); cluster = (1, S, 1) when S > 1; blockDim = 128.
+template <int NT>
+__global__ void __launch_bounds__(128) router_mma_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const __nv_bfloat16* __restrict__ bias, int T, int H, int E, int K, int chunks_per_cta,
+    int64_t* __restrict__ out_idx, __nv_bfloat16* __restrict__ out_scores,
+    float* __restrict__ out_weights_f32, __nv_bfloat16* __restrict__ out_logits,
+    __nv_bfloat16* __restrict__ zero_rows, int64_t zero_row_elems) {
+  constexpr int kEp = 32 * NT;                           // expert rows held (>= E)
+  constexpr int kRtStages = router_stages(NT);
+  extern __shared__ __align__(16) uint8_t router_smem[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(router_smem);                    // [stages][16][kRtLd]
+  __nv_bfloat16* ws = xs + kRtStages * kRtTok * kRtLd;                               // [stages][kEp][kRtLd]
+  float* part = reinterpret_cast<float*>(ws + kRtStages * kEp * kRtLd);              // [S][16][kEp]
+  pdl_trigger();
+  // A CTA may write into another CTA's shared memory only once that CTA runs: every
+  // rank arrives here and waits before its remote stores.
+  if (gridDim.y > 1) cluster_arrive_relaxed();
+  pdl_wait();
+
+  const int S = gridDim.y, split = blockIdx.y;
+  const int t0 = blockIdx.x * kRtTok;
+  const int ntok = min(kRtTok, T - t0);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int nchunks = (H + kRtKc - 1) / kRtKc;
+  const int c_begin = split * chunks_per_cta;
+  const int c_end = min(nchunks, c_begin + chunks_per_cta);
+
+  if (zero_rows != nullptr) {          // the combine adds into these rows
+    const int64_t vz = zero_row_elems >> 3;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    uint4* zr = reinterpret_cast<uint4*>(zero_rows + static_cast<int64_t>(t0) * zero_row_elems);
+    for (int64_t i = static_cast<int64_t>(split) * blockDim.x + tid; i < ntok * vz; i += static_cast<int64_t>(S) * blockDim.x)
+      zr[i] = z;
+  }
+
+  auto load_chunk = [&](int ck, int stage) {
+    const int k0 = ck * kRtKc;
+    constexpr int kVec = kRtKc / 8;     // 16-byte vectors per row chunk
+#pragma unroll
+    for (int i = 0; i < kRtTok * kVec / 128; ++i) {   // x: 16 rows
+      const int idx = tid + 128 * i;
+      const int r = idx / kVec, v = idx % kVec;
+      const int k = k0 + 8 * v;
+      const bool in = r < ntok && k < H;
+      const __nv_bfloat16* src = in ? x + static_cast<int64_t>(t0 + r) * H + k : x;
+      cp_async_16(smem_u32(xs + (stage * kRtTok + r) * kRtLd + 8 * v), src, in ? 16u : 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kEp * kVec / 128; ++i) {   // W: kEp rows
+      const int idx = tid + 128 * i;
+      const int r = idx / kVec, v = idx % kVec;
+      const int k = k0 + 8 * v;
+      const bool in = r < E && k < H;
+      const __nv_bfloat16* src = in ? w + static_cast<int64_t>(r) * H + k : w;
+      cp_async_16(smem_u32(ws + (stage * kEp + r) * kRtLd + 8 * v), src, in ? 16u : 0u);
+    }
+  };
+
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+
+#pragma unroll
+  for (int s = 0; s < kRtStages - 1; ++s) {
+    if (c_begin + s < c_end) load_chunk(c_begin + s, s);
+    cp_async_commit();
+  }
+  for (int ck = c_begin; ck < c_end; ++ck) {
+    cp_async_wait<kRtStages - 2>();
+    __syncthreads();
+    const int nxt = ck + kRtStages - 1;
+    if (nxt < c_end) load_chunk(nxt, (nxt - c_begin) % kRtStages);
+    cp_async_commit();
+    const int st = (ck - c_begin) % kRtStages;
+    const __nv_bfloat16* xa = xs + st * kRtTok * kRtLd;
+    const __nv_bfloat16* wb = ws + st * kEp * kRtLd;
+    // Each 64-deep chunk accumulates from zero on the tensor pipe and is then added to
+    // the running fp32 sums with round-to-nearest adds: the running sums never go
+    // through the MMA's internal adder, whose alignment of small terms to a large
+    // accumulator loses low bits.
+    float cacc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) cacc[j][0] = cacc[j][1] = cacc[j][2] = cacc[j][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < kRtKc / 16; ++kk) {
+      const int kb = kk * 16 + 2 * c;
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(xa + g * kRtLd + kb);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(xa + (g + 8) * kRtLd + kb);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(xa + g * kRtLd + kb + 8);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(xa + (g + 8) * kRtLd + kb + 8);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const __nv_bfloat16* wr = wb + ((warp * NT + j) * 8 + g) * kRtLd + kb;
+        mma_bf16_16816(cacc[j], a0, a1, a2, a3, *reinterpret_cast<const uint32_t*>(wr),
+                       *reinterpret_cast<const uint32_t*>(wr + 8));
       }
     }
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[j][q] = __fadd_rn(acc[j][q], cacc[j][q]);
+  }
+  cp_async_wait<0>();
+
+  // fp32 partial logits of this CTA's K range -> slot [split] of rank 0's buffer (remote
+  // stores into the leader's shared memory when the K dimension is split).
+  float* slot = part + split * (kRtTok * kEp);
+  if (S > 1) cluster_wait();
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int n = (warp * NT + j) * 8 + 2 * c;
+    const int idx[4] = {g * kEp + n, g * kEp + n + 1, (g + 8) * kEp + n, (g + 8) * kEp + n + 1};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (S > 1) dsmem_st_f32(dsmem_map(smem_u32(slot + idx[q]), 0), acc[j][q]);
+      else slot[idx[q]] = acc[j][q];
+    }
+  }
+  if (S > 1) {
+    cluster_sync();                    // the partials are in rank 0's shared memory
+    if (cluster_ctarank() != 0) return;
+  } else {
+    __syncthreads();
+  }
+  // rank 0: sum the ranks' partials in rank order, add the bias, round once to bf16
+  for (int i = tid; i < kRtTok * kEp; i += blockDim.x) {
+    float a = part[i];
+    for (int r = 1; r < S; ++r) a = __fadd_rn(a, part[r * (kRtTok * kEp) + i]);
+    const int e = i % kEp;
+    if (e < E) a = bf16_round(a + __bfloat162float(bias[e]));
+    part[i] = a;                       // only this thread touches element i
   }
   __syncthreads();
-
-  // Top-k (ties -> lower expert index first) and softmax over the selected logits; one
-  // warp per token, each lane holding experts lane, lane + 32, ...
-  for (int t = warp; t < ntok; t += nwarps) {
-    const float* lg = logits + t * E;
-    float lv[kMaxExperts / 32];
-#pragma unroll
-    for (int i = 0; i < kMaxExperts / 32; ++i) {
-      const int e = lane + 32 * i;
-      lv[i] = e < E ? lg[e] : -INFINITY;
-    }
-    int sel[kMaxTopK];
-    float val[kMaxTopK];
-    for (int j = 0; j < K; ++j) {
-      // lane-local best (NaN counts as largest, like torch.topk), then a warp argmax
-      float bv = -INFINITY;
-      int be = 0x7fffffff;                 // no candidate yet
-#pragma unroll
-      for (int i = 0; i < kMaxExperts / 32; ++i) {
-        const int e = lane + 32 * i;       // ascending, so a tie keeps the lower id
-        const bool better = lv[i] > bv || (lv[i] != lv[i] && bv == bv);
-        if (e < E && (be == 0x7fffffff || better)) { bv = lv[i]; be = e; }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-        const bool better = (ov > bv) || (ov != ov && bv == bv) || ((ov == bv || (ov != ov && bv != bv)) && oe < be);
-        if (better) { bv = ov; be = oe; }
-      }
-      sel[j] = be;
-      val[j] = bv;
-#pragma unroll
-      for (int i = 0; i < kMaxExperts / 32; ++i)
-        if (lane + 32 * i == be) lv[i] = -INFINITY;   // selected
-    }
-    if (lane == 0) {
-      const float m = val[0];
-      float ex[kMaxTopK], s = 0.0f;
-      for (int j = 0; j < K; ++j) { ex[j] = expf(__fsub_rn(val[j], m)); s = __fadd_rn(s, ex[j]); }
-      const float inv = __frcp_rn(s);
-      const int64_t tg = t0 + t;
-      for (int j = 0; j < K; ++j) {
-        const __nv_bfloat16 pr = __float2bfloat16_rn(__fmul_rn(ex[j], inv));
-        out_idx[tg * K + j] = sel[j];
-        if (out_scores) out_scores[tg * K + j] = pr;
-        if (out_weights_f32) out_weights_f32[tg * K + j] = __bfloat162float(pr);
-      }
-    }
-    if (out_logits)
-      for (int e = lane; e < E; e += 32) out_logits[(t0 + t) * static_cast<int64_t>(E) + e] = __float2bfloat16_rn(lg[e]);
-  }
+  if (tid < ntok) router_topk_token(part + tid * kEp, E, K, t0 + tid, out_idx, out_scores, out_weights_f32);
+  if (out_logits)
+    for (int i = tid; i < ntok * E; i += blockDim.x)
+      out_logits[static_cast<int64_t>(t0) * E + i] = __float2bfloat16_rn(part[(i / E) * kEp + i % E]);
 }
 
 // ----------------------------------------------------------------------------------
@@ -174,10 +248,12 @@ struct RouteSortParams {
   float* sorted_weight;            // [A]
   int32_t* counts;                 // [E]
   int32_t* offsets;                // [E]
-  // Optional blocked-scale bookkeeping for the fused path (nullptr to skip).
+  // Optional blocked-scale bookkeeping for the fused path (nullptr to skip). The
+  // padding rows of the scale blocks are left as they are: a padding row only feeds its
+  // own accumulator row (or column) of the GEMMs, which no epilogue stores.
   int32_t* sf_offsets_a;           // [E] bytes, act layout with g4_a k-atoms
   int g4_a, groups_a;              // k-atoms / valid groups of the GEMM1 A operand
-  uint8_t* sf_a;                   // zero the padding of this buffer
+  uint8_t* sf_a;
   int32_t* sf_offsets_b;           // [E] bytes, intermediate layout
   int g4_b, groups_b;
   uint8_t* sf_b;
@@ -188,26 +264,49 @@ struct RouteSortParams {
   int* err;                        // set if an index is outside [0, E)
 };
 
+// Assignments whose buckets one pass keeps in shared memory (uint16 codes, 32 KB).
+constexpr int kSortChunk = 16384;
+constexpr uint16_t kBktEmpty = 0xFFFF, kBktBad = 0xFFFE;
+
 __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
   __shared__ int hist[kMaxExperts];
-  __shared__ int warp_cnt[32];
-  __shared__ int s_base;
+  __shared__ int warp_tot[32];
+  __shared__ int s_chunk_total;
+  __shared__ uint16_t s_bkt[kSortChunk];
   pdl_trigger();
   pdl_wait();
   const int e = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nthr = static_cast<int>(blockDim.x);
   const int64_t dv = p.divisor > 1 ? p.divisor : 1;
-  for (int i = tid; i < p.E; i += blockDim.x) hist[i] = 0;
+  auto bucket = [&](int64_t v) -> uint16_t {
+    if (v < 0) return (p.allow_empty && v == -1) ? kBktEmpty : kBktBad;
+    const int64_t b = dv == 1 ? v : v / dv;
+    return b < p.E ? static_cast<uint16_t>(b) : kBktBad;
+  };
+  for (int i = tid; i < p.E; i += nthr) hist[i] = 0;
   __syncthreads();
-  // Pass 1: full histogram (every CTA builds it; A is small next to the GEMMs).
-  for (int i = tid; i < p.A; i += blockDim.x) {
-    const int64_t ex = p.router_indices[i] / dv;
-    if (p.allow_empty && p.router_indices[i] == -1) continue;
-    if (p.router_indices[i] < 0 || ex >= p.E) {
-      if (p.err) atomicCAS(p.err, 0, 0x201);
-      continue;
+  // Pass 1 (coalesced, 8 loads in flight per thread): full histogram -- every CTA
+  // builds it; A is small next to the GEMMs -- caching the first chunk's buckets.
+  for (int i0 = tid; i0 < p.A; i0 += 8 * nthr) {
+    int64_t v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + j * nthr;
+      v[j] = i < p.A ? p.router_indices[i] : -1;
     }
-    atomicAdd(&hist[ex], 1);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + j * nthr;
+      if (i >= p.A) break;
+      const uint16_t b = bucket(v[j]);
+      if (i < kSortChunk) s_bkt[i] = b;
+      if (b == kBktBad) {
+        if (p.err) atomicCAS(p.err, 0, 0x201);
+      } else if (b != kBktEmpty) {
+        atomicAdd(&hist[b], 1);
+      }
+    }
   }
   __syncthreads();
   // Exclusive prefixes of the counts and of both scale-region sizes, once, by warp 0
@@ -221,12 +320,14 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
     const int q0 = lane * per;
     int cl[8];
     int64_t al[8], bl[8];
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
       const int q = q0 + i;
-      const int c = q < p.E ? hist[q] : 0;
+      const bool v = i < per && q < p.E;
+      const int c = v ? hist[q] : 0;
       cl[i] = c;
-      al[i] = (q < p.E && p.sf_offsets_a) ? act_sf_cosize(c, p.g4_a * 4, p.spread != 0) : 0;
-      bl[i] = (q < p.E && p.sf_offsets_a) ? act_sf_cosize(c, p.g4_b * 4, p.spread != 0) : 0;
+      al[i] = (v && p.sf_offsets_a) ? act_sf_cosize(c, p.g4_a * 4, p.spread != 0) : 0;
+      bl[i] = (v && p.sf_offsets_a) ? act_sf_cosize(c, p.g4_b * 4, p.spread != 0) : 0;
       c_run += c; a_run += al[i]; b_run += bl[i];
     }
     int c_inc = c_run;
@@ -240,9 +341,10 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
     }
     int c_ex = c_inc - c_run;
     int64_t a_ex = a_inc - a_run, b_ex = b_inc - b_run;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
       const int q = q0 + i;
-      if (q < p.E) { s_off[q] = c_ex; s_sfa[q] = a_ex; s_sfb[q] = b_ex; }
+      if (i < per && q < p.E) { s_off[q] = c_ex; s_sfa[q] = a_ex; s_sfb[q] = b_ex; }
       c_ex += cl[i]; a_ex += al[i]; b_ex += bl[i];
     }
   }
@@ -252,58 +354,81 @@ __global__ void __launch_bounds__(1024) route_sort_kernel(RouteSortParams p) {
   if (tid == 0) {
     p.counts[e] = cnt;
     p.offsets[e] = off;
-    s_base = 0;
     if (p.sf_offsets_a != nullptr) {
       p.sf_offsets_a[e] = static_cast<int32_t>(s_sfa[e]);
       p.sf_offsets_b[e] = static_cast<int32_t>(s_sfb[e]);
     }
   }
-  // Zero this expert's blocked scale regions (16-byte stores); the quantisers that run
-  // after this kernel overwrite the valid entries, so the padding ends up zero.
-  if (p.sf_offsets_a != nullptr) {
-    for (int pass = 0; pass < 2; ++pass) {
-      uint8_t* buf = pass == 0 ? p.sf_a : p.sf_b;
-      const int gp = (pass == 0 ? p.g4_a : p.g4_b) * 4;
-      if (buf == nullptr) continue;
-      uint4* dst = reinterpret_cast<uint4*>(buf + (pass == 0 ? s_sfa[e] : s_sfb[e]));   // multiple of 512
-      const int64_t n16 = act_sf_cosize(cnt, gp, p.spread != 0) >> 4;
-      const uint4 z = make_uint4(0, 0, 0, 0);
-      for (int64_t i = tid; i < n16; i += blockDim.x) dst[i] = z;
-    }
-  }
-  // Entries past the last valid one (only when some index was out of range) get the
-  // sentinel -1, which every consumer of the sorted arrays skips.
+  // Entries past the last valid one (only when some index was out of range or an
+  // empty slot) get the sentinel -1, which every consumer of the sorted arrays skips.
   if (e == p.E - 1) {
-    for (int i = off + cnt + tid; i < p.A; i += blockDim.x) {
+    for (int i = off + cnt + tid; i < p.A; i += nthr) {
       p.sorted_token[i] = -1;
       p.sorted_expert[i] = -1;
       p.sorted_weight[i] = 0.0f;
       if (p.sorted_src) p.sorted_src[i] = -1;
     }
   }
-  __syncthreads();
-  // Pass 2: stable compaction of this expert's assignments, 1024 at a time.
-  for (int c0 = 0; c0 < p.A; c0 += blockDim.x) {
-    const int i = c0 + tid;
-    const bool mine = (i < p.A) && (p.router_indices[i] >= 0) && (p.router_indices[i] / dv == e);
-    const unsigned bal = __ballot_sync(0xffffffffu, mine);
-    if (lane == 0) warp_cnt[warp] = __popc(bal);
+  // Pass 2, chunk by chunk: each thread owns a contiguous segment of the chunk; an
+  // exclusive scan of the per-thread counts of expert e gives stable positions.
+  int run = off;
+  for (int c0 = 0; c0 < p.A; c0 += kSortChunk) {
+    const int len = min(kSortChunk, p.A - c0);
+    if (c0 > 0) {
+      __syncthreads();                 // the previous chunk is consumed
+      for (int i0 = tid; i0 < len; i0 += 8 * nthr) {
+        int64_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + j * nthr;
+          v[j] = i < len ? p.router_indices[c0 + i] : -1;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + j * nthr;
+          if (i < len) s_bkt[i] = bucket(v[j]);
+        }
+      }
+      __syncthreads();
+    }
+    const int seg = (len + nthr - 1) / nthr;
+    const int j0 = min(len, tid * seg), j1 = min(len, j0 + seg);
+    int mine = 0;
+    for (int j = j0; j < j1; ++j) mine += (s_bkt[j] == e);
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
     __syncthreads();
-    int before = 0;
-    for (int q = 0; q < warp; ++q) before += warp_cnt[q];
-    int chunk_total = 0;
-    if (tid == 0)
-      for (int q = 0; q < 32; ++q) chunk_total += warp_cnt[q];
-    if (mine) {
-      const int pos = off + s_base + before + __popc(bal & ((1u << lane) - 1u));
-      p.sorted_token[pos] = i / p.K;
-      p.sorted_expert[pos] = e;
-      if (p.sorted_src) p.sorted_src[pos] = i;
-      p.sorted_weight[pos] = p.routing_weights[i];
+    if (warp == 0) {
+      const int nw = nthr >> 5;
+      const int tot = lane < nw ? warp_tot[lane] : 0;
+      int x = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += v;
+      }
+      if (lane < nw) warp_tot[lane] = x - tot;    // exclusive
+      if (lane == 31) s_chunk_total = x;
     }
     __syncthreads();
-    if (tid == 0) s_base += chunk_total;
-    __syncthreads();
+    if (mine > 0) {
+      int pos = run + warp_tot[warp] + incl - mine;
+      for (int j = j0; j < j1; ++j) {
+        if (s_bkt[j] != e) continue;
+        const int i = c0 + j;
+        p.sorted_token[pos] = i / p.K;
+        p.sorted_expert[pos] = e;
+        if (p.sorted_src) p.sorted_src[pos] = i;
+        p.sorted_weight[pos] = p.routing_weights[i];
+        ++pos;
+      }
+    }
+    run += s_chunk_total;
   }
 }
 
@@ -370,6 +495,105 @@ __global__ void __launch_bounds__(256) gather_quant_kernel(
     if (sorted_token != nullptr) sf_blocked[sf_base + blocked_sf_offset(r_in, g, g4)] = sc;
     else sf_rowmajor[row * G + g] = sc;
   }
+}
+
+// |x| max of a packed bf16 pair word into a running packed maximum; NaN propagates like
+// torch.max (abs and max are exact in bf16, so the group maximum equals the fp32 one).
+__device__ __forceinline__ uint32_t bf16x2_absmax(uint32_t m, uint32_t w) {
+  uint32_t a, r;
+  asm("abs.bf16x2 %0, %1;" : "=r"(a) : "r"(w));
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+  return r;
+}
+
+// One bf16 row of H elements quantised by one warp, 1024 elements (32 groups of 32) per
+// pass. Lane l loads 16 bytes at 256q + 8l for q = 0..3 (512-byte coalesced warp loads);
+// the four lanes sharing a group combine their maxima with shuffles; lane g then
+// computes the UE8M0 scale of group g of the pass, so the division and reciprocal run
+// once per 32 groups; the scales go back to the lanes by shuffle, and lane 4a writes
+// k-atom a's four scale bytes as one 32-bit word at blocked row r_in (the blocked layout
+// keeps them contiguous; bytes of groups past H/32 are the zero padding).
+__device__ __forceinline__ void quantize_row_warp(const __nv_bfloat16* __restrict__ xr, int H,
+                                                  uint8_t* __restrict__ orow, uint8_t* __restrict__ sf_base,
+                                                  int64_t r_in, int g4, int lane) {
+  for (int base = 0; base < H; base += 1024) {
+    uint4 u[4];
+    float am[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e0 = base + 256 * q + 8 * lane;
+      u[q] = e0 < H ? __ldg(reinterpret_cast<const uint4*>(xr + e0)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t m = bf16x2_absmax(0u, u[q].x);
+      m = bf16x2_absmax(m, u[q].y);
+      m = bf16x2_absmax(m, u[q].z);
+      m = bf16x2_absmax(m, u[q].w);
+      m = bf16x2_absmax(m, m >> 16);        // low half now holds the maximum of all 8
+      float a = bf16_bits_lo(m);
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, a, o);
+        a = (ob > a || ob != ob) ? ob : a;
+      }
+      am[q] = a;                            // group 8q + lane/4 of this pass
+    }
+    // lane g <- maximum of group g = 8q + j (q = g / 8, j = g % 8), held by lane 4j
+    float mine = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float v = __shfl_sync(0xffffffffu, am[q], 4 * (lane & 7));
+      if ((lane >> 3) == q) mine = v;
+    }
+    const uint32_t rb = ue8m0_rounded_bits(mine);
+    const float inv_mine = inv_scale(scale_from_bits(rb));
+    const uint32_t sc = (rb >> 23) & 0xFFu;  // zero for groups past H/32 (their max is 0)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float inv = __shfl_sync(0xffffffffu, inv_mine, 8 * q + (lane >> 2));
+      const int e0 = base + 256 * q + 8 * lane;
+      if (e0 < H) {
+        const uint32_t w4[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+        uint32_t c[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float a = clamp_fp8(__fmul_rn(bf16_bits_lo(w4[2 * j]), inv));
+          const float b = clamp_fp8(__fmul_rn(bf16_bits_hi(w4[2 * j]), inv));
+          const float cc = clamp_fp8(__fmul_rn(bf16_bits_lo(w4[2 * j + 1]), inv));
+          const float d = clamp_fp8(__fmul_rn(bf16_bits_hi(w4[2 * j + 1]), inv));
+          c[j] = static_cast<uint32_t>(cvt_e4m3x2(a, b)) | (static_cast<uint32_t>(cvt_e4m3x2(cc, d)) << 16);
+        }
+        *reinterpret_cast<uint2*>(orow + e0) = make_uint2(c[0], c[1]);
+      }
+    }
+    const uint32_t s1 = __shfl_down_sync(0xffffffffu, sc, 1);
+    const uint32_t s2 = __shfl_down_sync(0xffffffffu, sc, 2);
+    const uint32_t s3 = __shfl_down_sync(0xffffffffu, sc, 3);
+    const int g0 = (base >> 5) + lane;      // first group of atom lane/4 when lane % 4 == 0
+    if ((lane & 3) == 0 && 32 * g0 < H)
+      *reinterpret_cast<uint32_t*>(sf_base + blocked_sf_offset(r_in, g0, g4)) =
+          sc | (s1 << 8) | (s2 << 16) | (s3 << 24);
+  }
+}
+
+// Fused-pipeline gather + quantise (bf16 input): one warp per expert-sorted row.
+__global__ void __launch_bounds__(256) gather_quant_rows_kernel(
+    const __nv_bfloat16* __restrict__ src, int64_t rows, int H, const int64_t* __restrict__ sorted_token,
+    const int64_t* __restrict__ sorted_expert, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ sf_offsets, int g4, int spread, uint8_t* __restrict__ out_codes,
+    uint8_t* __restrict__ sf_blocked) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;                  // warp-uniform
+  const int64_t src_row = sorted_token[row];
+  if (src_row < 0) return;                  // sentinel of an out-of-range router index
+  const int ex = static_cast<int>(sorted_expert[row]);
+  int64_t r_in = row - offsets[ex];
+  if (spread) r_in = act_sf_row<true>(r_in);
+  quantize_row_warp(src + src_row * H, H, out_codes + row * H, sf_blocked + sf_offsets[ex], r_in, g4, lane);
 }
 
 // Threads per row for gather_quant_kernel: a multiple of 32 covering the row's groups,
@@ -560,8 +784,8 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(
   const int64_t base = sf_offsets[ex];
   for (int v = threadIdx.x; v < H / 16; v += blockDim.x)
     reinterpret_cast<uint4*>(act_codes + p * H)[v] = reinterpret_cast<const uint4*>(src)[v];
-  for (int g = threadIdx.x; g < H / 32; g += blockDim.x)
-    act_sf[base + blocked_sf_offset(r_in, g, g4)] = src[H + g];
+  for (int g = threadIdx.x; g < 4 * g4; g += blockDim.x)   // K padding groups: zero
+    act_sf[base + blocked_sf_offset(r_in, g, g4)] = g < H / 32 ? src[H + g] : 0;
 }
 
 // Combine: out[t] = bf16 of the fp32 sum of the token's k returned rows, added in ascending

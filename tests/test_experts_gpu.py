@@ -201,3 +201,45 @@ def test_fused_route_quant_stage_bit_exact(pkg, dev, mode):
             for gg in range(G):
                 rows[o:o + m, gg] = blob[sfo[e] + O.blocked_sf_offset(srow, gg, g4)]
         assert hashlib.sha256(rows.tobytes()).hexdigest() == bytes(g["act_scales_sha"]).decode()
+
+
+@pytest.mark.parametrize("mode", ["tokens_m", "swap"])
+def test_workspace_garbage_does_not_leak(pkg, dev, mode):
+    # The padding rows of the blocked scale layouts are never cleared (a padding row only
+    # feeds accumulator rows no epilogue stores). Fill every workspace byte with 0xFF --
+    # NaN UE8M0 scales and NaN FP8 codes everywhere -- and the outputs must stay finite and
+    # equal to a run on a zeroed workspace (to the 1-ulp reordering of the bf16 combine).
+    import ctypes
+    for name in ("small", "decode"):
+        seed, E, H, I, T, k = MG.LAYERS[name]
+        d, idx, w = MG.layer_inputs(name)
+        m = build_experts(pkg, d, dev, E, H, I)
+        m.gemm_mode = MODES[mode]
+        h, ix, wv = d["hidden"].to(dev), idx.to(dev), w.to(dev)
+        outs = []
+        for fill in (0x00, 0xFF):
+            # staged path (separate routing kernels)
+            ws = pkg.ops.ExpertsWorkspace(T, k, E, H, I, dev)
+            ws.buf.fill_(fill)
+            out = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+            pkg.ops.route_quant(ws, h, ix, wv, MODES[mode])
+            pkg.ops.gemm1(ws, m.gate_up_proj_data, m.gate_up_proj_scales, m.gate_up_proj_bias.data,
+                          gemm_mode=MODES[mode])
+            pkg.ops.gemm2(ws, m.down_proj_data, m.down_proj_scales, m.down_proj_bias.data, out,
+                          gemm_mode=MODES[mode])
+            # fused entry point (one-launch decode prologue at these sizes)
+            wbuf = torch.full((pkg.ops.workspace_bytes(T, k, E, H, I),), fill, dtype=torch.uint8, device=dev)
+            out2 = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+            pkg._lib.call("gptoss_moe_experts_forward", h.data_ptr(), ix.data_ptr(), wv.data_ptr(), T, k, E, H, I,
+                          m.gate_up_proj_data.data_ptr(), m.gate_up_proj_scales.data_ptr(),
+                          m.gate_up_proj_scales.numel() // E, m.gate_up_proj_bias.data_ptr(),
+                          m.down_proj_data.data_ptr(), m.down_proj_scales.data_ptr(),
+                          m.down_proj_scales.numel() // E, m.down_proj_bias.data_ptr(), ctypes.c_float(1.702),
+                          ctypes.c_float(7.0), out2.data_ptr(), wbuf.data_ptr(), wbuf.numel(), MODES[mode],
+                          pkg.ops.status_tensor(dev).data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+            torch.cuda.synchronize()
+            assert pkg.ops.read_status(dev) == 0
+            assert torch.isfinite(out.float()).all() and torch.isfinite(out2.float()).all(), (name, mode, fill)
+            outs.append((out.float(), out2.float()))
+        for a, b in zip(outs[0], outs[1]):
+            assert (a - b).abs().max().item() <= 2 ** -7 * a.abs().max().item(), (name, mode)

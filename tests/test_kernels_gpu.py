@@ -32,6 +32,48 @@ def test_quantize_matches_oracle(pkg, dev, shape, dtype):
     assert np.array_equal(s.cpu().numpy(), sf)
 
 
+def _special_rows(H=2880):
+    # groups holding NaN (both signs), +-inf, values near the bf16 maximum, bf16
+    # subnormals, an all-zero group, and exact powers of two times 448
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(8, H, generator=g)
+    x[0, 5] = float("nan")
+    x[0, 40] = -float("nan")
+    x[1, 70] = float("inf")
+    x[1, 100] = -float("inf")
+    x[2, :] *= 3.0e38 / 4.0
+    x[3, :] *= 1e-39
+    x[4, 32:64] = 0.0
+    x[5, :32] = 448.0 * 2.0 ** torch.arange(-8, 24).float()
+    x[6, 64:96] = 7.0 * 2.0 ** -130
+    return x.to(torch.bfloat16)
+
+
+def test_quantize_special_values_match_oracle(pkg, dev):
+    # the plain quantiser and the fused gather path agree with the oracle on NaN / inf /
+    # saturating / subnormal / zero groups, byte for byte
+    # (a NaN code is compared as NaN: the sign of the NaN that inf / inf yields is the
+    # platform's choice, positive on the GPU and negative on x86)
+    def canon(codes):
+        codes = codes.copy()
+        codes[(codes & 0x7F) == 0x7F] = 0x7F
+        return codes
+
+    x = _special_rows()
+    c, sf = O.quantize_fp8_ue8m0(x)
+    c = canon(c)
+    q, s = pkg.quantize_activations_to_fp8(x.to(dev))
+    assert np.array_equal(s.cpu().numpy(), sf)
+    assert np.array_equal(canon(q.view(torch.uint8).cpu().numpy()), c)
+    T, E = x.shape[0], 4
+    idx = (torch.arange(T) % E).reshape(T, 1)
+    ws = pkg.ops.ExpertsWorkspace(T, 1, E, x.shape[1], 512, dev)
+    pkg.ops.route_quant(ws, x.to(dev), idx.to(dev), torch.ones(T, 1, device=dev), 1)
+    torch.cuda.synchronize()
+    st = ws.sorted_token.cpu().numpy()
+    assert np.array_equal(canon(ws.act_codes.cpu().numpy()), c[st])
+
+
 def test_quantize_empty(pkg, dev):
     q, s = pkg.quantize_activations_to_fp8(torch.empty(0, 64, dtype=torch.bfloat16, device=dev))
     assert q.shape == (0, 64) and s.shape == (0, 2)
