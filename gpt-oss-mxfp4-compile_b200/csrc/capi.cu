@@ -390,7 +390,8 @@ int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, 
 
 // Stage 2: GEMM1 + bias + SwiGLU + FP8 requantisation.
 int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit,
-                const WsPtrs& w, bool swap, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+                const WsPtrs& w, bool swap, int* status, const DeviceInfo& di, int dev, cudaStream_t st,
+                int prefetch_tiles = 0) {
   const int64_t Kh = pad128(H), Ki = pad128(I);
   GemmJob g1{};
   g1.act = w.act_codes; g1.act_rows = A; g1.lda = H; g1.wgt = wt.gu_data;
@@ -400,7 +401,7 @@ int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g1.p.out = w.inter_codes; g1.p.ld_out = I; g1.p.bias = wt.gu_bias; g1.p.out_sf = w.inter_sf;
   g1.p.out_sf_offsets = w.sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
   g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
-  g1.p.prefetch_tiles = swap ? 3 : 0;
+  g1.p.prefetch_tiles = swap ? prefetch_tiles : 0;
   return run_gemm<kEpiGemm1>(g1, swap, swap, di, dev, st);
 }
 
@@ -420,6 +421,10 @@ int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
 // ---------------------------------------------------------------- decode-sized prologue
 // Router (optional) + counting sort + quantisation in one cluster launch
 // (decode_prologue_kernel) for batches of at most kDpMaxTokens tokens.
+// Weight tiles per CTA that GEMM1 pulls into L2 while the decode prologue runs (three
+// measured best on B200 at T = 32: ~4 us off the layer; six thrash L2).
+constexpr int kPrefetchTilesAfterPrologue = 3;
+
 struct RouterArgs {
   const void* weight; const void* bias; int64_t* ridx_out; void* scores_out; float* rw_out;
 };
@@ -482,8 +487,12 @@ int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, i
   const bool swap = pick_swap(mode, T * k, E, 16);
   size_t smem = 0;
   int slice = 0;
+  // While the one-launch decode prologue runs on kDpCluster SMs, GEMM1 (launched behind it
+  // with programmatic serialisation) pulls its first weight tiles into L2.
+  int prefetch = 0;
   if (decode_prologue_fits(T, k, E, H, ra != nullptr, &smem, &slice)) {
     GPTOSS_TRY(run_decode_prologue(hidden, ra, ridx, rw, T, k, E, H, I, w, swap, out, status, smem, slice, dev, st));
+    prefetch = kPrefetchTilesAfterPrologue;
   } else {
     if (ra != nullptr) {
       GPTOSS_TRY(router_launch(hidden, ra->weight, ra->bias, T, H, E, k, ra->ridx_out, ra->scores_out, ra->rw_out,
@@ -495,7 +504,7 @@ int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, i
     if (ra == nullptr)
       GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
   }
-  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, swap, status, di, dev, st));
+  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, swap, status, di, dev, st, prefetch));
   return stage_gemm2(T * k, E, H, I, wt, out, w, swap, status, di, dev, st);
 }
 
