@@ -54,6 +54,9 @@ def parse_args():
     ap.add_argument("--config", choices=list(CONFIGS), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=45.0)
+    ap.add_argument("--ep-transport", choices=["auto", "p2p", "nccl"], default="auto",
+                    help="N>1 exchange: stores into peer-mapped buffers (p2p, fixed capacity) or NCCL "
+                         "all-to-alls; auto = p2p with the capacity layout, NCCL with exact splits")
     ap.add_argument("--ep-layout", choices=["auto", "capacity", "exact"], default="auto",
                     help="N>1 exchange layout: fixed-capacity segments (no host sync) or exact splits; "
                          "auto = capacity when W*T*k <= 8192 rows")
@@ -234,7 +237,11 @@ def run_ours(args):
         layout = args.ep_layout
         if layout == "auto":
             layout = "capacity" if world * T * k <= 8192 else "exact"
-        ep_experts = pkg.ep.ExpertParallelExperts(ex, E, capacity_tokens=T if layout == "capacity" else None)
+        transport = args.ep_transport
+        if transport == "auto":
+            transport = "p2p" if layout == "capacity" else "nccl"
+        ep_experts = pkg.ep.ExpertParallelExperts(ex, E, capacity_tokens=T if layout == "capacity" else None,
+                                                  transport=transport, top_k=k)
         layer = pkg.ep.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), k, ep_experts)
         g = torch.Generator().manual_seed(1000 + rank)
         x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
@@ -317,11 +324,16 @@ def run_ours(args):
         if epx.capacity_tokens:
             cap = epx.capacity_tokens * k
             sent = epx.last_send_counts.cpu().tolist()
-            ep_info = {"layout": "fixed capacity", "capacity_rows_per_peer": cap, "rank0_rows_used": sent,
-                       "rank0_nvlink_bytes_per_step": (world - 1) * cap * (rb + 2 * H), "host_syncs_per_step": 0}
+            if epx.transport == "p2p":
+                moved = (sum(sent) - sent[rank]) * (rb + 2 * H)
+            else:
+                moved = (world - 1) * cap * (rb + 2 * H)
+            ep_info = {"layout": "fixed capacity", "transport": epx.transport, "capacity_rows_per_peer": cap,
+                       "rank0_rows_used": sent, "rank0_nvlink_bytes_per_step": moved, "host_syncs_per_step": 0}
         else:
             s_send, s_recv = epx.last_splits
-            ep_info = {"layout": "exact splits", "rank0_rows_sent": s_send, "rank0_rows_received": s_recv,
+            ep_info = {"layout": "exact splits", "transport": "nccl", "rank0_rows_sent": s_send,
+                       "rank0_rows_received": s_recv,
                        "rank0_nvlink_bytes_per_step": (sum(s_send) - s_send[rank] + sum(s_recv) - s_recv[rank])
                        * (rb + 2 * H), "host_syncs_per_step": 1}
         ep_info.update({"experts_per_rank": E // world, "row_bytes_dispatch": rb, "row_bytes_combine": H * 2})
@@ -334,8 +346,9 @@ def run_ours(args):
             "data": "synthetic (seeded: random MXFP4 weights, N(0,1) bf16 hidden)",
             "config": {"workload": desc, "T": T, "T_per_rank": T, "E": E, "hidden": H, "intermediate": I,
                        "top_k": k,
-                       "parallelism": f"ep{world} (E/{world} experts per GPU, NCCL all-to-all)" if world > 1
-                       else "single GPU",
+                       "parallelism": (f"ep{world} (E/{world} experts per GPU, "
+                                       f"{'peer-memory stores' if ep_info and ep_info['transport'] == 'p2p' else 'NCCL all-to-all'})")
+                       if world > 1 else "single GPU",
                        "l2": "256 MiB written before every timed step (outside the events); weights 424 MB > L2"},
             "roofline": stages["roofline"] if stages else None,
             "clocks": clocks,
@@ -355,6 +368,7 @@ def run_ours(args):
             line["roofline_note"] = "per-kernel roofline is reported by the N=1 run"
         print(json.dumps(line), flush=True)
     if world > 1:
+        layer.experts.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

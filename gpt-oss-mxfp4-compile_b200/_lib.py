@@ -13,6 +13,7 @@ import threading
 from .build import LIB_PATH
 
 _c_int64 = ctypes.c_int64
+_c_int32 = ctypes.c_int32
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _f = ctypes.c_float
@@ -51,6 +52,18 @@ _SIGNATURES = {
     "gptoss_ep_expert_forward": (_i, [_vp, _c_int64, _i, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, _vp,
                                       _c_int64, _vp, _f, _f, _vp, _vp, _sz, _i, _vp, _vp]),
     "gptoss_ep_combine": (_i, [_vp, _c_int64, _vp, _vp, _c_int64, _i, _c_int64, _vp, _vp]),
+    "gptoss_ipc_handle_bytes": (_i, []),
+    "gptoss_ipc_alloc": (_i, [_sz, _vp, _vp]),
+    "gptoss_ipc_open": (_i, [_vp, _vp]),
+    "gptoss_ipc_close": (_i, [_vp]),
+    "gptoss_ipc_free": (_i, [_vp]),
+    "gptoss_ep_p2p_buffer_bytes": (_sz, [_i, _c_int64, _c_int64]),
+    "gptoss_ep_p2p_dispatch": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _i, _i, _c_int64, _c_int64, _vp, _c_int32,
+                                    _vp, _vp, _vp, _sz, _vp, _vp]),
+    "gptoss_ep_p2p_expert_forward": (_i, [_vp, _i, _i, _c_int64, _c_int32, _i, _c_int64, _c_int64, _vp, _vp,
+                                          _c_int64, _vp, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _vp, _vp, _sz, _i,
+                                          _vp, _vp]),
+    "gptoss_ep_p2p_combine": (_i, [_vp, _i, _c_int64, _c_int32, _vp, _vp, _c_int64, _i, _c_int64, _vp, _vp, _vp]),
     "gptoss_moe_route_quant": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64, _vp, _sz, _i, _vp, _vp]),
     "gptoss_moe_gemm1": (_i, [_c_int64, _i, _i, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _sz,
                               _i, _vp, _vp]),

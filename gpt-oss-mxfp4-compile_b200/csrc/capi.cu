@@ -19,6 +19,7 @@
 #include "routing.cuh"
 #include "gemm.cuh"
 #include "prologue.cuh"
+#include "ep_p2p.cuh"
 
 using namespace gptoss;
 
@@ -1054,6 +1055,188 @@ int gptoss_ep_combine(const void* back_rows, int64_t num_back_rows, const int32_
   return launch_pdl(ep_combine_kernel, dim3(static_cast<unsigned>(num_tokens)), dim3(256), 0,
                     static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(back_rows), pos_of,
                     router_indices, num_tokens, top_k, static_cast<int>(hidden_size), num_back_rows,
+                    static_cast<__nv_bfloat16*>(out));
+}
+
+// ---------------------------------------------------------------- peer memory (one node)
+int gptoss_ipc_handle_bytes(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+int gptoss_ipc_alloc(size_t bytes, void** ptr, void* handle_out) {
+  GPTOSS_CHECK(ptr != nullptr && handle_out != nullptr && bytes > 0, "ipc_alloc: bad arguments");
+  void* p = nullptr;
+  GPTOSS_CUDA(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) {
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) {
+      std::memcpy(handle_out, &h, sizeof(h));
+      *ptr = p;
+      return GPTOSS_OK;
+    }
+  }
+  cudaFree(p);
+  return fail(GPTOSS_ERR_CUDA, "ipc_alloc: %s", cudaGetErrorString(e));
+}
+
+int gptoss_ipc_open(const void* handle, void** ptr) {
+  GPTOSS_CHECK(handle != nullptr && ptr != nullptr, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  GPTOSS_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return GPTOSS_OK;
+}
+
+int gptoss_ipc_close(void* ptr) {
+  GPTOSS_CHECK(ptr != nullptr, "ipc_close: null pointer");
+  GPTOSS_CUDA(cudaIpcCloseMemHandle(ptr));
+  return GPTOSS_OK;
+}
+
+int gptoss_ipc_free(void* ptr) {
+  GPTOSS_CHECK(ptr != nullptr, "ipc_free: null pointer");
+  GPTOSS_CUDA(cudaFree(ptr));
+  return GPTOSS_OK;
+}
+
+size_t gptoss_ep_p2p_buffer_bytes(int world_size, int64_t capacity, int64_t hidden_size) {
+  if (world_size < 1 || world_size > kP2pMaxWorld || capacity < 1 || hidden_size <= 0 || hidden_size % 32) return 0;
+  return static_cast<size_t>(p2p_buffer_bytes(world_size, capacity, static_cast<int>(hidden_size)));
+}
+
+int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
+                           int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
+                           int64_t hidden_size, int64_t capacity, const uint64_t* peer_bases, int32_t epoch,
+                           int32_t* send_counts, int32_t* pos_of, void* workspace, size_t workspace_bytes,
+                           int32_t* status_dev, void* stream) {
+  GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld && rank >= 0 && rank < world_size,
+               "ep_p2p_dispatch: bad world_size / rank");
+  GPTOSS_CHECK(num_experts % world_size == 0, "ep_p2p_dispatch: num_experts must be a multiple of world_size");
+  GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK && top_k <= num_experts,
+               "ep_p2p_dispatch: bad sizes");
+  GPTOSS_CHECK(hidden_size > 0 && hidden_size % 32 == 0, "ep_p2p_dispatch: hidden size must be a multiple of 32");
+  GPTOSS_CHECK(capacity >= num_tokens * top_k && capacity > 0, "ep_p2p_dispatch: capacity below num_tokens * top_k");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(send_counts, "send_counts", &di));
+  GPTOSS_CHECK(peer_bases && workspace && (num_tokens == 0 || (hidden && router_indices && routing_weights && pos_of)),
+               "ep_p2p_dispatch: null pointer");
+  const size_t need = gptoss_ep_dispatch_workspace_bytes(num_tokens, top_k, world_size);
+  if (workspace_bytes < need) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t A = num_tokens * top_k;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  size_t o = 0;
+  auto take = [&](size_t bytes) { uint8_t* r = ws + o; o += align256(bytes); return r; };
+  RouteSortParams rp{};
+  rp.router_indices = router_indices; rp.routing_weights = routing_weights;
+  rp.A = static_cast<int>(A); rp.K = top_k; rp.E = world_size;
+  rp.sorted_token = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * A));
+  rp.sorted_expert = reinterpret_cast<int64_t*>(take(sizeof(int64_t) * A));
+  rp.sorted_weight = reinterpret_cast<float*>(take(sizeof(float) * A));
+  rp.sorted_src = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * A));
+  rp.offsets = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * world_size));
+  rp.counts = send_counts;
+  rp.divisor = num_experts / world_size;
+  rp.err = status_dev ? status_dev : di.status_sink;
+  GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(world_size), dim3(1024), 0, st, rp));
+  const int tpr = quant_threads_per_row(static_cast<int>(hidden_size));
+  const int rpb = 256 / tpr;
+  const int64_t rows = capacity * world_size;
+  GPTOSS_TRY(launch_pdl(ep_pack_p2p_kernel, dim3(static_cast<unsigned>((rows + rpb - 1) / rpb)), dim3(tpr * rpb), 0,
+                        st, static_cast<const __nv_bfloat16*>(hidden), static_cast<int>(hidden_size), top_k,
+                        num_experts / world_size, A, router_indices, routing_weights,
+                        static_cast<const int32_t*>(rp.sorted_src), capacity, world_size, rank,
+                        static_cast<const int32_t*>(send_counts), static_cast<const int32_t*>(rp.offsets), tpr,
+                        peer_bases, pos_of));
+  return launch_pdl(p2p_signal_kernel, dim3(1), dim3(kP2pMaxWorld), 0, st, peer_bases, world_size, rank, epoch);
+}
+
+int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int64_t capacity, int32_t epoch,
+                                 int num_local_experts, int64_t hidden_size, int64_t intermediate_size,
+                                 const uint8_t* gate_up_data, const uint8_t* gate_up_scales, int64_t ldb_gate_up,
+                                 const float* gate_up_bias, const uint8_t* down_data, const uint8_t* down_scales,
+                                 int64_t ldb_down, const float* down_bias, float swiglu_alpha, float swiglu_limit,
+                                 void* back_rows, const uint64_t* peer_bases, void* workspace, size_t workspace_bytes,
+                                 int gemm_mode, int32_t* status_dev, void* stream) {
+  GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld && rank >= 0 && rank < world_size,
+               "ep_p2p_expert_forward: bad world_size / rank");
+  const int64_t R = capacity * world_size;
+  GPTOSS_TRY(check_dims(R, 1, num_local_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                  down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(w, hidden_size, intermediate_size, num_local_experts));
+  GPTOSS_CHECK(local_base && back_rows && peer_bases && workspace, "ep_p2p_expert_forward: null pointer");
+  GPTOSS_CHECK(aligned(local_base, 256) && aligned(back_rows, 16) && aligned(workspace, 256),
+               "ep_p2p_expert_forward: misaligned pointer");
+  const Workspace L = plan_workspace(R, 1, num_local_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const WsPtrs p = ws_ptrs(ws, L);
+  int* status = status_dev ? status_dev : di.status_sink;
+  int64_t* lexp = reinterpret_cast<int64_t*>(ws + L.router_idx);
+  float* lw = reinterpret_cast<float*>(ws + L.router_w);
+  const bool swap = pick_swap(gemm_mode, R, num_local_experts, 16);
+  const int H = static_cast<int>(hidden_size);
+  const int64_t rb = ep_row_bytes(H);
+  const int64_t Kh = pad128(hidden_size), Ki = pad128(intermediate_size);
+  const uint8_t* recv = static_cast<const uint8_t*>(local_base) + p2p_recv_offset(0, capacity, rb);
+  const int32_t* flags = static_cast<const int32_t*>(local_base);
+  const int ublocks = static_cast<int>(std::min<int64_t>((R + 255) / 256, 4 * di.sms));
+  GPTOSS_TRY(launch_pdl(ep_unpack_meta_p2p_kernel, dim3(ublocks), dim3(256), 0, st, recv, R, H, flags, world_size,
+                        epoch, status, lexp, lw));
+  RouteSortParams rp{};
+  rp.router_indices = lexp; rp.routing_weights = lw;
+  rp.A = static_cast<int>(R); rp.K = 1; rp.E = num_local_experts;
+  rp.sorted_token = p.sorted_token; rp.sorted_expert = p.sorted_expert; rp.sorted_weight = p.sorted_weight;
+  rp.counts = p.counts; rp.offsets = p.offsets;
+  rp.sf_offsets_a = p.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = H / 32; rp.sf_a = p.act_sf;
+  rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
+  rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
+  rp.spread = swap ? 1 : 0;
+  rp.allow_empty = 1;
+  rp.err = status;
+  GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
+  GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st, recv, R, H,
+                        static_cast<const int64_t*>(p.sorted_token), static_cast<const int64_t*>(p.sorted_expert),
+                        static_cast<const int32_t*>(p.offsets), static_cast<const int32_t*>(p.sfoff_a),
+                        static_cast<int>(Kh / 128), swap ? 1 : 0, p.act_codes, p.act_sf));
+  GPTOSS_CUDA(cudaMemsetAsync(back_rows, 0, static_cast<size_t>(R * hidden_size) * sizeof(__nv_bfloat16), st));
+  GPTOSS_TRY(stage_gemm1(R, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p, swap,
+                         status, di, dev, st));
+  GPTOSS_TRY(stage_gemm2(R, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, swap, status, di,
+                         dev, st));
+  GPTOSS_TRY(launch_pdl(ep_return_p2p_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st,
+                        static_cast<const __nv_bfloat16*>(back_rows), static_cast<const int64_t*>(lexp), capacity,
+                        world_size, rank, H, peer_bases));
+  return launch_pdl(p2p_signal_kernel, dim3(1), dim3(kP2pMaxWorld), 0, st, peer_bases, world_size, world_size + rank,
+                    epoch);
+}
+
+int gptoss_ep_p2p_combine(const void* local_base, int world_size, int64_t capacity, int32_t epoch,
+                          const int32_t* pos_of, const int64_t* router_indices, int64_t num_tokens, int top_k,
+                          int64_t hidden_size, void* out, int32_t* status_dev, void* stream) {
+  GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld, "ep_p2p_combine: bad world_size");
+  GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK, "ep_p2p_combine: bad sizes");
+  GPTOSS_CHECK(hidden_size > 0 && hidden_size % 32 == 0, "ep_p2p_combine: hidden size must be a multiple of 32");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(local_base, "local_base", &di));
+  GPTOSS_CHECK(out != nullptr || num_tokens == 0, "ep_p2p_combine: null output");
+  const int64_t rb = ep_row_bytes(static_cast<int>(hidden_size));
+  const uint8_t* base = static_cast<const uint8_t*>(local_base);
+  const int32_t* flags = reinterpret_cast<const int32_t*>(base);
+  // With no tokens the kernel still runs one CTA: it consumes this call's return flags.
+  return launch_pdl(ep_combine_p2p_kernel, dim3(static_cast<unsigned>(std::max<int64_t>(num_tokens, 1))), dim3(256),
+                    0, static_cast<cudaStream_t>(stream),
+                    reinterpret_cast<const __nv_bfloat16*>(base + p2p_ret_offset(world_size, 0, capacity, rb,
+                                                                                  static_cast<int>(hidden_size))),
+                    flags, world_size, epoch, status_dev ? status_dev : di.status_sink, pos_of, router_indices,
+                    num_tokens, top_k, static_cast<int>(hidden_size), capacity * world_size,
                     static_cast<__nv_bfloat16*>(out));
 }
 

@@ -32,6 +32,11 @@ Two exchange layouts:
 The kernels sit behind :class:`CudaKernels`; a different object with the same three
 methods can stand in for it (the CPU tests use the oracle's restatement with the gloo
 backend).
+
+transport="p2p" (fixed capacity) replaces both all-to-alls with stores into peer-mapped
+buffers on the same node: the dispatch kernel quantises each row straight into the
+owner's receive buffer and the owner copies each output row straight into the source's
+return buffer, each followed by an epoch flag the consumer waits on (csrc/ep_p2p.cuh).
 """
 from __future__ import annotations
 
@@ -83,15 +88,52 @@ def shard_experts(experts: CutlassGptOssExperts, rank: int, world_size: int) -> 
     return loc
 
 
+class P2PExchange:
+    """The peer-mapped exchange buffers of one expert-parallel group (layout and protocol
+    in csrc/ep_p2p.cuh): this rank's buffer is allocated here, every other rank's buffer
+    is mapped through its IPC handle (gathered with torch.distributed over the group's
+    host-side object collective), and the W base addresses go to the device."""
+
+    def __init__(self, world_size: int, rank: int, capacity: int, hidden_size: int, device, group=None):
+        self.world_size, self.rank, self.capacity, self.group = world_size, rank, capacity, group
+        nbytes = _ops.ep_p2p_buffer_bytes(world_size, capacity, hidden_size)
+        if nbytes <= 0:
+            raise ValueError("p2p exchange: bad world_size / capacity / hidden size")
+        self.local, handle = _ops.ipc_alloc(nbytes)
+        handles = [None] * world_size
+        dist.all_gather_object(handles, handle, group=group)
+        self.peers = [self.local if r == rank else _ops.ipc_open(handles[r]) for r in range(world_size)]
+        self.peer_bases = torch.tensor(self.peers, dtype=torch.int64, device=device)
+        self.epoch = 0
+        dist.barrier(group=group)               # every rank has mapped every buffer
+
+    def close(self):
+        if self.local is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)          # nobody writes into a buffer about to go away
+        for r, ptr in enumerate(self.peers):
+            if r != self.rank:
+                _ops.ipc_close(ptr)
+        _ops.ipc_free(self.local)
+        self.local = None
+
+
 class ExpertParallelExperts(nn.Module):
     """Drop-in for CutlassGptOssExperts.forward across a process group: same
     (hidden_states, router_indices, routing_weights) -> out contract, router_indices
     holding GLOBAL expert ids; `local_experts` holds this rank's E/W experts."""
 
     def __init__(self, local_experts: CutlassGptOssExperts, num_experts: int, group=None, kernels=None,
-                 capacity_tokens: int | None = None):
+                 capacity_tokens: int | None = None, transport: str = "nccl", top_k: int = 4):
         super().__init__()
         self.capacity_tokens = capacity_tokens
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport must be 'nccl' or 'p2p', got {transport!r}")
+        if transport == "p2p" and not capacity_tokens:
+            raise ValueError("the p2p transport needs capacity_tokens (fixed-size peer buffers)")
+        self.transport = transport
+        self.top_k = top_k
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -103,6 +145,22 @@ class ExpertParallelExperts(nn.Module):
         self.kernels = kernels if kernels is not None else CudaKernels()
         self.last_splits = None        # exact splits: (send, recv) rows per peer of the last forward
         self.last_send_counts = None   # fixed capacity: device tensor of rows per destination
+        self.exchange = None
+        if transport == "p2p":
+            dev = local_experts.gate_up_proj_bias.device
+            cap = capacity_tokens * top_k
+            self.exchange = P2PExchange(self.world_size, self.rank, cap, self.hidden_size, dev, group)
+            R = self.world_size * cap
+            e_loc = local_experts.num_experts
+            self._back = torch.empty((R, self.hidden_size), dtype=torch.bfloat16, device=dev)
+            nbytes = _ops.workspace_bytes(R, 1, e_loc, self.hidden_size, local_experts.intermediate_size)
+            self._ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+
+    def close(self):
+        """Release the peer buffers (collective over the group)."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
 
     def forward(self, hidden_states: torch.Tensor, router_indices: torch.Tensor,
                 routing_weights: torch.Tensor) -> torch.Tensor:
@@ -112,6 +170,20 @@ class ExpertParallelExperts(nn.Module):
         idx = router_indices.reshape(h.shape[0], router_indices.shape[-1]).contiguous()
         w = routing_weights.reshape(idx.shape).to(torch.float32).contiguous()
         k, g = self.kernels, self.group
+        if self.transport == "p2p":
+            if h.shape[0] > self.capacity_tokens or idx.shape[1] != self.top_k:
+                raise RuntimeError(f"p2p exchange sized for {self.capacity_tokens} tokens x top-{self.top_k}")
+            ex, x = self.exchange, self.experts
+            ex.epoch += 1
+            cap = self.capacity_tokens * self.top_k
+            send_counts, pos_of = _ops.ep_p2p_dispatch(h, idx, w, self.num_experts, self.world_size, self.rank, cap,
+                                                       ex.peer_bases, ex.epoch)
+            _ops.ep_p2p_expert_forward(ex.local, self.world_size, self.rank, cap, ex.epoch, x.gate_up_proj_data,
+                                       x.gate_up_proj_scales, x.gate_up_proj_bias.data, x.down_proj_data,
+                                       x.down_proj_scales, x.down_proj_bias.data, self._back, self._ws,
+                                       ex.peer_bases, float(x.alpha), float(x.limit), int(x.gemm_mode))
+            self.last_send_counts = send_counts
+            return _ops.ep_p2p_combine(ex.local, self.world_size, cap, ex.epoch, pos_of, idx, H, h.device).view(shape)
         if self.capacity_tokens:
             if h.shape[0] > self.capacity_tokens:
                 raise RuntimeError(f"{h.shape[0]} tokens exceed capacity_tokens={self.capacity_tokens}")

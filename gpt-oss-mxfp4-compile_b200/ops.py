@@ -524,3 +524,85 @@ def ep_combine(back_rows, pos_of, router_indices):
     _lib.call("gptoss_ep_combine", back_rows.data_ptr(), back_rows.shape[0], pos_of.data_ptr(),
               router_indices.data_ptr(), T, k, H, out.data_ptr(), _stream(dev))
     return out
+
+
+# ------------------------------------------------------------------ peer-memory expert parallelism
+def ipc_alloc(nbytes: int):
+    """Zeroed device buffer of the current device plus its IPC handle -> (address, handle bytes)."""
+    hb = int(_lib.query("gptoss_ipc_handle_bytes"))
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * hb)()
+    _lib.call("gptoss_ipc_alloc", int(nbytes), ctypes.byref(ptr), handle)
+    return int(ptr.value), bytes(handle)
+
+
+def ipc_open(handle: bytes) -> int:
+    buf = (ctypes.c_uint8 * len(handle)).from_buffer_copy(handle)
+    ptr = ctypes.c_void_p()
+    _lib.call("gptoss_ipc_open", buf, ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int):
+    _lib.call("gptoss_ipc_close", ptr)
+
+
+def ipc_free(ptr: int):
+    _lib.call("gptoss_ipc_free", ptr)
+
+
+def ep_p2p_buffer_bytes(world_size: int, capacity: int, hidden_size: int) -> int:
+    return int(_lib.query("gptoss_ep_p2p_buffer_bytes", int(world_size), int(capacity), int(hidden_size)))
+
+
+def ep_p2p_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, rank: int,
+                    capacity: int, peer_bases, epoch: int):
+    """Quantised rows straight into the owners' receive rows + dispatch flags.
+    Returns (send_counts i32 [W], pos_of i32 [T*k])."""
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _cuda(router_indices, "router_indices")
+    _dtype(router_indices, (torch.int64,), "router_indices")
+    _cuda(routing_weights, "routing_weights")
+    _dtype(routing_weights, (torch.float32,), "routing_weights")
+    T, H = hidden.shape
+    k = router_indices.shape[1]
+    dev = hidden.device
+    send_counts = torch.empty(world_size, dtype=torch.int32, device=dev)
+    pos_of = torch.empty(T * k, dtype=torch.int32, device=dev)
+    nbytes = int(_lib.query("gptoss_ep_dispatch_workspace_bytes", T, k, world_size))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    _lib.call("gptoss_ep_p2p_dispatch", _p(hidden) if T else None, _p(router_indices) if T else None,
+              _p(routing_weights) if T else None, T, k, int(num_experts), int(world_size), int(rank), H,
+              int(capacity), peer_bases.data_ptr(), int(epoch), send_counts.data_ptr(),
+              pos_of.data_ptr() if T else None, ws.data_ptr(), ws.numel(), status_tensor(dev).data_ptr(),
+              _stream(dev))
+    return send_counts, pos_of
+
+
+def ep_p2p_expert_forward(local_base: int, world_size: int, rank: int, capacity: int, epoch: int, gu_data,
+                          gu_scales, gu_bias, dn_data, dn_scales, dn_bias, back_rows, workspace, peer_bases,
+                          alpha: float = 1.702, limit: float = 7.0, gemm_mode: int = GEMM_AUTO):
+    """Local experts on this rank's receive rows; outputs stored into the source ranks'
+    return rows + return flags. `back_rows` [W*cap, H] bf16 and `workspace` (u8, at least
+    workspace_bytes(W*cap, 1, E/W, H, I)) are this rank's scratch."""
+    _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias)
+    E_loc = gu_data.shape[0]
+    I = gu_data.shape[1] // 2
+    H = dn_data.shape[1]
+    dev = gu_data.device
+    _lib.call("gptoss_ep_p2p_expert_forward", int(local_base), int(world_size), int(rank), int(capacity), int(epoch),
+              E_loc, H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E_loc, gu_bias.data_ptr(),
+              dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E_loc, dn_bias.data_ptr(),
+              float(alpha), float(limit), back_rows.data_ptr(), peer_bases.data_ptr(), workspace.data_ptr(),
+              workspace.numel(), int(gemm_mode), status_tensor(dev).data_ptr(), _stream(dev))
+
+
+def ep_p2p_combine(local_base: int, world_size: int, capacity: int, epoch: int, pos_of, router_indices,
+                   hidden_size: int, device):
+    T, k = router_indices.shape
+    out = torch.empty((T, hidden_size), dtype=torch.bfloat16, device=device)
+    _lib.call("gptoss_ep_p2p_combine", int(local_base), int(world_size), int(capacity), int(epoch),
+              pos_of.data_ptr() if T else None, router_indices.data_ptr() if T else None, T, k, int(hidden_size),
+              out.data_ptr() if T else None, status_tensor(device).data_ptr(), _stream(device))
+    return out

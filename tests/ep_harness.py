@@ -145,13 +145,16 @@ def nccl_worker(rank: int, world: int, port: int, shapes, q):
             h = torch.randn(T + 8 * rank, hs, generator=g).to(torch.bfloat16)
             wv, ix = torch.topk(torch.randn(h.shape[0], e_tot, generator=g), K, dim=-1)
             wv = torch.softmax(wv, -1).float()
+            p2p = EP.ExpertParallelExperts(local, e_tot, capacity_tokens=T + 8 * world, transport="p2p", top_k=K)
             out = mod(h.to(dev), ix.to(dev), wv.to(dev))
             out_fixed = fixed(h.to(dev), ix.to(dev), wv.to(dev))
+            out_p2p = [p2p(h.to(dev), ix.to(dev), wv.to(dev)) for _ in range(3)]   # buffer reuse over epochs
             torch.cuda.synchronize()
             st = pkg.ops.read_status(dev)
+            p2p.close()
             ref = O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn)
             single = full(h.to(dev), ix.to(dev), wv.to(dev))
-            for o in (out, out_fixed):
+            for o in (out, out_fixed, *out_p2p):
                 results.append(("experts", e_tot, hs, st, rel_l2(o.cpu(), ref), max_abs_over_rms(o.cpu(), ref),
                                 (o.float() - single.float()).abs().max().item() / single.float().abs().max().item(),
                                 mod.last_splits))
