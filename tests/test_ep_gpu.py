@@ -144,3 +144,24 @@ def test_emulated_ranks_chain_capacity(pkg, dev):
         torch.cuda.synchronize()
         assert pkg.ops.read_status(dev) == 0
         assert_output_tolerance(out.cpu(), O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn), f"rank {r}")
+
+
+def test_p2p_wait_gives_up_with_status(pkg, dev):
+    # A flag nothing raises: the combine's bounded wait runs out after ~1 s, records
+    # 0x301 in the status word and the kernel returns; the device stays usable.
+    import time
+    world, cap, H = 1, 8, 512
+    base, _ = pkg.ops.ipc_alloc(pkg.ops.ep_p2p_buffer_bytes(world, cap, H))
+    try:
+        idx = torch.zeros(2, 4, dtype=torch.int64, device=dev)
+        pos = torch.zeros(8, dtype=torch.int32, device=dev)
+        t0 = time.time()
+        out = pkg.ops.ep_p2p_combine(base, world, cap, 7, pos, idx, H, dev)
+        torch.cuda.synchronize()
+        assert time.time() - t0 >= 0.9
+        assert pkg.ops.read_status(dev) == 0x301
+        assert out.shape == (2, H)
+        x = torch.ones(4, device=dev)
+        assert float((x * 2).sum()) == 8.0          # the context is healthy
+    finally:
+        pkg.ops.ipc_free(base)
