@@ -195,6 +195,23 @@ int make_wgt_map(CUtensorMap* m, const void* base, int E, int64_t N, int64_t K, 
   return GPTOSS_OK;
 }
 
+// Blocked scale buffer as rows of 256 bytes; a 512-byte chunk (one 128-row x 4-group
+// atom) is a 2-row box. Used by the CTA-pair GEMM, whose loads all complete on one barrier.
+int make_sf_map(CUtensorMap* m, const void* base, int64_t bytes) {
+  EncodeTiledFn enc;
+  GPTOSS_TRY(get_encode_fn(&enc));
+  GPTOSS_CHECK(bytes >= 512 && bytes % 256 == 0, "scale buffer of %lld bytes", (long long)bytes);
+  cuuint64_t dims[2] = {256u, static_cast<cuuint64_t>(bytes / 256)};
+  cuuint64_t strides[1] = {256u};
+  cuuint32_t box[2] = {256u, 2u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GPTOSS_ERR_CUDA, "cuTensorMapEncodeTiled(scales) failed: %d", (int)r);
+  return GPTOSS_OK;
+}
+
 // ---------------------------------------------------------------- GEMM launch
 struct GemmJob {
   const uint8_t* act;   // [act_rows, lda] e4m3
@@ -202,39 +219,45 @@ struct GemmJob {
   int64_t lda;
   const uint8_t* wgt;   // [E, N, K/2]
   GemmParams p;
+  int64_t sfa_bytes;    // sizes of the scale buffers (0: unknown -> no CTA-pair tiles)
+  int64_t sfb_bytes;
 };
 
-template <bool SWAP, bool SPREAD, int EPI>
+template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false>
 int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t st) {
-  using C = GemmConfig<SWAP, SPREAD>;
+  using C = GemmConfig<SWAP, SPREAD, PAIR>;
   if (job.act_rows <= 0) return GPTOSS_OK;
   CUtensorMap ta, ta32, ta16, tw;
   GPTOSS_TRY(make_act_map(&ta, job.act, job.act_rows, job.lda, C::kActRows));
   if (SWAP) {
     GPTOSS_TRY(make_act_map(&ta32, job.act, job.act_rows, job.lda, 32));
     GPTOSS_TRY(make_act_map(&ta16, job.act, job.act_rows, job.lda, 16));
+  } else if (PAIR) {
+    GPTOSS_TRY(make_sf_map(&ta32, job.p.sfa, job.sfa_bytes));
+    GPTOSS_TRY(make_sf_map(&ta16, job.p.sfb, job.sfb_bytes));
   } else {
     ta32 = ta;
     ta16 = ta;
   }
-  GPTOSS_TRY(make_wgt_map(&tw, job.wgt, job.p.num_experts, job.p.N, job.p.K, C::kWgtRows));
+  GPTOSS_TRY(make_wgt_map(&tw, job.wgt, job.p.num_experts, job.p.N, job.p.K, C::kWgtRowsCta));
   static uint64_t attr_done = 0;   // one bit per device
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(attr_done & (1ull << dev))) {
-      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, SPREAD, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(C::kSmemBytes)));
+      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, SPREAD, EPI, PAIR>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes)));
       attr_done |= (1ull << dev);
     }
   }
   GemmParams p = job.p;
   p.n_tiles = static_cast<int>((p.N + C::kWgtRows - 1) / C::kWgtRows);
-  const int64_t tiles_ub = (job.act_rows / C::kActRows + p.num_experts) * static_cast<int64_t>(p.n_tiles);
-  const int grid = static_cast<int>(std::min<int64_t>(di.sms, tiles_ub));
+  const int64_t tiles_ub = (job.act_rows / C::kTileM + p.num_experts) * static_cast<int64_t>(p.n_tiles);
+  const int grid = PAIR ? 2 * static_cast<int>(std::min<int64_t>(di.sms / 2, tiles_ub))
+                        : static_cast<int>(std::min<int64_t>(di.sms, tiles_ub));
   if (grid <= 0) return GPTOSS_OK;
-  return launch_pdl(moe_gemm_kernel<SWAP, SPREAD, EPI>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, st, ta, ta32,
-                    ta16, tw, p);
+  return launch_pdl_cluster(moe_gemm_kernel<SWAP, SPREAD, EPI, PAIR>, dim3(grid), dim3(C::kThreads), C::kSmemBytes,
+                            st, PAIR ? dim3(2, 1, 1) : dim3(1, 1, 1), ta, ta32, ta16, tw, p);
 }
 
 // GEMM orientation of one call. The fused pipeline switches to weights-on-M with 16-row
@@ -248,7 +271,11 @@ bool pick_swap(int mode, int64_t rows, int experts, int64_t max_avg) {
 
 template <int EPI>
 int run_gemm(const GemmJob& job, bool swap, bool spread, const DeviceInfo& di, int dev, cudaStream_t st) {
-  if (!swap) return launch_gemm<false, false, EPI>(job, di, dev, st);
+  if (!swap) {
+    // CTA-pair tiles when the scale buffers can be described as 256-byte rows
+    const bool pair = job.sfa_bytes > 0 && job.sfb_bytes > 0 && job.p.sfb_stride % 256 == 0 && di.sms >= 2;
+    return pair ? launch_gemm<false, false, EPI, true>(job, di, dev, st) : launch_gemm<false, false, EPI>(job, di, dev, st);
+  }
   return spread ? launch_gemm<true, true, EPI>(job, di, dev, st) : launch_gemm<true, false, EPI>(job, di, dev, st);
 }
 
@@ -349,6 +376,7 @@ struct WsPtrs {
   int64_t* sorted_token; int64_t* sorted_expert; float* sorted_weight;
   int32_t* counts; int32_t* offsets; int32_t* sfoff_a; int32_t* sfoff_b;
   uint8_t* act_codes; uint8_t* act_sf; uint8_t* inter_codes; uint8_t* inter_sf;
+  int64_t act_sf_cap, inter_sf_cap;
 };
 
 WsPtrs ws_ptrs(uint8_t* ws, const Workspace& L) {
@@ -364,6 +392,8 @@ WsPtrs ws_ptrs(uint8_t* ws, const Workspace& L) {
   w.act_sf = ws + L.act_sf;
   w.inter_codes = ws + L.inter_codes;
   w.inter_sf = ws + L.inter_sf;
+  w.act_sf_cap = L.act_sf_cap;
+  w.inter_sf_cap = L.inter_sf_cap;
   return w;
 }
 
@@ -403,6 +433,8 @@ int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g1.p.out_sf_offsets = w.sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
   g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
   g1.p.prefetch_tiles = swap ? prefetch_tiles : 0;
+  g1.sfa_bytes = w.act_sf_cap;
+  g1.sfb_bytes = wt.ldb_gu * E;
   return run_gemm<kEpiGemm1>(g1, swap, swap, di, dev, st);
 }
 
@@ -416,6 +448,8 @@ int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g2.p.m_sizes = w.counts; g2.p.m_stride = 1; g2.p.row_offsets = w.offsets; g2.p.sfa_offsets = w.sfoff_b;
   g2.p.sfa = w.inter_sf; g2.p.sfb = wt.dn_scales; g2.p.sfb_stride = wt.ldb_dn; g2.p.err = status;
   g2.p.out = out; g2.p.ld_out = H; g2.p.bias = wt.dn_bias; g2.p.token_idx = w.sorted_token; g2.p.row_weights = w.sorted_weight;
+  g2.sfa_bytes = w.inter_sf_cap;
+  g2.sfb_bytes = wt.ldb_dn * E;
   return run_gemm<kEpiGemm2>(g2, swap, swap, di, dev, st);
 }
 

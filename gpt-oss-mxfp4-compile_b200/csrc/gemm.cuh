@@ -68,22 +68,30 @@ struct GemmParams {
   int prefetch_tiles;
 };
 
-template <bool SWAP, bool SPREAD = false>
+// PAIR: tokens-on-M tiles computed by a CTA pair (cluster of 2, tcgen05 cta_group::2):
+// M = 256 activation rows (128 per CTA), N = 192 weight rows (each CTA loads 96 of them,
+// the MMA reads both halves), so per SM the weight bytes per MMA halve and the ring holds
+// 7 stages instead of 5. Each CTA still loads its activation-row scales and the full
+// tile's weight scales.
+template <bool SWAP, bool SPREAD = false, bool PAIR = false>
 struct GemmConfig {
   static_assert(SWAP || !SPREAD, "spread activation scales are a SWAP-mode layout");
+  static_assert(!(SWAP && PAIR), "CTA pairs are a tokens-on-M layout");
   static constexpr int kWgtRows = SWAP ? 128 : 192;   // weight rows per tile
+  static constexpr int kWgtRowsCta = PAIR ? kWgtRows / 2 : kWgtRows;   // weight rows this CTA loads
   // Activation rows per tile. SWAP with reference-layout scales uses 64-row chunks that
   // start 0 or 64 rows into a 128-row scale block (TMEM column offset 0 or 2); SPREAD
   // uses 16-row chunks (a 2 KB activation slot, so the ring holds 11 stages).
   static constexpr int kActRows = SWAP ? (SPREAD ? 16 : 64) : 128;
   static constexpr int kColChunks = (kActRows + 31) / 32;   // 32-column TMEM loads per tile
-  static constexpr int kMmaM = 128;
+  static constexpr int kTileM = PAIR ? 2 * kActRows : kActRows;   // activation rows per tile
+  static constexpr int kMmaM = PAIR ? 256 : 128;
   static constexpr int kMmaN = SWAP ? kActRows : kWgtRows;
-  static constexpr int kStages = SWAP ? (SPREAD ? 11 : 8) : 5;
+  static constexpr int kStages = SWAP ? (SPREAD ? 11 : 8) : (PAIR ? 7 : 5);
   static constexpr int kAccBufs = SWAP ? 4 : 2;
   static constexpr int kAccCols = kMmaN;              // fp32 columns per accumulator
   static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
-  static constexpr uint32_t kWgtTileBytes = kWgtRows * 128;   // 8-bit container in smem
+  static constexpr uint32_t kWgtTileBytes = kWgtRowsCta * 128;   // 8-bit container in smem
   static constexpr uint32_t kActTileBytes = kActRows * 128;
   static constexpr uint32_t kSfActBytes = 512;
   static constexpr uint32_t kSfWgtBytes = 512 * kWgtSfChunks;
@@ -122,13 +130,20 @@ __device__ __forceinline__ void load_bias32(const float* b, int valid, float (&o
   }
 }
 
-template <bool SWAP, bool SPREAD, int EPI>
-__global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
+// tm_aux0 / tm_aux1: SWAP: the 32- and 16-row activation maps; PAIR: the activation and
+// weight scale buffers viewed as rows of 256 bytes (512-byte chunks = 2 rows).
+template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false>
+__global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,
-                    const __grid_constant__ CUtensorMap tm_act32,
-                    const __grid_constant__ CUtensorMap tm_act16,
+                    const __grid_constant__ CUtensorMap tm_aux0,
+                    const __grid_constant__ CUtensorMap tm_aux1,
                     const __grid_constant__ CUtensorMap tm_wgt, const GemmParams p) {
-  using C = GemmConfig<SWAP, SPREAD>;
+  using C = GemmConfig<SWAP, SPREAD, PAIR>;
+  // CTA pair: rank inside the pair, pair index and count (a plain CTA is its own "pair")
+  const uint32_t prank = PAIR ? (cluster_ctarank() & 1u) : 0u;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const bool leader = prank == 0;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ int s_chunk_prefix[kMaxExpertsGemm + 1];
   __shared__ int s_chunks[kMaxExpertsGemm];
@@ -148,9 +163,9 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
   // ---- barriers, TMEM and descriptor prefetch overlap the previous kernel's tail
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_act);
-    if constexpr (SWAP) {
-      tma_prefetch_desc(&tm_act32);
-      tma_prefetch_desc(&tm_act16);
+    if constexpr (SWAP || PAIR) {
+      tma_prefetch_desc(&tm_aux0);
+      tma_prefetch_desc(&tm_aux1);
     }
     tma_prefetch_desc(&tm_wgt);
     for (int s = 0; s < C::kStages; ++s) {
@@ -159,14 +174,19 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
     }
     for (int b = 0; b < C::kAccBufs; ++b) {
       mbar_init(accf_bar(b), 1);
-      mbar_init(acce_bar(b), C::kEpiWarps);
+      mbar_init(acce_bar(b), PAIR ? 2 * C::kEpiWarps : C::kEpiWarps);   // both CTAs' epilogues
     }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&s_tmem_base), C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(&s_tmem_base), C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(&s_tmem_base), C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   if constexpr (SWAP) {
     // The weights do not depend on the previous kernel: while it (the routing prologue)
@@ -187,7 +207,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
   // ---- per-CTA tile map from the device-side counts
   for (int i = threadIdx.x; i < p.num_experts; i += blockDim.x) {
     const int m = p.m_sizes[i * p.m_stride];
-    s_chunks[i] = m > 0 ? (m + C::kActRows - 1) / C::kActRows : 0;
+    s_chunks[i] = m > 0 ? (m + C::kTileM - 1) / C::kTileM : 0;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -196,6 +216,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
     s_chunk_prefix[p.num_experts] = acc;
   }
   __syncthreads();
+  // barriers initialised and TMEM allocated in both CTAs before any cross-CTA signal
+  if constexpr (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = s_tmem_base;
   const int total_tiles = s_chunk_prefix[p.num_experts] * p.n_tiles;
@@ -235,51 +257,70 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < total_tiles && ok; t += nunits) {
         int e, nt, ch;
         decode(t, e, nt, ch);
-        const int act_row0 = p.row_offsets[e] + ch * C::kActRows;
-        const int wgt_row0 = nt * C::kWgtRows;
-        const int act_blk = static_cast<int>(act_sf_row<SPREAD>(static_cast<int64_t>(ch) * C::kActRows) >> 7);
-        const uint8_t* sfa_src = p.sfa + p.sfa_offsets[e] + static_cast<int64_t>(act_blk) * p.num_kb * 512;
-        const int wblk0 = wgt_row0 >> 7;
+        // this CTA's activation rows (PAIR: its 128-row half of the 256-row tile) and the
+        // weight rows it loads (PAIR: its 96-row half of the 192-row tile)
+        const int act_in0 = ch * C::kTileM + static_cast<int>(prank) * C::kActRows;
+        const int act_row0 = p.row_offsets[e] + act_in0;
+        const int wgt_row0 = nt * C::kWgtRows + static_cast<int>(prank) * C::kWgtRowsCta;
+        const int act_blk = static_cast<int>(act_sf_row<SPREAD>(static_cast<int64_t>(act_in0)) >> 7);
+        const int64_t sfa_off = p.sfa_offsets[e] + static_cast<int64_t>(act_blk) * p.num_kb * 512;
+        const int wblk0 = (nt * C::kWgtRows) >> 7;   // scale blocks of the whole tile
         const int nwblk_total = (p.N + 127) >> 7;
         const int nwchunks = min(C::kWgtSfChunks, nwblk_total - wblk0);
-        const uint8_t* sfb_src = p.sfb + static_cast<int64_t>(e) * p.sfb_stride +
-                                 static_cast<int64_t>(wblk0) * p.num_kb * 512;
+        const int64_t sfb_off = static_cast<int64_t>(e) * p.sfb_stride + static_cast<int64_t>(wblk0) * p.num_kb * 512;
         const int arows = act_rows_of(e, ch);
-        const CUtensorMap* amap = arows == 16 ? &tm_act16 : (arows == 32 ? &tm_act32 : &tm_act);
-        const uint32_t tx = arows * 128u + C::kWgtRows * 64 + C::kSfActBytes + 512u * nwchunks;
+        const CUtensorMap* amap = arows == 16 ? &tm_aux1 : (arows == 32 ? &tm_aux0 : &tm_act);
+        const uint32_t tx = (arows * 128u + C::kWgtRowsCta * 64 + C::kSfActBytes + 512u * nwchunks) * (PAIR ? 2u : 1u);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.err, kDevTimeoutProducer)) { ok = false; break; }
           const uint32_t sb = smem_base + stage * C::kStageBytes;
           const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
           const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
-          mbar_arrive_expect_tx(full_bar(stage), tx);
-          tma_load_2d(s_a, amap, full_bar(stage), kb * 128, act_row0, pol_a);
-          tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
-          bulk_load(s_sfa, sfa_src + kb * 512, 512, full_bar(stage), pol_a);
-          for (int c = 0; c < nwchunks; ++c)
-            bulk_load(s_sfw + 512u * c, sfb_src + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512, 512,
-                      full_bar(stage), pol_w);
+          if constexpr (PAIR) {
+            // every load of both CTAs completes on the even CTA's full barrier
+            const uint32_t fb = dsmem_map(full_bar(stage), 0);
+            if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
+            tma_load_2d_pair(s_a, &tm_act, fb, kb * 128, act_row0, pol_a);
+            tma_load_3d_pair(s_w, &tm_wgt, fb, kb * 128, wgt_row0, e, pol_w);
+            tma_load_2d_pair(s_sfa, &tm_aux0, fb, 0, static_cast<int32_t>((sfa_off + kb * 512) >> 8), pol_a);
+            for (int c = 0; c < nwchunks; ++c)
+              tma_load_2d_pair(s_sfw + 512u * c, &tm_aux1, fb, 0,
+                               static_cast<int32_t>((sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512) >> 8),
+                               pol_w);
+          } else {
+            mbar_arrive_expect_tx(full_bar(stage), tx);
+            tma_load_2d(s_a, amap, full_bar(stage), kb * 128, act_row0, pol_a);
+            tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
+            bulk_load(s_sfa, p.sfa + sfa_off + kb * 512, 512, full_bar(stage), pol_a);
+            for (int c = 0; c < nwchunks; ++c)
+              bulk_load(s_sfw + 512u * c, p.sfb + sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512, 512,
+                        full_bar(stage), pol_w);
+          }
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
       }
-      // Drain: make sure no copy is still landing in shared memory before exit.
-      for (int s = 0; s < C::kStages; ++s) {
-        // Stage s last received the load of phase (phase if s < stage else phase ^ 1).
-        const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
-        (void)mbar_wait(full_bar(s), ph, p.err, kDevTimeoutDrain);
+      // Drain: make sure no copy is still landing in shared memory before exit (in a pair
+      // the even CTA's barriers count both CTAs' copies; the odd CTA is held by the
+      // closing cluster barrier until then).
+      if (leader) {
+        for (int s = 0; s < C::kStages; ++s) {
+          // Stage s last received the load of phase (phase if s < stage else phase ^ 1).
+          const uint32_t ph = (s < stage) ? phase : (phase ^ 1u);
+          (void)mbar_wait(full_bar(s), ph, p.err, kDevTimeoutDrain);
+        }
       }
     }
   } else if (warp == 1) {
     // ================================================================ MMA issuer
-    if (elect_one()) {
+    if (elect_one() && !(PAIR && !leader)) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = unit; t < total_tiles && ok; t += nunits, ++local) {
         int e, nt, ch;
         decode(t, e, nt, ch);
         const int b = local % C::kAccBufs;
@@ -301,16 +342,27 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
           const uint32_t sb = smem_base + stage * C::kStageBytes;
           const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
           const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
-          tc_cp_32x128b_warpx4(t_sfa, desc_sf_block(s_sfa));
+          if constexpr (PAIR) {
+            // each CTA's scale chunks go from its own shared memory into its own TMEM
+            tc_cp_32x128b_warpx4_pair(t_sfa, desc_sf_block(s_sfa));
 #pragma unroll
-          for (int c = 0; c < C::kWgtSfChunks; ++c)
-            tc_cp_32x128b_warpx4(t_sfw + 4u * c, desc_sf_block(s_sfw + 512u * c));
+            for (int c = 0; c < C::kWgtSfChunks; ++c)
+              tc_cp_32x128b_warpx4_pair(t_sfw + 4u * c, desc_sf_block(s_sfw + 512u * c));
+          } else {
+            tc_cp_32x128b_warpx4(t_sfa, desc_sf_block(s_sfa));
+#pragma unroll
+            for (int c = 0; c < C::kWgtSfChunks; ++c)
+              tc_cp_32x128b_warpx4(t_sfw + 4u * c, desc_sf_block(s_sfw + 512u * c));
+          }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t da = desc_kmajor_sw128(s_a + 32u * k);
             const uint64_t dw = desc_kmajor_sw128(s_w + 32u * k);
             const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
-            if constexpr (SWAP) {
+            if constexpr (PAIR) {
+              mma_mxf8f6f4_pair(d_tmem, da, dw, idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, k, k), t_sfa, t_sfw + wshift,
+                                acc);
+            } else if constexpr (SWAP) {
               // A = weights (E2M1), B = activations (E4M3)
               mma_mxf8f6f4(d_tmem, dw, da, idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, k, k),
                            t_sfw, t_sfa + ashift, acc);
@@ -320,14 +372,20 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
                            t_sfa, t_sfw + wshift, acc);
             }
           }
-          tc_commit(empty_bar(stage));
+          if constexpr (PAIR) tc_commit_pair(empty_bar(stage), 0x3);   // both CTAs' producers
+          else tc_commit(empty_bar(stage));
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        tc_commit(accf_bar(b));
+        if constexpr (PAIR) tc_commit_pair(accf_bar(b), 0x3);   // both CTAs' epilogues
+        else tc_commit(accf_bar(b));
       }
       // Wait for every tcgen05 operation this thread issued before TMEM is released.
-      tc_commit(drain_bar);
+      if constexpr (PAIR) tc_commit_pair(drain_bar, 0x3);
+      else tc_commit(drain_bar);
+      (void)mbar_wait(drain_bar, 0u, p.err, kDevTimeoutDrain);
+    } else if (PAIR && !leader && elect_one()) {
+      // odd CTA of a pair: its TMEM is written by the even CTA's MMAs; wait for them
       (void)mbar_wait(drain_bar, 0u, p.err, kDevTimeoutDrain);
     }
   } else {
@@ -338,7 +396,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
     int local = 0;
     bool ok = true;   // after a timeout keep walking the tiles (named barriers stay
                       // matched across the four warps) but touch no TMEM or memory
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+    for (int t = unit; t < total_tiles; t += nunits, ++local) {
       int e, nt, ch;
       decode(t, e, nt, ch);
       const int b = local % C::kAccBufs;
@@ -356,7 +414,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
       const int row0 = p.row_offsets[e];
       if constexpr (!SWAP) {
         // thread <-> activation row
-        const int r_in = ch * C::kActRows + 32 * q + lane;   // row inside the expert
+        const int r_in = ch * C::kTileM + static_cast<int>(prank) * C::kActRows + 32 * q + lane;   // row in expert
         const bool vrow = r_in < m_e;
         const int64_t grow = static_cast<int64_t>(row0) + r_in;
         const int n_tile0 = nt * C::kWgtRows;
@@ -566,15 +624,22 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acce_bar(b));
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(dsmem_map(acce_bar(b), 0));   // the even CTA's MMA
+        else mbar_arrive(acce_bar(b));
+      }
     }
   }
 
-  __syncthreads();
+  // A pair stays alive until both CTAs are done: the even CTA's MMAs write the odd CTA's
+  // TMEM and the odd CTA's epilogue arrives on the even CTA's barriers.
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    else tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
