@@ -18,7 +18,7 @@ LIB_NAME = "libgptoss_moe.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
 SOURCES = ["capi.cu"]
-HEADERS = ["ptx.cuh", "numerics.cuh", "routing.cuh", "gemm.cuh"]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith(".cuh"))   # every header the sources include
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

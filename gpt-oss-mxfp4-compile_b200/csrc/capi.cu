@@ -1140,9 +1140,9 @@ size_t gptoss_ep_p2p_buffer_bytes(int world_size, int64_t capacity, int64_t hidd
 
 int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
                            int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
-                           int64_t hidden_size, int64_t capacity, const uint64_t* peer_bases, int32_t epoch,
-                           int32_t* send_counts, int32_t* pos_of, void* workspace, size_t workspace_bytes,
-                           int32_t* status_dev, void* stream) {
+                           int64_t hidden_size, int64_t capacity, void* local_base, const uint64_t* peer_bases,
+                           int32_t epoch, int32_t* send_counts, int32_t* pos_of, void* workspace,
+                           size_t workspace_bytes, int32_t* status_dev, void* stream) {
   GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld && rank >= 0 && rank < world_size,
                "ep_p2p_dispatch: bad world_size / rank");
   GPTOSS_CHECK(num_experts % world_size == 0, "ep_p2p_dispatch: num_experts must be a multiple of world_size");
@@ -1152,7 +1152,8 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
   GPTOSS_CHECK(capacity >= num_tokens * top_k && capacity > 0, "ep_p2p_dispatch: capacity below num_tokens * top_k");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(send_counts, "send_counts", &di));
-  GPTOSS_CHECK(peer_bases && workspace && (num_tokens == 0 || (hidden && router_indices && routing_weights && pos_of)),
+  GPTOSS_CHECK(local_base && peer_bases && workspace &&
+                   (num_tokens == 0 || (hidden && router_indices && routing_weights && pos_of)),
                "ep_p2p_dispatch: null pointer");
   const size_t need = gptoss_ep_dispatch_workspace_bytes(num_tokens, top_k, world_size);
   if (workspace_bytes < need) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, need);
@@ -1181,8 +1182,8 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
                         num_experts / world_size, A, router_indices, routing_weights,
                         static_cast<const int32_t*>(rp.sorted_src), capacity, world_size, rank,
                         static_cast<const int32_t*>(send_counts), static_cast<const int32_t*>(rp.offsets), tpr,
-                        peer_bases, pos_of));
-  return launch_pdl(p2p_signal_kernel, dim3(1), dim3(kP2pMaxWorld), 0, st, peer_bases, world_size, rank, epoch);
+                        peer_bases, pos_of, static_cast<int32_t*>(local_base) + kP2pCounterDispatch, epoch));
+  return GPTOSS_OK;
 }
 
 int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int64_t capacity, int32_t epoch,
@@ -1221,35 +1222,60 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
   const int64_t Kh = pad128(hidden_size), Ki = pad128(intermediate_size);
   const uint8_t* recv = static_cast<const uint8_t*>(local_base) + p2p_recv_offset(0, capacity, rb);
   const int32_t* flags = static_cast<const int32_t*>(local_base);
-  const int ublocks = static_cast<int>(std::min<int64_t>((R + 255) / 256, 4 * di.sms));
-  GPTOSS_TRY(launch_pdl(ep_unpack_meta_p2p_kernel, dim3(ublocks), dim3(256), 0, st, recv, R, H, flags, world_size,
-                        epoch, status, lexp, lw));
-  RouteSortParams rp{};
-  rp.router_indices = lexp; rp.routing_weights = lw;
-  rp.A = static_cast<int>(R); rp.K = 1; rp.E = num_local_experts;
-  rp.sorted_token = p.sorted_token; rp.sorted_expert = p.sorted_expert; rp.sorted_weight = p.sorted_weight;
-  rp.counts = p.counts; rp.offsets = p.offsets;
-  rp.sf_offsets_a = p.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = H / 32; rp.sf_a = p.act_sf;
-  rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
-  rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
-  rp.spread = swap ? 1 : 0;
-  rp.allow_empty = 1;
-  rp.err = status;
-  GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
-  GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st, recv, R, H,
-                        static_cast<const int64_t*>(p.sorted_token), static_cast<const int64_t*>(p.sorted_expert),
-                        static_cast<const int32_t*>(p.offsets), static_cast<const int32_t*>(p.sfoff_a),
-                        static_cast<int>(Kh / 128), swap ? 1 : 0, p.act_codes, p.act_sf));
-  GPTOSS_CUDA(cudaMemsetAsync(back_rows, 0, static_cast<size_t>(R * hidden_size) * sizeof(__nv_bfloat16), st));
+  int32_t* ret_counter = static_cast<int32_t*>(local_base) + kP2pCounterReturn;
+  const size_t rp_smem = recv_prologue_smem(R, num_local_experts);
+  int prefetch = 0;
+  if (R <= kRpMaxRows && rp_smem <= 200 * 1024) {
+    // one launch: flag wait, sort by local expert, gather into the blocked layout, zero back_rows
+    static uint64_t attr_done = 0;   // one bit per device
+    static std::mutex mu;
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      if (!(attr_done & (1ull << dev))) {
+        GPTOSS_CUDA(cudaFuncSetAttribute(ep_recv_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024));
+        attr_done |= (1ull << dev);
+      }
+    }
+    RecvPrologueParams rq{};
+    rq.recv = recv; rq.R = R; rq.H = H; rq.E = num_local_experts; rq.world = world_size; rq.epoch = epoch;
+    rq.flags = flags; rq.err = status; rq.lexp = lexp; rq.lw = lw;
+    rq.sorted_token = p.sorted_token; rq.sorted_expert = p.sorted_expert; rq.sorted_weight = p.sorted_weight;
+    rq.counts = p.counts; rq.offsets = p.offsets; rq.sf_offsets_a = p.sfoff_a; rq.sf_offsets_b = p.sfoff_b;
+    rq.g4_a = static_cast<int>(Kh / 128); rq.g4_b = static_cast<int>(Ki / 128); rq.spread = swap ? 1 : 0;
+    rq.act_codes = p.act_codes; rq.act_sf = p.act_sf; rq.back_rows = static_cast<__nv_bfloat16*>(back_rows);
+    const int grid = static_cast<int>(std::min<int64_t>(di.sms, std::max<int64_t>(R, 1)));
+    GPTOSS_TRY(launch_pdl(ep_recv_prologue_kernel, dim3(grid), dim3(256), rp_smem, st, rq));
+    prefetch = kPrefetchTilesAfterPrologue;
+  } else {
+    const int ublocks = static_cast<int>(std::min<int64_t>((R + 255) / 256, 4 * di.sms));
+    GPTOSS_TRY(launch_pdl(ep_unpack_meta_p2p_kernel, dim3(ublocks), dim3(256), 0, st, recv, R, H, flags, world_size,
+                          epoch, status, lexp, lw));
+    RouteSortParams rp{};
+    rp.router_indices = lexp; rp.routing_weights = lw;
+    rp.A = static_cast<int>(R); rp.K = 1; rp.E = num_local_experts;
+    rp.sorted_token = p.sorted_token; rp.sorted_expert = p.sorted_expert; rp.sorted_weight = p.sorted_weight;
+    rp.counts = p.counts; rp.offsets = p.offsets;
+    rp.sf_offsets_a = p.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = H / 32; rp.sf_a = p.act_sf;
+    rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
+    rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
+    rp.spread = swap ? 1 : 0;
+    rp.allow_empty = 1;
+    rp.err = status;
+    GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
+    GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st, recv, R, H,
+                          static_cast<const int64_t*>(p.sorted_token), static_cast<const int64_t*>(p.sorted_expert),
+                          static_cast<const int32_t*>(p.offsets), static_cast<const int32_t*>(p.sfoff_a),
+                          static_cast<int>(Kh / 128), swap ? 1 : 0, p.act_codes, p.act_sf));
+    GPTOSS_CUDA(cudaMemsetAsync(back_rows, 0, static_cast<size_t>(R * hidden_size) * sizeof(__nv_bfloat16), st));
+  }
   GPTOSS_TRY(stage_gemm1(R, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p, swap,
-                         status, di, dev, st));
+                         status, di, dev, st, prefetch));
   GPTOSS_TRY(stage_gemm2(R, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, swap, status, di,
                          dev, st));
-  GPTOSS_TRY(launch_pdl(ep_return_p2p_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st,
-                        static_cast<const __nv_bfloat16*>(back_rows), static_cast<const int64_t*>(lexp), capacity,
-                        world_size, rank, H, peer_bases));
-  return launch_pdl(p2p_signal_kernel, dim3(1), dim3(kP2pMaxWorld), 0, st, peer_bases, world_size, world_size + rank,
-                    epoch);
+  return launch_pdl(ep_return_p2p_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st,
+                    static_cast<const __nv_bfloat16*>(back_rows), static_cast<const int64_t*>(lexp), capacity,
+                    world_size, rank, H, peer_bases, ret_counter, epoch);
 }
 
 int gptoss_ep_p2p_combine(const void* local_base, int world_size, int64_t capacity, int32_t epoch,

@@ -2,7 +2,7 @@
 // path). Every rank owns one peer-mapped exchange buffer (cudaIpc, mapped on every other
 // rank of the node):
 //
-//   [ flags: 2 * kP2pMaxWorld int32 | recv rows [W][cap][row_bytes] | ret rows [W][cap][H] bf16 ]
+//   [ header: flags + counters (1 KB) | recv rows [W][cap][row_bytes] | ret rows [W][cap][H] bf16 ]
 //
 //   dispatch  rank s packs (quantises) each assignment's row straight into the receive
 //             rows of the owning rank q at segment s (st.global to q's memory); rows of
@@ -30,7 +30,10 @@ namespace gptoss {
 
 constexpr int kP2pMaxWorld = 64;
 constexpr int kDevTimeoutPeer = 0x301;    // a peer's flag did not arrive within the timeout
-constexpr uint32_t kP2pFlagBytes = 2 * kP2pMaxWorld * 4;
+// header: dispatch flags [0, 64), return flags [64, 128), completion counters [128, 130)
+constexpr uint32_t kP2pFlagBytes = 4 * kP2pMaxWorld * 4;
+constexpr int kP2pCounterDispatch = 2 * kP2pMaxWorld;
+constexpr int kP2pCounterReturn = 2 * kP2pMaxWorld + 1;
 
 __host__ __device__ __forceinline__ int64_t p2p_recv_offset(int rank_s, int64_t cap, int64_t rb) {
   return kP2pFlagBytes + static_cast<int64_t>(rank_s) * cap * rb;
@@ -71,26 +74,29 @@ __device__ __forceinline__ void p2p_wait_flags(const int32_t* flags, int first, 
   __syncthreads();
 }
 
-// One CTA, blockDim >= world: after the previous kernel on the stream (whose stores went to
-// the peers) completed, raise flags[slot] on every peer to `epoch`.
-__global__ void p2p_signal_kernel(const uint64_t* __restrict__ peer_bases, int world, int slot, int32_t epoch) {
-  pdl_trigger();
-  pdl_wait();
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  const int q = threadIdx.x;
-  if (q < world) st_release_sys(reinterpret_cast<int32_t*>(peer_bases[q]) + slot, epoch);
+// Called by thread 0 of every CTA after the CTA's stores to the peers: the last CTA to
+// get here raises flags[slot] on every peer to `epoch` (the threadfence-reduction pattern:
+// every CTA fences its stores at system scope before counting itself) and resets the
+// counter for the next call.
+__device__ __forceinline__ void p2p_last_cta_signal(int32_t* counter, const uint64_t* peer_bases, int world,
+                                                    int slot, int32_t epoch) {
+  __threadfence_system();
+  const int prev = atomicAdd(counter, 1);
+  if (prev == static_cast<int>(gridDim.x * gridDim.y * gridDim.z) - 1) {
+    __threadfence_system();
+    for (int q = 0; q < world; ++q) st_release_sys(reinterpret_cast<int32_t*>(peer_bases[q]) + slot, epoch);
+    atomicExch(counter, 0);
+  }
 }
 
-// Dispatch: like ep_pack_kernel with the fixed-capacity layout, but row j of destination q
-// goes to peer q's receive rows, segment `rank`.
-__global__ void __launch_bounds__(256) ep_pack_p2p_kernel(
-    const __nv_bfloat16* __restrict__ hidden, int H, int K, int experts_per_rank, int64_t A,
+// Row r of the fixed-capacity send layout (destination q = r / cap, slot j = r % cap):
+// quantised into peer q's receive rows, segment `rank`, or marked empty past the count.
+__device__ __forceinline__ void ep_pack_p2p_row(
+    const __nv_bfloat16* __restrict__ hidden, int H, int K, int experts_per_rank,
     const int64_t* __restrict__ router_indices, const float* __restrict__ routing_weights,
     const int32_t* __restrict__ sorted_src, int64_t cap, int world, int rank,
     const int32_t* __restrict__ dest_counts, const int32_t* __restrict__ dest_offsets, int tpr,
     const uint64_t* __restrict__ peer_bases, int32_t* __restrict__ pos_of) {
-  pdl_trigger();
-  pdl_wait();
   const int rows_per_block = blockDim.x / tpr;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * rows_per_block + threadIdx.x / tpr;
   if (r >= cap * world) return;
@@ -143,6 +149,24 @@ __global__ void __launch_bounds__(256) ep_pack_p2p_kernel(
   }
 }
 
+// Dispatch: like ep_pack_kernel with the fixed-capacity layout, but row j of destination q
+// goes to peer q's receive rows, segment `rank`.
+__global__ void __launch_bounds__(256) ep_pack_p2p_kernel(
+    const __nv_bfloat16* __restrict__ hidden, int H, int K, int experts_per_rank, int64_t A,
+    const int64_t* __restrict__ router_indices, const float* __restrict__ routing_weights,
+    const int32_t* __restrict__ sorted_src, int64_t cap, int world, int rank,
+    const int32_t* __restrict__ dest_counts, const int32_t* __restrict__ dest_offsets, int tpr,
+    const uint64_t* __restrict__ peer_bases, int32_t* __restrict__ pos_of, int32_t* __restrict__ counter,
+    int32_t epoch) {
+  pdl_trigger();
+  pdl_wait();
+  ep_pack_p2p_row(hidden, H, K, experts_per_rank, router_indices, routing_weights, sorted_src, cap, world, rank,
+                  dest_counts, dest_offsets, tpr, peer_bases, pos_of);
+  __syncthreads();
+  if (threadIdx.x == 0) p2p_last_cta_signal(counter, peer_bases, world, rank, epoch);
+}
+
+
 // Receiving rank: wait for every sender's dispatch flag, then row r's (local expert,
 // weight) -> the arrays route_sort_kernel reads (empty slots carry expert -1).
 __global__ void ep_unpack_meta_p2p_kernel(const uint8_t* __restrict__ recv_rows, int64_t R, int H,
@@ -162,21 +186,174 @@ __global__ void ep_unpack_meta_p2p_kernel(const uint8_t* __restrict__ recv_rows,
 
 // Owner: output row r of the local expert forward (received row r = segment s, slot j)
 // -> ret rows of source rank s, segment `rank`, slot j. One CTA per row; empty rows skip.
+// The last CTA raises return flag[W + rank] on every peer.
 __global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* __restrict__ back_rows,
                                                             const int64_t* __restrict__ expert, int64_t cap,
                                                             int world, int rank, int H,
-                                                            const uint64_t* __restrict__ peer_bases) {
+                                                            const uint64_t* __restrict__ peer_bases,
+                                                            int32_t* __restrict__ counter, int32_t epoch) {
   pdl_trigger();
   pdl_wait();
   const int64_t r = blockIdx.x;
-  if (r >= cap * world || expert[r] < 0) return;
-  const int s = static_cast<int>(r / cap);
-  const int64_t j = r - static_cast<int64_t>(s) * cap;
-  const int64_t rb = ep_row_bytes(H);
-  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peer_bases[s]) +
-                                        p2p_ret_offset(world, rank, cap, rb, H) + j * H * 2);
-  const uint4* src = reinterpret_cast<const uint4*>(back_rows + r * H);
-  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) dst[v] = src[v];
+  if (r < cap * world && expert[r] >= 0) {
+    const int s = static_cast<int>(r / cap);
+    const int64_t j = r - static_cast<int64_t>(s) * cap;
+    const int64_t rb = ep_row_bytes(H);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peer_bases[s]) +
+                                          p2p_ret_offset(world, rank, cap, rb, H) + j * H * 2);
+    const uint4* src = reinterpret_cast<const uint4*>(back_rows + r * H);
+    for (int v = threadIdx.x; v < H / 8; v += blockDim.x) dst[v] = src[v];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) p2p_last_cta_signal(counter, peer_bases, world, world + rank, epoch);
+}
+
+// ---------------------------------------------------------------- receiving rank, one launch
+// Wait for every sender's flag, then (every CTA, redundantly) read the W * cap row
+// headers into shared memory and run the stable counting sort by local expert (empty slots
+// skipped; the order of route_sort_kernel); CTA 0 writes the routed layout. Then CTA c
+// copies the sorted rows c, c + gridDim.x, ... -- FP8 codes into the GEMM's activation
+// rows, the row's UE8M0 bytes as 32-bit words into the blocked layout (the padding groups
+// of the last k-atom travel as zeros) -- and every CTA zeroes a share of the output rows the
+// GEMM2 combine adds into.
+constexpr int kRpMaxRows = 8192;
+
+struct RecvPrologueParams {
+  const uint8_t* recv;         // [R, row_bytes]
+  int64_t R;
+  int H, E, world;
+  int32_t epoch;
+  const int32_t* flags;
+  int* err;
+  int64_t* lexp;               // [R] local expert of each row (-1: empty), for the return
+  float* lw;                   // [R]
+  int64_t* sorted_token;       // sorted position -> received row
+  int64_t* sorted_expert;
+  float* sorted_weight;
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* sf_offsets_a;
+  int32_t* sf_offsets_b;
+  int g4_a, g4_b, spread;
+  uint8_t* act_codes;
+  uint8_t* act_sf;
+  __nv_bfloat16* back_rows;    // [R, H], zeroed here
+};
+
+__host__ __device__ inline size_t recv_prologue_smem(int64_t R, int E) {
+  return static_cast<size_t>(R) * 12 + static_cast<size_t>(E) * 20 + 64;
+}
+
+__global__ void __launch_bounds__(256) ep_recv_prologue_kernel(const RecvPrologueParams p) {
+  extern __shared__ __align__(16) uint8_t rp_smem[];
+  const int R = static_cast<int>(p.R), E = p.E;
+  int* s_e = reinterpret_cast<int*>(rp_smem);
+  float* s_w = reinterpret_cast<float*>(s_e + R);
+  int* srow = reinterpret_cast<int*>(s_w + R);
+  int* cnt = srow + R;
+  int* off = cnt + E;
+  int* sfa = off + E;
+  int* sfb = sfa + E;
+  int* run = sfb + E;
+  pdl_trigger();
+  pdl_wait();
+  p2p_wait_flags(p.flags, 0, p.world, p.epoch, p.err);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool writer = blockIdx.x == 0;
+  const int64_t rb = ep_row_bytes(p.H);
+  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int r = tid; r < R; r += blockDim.x) {
+    const int32_t* meta = reinterpret_cast<const int32_t*>(p.recv + r * rb + rb - 8);
+    int e = meta[0];
+    const float w = __int_as_float(meta[1]);
+    if (e >= E || e < -1) {
+      if (writer && p.err) atomicCAS(p.err, 0, 0x201);
+      e = -1;
+    }
+    s_e[r] = e;
+    s_w[r] = w;
+    if (e >= 0) atomicAdd(&cnt[e], 1);
+    if (writer) { p.lexp[r] = e; p.lw[r] = w; }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int c_run = 0, a_run = 0, b_run = 0;
+    const int per = (E + 31) / 32;
+    const int q0 = lane * per;
+    for (int i = 0; i < per; ++i) {
+      const int q = q0 + i;
+      if (q < E) {
+        c_run += cnt[q];
+        a_run += static_cast<int>(act_sf_cosize(cnt[q], p.g4_a * 4, p.spread != 0));
+        b_run += static_cast<int>(act_sf_cosize(cnt[q], p.g4_b * 4, p.spread != 0));
+      }
+    }
+    int ci = c_run, ai = a_run, bi = b_run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int c2 = __shfl_up_sync(0xffffffffu, ci, o);
+      const int a2 = __shfl_up_sync(0xffffffffu, ai, o);
+      const int b2 = __shfl_up_sync(0xffffffffu, bi, o);
+      if (lane >= o) { ci += c2; ai += a2; bi += b2; }
+    }
+    int ce = ci - c_run, ae = ai - a_run, be = bi - b_run;
+    for (int i = 0; i < per; ++i) {
+      const int q = q0 + i;
+      if (q < E) {
+        off[q] = ce; run[q] = ce; sfa[q] = ae; sfb[q] = be;
+        if (writer) { p.counts[q] = cnt[q]; p.offsets[q] = ce; p.sf_offsets_a[q] = ae; p.sf_offsets_b[q] = be; }
+        ce += cnt[q];
+        ae += static_cast<int>(act_sf_cosize(cnt[q], p.g4_a * 4, p.spread != 0));
+        be += static_cast<int>(act_sf_cosize(cnt[q], p.g4_b * 4, p.spread != 0));
+      }
+    }
+    __syncwarp();
+    for (int i0 = 0; i0 < R; i0 += 32) {
+      const int r = i0 + lane;
+      const int e = r < R ? s_e[r] : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0) {
+        const int pos = run[e] + __popc(peers & ((1u << lane) - 1u));
+        srow[pos] = r;
+        if (writer) {
+          p.sorted_token[pos] = r;
+          p.sorted_expert[pos] = e;
+          p.sorted_weight[pos] = s_w[r];
+        }
+      }
+      __syncwarp();
+      if (e >= 0 && lane == __ffs(peers) - 1) run[e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int total = E > 0 ? off[E - 1] + cnt[E - 1] : 0;
+  if (writer) {
+    for (int i = total + tid; i < R; i += blockDim.x) {
+      p.sorted_token[i] = -1;
+      p.sorted_expert[i] = -1;
+      p.sorted_weight[i] = 0.0f;
+    }
+  }
+  const int H = p.H;
+  for (int pos = blockIdx.x; pos < total; pos += gridDim.x) {
+    const int r = srow[pos];
+    const int e = s_e[r];
+    const int j = pos - off[e];
+    const int64_t r_in = p.spread ? act_sf_row<true>(j) : j;
+    const uint8_t* src = p.recv + r * rb;
+    for (int v = tid; v < H / 16; v += blockDim.x)
+      reinterpret_cast<uint4*>(p.act_codes + static_cast<int64_t>(pos) * H)[v] = reinterpret_cast<const uint4*>(src)[v];
+    for (int a = tid; a < p.g4_a; a += blockDim.x)   // bytes past H/32 are the zero padding of the row
+      *reinterpret_cast<uint32_t*>(p.act_sf + sfa[e] + blocked_sf_offset(r_in, 4 * a, p.g4_a)) =
+          *reinterpret_cast<const uint32_t*>(src + H + 4 * a);
+  }
+  const int64_t n16 = static_cast<int64_t>(R) * H / 8;
+  uint4* z = reinterpret_cast<uint4*>(p.back_rows);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    z[i] = make_uint4(0, 0, 0, 0);
 }
 
 // Source: wait for every owner's return flag, then the combine of ep_combine_kernel over

@@ -675,7 +675,9 @@ __global__ void swiglu_kernel(const T* __restrict__ in, int64_t rows, int64_t n,
 // padded to a multiple of 16 bytes (H = 2880: 2992 bytes). Rows are quantised before they
 // are sent (quantisation is per row, so the codes equal the single-GPU ones).
 __host__ __device__ __forceinline__ int64_t ep_row_bytes(int H) {
-  return ((static_cast<int64_t>(H) + H / 32 + 8 + 15) / 16) * 16;
+  // the scale bytes are padded to whole k-atoms (4 groups) so a receiver can read them as
+  // 32-bit words
+  return ((static_cast<int64_t>(H) + (H / 32 + 3) / 4 * 4 + 8 + 15) / 16) * 16;
 }
 
 // Pack: entry p of the destination-sorted order (route_sort_kernel with divisor =

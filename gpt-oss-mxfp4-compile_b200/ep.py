@@ -177,7 +177,7 @@ class ExpertParallelExperts(nn.Module):
             ex.epoch += 1
             cap = self.capacity_tokens * self.top_k
             send_counts, pos_of = _ops.ep_p2p_dispatch(h, idx, w, self.num_experts, self.world_size, self.rank, cap,
-                                                       ex.peer_bases, ex.epoch)
+                                                       ex.local, ex.peer_bases, ex.epoch)
             _ops.ep_p2p_expert_forward(ex.local, self.world_size, self.rank, cap, ex.epoch, x.gate_up_proj_data,
                                        x.gate_up_proj_scales, x.gate_up_proj_bias.data, x.down_proj_data,
                                        x.down_proj_scales, x.down_proj_bias.data, self._back, self._ws,

@@ -556,7 +556,7 @@ def ep_p2p_buffer_bytes(world_size: int, capacity: int, hidden_size: int) -> int
 
 
 def ep_p2p_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, rank: int,
-                    capacity: int, peer_bases, epoch: int):
+                    capacity: int, local_base: int, peer_bases, epoch: int):
     """Quantised rows straight into the owners' receive rows + dispatch flags.
     Returns (send_counts i32 [W], pos_of i32 [T*k])."""
     _cuda(hidden, "hidden_states")
@@ -574,7 +574,7 @@ def ep_p2p_dispatch(hidden, router_indices, routing_weights, num_experts: int, w
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     _lib.call("gptoss_ep_p2p_dispatch", _p(hidden) if T else None, _p(router_indices) if T else None,
               _p(routing_weights) if T else None, T, k, int(num_experts), int(world_size), int(rank), H,
-              int(capacity), peer_bases.data_ptr(), int(epoch), send_counts.data_ptr(),
+              int(capacity), int(local_base), peer_bases.data_ptr(), int(epoch), send_counts.data_ptr(),
               pos_of.data_ptr() if T else None, ws.data_ptr(), ws.numel(), status_tensor(dev).data_ptr(),
               _stream(dev))
     return send_counts, pos_of

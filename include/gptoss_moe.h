@@ -301,9 +301,10 @@ int gptoss_ep_combine(const void* back_rows, int64_t num_back_rows, const int32_
 /* ---- Expert parallelism over peer memory (one node; no collective library on the data
  * path). Each rank allocates one exchange buffer of gptoss_ep_p2p_buffer_bytes(W, cap, H)
  * with gptoss_ipc_alloc (zeroed; the handle goes to every other rank, which maps it with
- * gptoss_ipc_open), and passes the W base addresses (its own at index `rank`) as a device
- * array `peer_bases`. Layout of a buffer: 2 * 64 int32 flags, receive rows [W][cap]
- * [row_bytes], return rows [W][cap][H] bf16. One layer, with `epoch` = 1, 2, ... per call
+ * gptoss_ipc_open), and passes its own base (`local_base`) and the W base addresses (its
+ * own at index `rank`) as a device array `peer_bases`. Layout of a buffer: a 1 KB header of
+ * flags and completion counters, receive rows [W][cap][row_bytes], return rows [W][cap][H]
+ * bf16. One layer, with `epoch` = 1, 2, ... per call
  * and identical on every rank:
  *   gptoss_ep_p2p_dispatch        quantised rows stored straight into the owners' receive
  *                                 rows, then dispatch flag[rank] raised on every peer;
@@ -322,9 +323,10 @@ int gptoss_ipc_free(void* ptr);
 size_t gptoss_ep_p2p_buffer_bytes(int world_size, int64_t capacity, int64_t hidden_size);
 int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
                            int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
-                           int64_t hidden_size, int64_t capacity, const uint64_t* peer_bases,
-                           int32_t epoch, int32_t* send_counts, int32_t* pos_of, void* workspace,
-                           size_t workspace_bytes, int32_t* status_dev, void* stream);
+                           int64_t hidden_size, int64_t capacity, void* local_base,
+                           const uint64_t* peer_bases, int32_t epoch, int32_t* send_counts,
+                           int32_t* pos_of, void* workspace, size_t workspace_bytes,
+                           int32_t* status_dev, void* stream);
 int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int64_t capacity,
                                  int32_t epoch, int num_local_experts, int64_t hidden_size,
                                  int64_t intermediate_size, const uint8_t* gate_up_data,

@@ -378,8 +378,9 @@ __all__.append("DequantCPULayer")
 # scatter_add_ does in w4a8_experts_forward on the CPU (fp32 accumulation in ascending
 # expert order, one bf16 rounding).
 def ep_row_bytes(H: int) -> int:
-    """[codes H | scales H/32 | pad | local expert i32 | weight f32], 16-byte multiple."""
-    return (H + H // 32 + 8 + 15) // 16 * 16
+    """[codes H | scales H/32 | pad | local expert i32 | weight f32], 16-byte multiple,
+    with at least the scale bytes of whole k-atoms (4 groups) before the meta."""
+    return (H + (H // 32 + 3) // 4 * 4 + 8 + 15) // 16 * 16
 
 
 def ep_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, capacity: int = 0):
