@@ -264,9 +264,31 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
 // activation chunks (and SPREAD activation scales) when the average expert holds at
 // most 16 rows; the reference-layout op uses 64-row chunks up to 48 rows per expert.
 bool pick_swap(int mode, int64_t rows, int experts, int64_t max_avg) {
-  if (mode == GPTOSS_GEMM_SWAP) return true;
+  if (mode == GPTOSS_GEMM_SWAP || mode == GPTOSS_GEMM_SWAP_WIDE) return true;
   if (mode == GPTOSS_GEMM_TOKENS_M) return false;
   return rows <= max_avg * experts;
+}
+
+// Tile orientation and activation-scale row layout of one expert forward. Weights-on-M
+// tiles multiply 16-row activation chunks (SPREAD scale rows) while experts hold few rows:
+// every chunk re-streams the expert's weight tiles, so an expert of 17..32 rows would read
+// its weights twice. Past kSpreadMaxAvg rows per expert on average the 64-row chunks
+// (reference scale rows; 16/32/64-row loads) take over, and past kSwapMaxAvg the
+// tokens-on-M tiles.
+constexpr int64_t kSpreadMaxAvg = 8;
+constexpr int64_t kSwapMaxAvg = 16;
+
+struct GemmLayout {
+  bool swap;
+  bool spread;
+};
+
+GemmLayout pick_layout(int mode, int64_t rows, int experts) {
+  if (mode == GPTOSS_GEMM_TOKENS_M) return {false, false};
+  if (mode == GPTOSS_GEMM_SWAP) return {true, true};
+  if (mode == GPTOSS_GEMM_SWAP_WIDE) return {true, false};
+  if (rows > kSwapMaxAvg * experts) return {false, false};
+  return {true, rows <= kSpreadMaxAvg * experts};
 }
 
 template <int EPI>
@@ -421,7 +443,7 @@ int stage_route_quant(const void* hidden, const int64_t* ridx, const float* rw, 
 
 // Stage 2: GEMM1 + bias + SwiGLU + FP8 requantisation.
 int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit,
-                const WsPtrs& w, bool swap, int* status, const DeviceInfo& di, int dev, cudaStream_t st,
+                const WsPtrs& w, GemmLayout lay, int* status, const DeviceInfo& di, int dev, cudaStream_t st,
                 int prefetch_tiles = 0) {
   const int64_t Kh = pad128(H), Ki = pad128(I);
   GemmJob g1{};
@@ -432,15 +454,15 @@ int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g1.p.out = w.inter_codes; g1.p.ld_out = I; g1.p.bias = wt.gu_bias; g1.p.out_sf = w.inter_sf;
   g1.p.out_sf_offsets = w.sfoff_b; g1.p.out_g4 = static_cast<int>(Ki / 128); g1.p.out_features = static_cast<int>(I);
   g1.p.swiglu_alpha = sw_alpha; g1.p.swiglu_limit = sw_limit;
-  g1.p.prefetch_tiles = swap ? prefetch_tiles : 0;
+  g1.p.prefetch_tiles = lay.swap ? prefetch_tiles : 0;
   g1.sfa_bytes = w.act_sf_cap;
   g1.sfb_bytes = wt.ldb_gu * E;
-  return run_gemm<kEpiGemm1>(g1, swap, swap, di, dev, st);
+  return run_gemm<kEpiGemm1>(g1, lay.swap, lay.spread, di, dev, st);
 }
 
 // Stage 3: GEMM2 + bias, x routing weight, bf16 scatter-add into out (accumulates).
 int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, void* out, const WsPtrs& w,
-                bool swap, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+                GemmLayout lay, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
   const int64_t Ki = pad128(I);
   GemmJob g2{};
   g2.act = w.inter_codes; g2.act_rows = A; g2.lda = I; g2.wgt = wt.dn_data;
@@ -450,7 +472,7 @@ int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g2.p.out = out; g2.p.ld_out = H; g2.p.bias = wt.dn_bias; g2.p.token_idx = w.sorted_token; g2.p.row_weights = w.sorted_weight;
   g2.sfa_bytes = w.inter_sf_cap;
   g2.sfb_bytes = wt.ldb_dn * E;
-  return run_gemm<kEpiGemm2>(g2, swap, swap, di, dev, st);
+  return run_gemm<kEpiGemm2>(g2, lay.swap, lay.spread, di, dev, st);
 }
 
 // ---------------------------------------------------------------- decode-sized prologue
@@ -519,14 +541,14 @@ int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, i
                      uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
                      cudaStream_t st, const RouterArgs* ra = nullptr) {
   const WsPtrs w = ws_ptrs(ws, L);
-  const bool swap = pick_swap(mode, T * k, E, 16);
+  const GemmLayout lay = pick_layout(mode, T * k, E);
   size_t smem = 0;
   int slice = 0;
   // While the one-launch decode prologue runs on kDpCluster SMs, GEMM1 (launched behind it
   // with programmatic serialisation) pulls its first weight tiles into L2.
   int prefetch = 0;
   if (decode_prologue_fits(T, k, E, H, ra != nullptr, &smem, &slice)) {
-    GPTOSS_TRY(run_decode_prologue(hidden, ra, ridx, rw, T, k, E, H, I, w, swap, out, status, smem, slice, dev, st));
+    GPTOSS_TRY(run_decode_prologue(hidden, ra, ridx, rw, T, k, E, H, I, w, lay.spread, out, status, smem, slice, dev, st));
     prefetch = kPrefetchTilesAfterPrologue;
   } else {
     if (ra != nullptr) {
@@ -535,12 +557,12 @@ int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, i
       ridx = ra->ridx_out;
       rw = ra->rw_out;
     }
-    GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, swap, status, st));
+    GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, lay.spread, status, st));
     if (ra == nullptr)
       GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
   }
-  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, swap, status, di, dev, st, prefetch));
-  return stage_gemm2(T * k, E, H, I, wt, out, w, swap, status, di, dev, st);
+  GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, lay, status, di, dev, st, prefetch));
+  return stage_gemm2(T * k, E, H, I, wt, out, w, lay, status, di, dev, st);
 }
 
 int check_dims(int64_t T, int k, int E, int64_t H, int64_t I) {
@@ -744,7 +766,7 @@ int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t ld
   GPTOSS_CHECK(n > 0 && n % 8 == 0 && n < (1LL << 31), "fp4_group_mm: N=%lld must be a positive multiple of 8",
                (long long)n);
   GPTOSS_CHECK(m_total >= 0 && lda > 0 && lda <= k && lda % 16 == 0, "fp4_group_mm: a must be [M, lda<=K], lda %% 16 == 0");
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "fp4_group_mm: bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "fp4_group_mm: bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(b, "b", &di));
   GPTOSS_CHECK(aligned(b, 32), "fp4_group_mm: b must be 32-byte aligned");
@@ -784,7 +806,7 @@ int gptoss_moe_experts_forward(const void* hidden, const int64_t* router_indices
                                float swiglu_alpha, float swiglu_limit, void* out, void* workspace,
                                size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
   ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
@@ -813,7 +835,7 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, cons
                              void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
                              void* stream) {
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   GPTOSS_CHECK(hidden_size % 8 == 0, "hidden size must be a multiple of 8");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
@@ -866,7 +888,7 @@ int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices, co
   if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
   return stage_route_quant(hidden, router_indices, routing_weights, num_tokens, top_k, num_experts, hidden_size,
                            intermediate_size, ws_ptrs(static_cast<uint8_t*>(workspace), L),
-                           pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
+                           pick_layout(gemm_mode, num_tokens * top_k, num_experts).spread,
                            status_dev ? status_dev : di.status_sink, static_cast<cudaStream_t>(stream));
 }
 
@@ -875,7 +897,7 @@ int gptoss_moe_gemm1(int64_t num_tokens, int top_k, int num_experts, int64_t hid
                      const float* gate_up_bias, float swiglu_alpha, float swiglu_limit, void* workspace,
                      size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
   GPTOSS_CHECK(gate_up_scales && gate_up_bias && aligned(gate_up_data, 32) && aligned(gate_up_scales, 16) &&
@@ -891,7 +913,7 @@ int gptoss_moe_gemm1(int64_t num_tokens, int top_k, int num_experts, int64_t hid
   ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias, nullptr, nullptr, 0, nullptr};
   return stage_gemm1(num_tokens * top_k, num_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit,
                      ws_ptrs(static_cast<uint8_t*>(workspace), L),
-                     pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
+                     pick_layout(gemm_mode, num_tokens * top_k, num_experts),
                      status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream));
 }
 
@@ -900,7 +922,7 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
                      void* out, void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
                      void* stream) {
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(down_data, "down_proj_data", &di));
   GPTOSS_CHECK(down_scales && down_bias && aligned(down_data, 32) && aligned(down_scales, 16) && ldb_down % 16 == 0 &&
@@ -915,7 +937,7 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
   ExpertWeights w{nullptr, nullptr, 0, nullptr, down_data, down_scales, ldb_down, down_bias};
   return stage_gemm2(num_tokens * top_k, num_experts, hidden_size, intermediate_size, w, out,
                      ws_ptrs(static_cast<uint8_t*>(workspace), L),
-                     pick_swap(gemm_mode, num_tokens * top_k, num_experts, 16),
+                     pick_layout(gemm_mode, num_tokens * top_k, num_experts),
                      status_dev ? status_dev : di.status_sink, di, dev, static_cast<cudaStream_t>(stream));
 }
 
@@ -927,7 +949,7 @@ int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router
                                        const float* down_bias, float swiglu_alpha, float swiglu_limit, void* out,
                                        int gemm_mode, int32_t* status_dev, void* stream) {
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
   ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
@@ -1027,7 +1049,7 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
                              float swiglu_alpha, float swiglu_limit, void* back_rows, void* workspace,
                              size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
   GPTOSS_TRY(check_dims(num_rows, 1, num_local_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
   ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
@@ -1047,7 +1069,7 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
   int* status = status_dev ? status_dev : di.status_sink;
   int64_t* lexp = reinterpret_cast<int64_t*>(ws + L.router_idx);
   float* lw = reinterpret_cast<float*>(ws + L.router_w);
-  const bool swap = pick_swap(gemm_mode, num_rows, num_local_experts, 16);
+  const GemmLayout lay = pick_layout(gemm_mode, num_rows, num_local_experts);
   const int H = static_cast<int>(hidden_size);
   const int64_t Kh = pad128(hidden_size), Ki = pad128(intermediate_size);
   const int ublocks = static_cast<int>(std::min<int64_t>((num_rows + 255) / 256, 4 * di.sms));
@@ -1060,19 +1082,19 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
   rp.sf_offsets_a = p.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = H / 32; rp.sf_a = p.act_sf;
   rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
   rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
-  rp.spread = swap ? 1 : 0;
+  rp.spread = lay.spread ? 1 : 0;
   rp.allow_empty = 1;
   rp.err = status;
   GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
   GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(num_rows)), dim3(256), 0, st, recv_rows,
                         num_rows, H, static_cast<const int64_t*>(p.sorted_token),
                         static_cast<const int64_t*>(p.sorted_expert), static_cast<const int32_t*>(p.offsets),
-                        static_cast<const int32_t*>(p.sfoff_a), static_cast<int>(Kh / 128), swap ? 1 : 0,
+                        static_cast<const int32_t*>(p.sfoff_a), static_cast<int>(Kh / 128), lay.spread ? 1 : 0,
                         p.act_codes, p.act_sf));
   GPTOSS_CUDA(cudaMemsetAsync(back_rows, 0, static_cast<size_t>(num_rows * hidden_size) * sizeof(__nv_bfloat16), st));
   GPTOSS_TRY(stage_gemm1(num_rows, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p,
-                         swap, status, di, dev, st));
-  return stage_gemm2(num_rows, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, swap, status, di,
+                         lay, status, di, dev, st));
+  return stage_gemm2(num_rows, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, lay, status, di,
                      dev, st);
 }
 
@@ -1197,7 +1219,7 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
                "ep_p2p_expert_forward: bad world_size / rank");
   const int64_t R = capacity * world_size;
   GPTOSS_TRY(check_dims(R, 1, num_local_experts, hidden_size, intermediate_size));
-  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 2, "bad gemm_mode");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
   GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
   ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
@@ -1216,7 +1238,8 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
   int* status = status_dev ? status_dev : di.status_sink;
   int64_t* lexp = reinterpret_cast<int64_t*>(ws + L.router_idx);
   float* lw = reinterpret_cast<float*>(ws + L.router_w);
-  const bool swap = pick_swap(gemm_mode, R, num_local_experts, 16);
+  // rows expected here under balanced routing: W sources x capacity / W
+  const GemmLayout lay = pick_layout(gemm_mode, capacity, num_local_experts);
   const int H = static_cast<int>(hidden_size);
   const int64_t rb = ep_row_bytes(H);
   const int64_t Kh = pad128(hidden_size), Ki = pad128(intermediate_size);
@@ -1242,7 +1265,7 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
     rq.flags = flags; rq.err = status; rq.lexp = lexp; rq.lw = lw;
     rq.sorted_token = p.sorted_token; rq.sorted_expert = p.sorted_expert; rq.sorted_weight = p.sorted_weight;
     rq.counts = p.counts; rq.offsets = p.offsets; rq.sf_offsets_a = p.sfoff_a; rq.sf_offsets_b = p.sfoff_b;
-    rq.g4_a = static_cast<int>(Kh / 128); rq.g4_b = static_cast<int>(Ki / 128); rq.spread = swap ? 1 : 0;
+    rq.g4_a = static_cast<int>(Kh / 128); rq.g4_b = static_cast<int>(Ki / 128); rq.spread = lay.spread ? 1 : 0;
     rq.act_codes = p.act_codes; rq.act_sf = p.act_sf; rq.back_rows = static_cast<__nv_bfloat16*>(back_rows);
     const int grid = static_cast<int>(std::min<int64_t>(di.sms, std::max<int64_t>(R, 1)));
     GPTOSS_TRY(launch_pdl(ep_recv_prologue_kernel, dim3(grid), dim3(256), rp_smem, st, rq));
@@ -1259,19 +1282,19 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
     rp.sf_offsets_a = p.sfoff_a; rp.g4_a = static_cast<int>(Kh / 128); rp.groups_a = H / 32; rp.sf_a = p.act_sf;
     rp.sf_offsets_b = p.sfoff_b; rp.g4_b = static_cast<int>(Ki / 128);
     rp.groups_b = static_cast<int>(intermediate_size / 32); rp.sf_b = p.inter_sf;
-    rp.spread = swap ? 1 : 0;
+    rp.spread = lay.spread ? 1 : 0;
     rp.allow_empty = 1;
     rp.err = status;
     GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(num_local_experts), dim3(1024), 0, st, rp));
     GPTOSS_TRY(launch_pdl(ep_gather_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st, recv, R, H,
                           static_cast<const int64_t*>(p.sorted_token), static_cast<const int64_t*>(p.sorted_expert),
                           static_cast<const int32_t*>(p.offsets), static_cast<const int32_t*>(p.sfoff_a),
-                          static_cast<int>(Kh / 128), swap ? 1 : 0, p.act_codes, p.act_sf));
+                          static_cast<int>(Kh / 128), lay.spread ? 1 : 0, p.act_codes, p.act_sf));
     GPTOSS_CUDA(cudaMemsetAsync(back_rows, 0, static_cast<size_t>(R * hidden_size) * sizeof(__nv_bfloat16), st));
   }
-  GPTOSS_TRY(stage_gemm1(R, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p, swap,
+  GPTOSS_TRY(stage_gemm1(R, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p, lay,
                          status, di, dev, st, prefetch));
-  GPTOSS_TRY(stage_gemm2(R, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, swap, status, di,
+  GPTOSS_TRY(stage_gemm2(R, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, lay, status, di,
                          dev, st));
   return launch_pdl(ep_return_p2p_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st,
                     static_cast<const __nv_bfloat16*>(back_rows), static_cast<const int64_t*>(lexp), capacity,

@@ -87,7 +87,12 @@ struct GemmConfig {
   static constexpr int kTileM = PAIR ? 2 * kActRows : kActRows;   // activation rows per tile
   static constexpr int kMmaM = PAIR ? 256 : 128;
   static constexpr int kMmaN = SWAP ? kActRows : kWgtRows;
-  static constexpr int kStages = SWAP ? (SPREAD ? 11 : 8) : (PAIR ? 7 : 5);
+  // K blocks (128 codes each) per pipeline stage. The TMA engine completes about one
+  // mbarrier transaction group per ~300 ns per SM whatever its size (measured on B200:
+  // 8 KB fp4 weight boxes stream at ~4 TB/s one per stage and ~6.7 TB/s two per stage,
+  // at any ring depth), so weights-on-M tiles load two k blocks behind each barrier.
+  static constexpr int kSubs = SWAP ? 2 : 1;
+  static constexpr int kStages = SWAP ? (SPREAD ? 5 : 4) : (PAIR ? 7 : 5);
   static constexpr int kAccBufs = SWAP ? 4 : 2;
   static constexpr int kAccCols = kMmaN;              // fp32 columns per accumulator
   static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
@@ -95,15 +100,18 @@ struct GemmConfig {
   static constexpr uint32_t kActTileBytes = kActRows * 128;
   static constexpr uint32_t kSfActBytes = 512;
   static constexpr uint32_t kSfWgtBytes = 512 * kWgtSfChunks;
-  static constexpr uint32_t kStageBytes =
+  static constexpr uint32_t kSubBytes =   // one k block: weights | activations | scales
       ((kWgtTileBytes + kActTileBytes + kSfActBytes + kSfWgtBytes + 1023) / 1024) * 1024;
+  static constexpr uint32_t kStageBytes = kSubs * kSubBytes;
   static constexpr uint32_t kTmemAccCols = kAccBufs * kAccCols;
   static constexpr uint32_t kSfActCol = kTmemAccCols;           // 4 columns
   static constexpr uint32_t kSfWgtCol = kTmemAccCols + 4;       // 4 per chunk
   static constexpr uint32_t kTmemCols = (kSfWgtCol + 4 * kWgtSfChunks) <= 128 ? 128
                                         : (kSfWgtCol + 4 * kWgtSfChunks) <= 256 ? 256 : 512;
   static constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + 2 * kAccBufs + 1) + 16;
-  static constexpr uint32_t kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 2048;
+  static constexpr uint32_t kEpiStageBytes = SWAP ? 16384 : 0;   // weights-on-M epilogue staging
+  static constexpr uint32_t kSmemBytes =
+      1024 + kStages * kStageBytes + ((kBarrierBytes + 127) & ~127u) + kEpiStageBytes + 2048;
   // Epilogue warps: one warpgroup for weights-on-M tiles (their GEMM1 epilogue reduces
   // across the warpgroup); tokens-on-M tiles give each warpgroup one 64-column slice, so
   // three warps share every TMEM lane quarter and hide each other's latency.
@@ -148,7 +156,6 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
   __shared__ int s_chunk_prefix[kMaxExpertsGemm + 1];
   __shared__ int s_chunks[kMaxExpertsGemm];
   __shared__ uint32_t s_tmem_base;
-  __shared__ float s_amax[4][32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -158,6 +165,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
   auto accf_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + b); };
   auto acce_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + C::kAccBufs + b); };
   const uint32_t drain_bar = bar_base + 8u * (2 * C::kStages + 2 * C::kAccBufs);
+  const uint32_t epi_base = bar_base + ((C::kBarrierBytes + 127u) & ~127u);   // epilogue staging
 
   pdl_trigger();
   // ---- barriers, TMEM and descriptor prefetch overlap the previous kernel's tail
@@ -274,30 +282,33 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         const int arows = act_rows_of(e, ch);
         const CUtensorMap* amap = arows == 16 ? &tm_aux1 : (arows == 32 ? &tm_aux0 : &tm_act);
         const uint32_t tx = (arows * 128u + C::kWgtRowsCta * 64 + C::kSfActBytes + 512u * nwchunks) * (PAIR ? 2u : 1u);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb0 = 0; kb0 < p.num_kb; kb0 += C::kSubs) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.err, kDevTimeoutProducer)) { ok = false; break; }
-          const uint32_t sb = smem_base + stage * C::kStageBytes;
-          const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
-          const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
-          if constexpr (PAIR) {
-            // every load of both CTAs completes on the even CTA's full barrier
-            const uint32_t fb = dsmem_map(full_bar(stage), 0);
-            if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
-            tma_load_2d_pair(s_a, &tm_act, fb, kb * 128, act_row0, pol_a);
-            tma_load_3d_pair(s_w, &tm_wgt, fb, kb * 128, wgt_row0, e, pol_w);
-            tma_load_2d_pair(s_sfa, &tm_aux0, fb, 0, static_cast<int32_t>((sfa_off + kb * 512) >> 8), pol_a);
-            for (int c = 0; c < nwchunks; ++c)
-              tma_load_2d_pair(s_sfw + 512u * c, &tm_aux1, fb, 0,
-                               static_cast<int32_t>((sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512) >> 8),
-                               pol_w);
-          } else {
-            mbar_arrive_expect_tx(full_bar(stage), tx);
-            tma_load_2d(s_a, amap, full_bar(stage), kb * 128, act_row0, pol_a);
-            tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
-            bulk_load(s_sfa, p.sfa + sfa_off + kb * 512, 512, full_bar(stage), pol_a);
-            for (int c = 0; c < nwchunks; ++c)
-              bulk_load(s_sfw + 512u * c, p.sfb + sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512, 512,
-                        full_bar(stage), pol_w);
+          const int nsub = min(C::kSubs, p.num_kb - kb0);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), tx * static_cast<uint32_t>(nsub));
+          for (int j = 0; j < nsub; ++j) {
+            const int kb = kb0 + j;
+            const uint32_t sb = smem_base + stage * C::kStageBytes + j * C::kSubBytes;
+            const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
+            const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
+            if constexpr (PAIR) {
+              // every load of both CTAs completes on the even CTA's full barrier
+              const uint32_t fb = dsmem_map(full_bar(stage), 0);
+              tma_load_2d_pair(s_a, &tm_act, fb, kb * 128, act_row0, pol_a);
+              tma_load_3d_pair(s_w, &tm_wgt, fb, kb * 128, wgt_row0, e, pol_w);
+              tma_load_2d_pair(s_sfa, &tm_aux0, fb, 0, static_cast<int32_t>((sfa_off + kb * 512) >> 8), pol_a);
+              for (int c = 0; c < nwchunks; ++c)
+                tma_load_2d_pair(s_sfw + 512u * c, &tm_aux1, fb, 0,
+                                 static_cast<int32_t>((sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512) >> 8),
+                                 pol_w);
+            } else {
+              tma_load_2d(s_a, amap, full_bar(stage), kb * 128, act_row0, pol_a);
+              tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
+              bulk_load(s_sfa, p.sfa + sfa_off + kb * 512, 512, full_bar(stage), pol_a);
+              for (int c = 0; c < nwchunks; ++c)
+                bulk_load(s_sfw + 512u * c, p.sfb + sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512, 512,
+                          full_bar(stage), pol_w);
+            }
           }
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
@@ -336,40 +347,49 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         const uint32_t t_sfa = tmem_base + C::kSfActCol;
         const uint32_t t_sfw = tmem_base + C::kSfWgtCol;
         const uint32_t mma_n = SWAP ? static_cast<uint32_t>(act_rows_of(e, ch)) : static_cast<uint32_t>(C::kMmaN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        // The issue loop is lean on purpose: one thread issues every tcgen05 op of the CTA
+        // and small-N block-scaled MMAs cost ~75 cycles of issue each, so descriptors and
+        // the instruction word are formed once per tile / stage and advanced by adds
+        // (a 32-byte K step is +2 in the descriptor's 16-byte address field).
+        const uint32_t idesc0 = SWAP ? idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, 0, 0)
+                                     : idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, 0, 0);
+        const uint32_t sf_a_t = SWAP ? t_sfw : t_sfa;                       // scales of MMA operand A
+        const uint32_t sf_b_t = SWAP ? t_sfa + ashift : t_sfw + wshift;     // scales of MMA operand B
+        for (int kb0 = 0; kb0 < p.num_kb; kb0 += C::kSubs) {
           if (!mbar_wait(full_bar(stage), phase, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sb = smem_base + stage * C::kStageBytes;
-          const uint32_t s_w = sb, s_a = sb + C::kWgtTileBytes;
-          const uint32_t s_sfa = s_a + C::kActTileBytes, s_sfw = s_sfa + C::kSfActBytes;
-          if constexpr (PAIR) {
-            // each CTA's scale chunks go from its own shared memory into its own TMEM
-            tc_cp_32x128b_warpx4_pair(t_sfa, desc_sf_block(s_sfa));
+          const int nsub = min(C::kSubs, p.num_kb - kb0);
+          const uint32_t sb0 = smem_base + stage * C::kStageBytes;
+          const uint64_t dw0 = desc_kmajor_sw128(sb0);
+          const uint64_t da0 = desc_kmajor_sw128(sb0 + C::kWgtTileBytes);
+          const uint64_t dsa0 = desc_sf_block(sb0 + C::kWgtTileBytes + C::kActTileBytes);
+          const uint64_t dsw0 = dsa0 + (C::kSfActBytes >> 4);
 #pragma unroll
-            for (int c = 0; c < C::kWgtSfChunks; ++c)
-              tc_cp_32x128b_warpx4_pair(t_sfw + 4u * c, desc_sf_block(s_sfw + 512u * c));
-          } else {
-            tc_cp_32x128b_warpx4(t_sfa, desc_sf_block(s_sfa));
-#pragma unroll
-            for (int c = 0; c < C::kWgtSfChunks; ++c)
-              tc_cp_32x128b_warpx4(t_sfw + 4u * c, desc_sf_block(s_sfw + 512u * c));
-          }
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t da = desc_kmajor_sw128(s_a + 32u * k);
-            const uint64_t dw = desc_kmajor_sw128(s_w + 32u * k);
-            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+          for (int j = 0; j < C::kSubs; ++j) {
+            if (j >= nsub) break;
+            const uint64_t joff = (static_cast<uint64_t>(j) * C::kSubBytes) >> 4;
             if constexpr (PAIR) {
-              mma_mxf8f6f4_pair(d_tmem, da, dw, idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, k, k), t_sfa, t_sfw + wshift,
-                                acc);
-            } else if constexpr (SWAP) {
-              // A = weights (E2M1), B = activations (E4M3)
-              mma_mxf8f6f4(d_tmem, dw, da, idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, k, k),
-                           t_sfw, t_sfa + ashift, acc);
+              // each CTA's scale chunks go from its own shared memory into its own TMEM
+              tc_cp_32x128b_warpx4_pair(t_sfa, dsa0 + joff);
+#pragma unroll
+              for (int c = 0; c < C::kWgtSfChunks; ++c) tc_cp_32x128b_warpx4_pair(t_sfw + 4u * c, dsw0 + joff + 32u * c);
             } else {
-              // A = activations (E4M3), B = weights (E2M1)
-              mma_mxf8f6f4(d_tmem, da, dw, idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, k, k),
-                           t_sfa, t_sfw + wshift, acc);
+              tc_cp_32x128b_warpx4(t_sfa, dsa0 + joff);
+#pragma unroll
+              for (int c = 0; c < C::kWgtSfChunks; ++c) tc_cp_32x128b_warpx4(t_sfw + 4u * c, dsw0 + joff + 32u * c);
+            }
+            const uint64_t dw = dw0 + joff, da = da0 + joff;
+            // operand A / B descriptors: weights are A in SWAP tiles, activations otherwise
+            const uint64_t dA = SWAP ? dw : da, dB = SWAP ? da : dw;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t idesc = idesc0 | (static_cast<uint32_t>(k) << 4) | (static_cast<uint32_t>(k) << 29);
+              const uint32_t acc = (kb0 | j | k) != 0 ? 1u : 0u;
+              if constexpr (PAIR) {
+                mma_mxf8f6f4_pair(d_tmem, dA + 2u * k, dB + 2u * k, idesc, sf_a_t, sf_b_t, acc);
+              } else {
+                mma_mxf8f6f4(d_tmem, dA + 2u * k, dB + 2u * k, idesc, sf_a_t, sf_b_t, acc);
+              }
             }
           }
           if constexpr (PAIR) tc_commit_pair(empty_bar(stage), 0x3);   // both CTAs' producers
@@ -390,6 +410,14 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
     }
   } else {
     // ================================================================ epilogue
+    // staging of the weights-on-M GEMM1 / GEMM2 epilogue: kEpiTok activation rows x kEpiFeat
+    // fp32 values per buffer, double-buffered when two fit
+    constexpr int kEpiTok = C::kActRows < 32 ? C::kActRows : 32;
+    constexpr int kEpiFeat = EPI == kEpiGemm1 ? C::kWgtRows / 2 : C::kWgtRows;
+    constexpr uint32_t kEpiBufBytes = static_cast<uint32_t>(kEpiTok * kEpiFeat * 4);
+    constexpr int kEpiBufs = 2 * kEpiBufBytes <= C::kEpiStageBytes ? 2 : 1;
+    static_assert(!SWAP || EPI == kEpiPlain || kEpiBufBytes <= C::kEpiStageBytes, "epilogue staging too small");
+    float* const epi_f = reinterpret_cast<float*>(smem_raw + (epi_base - smem_u32(smem_raw)));
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int wg = (warp - 2) >> 2;         // epilogue warpgroup
     constexpr int kWgs = C::kEpiWarps / 4;
@@ -403,8 +431,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
       const uint32_t acc_phase = static_cast<uint32_t>(local / C::kAccBufs) & 1u;
       if (ok) ok = mbar_wait(accf_bar(b), acc_phase, p.err, kDevTimeoutEpilogue);
       if (!ok) {
-        if constexpr (SWAP && EPI == kEpiGemm1) {
-          for (int c = 0; c < 2 * C::kColChunks; ++c) asm volatile("bar.sync 1, 128;" ::: "memory");
+        if constexpr (SWAP && EPI != kEpiPlain) {
+          for (int c = 0; c < C::kColChunks * (kEpiBufs == 1 ? 2 : 1); ++c) asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         continue;
       }
@@ -518,12 +546,11 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
             }  // vrow && nb < N
           }
         }
-      } else {
+      } else if constexpr (EPI == kEpiPlain) {
         // thread <-> weight row (output feature); column j = activation row ch*64 + j,
         // walked in two 32-column halves.
         const int wrow_i = nt * C::kWgtRows + 32 * q + lane;    // weight row / feature
         const bool vcol = wrow_i < p.N;
-        const float bsv = (EPI != kEpiPlain && vcol) ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
 #pragma unroll 1
         for (int c = 0; c < C::kColChunks; ++c) {
           const int a0 = ch * C::kActRows + c * 32;             // first row inside expert
@@ -535,7 +562,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
             tmem_ld_32x32b_x32(t_acc + c * 32, r);
             tmem_ld_wait();
           }
-          if constexpr (EPI == kEpiPlain) {
+          {
             if (live) {
               const float alpha = p.alphas ? p.alphas[e] : 1.0f;
               __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
@@ -546,81 +573,139 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
                       __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
               }
             }
-          } else if constexpr (EPI == kEpiGemm2) {
-            if (live) {
-              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
-#pragma unroll 4
-              for (int j = 0; j < 32; ++j) {
-                if (a0 + j >= a_end) break;                     // warp-uniform
-                const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
-                const int64_t tok = p.token_idx[grow];
-                const float wr = p.row_weights[grow];
-                const float y = __fmul_rn(__fadd_rn(bf16_round(__uint_as_float(r[j])), bsv), wr);
-                const float yo = __shfl_xor_sync(0xffffffffu, y, 1);
-                if ((lane & 1) == 0 && vcol) {
-                  __nv_bfloat16* dst = o + tok * p.ld_out + wrow_i;
-                  if (wrow_i + 1 < p.N) atomicAdd(reinterpret_cast<__nv_bfloat162*>(dst), __floats2bfloat162_rn(y, yo));
-                  else atomicAdd(dst, __float2bfloat16_rn(y));
-                }
-              }
-            }
-          } else {  // kEpiGemm1: lanes (2f, 2f+1) hold gate / up of feature f
-            const int f = wrow_i >> 1;                          // intermediate feature
-            const int grp = f >> 5;                             // quant group (2 warps)
-            float hv[32];
-            const int nv = min(32, a_end - a0);                 // valid rows, warp-uniform
-            if (live) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (j < nv) {
-                  const float v = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
-                  const float up = __shfl_xor_sync(0xffffffffu, v, 1);
-                  hv[j] = swiglu_pair(v, up, p.swiglu_alpha, p.swiglu_limit);   // valid on even lanes
-                }
-              }
-              // group absmax over the 32 features held by the even lanes of warps (q, q^1)
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (j >= nv) break;
-                float a = (lane & 1) == 0 ? fabsf(hv[j]) : 0.0f;
-                if (hv[j] != hv[j] && (lane & 1) == 0) a = hv[j];
-#pragma unroll
-                for (int o2 = 2; o2 < 32; o2 <<= 1) {
-                  const float ob = __shfl_xor_sync(0xffffffffu, a, o2);
-                  a = (ob > a || ob != ob) ? ob : a;
-                }
-                if (lane == 0) s_amax[q][j] = a;
-              }
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (live) {
-              const int qp = q ^ 1;
-              uint8_t* codes_out = static_cast<uint8_t*>(p.out);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (j >= nv) break;
-                const float a_self = s_amax[q][j], a_pair = s_amax[qp][j];
-                const float amax = (a_pair > a_self || a_pair != a_pair) ? a_pair : a_self;
-                const uint32_t rb = ue8m0_rounded_bits(amax);
-                const float qv = clamp_fp8(__fmul_rn(hv[j], inv_scale(scale_from_bits(rb))));
-                const uint16_t c2 = cvt_e4m3x2(qv, 0.0f);
-                const int64_t grow = static_cast<int64_t>(row0) + a0 + j;
-                if ((lane & 1) == 0 && vcol && f < p.out_features)
-                  codes_out[grow * p.ld_out + f] = static_cast<uint8_t>(c2 & 0xFFu);
-                if (lane == 0 && (q & 1) == 0 && f < p.out_features) {
-                  uint8_t* sfb_e = p.out_sf + p.out_sf_offsets[e];
-                  const int64_t srow_j = act_sf_row<SPREAD>(a0 + j);
-                  sfb_e[blocked_sf_offset(srow_j, grp, p.out_g4)] = static_cast<uint8_t>((rb >> 23) & 0xFFu);
-                  // the K padding groups of the row's last k-atom read as zero scales in GEMM2
-                  if (grp == (p.out_features >> 5) - 1)
-                    for (int gz = p.out_features >> 5; gz < 4 * p.out_g4; ++gz)
-                      sfb_e[blocked_sf_offset(srow_j, gz, p.out_g4)] = 0;
-                }
-              }
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
           }
         }
+      } else {
+        // Weights-on-M GEMM1 / GEMM2 epilogue in two passes per chunk of kEpiTok activation
+        // rows. Pass 1 (thread <-> weight row = TMEM lane): accumulator -> bf16 rounding +
+        // bias (GEMM1: SwiGLU of the gate/up lane pair, the two lanes splitting the rows)
+        // into shared memory, and the accumulator goes back to the MMA right after its last
+        // load. Pass 2 regroups by activation row: GEMM1 quantises each 32-feature group in a
+        // team of 4 lanes (8 features each, one 8-byte store); GEMM2 scales 8 outputs by the
+        // routing weight and adds them with one 16-byte bf16x2 reduction.
+        const int wrow_i = nt * C::kWgtRows + 32 * q + lane;    // weight row
+        const bool vcol = wrow_i < p.N;
+        const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
+        const int a_end = min(m_e, ch * C::kActRows + C::kActRows);
+        const int etid = static_cast<int>(threadIdx.x) - 64;   // 0..127
+#pragma unroll 1
+        for (int c = 0; c < C::kColChunks; ++c) {
+          const int a0 = ch * C::kActRows + c * kEpiTok;        // first row inside expert
+          const bool live = a0 < a_end;                         // uniform over the CTA
+          const int nv = min(kEpiTok, a_end - a0);
+          float* sh = epi_f + ((local * C::kColChunks + c) % kEpiBufs) * (kEpiBufBytes / 4);
+          if (live) {
+            uint32_t r[kEpiTok];
+            __syncwarp();
+            if constexpr (kEpiTok == 16) tmem_ld_32x32b_x16(t_acc + c * kEpiTok, r);
+            else tmem_ld_32x32b_x32(t_acc + c * kEpiTok, r);
+            tmem_ld_wait();
+            if (c == C::kColChunks - 1 || a0 + kEpiTok >= a_end) {   // last load of this tile
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(acce_bar(b));
+            }
+            if constexpr (EPI == kEpiGemm1) {
+              // lanes (2f, 2f+1) hold gate / up of feature f: the even lane finishes rows
+              // [0, kHalf), the odd lane rows [kHalf, kEpiTok), one exchange per row pair
+              constexpr int kHalf = kEpiTok / 2;
+              const bool odd = (lane & 1) != 0;
+              const int fl = (32 * q + lane) >> 1;
+#pragma unroll
+              for (int j = 0; j < kHalf; ++j) {
+                const float vlo = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
+                const float vhi = __fadd_rn(bf16_round(__uint_as_float(r[kHalf + j])), bsv);
+                const float other = __shfl_xor_sync(0xffffffffu, odd ? vlo : vhi, 1);
+                const float h = odd ? swiglu_pair(other, vhi, p.swiglu_alpha, p.swiglu_limit)
+                                    : swiglu_pair(vlo, other, p.swiglu_alpha, p.swiglu_limit);
+                sh[(odd ? kHalf + j : j) * kEpiFeat + fl] = h;
+              }
+            } else {
+              const int fl = 32 * q + lane;
+#pragma unroll
+              for (int j = 0; j < kEpiTok; ++j) sh[j * kEpiFeat + fl] = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (live) {
+            if constexpr (EPI == kEpiGemm1) {
+              constexpr int kGroups = kEpiFeat / 32;                // quantisation groups per row
+              uint8_t* codes_out = static_cast<uint8_t*>(p.out);
+              uint8_t* sfb_e = p.out_sf + p.out_sf_offsets[e];
+#pragma unroll 1
+              for (int i0 = 0; i0 < kEpiTok * kGroups * 4; i0 += 128) {
+                const int idx = i0 + etid;
+                const int unit = idx >> 2, sub = idx & 3;
+                const int tok = unit / kGroups, grp = unit % kGroups;
+                const float* src = sh + tok * kEpiFeat + grp * 32 + sub * 8;
+                const float4 x0 = *reinterpret_cast<const float4*>(src);
+                const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+                float amax = 0.0f;
+                amax = torch_max_abs(amax, x0.x); amax = torch_max_abs(amax, x0.y);
+                amax = torch_max_abs(amax, x0.z); amax = torch_max_abs(amax, x0.w);
+                amax = torch_max_abs(amax, x1.x); amax = torch_max_abs(amax, x1.y);
+                amax = torch_max_abs(amax, x1.z); amax = torch_max_abs(amax, x1.w);
+#pragma unroll
+                for (int o = 1; o < 4; o <<= 1) {
+                  const float ob = __shfl_xor_sync(0xffffffffu, amax, o);
+                  amax = (ob > amax || ob != ob) ? ob : amax;
+                }
+                const uint32_t rb = ue8m0_rounded_bits(amax);
+                const float inv = inv_scale(scale_from_bits(rb));
+                const int f0 = nt * (C::kWgtRows / 2) + grp * 32 + sub * 8;   // intermediate feature
+                if (tok < nv && f0 < p.out_features) {
+                  const uint32_t lo = static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x0.x, inv)),
+                                                                       clamp_fp8(__fmul_rn(x0.y, inv)))) |
+                                      (static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x0.z, inv)),
+                                                                        clamp_fp8(__fmul_rn(x0.w, inv)))) << 16);
+                  const uint32_t hi = static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x1.x, inv)),
+                                                                       clamp_fp8(__fmul_rn(x1.y, inv)))) |
+                                      (static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x1.z, inv)),
+                                                                        clamp_fp8(__fmul_rn(x1.w, inv)))) << 16);
+                  const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
+                  *reinterpret_cast<uint2*>(codes_out + grow * p.ld_out + f0) = make_uint2(lo, hi);
+                  if (sub == 0) {
+                    const int64_t srow = act_sf_row<SPREAD>(a0 + tok);
+                    const int g = f0 >> 5;
+                    sfb_e[blocked_sf_offset(srow, g, p.out_g4)] = static_cast<uint8_t>((rb >> 23) & 0xFFu);
+                    // the K padding groups of the row's last k-atom read as zero scales in GEMM2
+                    if (g == (p.out_features >> 5) - 1)
+                      for (int gz = p.out_features >> 5; gz < 4 * p.out_g4; ++gz)
+                        sfb_e[blocked_sf_offset(srow, gz, p.out_g4)] = 0;
+                  }
+                }
+              }
+            } else {
+              constexpr int kSegs = kEpiFeat / 8;                   // 8-output segments per row
+              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+              for (int i0 = 0; i0 < kEpiTok * kSegs; i0 += 128) {
+                const int idx = i0 + etid;
+                const int tok = idx / kSegs, seg = idx % kSegs;
+                const int n0 = nt * C::kWgtRows + seg * 8;           // output feature
+                if (tok < nv && n0 < p.N) {
+                  const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
+                  const int64_t tk = p.token_idx[grow];
+                  const float wr = p.row_weights[grow];
+                  const float* src = sh + tok * kEpiFeat + seg * 8;
+                  const float4 z0 = *reinterpret_cast<const float4*>(src);
+                  const float4 z1 = *reinterpret_cast<const float4*>(src + 4);
+                  const __nv_bfloat162 v0 = __floats2bfloat162_rn(__fmul_rn(z0.x, wr), __fmul_rn(z0.y, wr));
+                  const __nv_bfloat162 v1 = __floats2bfloat162_rn(__fmul_rn(z0.z, wr), __fmul_rn(z0.w, wr));
+                  const __nv_bfloat162 v2 = __floats2bfloat162_rn(__fmul_rn(z1.x, wr), __fmul_rn(z1.y, wr));
+                  const __nv_bfloat162 v3 = __floats2bfloat162_rn(__fmul_rn(z1.z, wr), __fmul_rn(z1.w, wr));
+                  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(o + tk * p.ld_out + n0),
+                               "r"(*reinterpret_cast<const uint32_t*>(&v0)), "r"(*reinterpret_cast<const uint32_t*>(&v1)),
+                               "r"(*reinterpret_cast<const uint32_t*>(&v2)), "r"(*reinterpret_cast<const uint32_t*>(&v3))
+                               : "memory");
+                }
+              }
+            }
+          }
+          // single staging buffer: the next chunk's pass 1 waits for this pass 2
+          if constexpr (kEpiBufs == 1) asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        continue;   // the accumulator went back to the MMA after its last load
       }
       tc_fence_before();
       __syncwarp();

@@ -21,7 +21,7 @@ import torch
 
 from . import _lib
 
-GEMM_AUTO, GEMM_TOKENS_M, GEMM_SWAP = 0, 1, 2
+GEMM_AUTO, GEMM_TOKENS_M, GEMM_SWAP, GEMM_SWAP_WIDE = 0, 1, 2, 3
 DTYPE_BF16, DTYPE_F32 = 0, 1
 
 _status = {}

@@ -40,12 +40,14 @@ enum {
 
 enum { GPTOSS_DTYPE_BF16 = 0, GPTOSS_DTYPE_F32 = 1 };
 
-/* GEMM orientation: AUTO picks SWAP (weights on the MMA M side) when the average
- * expert holds few rows (<= 16 in the fused expert forward and its stages, <= 48 in
- * gptoss_fp4_group_mm), else TOKENS_M. Results agree to fp32 accumulation order. The
- * stages of one forward (route_quant, gemm1, gemm2) must be called with the same mode:
- * it also selects the row layout of the activation scales in the workspace. */
-enum { GPTOSS_GEMM_AUTO = 0, GPTOSS_GEMM_TOKENS_M = 1, GPTOSS_GEMM_SWAP = 2 };
+/* GEMM orientation: SWAP puts the weights on the MMA M side and multiplies 16-row
+ * activation chunks; SWAP_WIDE does the same with 64-row chunks (16/32/64-row loads);
+ * TOKENS_M puts the tokens on M. AUTO picks SWAP while the average expert holds <= 8
+ * rows, SWAP_WIDE up to 16, else TOKENS_M (gptoss_fp4_group_mm: SWAP_WIDE up to 48).
+ * Results agree to fp32 accumulation order. The stages of one forward (route_quant,
+ * gemm1, gemm2) must be called with the same mode: it also selects the row layout of
+ * the activation scales in the workspace. */
+enum { GPTOSS_GEMM_AUTO = 0, GPTOSS_GEMM_TOKENS_M = 1, GPTOSS_GEMM_SWAP = 2, GPTOSS_GEMM_SWAP_WIDE = 3 };
 
 /* Message for the last failing call on this thread ("" if none). */
 const char* gptoss_last_error(void);

@@ -59,7 +59,7 @@ def test_expert_rows_and_combine(pkg, dev):
     c0 = int(counts[0])
     for q, (lo, hi) in enumerate(((0, c0), (c0, rows.shape[0]))):
         loc = pkg.ep.shard_experts(m, q, 2)
-        for mode in (1, 2):
+        for mode in (1, 2, 3):
             loc.gemm_mode = mode
             back = pkg.ep.CudaKernels.expert_forward(torch.from_numpy(rows[lo:hi]).to(dev), loc)
             torch.cuda.synchronize()

@@ -11,7 +11,7 @@ from helpers import Cfg, assert_output_tolerance, bf16_from_int16, build_experts
 
 pytestmark = pytest.mark.gpu
 
-MODES = {"auto": 0, "tokens_m": 1, "swap": 2}
+MODES = {"auto": 0, "tokens_m": 1, "swap": 2, "swap_wide": 3}
 
 
 @pytest.mark.parametrize("mode", list(MODES))
@@ -171,7 +171,7 @@ def test_cfg_roundtrip():
     assert Cfg(4, 8, 8).num_local_experts == 4
 
 
-@pytest.mark.parametrize("mode", ["tokens_m", "swap"])
+@pytest.mark.parametrize("mode", ["tokens_m", "swap", "swap_wide"])
 def test_fused_route_quant_stage_bit_exact(pkg, dev, mode):
     # The fused path's first stage (counting sort + gather + FP8 quantisation straight into
     # the blocked scale layout) reproduces the reference's GEMM1 inputs byte for byte.
@@ -203,7 +203,7 @@ def test_fused_route_quant_stage_bit_exact(pkg, dev, mode):
         assert hashlib.sha256(rows.tobytes()).hexdigest() == bytes(g["act_scales_sha"]).decode()
 
 
-@pytest.mark.parametrize("mode", ["tokens_m", "swap"])
+@pytest.mark.parametrize("mode", ["tokens_m", "swap", "swap_wide"])
 def test_workspace_garbage_does_not_leak(pkg, dev, mode):
     # The padding rows of the blocked scale layouts are never cleared (a padding row only
     # feeds accumulator rows no epilogue stores). Fill every workspace byte with 0xFF --
