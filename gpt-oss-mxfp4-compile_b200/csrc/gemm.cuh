@@ -93,8 +93,13 @@ struct GemmConfig {
   // at any ring depth), so weights-on-M tiles load two k blocks behind each barrier.
   static constexpr int kSubs = SWAP ? 2 : 1;
   static constexpr int kStages = SWAP ? (SPREAD ? 5 : 4) : (PAIR ? 7 : 5);
-  static constexpr int kAccBufs = SWAP ? 4 : 2;
-  static constexpr int kAccCols = kMmaN;              // fp32 columns per accumulator
+  // MMA issuing threads. A small-N block-scaled MMA costs ~75 cycles of issue, so one
+  // thread cannot keep up with the weight stream of weights-on-M tiles: two warps issue
+  // alternate k blocks of each stage into two partial accumulators that the epilogue adds.
+  static constexpr int kIssuers = SWAP ? 2 : 1;
+  static constexpr int kAccBufs = SWAP ? (SPREAD ? 4 : 3) : 2;
+  static constexpr int kAccCols = kMmaN;              // fp32 columns per partial accumulator
+  static constexpr int kAccStride = kIssuers * kAccCols;   // columns per accumulator buffer
   static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
   static constexpr uint32_t kWgtTileBytes = kWgtRowsCta * 128;   // 8-bit container in smem
   static constexpr uint32_t kActTileBytes = kActRows * 128;
@@ -103,11 +108,14 @@ struct GemmConfig {
   static constexpr uint32_t kSubBytes =   // one k block: weights | activations | scales
       ((kWgtTileBytes + kActTileBytes + kSfActBytes + kSfWgtBytes + 1023) / 1024) * 1024;
   static constexpr uint32_t kStageBytes = kSubs * kSubBytes;
-  static constexpr uint32_t kTmemAccCols = kAccBufs * kAccCols;
-  static constexpr uint32_t kSfActCol = kTmemAccCols;           // 4 columns
-  static constexpr uint32_t kSfWgtCol = kTmemAccCols + 4;       // 4 per chunk
-  static constexpr uint32_t kTmemCols = (kSfWgtCol + 4 * kWgtSfChunks) <= 128 ? 128
-                                        : (kSfWgtCol + 4 * kWgtSfChunks) <= 256 ? 256 : 512;
+  static constexpr uint32_t kTmemAccCols = kAccBufs * kAccStride;
+  // scale columns of each issuer: activation 4, then weights 4 per chunk
+  static constexpr uint32_t kSfCols = 4 + 4 * kWgtSfChunks;
+  static constexpr uint32_t kSfActCol = kTmemAccCols;
+  static constexpr uint32_t kSfWgtCol = kTmemAccCols + 4;
+  static constexpr uint32_t kTmemUsed = kTmemAccCols + kIssuers * kSfCols;
+  static constexpr uint32_t kTmemCols = kTmemUsed <= 128 ? 128 : kTmemUsed <= 256 ? 256 : 512;
+  static_assert(kTmemUsed <= 512, "TMEM budget");
   static constexpr uint32_t kBarrierBytes = 8 * (2 * kStages + 2 * kAccBufs + 1) + 16;
   static constexpr uint32_t kEpiStageBytes = SWAP ? 16384 : 0;   // weights-on-M epilogue staging
   static constexpr uint32_t kSmemBytes =
@@ -116,7 +124,7 @@ struct GemmConfig {
   // across the warpgroup); tokens-on-M tiles give each warpgroup one 64-column slice, so
   // three warps share every TMEM lane quarter and hide each other's latency.
   static constexpr int kEpiWarps = SWAP ? 4 : 4 * (kWgtRows / 64);
-  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps + 32 * (kIssuers - 1);   // 2nd issuer: last warp
 };
 
 constexpr int kMaxExpertsGemm = 256;
@@ -178,13 +186,13 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
     tma_prefetch_desc(&tm_wgt);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1);
+      mbar_init(empty_bar(s), C::kIssuers);   // one commit per MMA issuer
     }
     for (int b = 0; b < C::kAccBufs; ++b) {
-      mbar_init(accf_bar(b), 1);
+      mbar_init(accf_bar(b), C::kIssuers);
       mbar_init(acce_bar(b), PAIR ? 2 * C::kEpiWarps : C::kEpiWarps);   // both CTAs' epilogues
     }
-    mbar_init(drain_bar, 1);
+    mbar_init(drain_bar, C::kIssuers);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -324,8 +332,10 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ================================================================ MMA issuer
+  } else if (warp == 1 || (C::kIssuers > 1 && warp == 2 + C::kEpiWarps)) {
+    // ================================================================ MMA issuer(s)
+    // issuer i takes the k blocks j of each stage with j % kIssuers == i
+    const int issuer = warp == 1 ? 0 : 1;
     if (elect_one() && !(PAIR && !leader)) {
       int stage = 0;
       uint32_t phase = 0;
@@ -338,19 +348,19 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         const uint32_t acc_phase = static_cast<uint32_t>(local / C::kAccBufs) & 1u;
         if (!mbar_wait(acce_bar(b), acc_phase ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * C::kAccCols;
+        const uint32_t d_tmem = tmem_base + b * C::kAccStride + issuer * C::kAccCols;
         // Column shift selecting the 32-row groups this tile starts at inside the
         // copied 128-row scale blocks.
         const uint32_t wshift = SWAP ? 0u : static_cast<uint32_t>(((nt * C::kWgtRows) & 127) >> 5);
         const uint32_t ashift =
             SWAP ? static_cast<uint32_t>((act_sf_row<SPREAD>(static_cast<int64_t>(ch) * C::kActRows) & 127) >> 5) : 0u;
-        const uint32_t t_sfa = tmem_base + C::kSfActCol;
-        const uint32_t t_sfw = tmem_base + C::kSfWgtCol;
+        const uint32_t t_sfa = tmem_base + C::kSfActCol + issuer * C::kSfCols;
+        const uint32_t t_sfw = tmem_base + C::kSfWgtCol + issuer * C::kSfCols;
         const uint32_t mma_n = SWAP ? static_cast<uint32_t>(act_rows_of(e, ch)) : static_cast<uint32_t>(C::kMmaN);
-        // The issue loop is lean on purpose: one thread issues every tcgen05 op of the CTA
-        // and small-N block-scaled MMAs cost ~75 cycles of issue each, so descriptors and
-        // the instruction word are formed once per tile / stage and advanced by adds
-        // (a 32-byte K step is +2 in the descriptor's 16-byte address field).
+        // The issue loop is lean on purpose (small-N block-scaled MMAs cost ~75 cycles of
+        // issue each): descriptors and the instruction word are formed once per tile /
+        // stage and advanced by adds (a 32-byte K step is +2 in the descriptor's 16-byte
+        // address field).
         const uint32_t idesc0 = SWAP ? idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, 0, 0)
                                      : idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, 0, 0);
         const uint32_t sf_a_t = SWAP ? t_sfw : t_sfa;                       // scales of MMA operand A
@@ -367,6 +377,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < C::kSubs; ++j) {
             if (j >= nsub) break;
+            if (j % C::kIssuers != issuer) continue;
             const uint64_t joff = (static_cast<uint64_t>(j) * C::kSubBytes) >> 4;
             if constexpr (PAIR) {
               // each CTA's scale chunks go from its own shared memory into its own TMEM
@@ -384,7 +395,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t idesc = idesc0 | (static_cast<uint32_t>(k) << 4) | (static_cast<uint32_t>(k) << 29);
-              const uint32_t acc = (kb0 | j | k) != 0 ? 1u : 0u;
+              // the first MMA of each issuer in a tile starts its partial accumulator
+              const uint32_t acc = (kb0 != 0 || j >= C::kIssuers || k != 0) ? 1u : 0u;
               if constexpr (PAIR) {
                 mma_mxf8f6f4_pair(d_tmem, dA + 2u * k, dB + 2u * k, idesc, sf_a_t, sf_b_t, acc);
               } else {
@@ -400,7 +412,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         if constexpr (PAIR) tc_commit_pair(accf_bar(b), 0x3);   // both CTAs' epilogues
         else tc_commit(accf_bar(b));
       }
-      // Wait for every tcgen05 operation this thread issued before TMEM is released.
+      // Wait for every tcgen05 operation the issuers issued before TMEM is released.
       if constexpr (PAIR) tc_commit_pair(drain_bar, 0x3);
       else tc_commit(drain_bar);
       (void)mbar_wait(drain_bar, 0u, p.err, kDevTimeoutDrain);
@@ -418,6 +430,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
     constexpr int kEpiBufs = 2 * kEpiBufBytes <= C::kEpiStageBytes ? 2 : 1;
     static_assert(!SWAP || EPI == kEpiPlain || kEpiBufBytes <= C::kEpiStageBytes, "epilogue staging too small");
     float* const epi_f = reinterpret_cast<float*>(smem_raw + (epi_base - smem_u32(smem_raw)));
+    // the second issuer's partial accumulator holds something once a tile has 2 k blocks
+    const bool has_b = C::kIssuers > 1 && p.num_kb > 1;
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int wg = (warp - 2) >> 2;         // epilogue warpgroup
     constexpr int kWgs = C::kEpiWarps / 4;
@@ -437,7 +451,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         continue;
       }
       tc_fence_after();
-      const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + b * C::kAccCols;
+      const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + b * C::kAccStride;
       const int m_e = p.m_sizes[e * p.m_stride];
       const int row0 = p.row_offsets[e];
       if constexpr (!SWAP) {
@@ -560,7 +574,15 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
           if (live) {
             __syncwarp();
             tmem_ld_32x32b_x32(t_acc + c * 32, r);
-            tmem_ld_wait();
+            if (has_b) {
+              uint32_t r2[32];
+              tmem_ld_32x32b_x32(t_acc + C::kAccCols + c * 32, r2);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(r2[j])));
+            } else {
+              tmem_ld_wait();
+            }
           }
           {
             if (live) {
@@ -595,11 +617,25 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
           const int nv = min(kEpiTok, a_end - a0);
           float* sh = epi_f + ((local * C::kColChunks + c) % kEpiBufs) * (kEpiBufBytes / 4);
           if (live) {
-            uint32_t r[kEpiTok];
+            float v[kEpiTok];   // accumulator column j (the two issuers' partial sums added)
             __syncwarp();
-            if constexpr (kEpiTok == 16) tmem_ld_32x32b_x16(t_acc + c * kEpiTok, r);
-            else tmem_ld_32x32b_x32(t_acc + c * kEpiTok, r);
-            tmem_ld_wait();
+            if constexpr (kEpiTok == 16) {
+              static_assert(kEpiTok != 16 || C::kAccCols == 16, "16-row chunks fill one partial accumulator");
+              uint32_t r[32];   // partial accumulators of both issuers are adjacent: one load
+              tmem_ld_32x32b_x32(t_acc, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                v[j] = has_b ? __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r[16 + j])) : __uint_as_float(r[j]);
+            } else {
+              uint32_t r[32], r2[32];
+              tmem_ld_32x32b_x32(t_acc + c * 32, r);
+              if (has_b) tmem_ld_32x32b_x32(t_acc + C::kAccCols + c * 32, r2);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                v[j] = has_b ? __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r2[j])) : __uint_as_float(r[j]);
+            }
             if (c == C::kColChunks - 1 || a0 + kEpiTok >= a_end) {   // last load of this tile
               tc_fence_before();
               __syncwarp();
@@ -613,8 +649,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
               const int fl = (32 * q + lane) >> 1;
 #pragma unroll
               for (int j = 0; j < kHalf; ++j) {
-                const float vlo = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
-                const float vhi = __fadd_rn(bf16_round(__uint_as_float(r[kHalf + j])), bsv);
+                const float vlo = __fadd_rn(bf16_round(v[j]), bsv);
+                const float vhi = __fadd_rn(bf16_round(v[kHalf + j]), bsv);
                 const float other = __shfl_xor_sync(0xffffffffu, odd ? vlo : vhi, 1);
                 const float h = odd ? swiglu_pair(other, vhi, p.swiglu_alpha, p.swiglu_limit)
                                     : swiglu_pair(vlo, other, p.swiglu_alpha, p.swiglu_limit);
@@ -623,7 +659,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
             } else {
               const int fl = 32 * q + lane;
 #pragma unroll
-              for (int j = 0; j < kEpiTok; ++j) sh[j * kEpiFeat + fl] = __fadd_rn(bf16_round(__uint_as_float(r[j])), bsv);
+              for (int j = 0; j < kEpiTok; ++j) sh[j * kEpiFeat + fl] = __fadd_rn(bf16_round(v[j]), bsv);
             }
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");

@@ -42,8 +42,8 @@ enum { GPTOSS_DTYPE_BF16 = 0, GPTOSS_DTYPE_F32 = 1 };
 
 /* GEMM orientation: SWAP puts the weights on the MMA M side and multiplies 16-row
  * activation chunks; SWAP_WIDE does the same with 64-row chunks (16/32/64-row loads);
- * TOKENS_M puts the tokens on M. AUTO picks SWAP while the average expert holds <= 8
- * rows, SWAP_WIDE up to 16, else TOKENS_M (gptoss_fp4_group_mm: SWAP_WIDE up to 48).
+ * TOKENS_M puts the tokens on M. AUTO picks SWAP while the average expert holds <= 12
+ * rows, SWAP_WIDE up to 80, else TOKENS_M (gptoss_fp4_group_mm: SWAP_WIDE up to 48).
  * Results agree to fp32 accumulation order. The stages of one forward (route_quant,
  * gemm1, gemm2) must be called with the same mode: it also selects the row layout of
  * the activation scales in the workspace. */
