@@ -38,7 +38,7 @@ CONFIGS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from
 # the ncu capture summarised in profiles/ (None until captured for this kernel/config).
-NCU_TRAFFIC_BYTES = {"decode": 294_178_560,     # profiles/moe_gemm_swap_decode_T32.md
+NCU_TRAFFIC_BYTES = {"decode": 294_617_088,     # profiles/moe_gemm_swap_decode_T32.md
                      "prefill": 769_571_328}    # profiles/moe_gemm_pair_prefill_T8192.md (GEMM1)
 
 KERNELS_PER_STEP = 5   # router, route_sort, gather_quant, gemm1, gemm2
