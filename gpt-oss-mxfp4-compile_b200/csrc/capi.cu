@@ -260,9 +260,8 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
                             st, PAIR ? dim3(2, 1, 1) : dim3(1, 1, 1), ta, ta32, ta16, tw, p);
 }
 
-// GEMM orientation of one call. The fused pipeline switches to weights-on-M with 16-row
-// activation chunks (and SPREAD activation scales) when the average expert holds at
-// most 16 rows; the reference-layout op uses 64-row chunks up to 48 rows per expert.
+// GEMM orientation of one call (pick_layout for the fused forwards; the reference-layout
+// group GEMM uses 64-row chunks up to 48 rows per expert).
 bool pick_swap(int mode, int64_t rows, int experts, int64_t max_avg) {
   if (mode == GPTOSS_GEMM_SWAP || mode == GPTOSS_GEMM_SWAP_WIDE) return true;
   if (mode == GPTOSS_GEMM_TOKENS_M) return false;

@@ -35,11 +35,13 @@ class GptOssMoELayer(nn.Module):
         ex = self.experts
         shape = hidden_states.shape
         h = hidden_states.reshape(-1, self.hidden_size).contiguous()
-        out, scores, idx = torch.ops.gptoss.moe_layer_forward(
-            h, self.router_weight.data, self.router_bias.data, int(self.top_k),
-            ex.gate_up_proj_data, ex.gate_up_proj_scales, ex.gate_up_proj_bias.data,
-            ex.down_proj_data, ex.down_proj_scales, ex.down_proj_bias.data,
-            float(ex.alpha), float(ex.limit), int(ex.gemm_mode))
+        # plain tensors in eager mode call the implementation directly (the dispatcher of a
+        # Python custom op costs ~30 us of host time per call); tracing goes through the op
+        fn = _ops.moe_layer_forward_impl if _ops.eager_call(h) else torch.ops.gptoss.moe_layer_forward
+        out, scores, idx = fn(h, self.router_weight, self.router_bias, int(self.top_k),
+                              ex.gate_up_proj_data, ex.gate_up_proj_scales, ex.gate_up_proj_bias,
+                              ex.down_proj_data, ex.down_proj_scales, ex.down_proj_bias,
+                              float(ex.alpha), float(ex.limit), int(ex.gemm_mode))
         return out.view(shape), scores, idx
 
     def route(self, hidden_states: torch.Tensor):
@@ -50,4 +52,3 @@ class GptOssMoELayer(nn.Module):
 
 
 __all__ = ["GptOssMoELayer"]
-_ = _ops

@@ -29,7 +29,33 @@ _status_lock = threading.Lock()
 
 
 def _stream(dev: torch.device) -> int:
-    return torch.cuda.current_stream(dev).cuda_stream
+    """Raw handle of the current stream of `dev` (the fast path skips the Stream object)."""
+    try:
+        return torch._C._cuda_getCurrentRawStream(dev.index if dev.index is not None else torch.cuda.current_device())
+    except AttributeError:
+        return torch.cuda.current_stream(dev).cuda_stream
+
+
+# Per (device, stream) scratch of the fused forwards, reused across calls: calls on one
+# stream run in order on the GPU, so one buffer per stream is never used twice at once.
+_ws_cache = {}
+_ws_bytes = {}
+
+
+def _scratch(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (dev.index, stream)
+    t = _ws_cache.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        _ws_cache[key] = t
+    return t
+
+
+def eager_call(t) -> bool:
+    """True when an op can run its implementation directly (a plain CUDA tensor outside
+    torch.compile tracing), skipping the dispatcher; fake, meta or traced tensors go
+    through the registered torch.library op."""
+    return type(t) is torch.Tensor and not torch.compiler.is_compiling()
 
 
 def _p(t):
@@ -52,6 +78,9 @@ def status_tensor(device) -> torch.Tensor:
     """Per-device int32 word the kernels set on a timed-out wait or a bad index."""
     device = torch.device(device)
     key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(key)
+    if t is not None:
+        return t
     with _status_lock:
         t = _status.get(key)
         if t is None:
@@ -221,7 +250,12 @@ def router_topk_impl(hidden, weight, bias, top_k: int):
 
 
 def workspace_bytes(T, k, E, H, I) -> int:
-    return int(_lib.query("gptoss_moe_workspace_bytes", T, k, E, H, I))
+    key = (T, k, E, H, I)
+    n = _ws_bytes.get(key)
+    if n is None:
+        n = int(_lib.query("gptoss_moe_workspace_bytes", T, k, E, H, I))
+        _ws_bytes[key] = n
+    return n
 
 
 def _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias):
@@ -247,13 +281,15 @@ def moe_experts_forward_impl(hidden, router_indices, routing_weights, gu_data, g
     k = router_indices.shape[1]
     E = gu_data.shape[0]
     I = gu_data.shape[1] // 2
-    out = torch.empty((T, H), dtype=torch.bfloat16, device=hidden.device)
-    ws = torch.empty(max(workspace_bytes(T, k, E, H, I), 256), dtype=torch.uint8, device=hidden.device)
+    dev = hidden.device
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    st = _stream(dev)
+    ws = _scratch(dev, st, workspace_bytes(T, k, E, H, I))
     _lib.call("gptoss_moe_experts_forward", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(),
               T, k, E, H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E, gu_bias.data_ptr(),
               dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E, dn_bias.data_ptr(), float(alpha),
               float(limit), out.data_ptr(), ws.data_ptr(), ws.numel(), int(gemm_mode),
-              status_tensor(hidden.device).data_ptr(), _stream(hidden.device))
+              status_tensor(dev).data_ptr(), st)
     return out
 
 
@@ -273,12 +309,13 @@ def moe_layer_forward_impl(hidden, router_weight, router_bias, top_k: int, gu_da
     out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     idx = torch.empty((T, top_k), dtype=torch.int64, device=dev)
     scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
-    ws = torch.empty(max(workspace_bytes(T, top_k, E, H, I), 256), dtype=torch.uint8, device=dev)
+    st = _stream(dev)
+    ws = _scratch(dev, st, workspace_bytes(T, top_k, E, H, I))
     _lib.call("gptoss_moe_layer_forward", hidden.data_ptr(), router_weight.data_ptr(), router_bias.data_ptr(), T,
               top_k, E, H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E, gu_bias.data_ptr(),
               dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E, dn_bias.data_ptr(), float(alpha),
               float(limit), out.data_ptr(), idx.data_ptr(), scores.data_ptr(), ws.data_ptr(), ws.numel(),
-              int(gemm_mode), status_tensor(dev).data_ptr(), _stream(dev))
+              int(gemm_mode), status_tensor(dev).data_ptr(), st)
     return out, scores, idx
 
 
