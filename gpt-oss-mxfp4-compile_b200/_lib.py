@@ -60,6 +60,8 @@ _SIGNATURES = {
     "gptoss_ep_p2p_buffer_bytes": (_sz, [_i, _c_int64, _c_int64]),
     "gptoss_ep_p2p_dispatch": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _i, _i, _c_int64, _c_int64, _vp, _vp,
                                     _c_int32, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "gptoss_ep_p2p_route_dispatch": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _i, _i, _c_int64, _c_int64, _vp, _vp,
+                                          _c_int32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "gptoss_ep_p2p_expert_forward": (_i, [_vp, _i, _i, _c_int64, _c_int32, _i, _c_int64, _c_int64, _vp, _vp,
                                           _c_int64, _vp, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _vp, _vp, _sz, _i,
                                           _vp, _vp]),

@@ -1159,11 +1159,16 @@ size_t gptoss_ep_p2p_buffer_bytes(int world_size, int64_t capacity, int64_t hidd
   return static_cast<size_t>(p2p_buffer_bytes(world_size, capacity, static_cast<int>(hidden_size)));
 }
 
-int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
-                           int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
-                           int64_t hidden_size, int64_t capacity, void* local_base, const uint64_t* peer_bases,
-                           int32_t epoch, int32_t* send_counts, int32_t* pos_of, void* workspace,
-                           size_t workspace_bytes, int32_t* status_dev, void* stream) {
+}  // extern "C"
+
+// Peer-memory dispatch (routing given, or computed first when `ra` is set). Decode-sized
+// batches run as one cluster launch (decode_prologue_kernel in dispatch mode); larger ones
+// as route_sort_kernel (by owning rank) + ep_pack_p2p_kernel, after router_launch if `ra`.
+int ep_p2p_dispatch_impl(const void* hidden, const RouterArgs* ra, const int64_t* router_indices,
+                         const float* routing_weights, int64_t num_tokens, int top_k, int num_experts,
+                         int world_size, int rank, int64_t hidden_size, int64_t capacity, void* local_base,
+                         const uint64_t* peer_bases, int32_t epoch, int32_t* send_counts, int32_t* pos_of,
+                         void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream) {
   GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld && rank >= 0 && rank < world_size,
                "ep_p2p_dispatch: bad world_size / rank");
   GPTOSS_CHECK(num_experts % world_size == 0, "ep_p2p_dispatch: num_experts must be a multiple of world_size");
@@ -1174,11 +1179,58 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
   DeviceInfo di;
   GPTOSS_TRY(bind_device(send_counts, "send_counts", &di));
   GPTOSS_CHECK(local_base && peer_bases && workspace &&
-                   (num_tokens == 0 || (hidden && router_indices && routing_weights && pos_of)),
+                   (num_tokens == 0 || (hidden && (ra != nullptr || (router_indices && routing_weights)) && pos_of)),
                "ep_p2p_dispatch: null pointer");
   const size_t need = gptoss_ep_dispatch_workspace_bytes(num_tokens, top_k, world_size);
   if (workspace_bytes < need) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* status = status_dev ? status_dev : di.status_sink;
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  size_t smem = 0;
+  int slice = 0;
+  if (num_tokens > 0 && decode_prologue_fits(num_tokens, top_k, num_experts, hidden_size, ra != nullptr, &smem, &slice)) {
+    static uint64_t attr_done = 0;   // one bit per device
+    static std::mutex mu;
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      if (!(attr_done & (1ull << dev))) {
+        GPTOSS_CUDA(cudaFuncSetAttribute(decode_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kDpMaxSmem)));
+        attr_done |= (1ull << dev);
+      }
+    }
+    DecodePrologueParams p{};
+    p.x = static_cast<const __nv_bfloat16*>(hidden);
+    if (ra != nullptr) {
+      p.w = static_cast<const __nv_bfloat16*>(ra->weight);
+      p.bias = static_cast<const __nv_bfloat16*>(ra->bias);
+      p.ridx_out = ra->ridx_out;
+      p.scores_out = static_cast<__nv_bfloat16*>(ra->scores_out);
+      p.rw_out = ra->rw_out;
+    } else {
+      p.ridx_in = router_indices;
+      p.rw_in = routing_weights;
+    }
+    p.T = static_cast<int>(num_tokens); p.H = static_cast<int>(hidden_size); p.E = num_experts; p.K = top_k;
+    p.slice_chunks = slice;
+    p.err = status;
+    p.ep_world = world_size; p.ep_rank = rank; p.ep_epr = num_experts / world_size;
+    p.ep_rb = static_cast<int>(ep_row_bytes(static_cast<int>(hidden_size)));
+    p.ep_cap = capacity;
+    p.peer_bases = peer_bases;
+    p.send_counts = send_counts;
+    p.pos_of = pos_of;
+    p.epoch = epoch;
+    return launch_pdl_cluster(decode_prologue_kernel, dim3(kDpCluster), dim3(kDpThreads), smem, st,
+                              dim3(kDpCluster, 1, 1), p);
+  }
+  if (ra != nullptr && num_tokens > 0) {
+    GPTOSS_TRY(router_launch(hidden, ra->weight, ra->bias, num_tokens, hidden_size, num_experts, top_k, ra->ridx_out,
+                             ra->scores_out, ra->rw_out, nullptr, nullptr, 0, di.sms, dev, st));
+    router_indices = ra->ridx_out;
+    routing_weights = ra->rw_out;
+  }
   const int64_t A = num_tokens * top_k;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   size_t o = 0;
@@ -1193,7 +1245,7 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
   rp.offsets = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * world_size));
   rp.counts = send_counts;
   rp.divisor = num_experts / world_size;
-  rp.err = status_dev ? status_dev : di.status_sink;
+  rp.err = status;
   GPTOSS_TRY(launch_pdl(route_sort_kernel, dim3(world_size), dim3(1024), 0, st, rp));
   const int tpr = quant_threads_per_row(static_cast<int>(hidden_size));
   const int rpb = 256 / tpr;
@@ -1205,6 +1257,33 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
                         static_cast<const int32_t*>(send_counts), static_cast<const int32_t*>(rp.offsets), tpr,
                         peer_bases, pos_of, static_cast<int32_t*>(local_base) + kP2pCounterDispatch, epoch));
   return GPTOSS_OK;
+}
+
+extern "C" {
+
+int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, const float* routing_weights,
+                           int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
+                           int64_t hidden_size, int64_t capacity, void* local_base, const uint64_t* peer_bases,
+                           int32_t epoch, int32_t* send_counts, int32_t* pos_of, void* workspace,
+                           size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  return ep_p2p_dispatch_impl(hidden, nullptr, router_indices, routing_weights, num_tokens, top_k, num_experts,
+                              world_size, rank, hidden_size, capacity, local_base, peer_bases, epoch, send_counts,
+                              pos_of, workspace, workspace_bytes, status_dev, stream);
+}
+
+int gptoss_ep_p2p_route_dispatch(const void* hidden, const void* router_weight, const void* router_bias,
+                                 int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
+                                 int64_t hidden_size, int64_t capacity, void* local_base, const uint64_t* peer_bases,
+                                 int32_t epoch, int64_t* router_indices_out, void* router_scores_out,
+                                 float* routing_weights_out, int32_t* send_counts, int32_t* pos_of, void* workspace,
+                                 size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  GPTOSS_CHECK(num_tokens == 0 || (router_weight && router_bias && router_indices_out && routing_weights_out),
+               "ep_p2p_route_dispatch: null pointer");
+  GPTOSS_CHECK(hidden_size % 8 == 0, "ep_p2p_route_dispatch: hidden size must be a multiple of 8");
+  const RouterArgs ra{router_weight, router_bias, router_indices_out, router_scores_out, routing_weights_out};
+  return ep_p2p_dispatch_impl(hidden, &ra, nullptr, nullptr, num_tokens, top_k, num_experts, world_size, rank,
+                              hidden_size, capacity, local_base, peer_bases, epoch, send_counts, pos_of, workspace,
+                              workspace_bytes, status_dev, stream);
 }
 
 int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int64_t capacity, int32_t epoch,

@@ -21,12 +21,20 @@
 // Semantics and outputs are those of router_mma_kernel + route_sort_kernel +
 // gather_quant_rows_kernel. With `w == nullptr` the routing is an input (phases 1-2 are
 // skipped and rank 0 reads ridx_in / rw_in).
+//
+// Expert-parallel dispatch mode (ep_world > 0) replaces the local layout with the
+// peer-memory dispatch of ep_pack_p2p_kernel: phase 3 sorts the assignments by owning rank
+// (stable, as route_sort_kernel with divisor = experts per rank), phase 4 stores each rank's
+// K slice of every row straight into the owner's receive rows (segment ep_rank), rank 0
+// adds the row metadata, the empty-slot markers, pos_of and send_counts, and after a third
+// cluster barrier rank 0 raises dispatch flag[ep_rank] of every peer to the epoch.
 #pragma once
 #include <cstdint>
 #include <cuda_bf16.h>
 #include "ptx.cuh"
 #include "numerics.cuh"
 #include "routing.cuh"
+#include "ep_p2p.cuh"
 
 namespace gptoss {
 
@@ -60,6 +68,13 @@ struct DecodePrologueParams {
   int g4_a, g4_b, spread;
   __nv_bfloat16* zero_out;      // [T, H] zeroed for the GEMM2 combine, or nullptr
   int* err;
+  // expert-parallel dispatch mode (ep_world > 0)
+  int ep_world, ep_rank, ep_epr, ep_rb;
+  int64_t ep_cap;
+  const uint64_t* peer_bases;   // [ep_world] exchange buffers, this rank's own included
+  int32_t* send_counts;         // [ep_world]
+  int32_t* pos_of;              // [T, K] assignment -> row of the return layout (-1: none)
+  int32_t epoch;
 };
 
 struct DpLayout {
@@ -103,6 +118,71 @@ __host__ __device__ inline DpLayout dp_layout(int T, int E, int K, int slice_chu
 __device__ __forceinline__ bool topk_ahead(float a, int e, float b, int f) {
   const bool an = a != a, bn = b != b;
   return a > b || (an && !bn) || ((a == b || (an && bn)) && e < f);
+}
+
+// Expert-parallel phase 4: this rank's K slice of every row (codes, then the slice's
+// UE8M0 bytes) into row j of peer q's receive rows, segment ep_rank; rank 0 writes the
+// padding bytes, the (local expert, weight) metadata and the empty-slot markers. Then the
+// cluster barrier orders every rank's peer stores (fenced at system scope) before rank 0
+// raises flag[ep_rank] of every peer.
+__device__ __forceinline__ void ep_dispatch_phase4(const DecodePrologueParams& p, uint32_t rank,
+                                                   const uint8_t* codes, const uint8_t* sfs, const int* srow,
+                                                   const int* sasg, const int* sel, const float* wts,
+                                                   const int* cnt, const int* off, int sl, int slv, int gs,
+                                                   int k0) {
+  const int tid = threadIdx.x;
+  const int H = p.H, W = p.ep_world, G = H >> 5;
+  const int64_t rb = p.ep_rb, cap = p.ep_cap;
+  const int total = off[W - 1] + cnt[W - 1];
+  auto row_of = [&](int pos, int& q) -> uint8_t* {
+    const int i = sasg[pos];
+    q = sel[i] / p.ep_epr;
+    const int64_t j = pos - off[q];
+    return reinterpret_cast<uint8_t*>(p.peer_bases[q]) + p2p_recv_offset(p.ep_rank, cap, rb) + j * rb;
+  };
+  if (slv > 0) {
+    const int v16 = slv / 16;
+    for (int q2 = tid; q2 < total * v16; q2 += kDpThreads) {
+      const int pos = q2 / v16, v = q2 - pos * v16;
+      int q;
+      uint8_t* row = row_of(pos, q);
+      reinterpret_cast<uint4*>(row + k0)[v] = reinterpret_cast<const uint4*>(codes + srow[pos] * sl)[v];
+    }
+    const int gv = slv / 32;
+    for (int q2 = tid; q2 < total * gv; q2 += kDpThreads) {
+      const int pos = q2 / gv, gi = q2 - pos * gv;
+      int q;
+      uint8_t* row = row_of(pos, q);
+      row[H + (k0 >> 5) + gi] = sfs[srow[pos] * gs + gi];
+    }
+  }
+  if (rank == 0) {
+    for (int pos = tid; pos < total; pos += kDpThreads) {
+      int q;
+      uint8_t* row = row_of(pos, q);
+      const int i = sasg[pos];
+      for (int64_t b = H + G; b < rb - 8; ++b) row[b] = 0;   // padding travels as zeros
+      int32_t* meta = reinterpret_cast<int32_t*>(row + rb - 8);
+      meta[0] = sel[i] - q * p.ep_epr;
+      meta[1] = __float_as_int(wts[i]);
+    }
+    for (int64_t r = tid; r < cap * W; r += kDpThreads) {     // empty slots past each count
+      const int q = static_cast<int>(r / cap);
+      const int64_t j = r - static_cast<int64_t>(q) * cap;
+      if (j >= cnt[q]) {
+        int32_t* meta = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(p.peer_bases[q]) +
+                                                   p2p_recv_offset(p.ep_rank, cap, rb) + j * rb + rb - 8);
+        meta[0] = -1;
+        meta[1] = 0;
+      }
+    }
+  }
+  __threadfence_system();
+  cluster_sync();
+  if (rank == 0 && tid == 0) {
+    __threadfence_system();
+    for (int q = 0; q < W; ++q) st_release_sys(reinterpret_cast<int32_t*>(p.peer_bases[q]) + p.ep_rank, p.epoch);
+  }
 }
 
 // grid = kDpCluster CTAs forming one cluster; blockDim = kDpThreads.
@@ -284,6 +364,9 @@ __global__ void __launch_bounds__(kDpThreads, 1) decode_prologue_kernel(const De
   // ---- phase 3 (every rank, redundantly): the stable counting sort of the assignments;
   // rank 0 writes the routed layout to global memory
   const bool writer = rank == 0;
+  const bool epm = p.ep_world > 0;
+  const int nb = epm ? p.ep_world : E;           // sort buckets: owning ranks or experts
+  const int epr = epm ? p.ep_epr : 1;
   if (!router) {
     for (int i = tid; i < A; i += kDpThreads) {
       const int64_t v = p.ridx_in[i];
@@ -296,21 +379,23 @@ __global__ void __launch_bounds__(kDpThreads, 1) decode_prologue_kernel(const De
       wts[i] = p.rw_in[i];
     }
   }
-  for (int e = tid; e < E; e += kDpThreads) cnt[e] = 0;
+  for (int e = tid; e < nb; e += kDpThreads) cnt[e] = 0;
   __syncthreads();
   for (int i = tid; i < A; i += kDpThreads)
-    if (sel[i] >= 0) atomicAdd(&cnt[sel[i]], 1);
+    if (sel[i] >= 0) atomicAdd(&cnt[sel[i] / epr], 1);
   __syncthreads();
-  if (warp == 0) {                                // exclusive scans over the experts
+  if (warp == 0) {                                // exclusive scans over the buckets
     int c_run = 0, a_run = 0, b_run = 0;
-    const int per = (E + 31) / 32;
+    const int per = (nb + 31) / 32;
     const int q0 = lane * per;
     for (int i = 0; i < per; ++i) {
       const int q = q0 + i;
-      if (q < E) {
+      if (q < nb) {
         c_run += cnt[q];
-        a_run += static_cast<int>(act_sf_cosize(cnt[q], p.g4_a * 4, p.spread != 0));
-        b_run += static_cast<int>(act_sf_cosize(cnt[q], p.g4_b * 4, p.spread != 0));
+        if (!epm) {
+          a_run += static_cast<int>(act_sf_cosize(cnt[q], p.g4_a * 4, p.spread != 0));
+          b_run += static_cast<int>(act_sf_cosize(cnt[q], p.g4_b * 4, p.spread != 0));
+        }
       }
     }
     int ci = c_run, ai = a_run, bi = b_run;
@@ -324,30 +409,43 @@ __global__ void __launch_bounds__(kDpThreads, 1) decode_prologue_kernel(const De
     int ce = ci - c_run, ae = ai - a_run, be = bi - b_run;
     for (int i = 0; i < per; ++i) {
       const int q = q0 + i;
-      if (q < E) {
-        off[q] = ce; run[q] = ce; sfa[q] = ae; sfb[q] = be;
-        if (writer) { p.counts[q] = cnt[q]; p.offsets[q] = ce; p.sf_offsets_a[q] = ae; p.sf_offsets_b[q] = be; }
+      if (q < nb) {
+        off[q] = ce; run[q] = ce;
+        if (epm) {
+          if (writer) p.send_counts[q] = cnt[q];
+        } else {
+          sfa[q] = ae; sfb[q] = be;
+          if (writer) { p.counts[q] = cnt[q]; p.offsets[q] = ce; p.sf_offsets_a[q] = ae; p.sf_offsets_b[q] = be; }
+          ae += static_cast<int>(act_sf_cosize(cnt[q], p.g4_a * 4, p.spread != 0));
+          be += static_cast<int>(act_sf_cosize(cnt[q], p.g4_b * 4, p.spread != 0));
+        }
         ce += cnt[q];
-        ae += static_cast<int>(act_sf_cosize(cnt[q], p.g4_a * 4, p.spread != 0));
-        be += static_cast<int>(act_sf_cosize(cnt[q], p.g4_b * 4, p.spread != 0));
       }
     }
     __syncwarp();
-    // stable positions, 32 assignments at a time: lanes with the same expert rank
-    // themselves by lane order on top of the expert's running count
+    // stable positions, 32 assignments at a time: lanes with the same bucket rank
+    // themselves by lane order on top of the bucket's running count
     for (int i0 = 0; i0 < A; i0 += 32) {
       const int i = i0 + lane;
-      const int e = i < A ? sel[i] : -1;
+      const int e = i < A ? (sel[i] >= 0 ? sel[i] / epr : -1) : -2;
       const unsigned peers = __match_any_sync(0xffffffffu, e);
       if (e >= 0) {
         const int pos = run[e] + __popc(peers & ((1u << lane) - 1u));
-        if (writer) {
-          p.sorted_token[pos] = i / K;
-          p.sorted_expert[pos] = e;
-          p.sorted_weight[pos] = wts[i];
+        if (epm) {
+          srow[pos] = i / K;
+          sexp[pos] = i;                          // the assignment itself
+          if (writer) p.pos_of[i] = e * static_cast<int>(p.ep_cap) + (pos - off[e]);
+        } else {
+          if (writer) {
+            p.sorted_token[pos] = i / K;
+            p.sorted_expert[pos] = e;
+            p.sorted_weight[pos] = wts[i];
+          }
+          srow[pos] = i / K;
+          sexp[pos] = e;
         }
-        srow[pos] = i / K;
-        sexp[pos] = e;
+      } else if (e == -1 && epm && writer) {
+        p.pos_of[i] = -1;                         // out-of-range expert id: nothing returns
       }
       __syncwarp();
       if (e >= 0 && lane == __ffs(peers) - 1) run[e] += __popc(peers);
@@ -355,6 +453,10 @@ __global__ void __launch_bounds__(kDpThreads, 1) decode_prologue_kernel(const De
     }
   }
   __syncthreads();
+  if (epm) {
+    ep_dispatch_phase4(p, rank, codes, sfs, srow, sexp, sel, wts, cnt, off, sl, slv, gs, k0);
+    return;
+  }
   if (writer) {
     const int total = off[E - 1] + cnt[E - 1];
     for (int i = total + tid; i < A; i += kDpThreads) {   // out-of-range indices: sentinel

@@ -162,6 +162,32 @@ class ExpertParallelExperts(nn.Module):
             self.exchange.close()
             self.exchange = None
 
+    def _p2p_finish(self, h, idx, send_counts, pos_of, cap):
+        """Local experts on the received rows, return rows to their senders, combine."""
+        ex, x = self.exchange, self.experts
+        _ops.ep_p2p_expert_forward(ex.local, self.world_size, self.rank, cap, ex.epoch, x.gate_up_proj_data,
+                                   x.gate_up_proj_scales, x.gate_up_proj_bias, x.down_proj_data,
+                                   x.down_proj_scales, x.down_proj_bias, self._back, self._ws,
+                                   ex.peer_bases, float(x.alpha), float(x.limit), int(x.gemm_mode))
+        self.last_send_counts = send_counts
+        return _ops.ep_p2p_combine(ex.local, self.world_size, cap, ex.epoch, pos_of, idx, self.hidden_size, h.device)
+
+    def forward_with_router(self, h: torch.Tensor, router_weight: torch.Tensor, router_bias: torch.Tensor):
+        """p2p transport: router + dispatch in one call (one launch at decode sizes), then
+        the local experts and the combine. h [T, H] bf16 -> (out [T, H], scores [T, k] bf16,
+        router_indices [T, k] int64)."""
+        if self.transport != "p2p":
+            raise RuntimeError("forward_with_router needs the p2p transport")
+        if h.shape[0] > self.capacity_tokens:
+            raise RuntimeError(f"p2p exchange sized for {self.capacity_tokens} tokens")
+        ex = self.exchange
+        ex.epoch += 1
+        cap = self.capacity_tokens * self.top_k
+        scores, idx, send_counts, pos_of = _ops.ep_p2p_route_dispatch(
+            h, router_weight, router_bias, self.top_k, self.world_size, self.rank, cap, ex.local, ex.peer_bases,
+            ex.epoch)
+        return self._p2p_finish(h, idx, send_counts, pos_of, cap), scores, idx
+
     def forward(self, hidden_states: torch.Tensor, router_indices: torch.Tensor,
                 routing_weights: torch.Tensor) -> torch.Tensor:
         shape = hidden_states.shape
@@ -173,17 +199,12 @@ class ExpertParallelExperts(nn.Module):
         if self.transport == "p2p":
             if h.shape[0] > self.capacity_tokens or idx.shape[1] != self.top_k:
                 raise RuntimeError(f"p2p exchange sized for {self.capacity_tokens} tokens x top-{self.top_k}")
-            ex, x = self.exchange, self.experts
+            ex = self.exchange
             ex.epoch += 1
             cap = self.capacity_tokens * self.top_k
             send_counts, pos_of = _ops.ep_p2p_dispatch(h, idx, w, self.num_experts, self.world_size, self.rank, cap,
                                                        ex.local, ex.peer_bases, ex.epoch)
-            _ops.ep_p2p_expert_forward(ex.local, self.world_size, self.rank, cap, ex.epoch, x.gate_up_proj_data,
-                                       x.gate_up_proj_scales, x.gate_up_proj_bias.data, x.down_proj_data,
-                                       x.down_proj_scales, x.down_proj_bias.data, self._back, self._ws,
-                                       ex.peer_bases, float(x.alpha), float(x.limit), int(x.gemm_mode))
-            self.last_send_counts = send_counts
-            return _ops.ep_p2p_combine(ex.local, self.world_size, cap, ex.epoch, pos_of, idx, H, h.device).view(shape)
+            return self._p2p_finish(h, idx, send_counts, pos_of, cap).view(shape)
         if self.capacity_tokens:
             if h.shape[0] > self.capacity_tokens:
                 raise RuntimeError(f"{h.shape[0]} tokens exceed capacity_tokens={self.capacity_tokens}")
@@ -227,6 +248,9 @@ class ExpertParallelMoELayer(nn.Module):
     def forward(self, hidden_states: torch.Tensor):
         _ops.register_ops()
         h = hidden_states.reshape(-1, self.experts.hidden_size).contiguous()
+        if self.experts.transport == "p2p" and self.top_k == self.experts.top_k:
+            out, scores, idx = self.experts.forward_with_router(h, self.router_weight, self.router_bias)
+            return out.view(hidden_states.shape), scores, idx
         _, scores, idx = torch.ops.gptoss.router_topk(h, self.router_weight.data, self.router_bias.data,
                                                       int(self.top_k))
         out = self.experts(h, idx, scores.float())

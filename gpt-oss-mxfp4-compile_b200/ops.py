@@ -592,6 +592,33 @@ def ep_p2p_buffer_bytes(world_size: int, capacity: int, hidden_size: int) -> int
     return int(_lib.query("gptoss_ep_p2p_buffer_bytes", int(world_size), int(capacity), int(hidden_size)))
 
 
+def ep_p2p_route_dispatch(hidden, router_weight, router_bias, top_k: int, world_size: int, rank: int,
+                          capacity: int, local_base: int, peer_bases, epoch: int):
+    """Router + dispatch in one call (one launch at decode sizes). Returns
+    (scores bf16 [T, k], router_indices i64 [T, k], send_counts i32 [W], pos_of i32 [T*k])."""
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _cuda(router_weight, "router weight")
+    _dtype(router_weight, (torch.bfloat16,), "router weight")
+    _dtype(router_bias, (torch.bfloat16,), "router bias")
+    T, H = hidden.shape
+    E = router_weight.shape[0]
+    dev = hidden.device
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=dev)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
+    wf = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+    send_counts = torch.empty(world_size, dtype=torch.int32, device=dev)
+    pos_of = torch.empty(T * top_k, dtype=torch.int32, device=dev)
+    st = _stream(dev)
+    ws = _scratch(dev, st, int(_lib.query("gptoss_ep_dispatch_workspace_bytes", T, top_k, world_size)))
+    _lib.call("gptoss_ep_p2p_route_dispatch", _p(hidden) if T else None, router_weight.data_ptr(),
+              router_bias.data_ptr(), T, int(top_k), int(E), int(world_size), int(rank), H, int(capacity),
+              int(local_base), peer_bases.data_ptr(), int(epoch), idx.data_ptr() if T else None,
+              scores.data_ptr() if T else None, wf.data_ptr() if T else None, send_counts.data_ptr(),
+              pos_of.data_ptr() if T else None, ws.data_ptr(), ws.numel(), status_tensor(dev).data_ptr(), st)
+    return scores, idx, send_counts, pos_of
+
+
 def ep_p2p_dispatch(hidden, router_indices, routing_weights, num_experts: int, world_size: int, rank: int,
                     capacity: int, local_base: int, peer_bases, epoch: int):
     """Quantised rows straight into the owners' receive rows + dispatch flags.

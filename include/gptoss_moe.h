@@ -309,7 +309,10 @@ int gptoss_ep_combine(const void* back_rows, int64_t num_back_rows, const int32_
  * bf16. One layer, with `epoch` = 1, 2, ... per call
  * and identical on every rank:
  *   gptoss_ep_p2p_dispatch        quantised rows stored straight into the owners' receive
- *                                 rows, then dispatch flag[rank] raised on every peer;
+ *                                 rows, then dispatch flag[rank] raised on every peer
+ *                                 (one cluster launch up to 64 tokens x top-k <= 512);
+ *   gptoss_ep_p2p_route_dispatch  the router (logits, top-k, softmax, as gptoss_router_topk)
+ *                                 and the dispatch, one launch at decode sizes;
  *   gptoss_ep_p2p_expert_forward  waits for every sender's flag, runs the local experts,
  *                                 stores each output row into its source rank's return
  *                                 rows, raises return flag[W + rank] on every peer;
@@ -329,6 +332,16 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
                            const uint64_t* peer_bases, int32_t epoch, int32_t* send_counts,
                            int32_t* pos_of, void* workspace, size_t workspace_bytes,
                            int32_t* status_dev, void* stream);
+/* Router + dispatch: router_indices_out [T, k] i64, router_scores_out [T, k] bf16 (may be
+ * NULL), routing_weights_out [T, k] f32 (the scores as f32); the rest as
+ * gptoss_ep_p2p_dispatch. */
+int gptoss_ep_p2p_route_dispatch(const void* hidden, const void* router_weight, const void* router_bias,
+                                 int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
+                                 int64_t hidden_size, int64_t capacity, void* local_base,
+                                 const uint64_t* peer_bases, int32_t epoch, int64_t* router_indices_out,
+                                 void* router_scores_out, float* routing_weights_out, int32_t* send_counts,
+                                 int32_t* pos_of, void* workspace, size_t workspace_bytes,
+                                 int32_t* status_dev, void* stream);
 int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int64_t capacity,
                                  int32_t epoch, int num_local_experts, int64_t hidden_size,
                                  int64_t intermediate_size, const uint8_t* gate_up_data,

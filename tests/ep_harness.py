@@ -166,6 +166,16 @@ def nccl_worker(rank: int, world: int, port: int, shapes, q):
             torch.cuda.synchronize()
             results.append(("layer", e_tot, hs, pkg.ops.read_status(dev), bool(torch.equal(i1, i2)),
                             bool(torch.equal(s1, s2)), rel_l2(o1.cpu(), o2.cpu()), None))
+            # the same layer over peer memory: router and dispatch in one call
+            p2p_l = EP.ExpertParallelExperts(local, e_tot, capacity_tokens=T + 8 * world, transport="p2p", top_k=K)
+            ep_layer_p2p = EP.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), K, p2p_l)
+            for _ in range(2):
+                o3, s3, i3 = ep_layer_p2p(h.to(dev))
+            torch.cuda.synchronize()
+            st3 = pkg.ops.read_status(dev)
+            p2p_l.close()
+            results.append(("layer", e_tot, hs, st3, bool(torch.equal(i3, i2)), bool(torch.equal(s3, s2)),
+                            rel_l2(o3.cpu(), o2.cpu()), None))
         q.put((rank, results, None))
     except Exception as e:  # reported to the parent, which fails the test
         import traceback

@@ -165,3 +165,77 @@ def test_p2p_wait_gives_up_with_status(pkg, dev):
         assert float((x * 2).sum()) == 8.0          # the context is healthy
     finally:
         pkg.ops.ipc_free(base)
+
+
+def _device_bytes(addr: int, n: int) -> np.ndarray:
+    """n bytes of device memory at a raw address (the exchange buffers are not tensors)."""
+    from cuda.bindings import runtime as rt
+    out = np.empty(n, dtype=np.uint8)
+    err, = rt.cudaMemcpy(out.ctypes.data, addr, n, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+    assert err == rt.cudaError_t.cudaSuccess, err
+    return out
+
+
+@pytest.mark.parametrize("world,T,router", [(1, 24, False), (2, 24, True), (4, 24, False), (4, 24, True),
+                                            (2, 80, False), (2, 80, True)])
+def test_p2p_emulated_ranks(pkg, dev, world, T, router):
+    # The peer-memory protocol with every rank's exchange buffer on this one GPU: all
+    # dispatches, then every owner's expert forward, then every combine, in stream order
+    # (each wait finds its flags already raised). T = 24 runs the one-launch dispatch
+    # (router and quantiser fused into a cluster kernel), T = 80 the separate kernels.
+    E, H, I, k = 8 * world if world > 1 else 8, 512, 512, 4
+    d = O.synth_layer(40 + world, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    full = build_experts(pkg, d, dev, E, H, I)
+    locs = [pkg.ep.shard_experts(full, q, world) for q in range(world)]
+    cap = (T + 4 * world) * k
+    rb = pkg.ops.ep_row_bytes(H)
+    bases = [pkg.ops.ipc_alloc(pkg.ops.ep_p2p_buffer_bytes(world, cap, H))[0] for _ in range(world)]
+    peer_bases = torch.tensor(bases, dtype=torch.int64, device=dev)
+    rw, rbias = d["router_w"].to(dev), d["router_b"].to(dev)
+    try:
+        for epoch in (1, 2):                             # the second call reuses the buffers
+            ins, disp = [], []
+            for r in range(world):
+                h, ix, wv = _inputs(100 * epoch + r, T + 4 * r, E, H, k)
+                hd = h.to(dev)
+                if router:
+                    sc, ixd, cnt, pos = pkg.ops.ep_p2p_route_dispatch(hd, rw, rbias, k, world, r, cap, bases[r],
+                                                                      peer_bases, epoch)
+                    _, sc_ref, ix_ref = pkg.ops.router_topk_impl(hd, rw, rbias, k)
+                    assert torch.equal(ixd, ix_ref) and torch.equal(sc, sc_ref), f"routing, rank {r}"
+                    ix, wv = ixd.cpu(), sc.float().cpu()
+                else:
+                    ixd = ix.to(dev)
+                    cnt, pos = pkg.ops.ep_p2p_dispatch(hd, ixd, wv.to(dev), E, world, r, cap, bases[r], peer_bases,
+                                                       epoch)
+                ins.append((h, ix, wv, ixd, pos, cnt))
+            backs = []
+            for q in range(world):
+                x = locs[q]
+                back = torch.empty((world * cap, H), dtype=torch.bfloat16, device=dev)
+                ws = torch.empty(pkg.ops.workspace_bytes(world * cap, 1, E // world, H, I), dtype=torch.uint8,
+                                 device=dev)
+                pkg.ops.ep_p2p_expert_forward(bases[q], world, q, cap, epoch, x.gate_up_proj_data,
+                                              x.gate_up_proj_scales, x.gate_up_proj_bias, x.down_proj_data,
+                                              x.down_proj_scales, x.down_proj_bias, back, ws, peer_bases)
+                backs.append((back, ws))
+            for r, (h, ix, wv, ixd, pos, cnt) in enumerate(ins):
+                out = pkg.ops.ep_p2p_combine(bases[r], world, cap, epoch, pos, ixd, H, dev)
+                torch.cuda.synchronize()
+                assert pkg.ops.read_status(dev) == 0
+                # the dispatch rows equal the packed send rows of the fixed-capacity layout
+                rows, counts, pos_ref = pkg.ops.ep_dispatch(h.to(dev), ixd, wv.to(dev), E, world, cap)
+                assert torch.equal(cnt, counts) and torch.equal(pos, pos_ref), f"layout, rank {r}"
+                rows = rows.cpu().numpy()
+                for q in range(world):
+                    seg = _device_bytes(bases[q] + 4 * 64 * 4 + r * cap * rb, cap * rb).reshape(cap, rb)
+                    c = int(counts[q])
+                    assert np.array_equal(seg[:c], rows[q * cap:q * cap + c]), f"rows {r}->{q}"
+                    assert np.array_equal(seg[c:, rb - 8:], rows[q * cap + c:(q + 1) * cap, rb - 8:]), "markers"
+                assert_output_tolerance(out.cpu(), O.w4a8_experts_forward(h, ix.numpy(), wv.numpy(), wn),
+                                        f"world {world} rank {r} epoch {epoch}")
+    finally:
+        torch.cuda.synchronize()
+        for b in bases:
+            pkg.ops.ipc_free(b)
