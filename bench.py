@@ -41,9 +41,6 @@ CONFIGS = {
 NCU_TRAFFIC_BYTES = {"decode": 294_617_088,     # profiles/moe_gemm_swap_decode_T32.md
                      "prefill": 769_571_328}    # profiles/moe_gemm_pair_prefill_T8192.md (GEMM1)
 
-KERNELS_PER_STEP = 5   # router, route_sort, gather_quant, gemm1, gemm2
-# router; dispatch: route_sort + pack; local: unpack, route_sort, gather, gemm1, gemm2; combine
-KERNELS_PER_STEP_EP = 9
 
 
 def parse_args():
@@ -269,11 +266,13 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     sampler = clock_sampler_start(dev.index)
     time.sleep(0.3)
+    launches0 = pkg._lib.query("gptoss_kernel_launch_count")
     for i in range(K):
         flush.zero_()
         ev[i][0].record(stream)
         step()
         ev[i][1].record(stream)
+    launches = int(pkg._lib.query("gptoss_kernel_launch_count") - launches0)   # this library's kernels
     torch.cuda.synchronize(dev)
     clocks = clock_sampler_stop(sampler)
     barrier()
@@ -357,7 +356,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": T * H * 2,
                     "d2h_bytes_per_step": T * H * 2 + (2 * world * 4 if ep_info and ep_info["host_syncs_per_step"]
                                                        else 0)},
-            "gpu_launches": K * (KERNELS_PER_STEP if world == 1 else KERNELS_PER_STEP_EP),
+            "gpu_launches": launches,
             "cpu_baseline": cpu,
         }
         if stages:

@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -57,6 +58,9 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 constexpr int kMaxDevices = 64;
+
+// Kernels this library launched in this process (every device), for launch accounting.
+std::atomic<uint64_t> g_kernel_launches{0};
 
 struct DeviceInfo {
   int sms = 0;
@@ -135,6 +139,7 @@ int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.attrs = attr;
   cfg.numAttrs = n;
   GPTOSS_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return GPTOSS_OK;
 }
 
@@ -607,6 +612,8 @@ const char* gptoss_last_error(void) { return g_last_error.c_str(); }
 
 int gptoss_abi_version(void) { return 1; }
 
+uint64_t gptoss_kernel_launch_count(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
+
 int gptoss_read_status(int32_t* status_dev, int32_t* status_host, void* stream) {
   GPTOSS_CHECK(status_host != nullptr, "status_host is null");
   DeviceInfo di;
@@ -704,6 +711,7 @@ int gptoss_swiglu(const void* x, int dtype, int64_t rows, int64_t cols, void* ou
     swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, n,
                                                          static_cast<__nv_bfloat16*>(out), alpha, limit);
   GPTOSS_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return GPTOSS_OK;
 }
 
@@ -729,6 +737,7 @@ int gptoss_convert_scales_blocked(const uint8_t* scales_rowmajor, int64_t rows, 
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
   convert_scales_kernel<<<blocks, 256, 0, st>>>(scales_rowmajor, rows, G, g4, blocked);
   GPTOSS_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return GPTOSS_OK;
 }
 
@@ -750,6 +759,7 @@ int gptoss_batch_convert_a_scales(const uint8_t* scales_rowmajor, const int32_t*
   batch_convert_scales_kernel<<<num_experts, 256, 0, st>>>(scales_rowmajor, expert_counts, expert_offsets, num_experts,
                                                            G, (G + 3) / 4, blocked, sf_offsets);
   GPTOSS_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return GPTOSS_OK;
 }
 

@@ -55,6 +55,10 @@ const char* gptoss_last_error(void);
 /* ABI version of this header (bumped on any signature change). */
 int gptoss_abi_version(void);
 
+/* Kernels this library has launched in this process, on every device (launch accounting
+ * for benchmarks; no counterpart in the reference). */
+uint64_t gptoss_kernel_launch_count(void);
+
 /* Copies the 4-byte device status word that kernels set when a bounded wait times out
  * or an expert index is out of range (0 = ok) into *status_host and clears it.
  * Synchronises `stream`. */
