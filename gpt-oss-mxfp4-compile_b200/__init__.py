@@ -8,8 +8,8 @@ Public surface (mirrors kernels/cutlass_experts.py of the reference):
   CutlassGptOssExperts, load_cutlass_weights, quantize_activations_to_fp8, swiglu,
   pad_k_to_tile, pad_fp4_weights, pad_fp8_activations, get_cutlass_extension,
   ensure_custom_op_registered, MXFP_BLOCK_SIZE, MMA_TILE_K
-plus the fused layer (router + experts): :class:`GptOssMoELayer`, and expert
-parallelism over NCCL in :mod:`.ep`.
+plus the fused layer (router + experts): :class:`GptOssMoELayer`, expert parallelism
+(peer memory or NCCL) in :mod:`.ep`, and Hugging Face model integration in :mod:`.hf`.
 """
 from . import _lib, ops  # noqa: F401
 from .cutlass_experts import (  # noqa: F401
@@ -27,3 +27,4 @@ from .cutlass_experts import (  # noqa: F401
 )
 from .layer import GptOssMoELayer  # noqa: F401
 from . import ep  # noqa: F401,E402
+from . import hf  # noqa: F401,E402

@@ -172,7 +172,8 @@ class CutlassGptOssExperts(nn.Module):
         self.intermediate_size = config.intermediate_size
         self.hidden_size = config.hidden_size
         self.alpha = 1.702
-        self.limit = getattr(config, "swiglu_limit", 7.0)
+        limit = getattr(config, "swiglu_limit", 7.0)
+        self.limit = 7.0 if limit is None else limit   # HF configs may carry swiglu_limit=None
         self.gemm_mode = _ops.GEMM_AUTO
 
         self.gate_up_proj_bias = nn.Parameter(
