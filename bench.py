@@ -2,7 +2,7 @@
 """GPT-OSS-20B MoE layer benchmark on B200 (router + W4A8 experts, one step = one layer
 forward over one batch of synthetic tokens).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config decode|prefill]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config decode|prefill|stack|zipf]
   python bench.py --impl reference ...     CPU baseline arm (rank 0 only)
 
 Workload at N=1 is BASELINE config 1 (decode, T=32 tokens, E=32, H=I=2880, top-4,
@@ -34,7 +34,13 @@ CONFIGS = {
     # name: (T, E, H, I, top_k, skew, description)
     "decode": (32, 32, 2880, 2880, 4, None, "GPT-OSS-20B MoE layer decode, T=32 (BASELINE config 1)"),
     "prefill": (8192, 32, 2880, 2880, 4, "prefill", "GPT-OSS-20B MoE layer prefill, T=8192, loads +-50% (BASELINE config 2)"),
+    "stack": (4096, 32, 2880, 2880, 4, None,
+              "GPT-OSS-20B-shaped 24-layer stack (RMSNorm -> MoE -> residual), T=4096 (BASELINE config 3)"),
+    "zipf": (16384, 128, 2880, 2880, 4, "zipf",
+             "GPT-OSS-120B-shaped MoE layer, 1.5 log-Zipf(1.1) router bias, T=16384 (BASELINE config 4)"),
 }
+STACK_LAYERS = 24
+CPU_BASELINE_CONFIGS = ("decode", "prefill")   # the others are minutes of CPU work per step
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from
 # the ncu capture summarised in profiles/ (None until captured for this kernel/config).
@@ -162,8 +168,12 @@ def cpu_baseline(cfg_name: str, steps_cap: int, budget_s: float):
         layer(h)
         times.append(time.perf_counter() - t)
     per = statistics.median(times)
+    what = f"{n} full {cfg_name} steps (T={T})"
+    if cfg_name == "stack":   # one MoE layer timed; the stack is STACK_LAYERS of them (norms not counted)
+        per *= STACK_LAYERS
+        what = f"{n} single-layer steps (T={T}) x {STACK_LAYERS} layers"
     return {"value": T / per, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} full {cfg_name} steps (T={T}) of the dequantised bf16 expert path + HF router, "
+            "sample": f"{what} of the dequantised bf16 expert path + HF router, "
                       f"median {per * 1e3:.1f} ms/step; weights dequantised once beforehand ({dequant_s:.1f} s)",
             "ms_per_step": per * 1e3, "steps_run": n}
 
@@ -187,6 +197,52 @@ def run_reference(args):
     return 0
 
 
+def device_layer_weights(E, H, I, seed, dev):
+    """One layer's random weights with the synthetic recipe's distributions, drawn on the
+    device (the 24-layer stack's 10 GB would take minutes on the host)."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    d = {"router_w": (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+         "router_b": (torch.randn(E, generator=g, device=dev) * 0.01).to(torch.bfloat16)}
+    for pre, n, kk in (("gu", 2 * I, H), ("dn", H, I)):
+        d[f"{pre}_blocks"] = torch.randint(0, 256, (E, n, kk // 2), generator=g, device=dev, dtype=torch.uint8)
+        d[f"{pre}_scales"] = torch.randint(119, 124, (E, n, kk // 32), generator=g, device=dev, dtype=torch.uint8)
+        d[f"{pre}_bias"] = (torch.randn(E, n, generator=g, device=dev) * 0.01).to(torch.bfloat16).float()
+    return d
+
+
+def build_stack(pkg, Cfg, world, rank, dev, args, T, E, H, I, k):
+    """STACK_LAYERS layers of RMSNorm -> MoE layer -> residual, fresh
+    weights per layer (identical on every rank); under torchrun each rank keeps its E/N
+    experts of every layer (NCCL all-to-alls with exact splits)."""
+    import torch
+    layers = []
+    e_loc = E // world
+    lo, hi = rank * e_loc, (rank + 1) * e_loc
+
+    class LocalCfg(Cfg):
+        num_local_experts = e_loc
+
+    for li in range(STACK_LAYERS):
+        d = device_layer_weights(E, H, I, 7000 + li, dev)
+        ex = pkg.CutlassGptOssExperts(LocalCfg()).to(dev)
+        ex.gate_up_proj_bias.data.copy_(d["gu_bias"][lo:hi])
+        ex.down_proj_bias.data.copy_(d["dn_bias"][lo:hi])
+        pkg.load_cutlass_weights(ex, d["gu_blocks"][lo:hi], d["gu_scales"][lo:hi], d["dn_blocks"][lo:hi],
+                                 d["dn_scales"][lo:hi], dev)
+        if world == 1:
+            lay = pkg.GptOssMoELayer(Cfg()).to(dev)
+            lay.experts = ex
+            lay.router_weight.data.copy_(d["router_w"])
+            lay.router_bias.data.copy_(d["router_b"])
+        else:
+            ep_ex = pkg.ep.ExpertParallelExperts(ex, E, top_k=k)
+            lay = pkg.ep.ExpertParallelMoELayer(d["router_w"], d["router_b"], k, ep_ex)
+        layers.append(lay)
+        del d
+    return layers, torch.ones(H, dtype=torch.bfloat16, device=dev)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -207,7 +263,18 @@ def run_ours(args):
         num_experts_per_tok = k
         swiglu_limit = 7.0
 
-    if world == 1:
+    stack = args.config == "stack"
+    if stack:
+        layers, norm_w = build_stack(pkg, Cfg, world, rank, dev, args, T, E, H, I, k)
+        g = torch.Generator().manual_seed(1000 + rank)
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
+        layer, ex = layers[0], None
+
+        def forward(t):
+            for lay in layers:
+                t = t + lay(torch.nn.functional.rms_norm(t, (H,), norm_w, 1e-5))[0]
+            return t
+    elif world == 1:
         d = O.synth_layer(rank, E=E, H=H, I=I, T=T, skew=skew)
         layer = pkg.GptOssMoELayer(Cfg()).to(dev)
         layer.router_weight.data.copy_(d["router_w"])
@@ -243,7 +310,11 @@ def run_ours(args):
         layer = pkg.ep.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), k, ep_experts)
         g = torch.Generator().manual_seed(1000 + rank)
         x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
-    del d
+    if not stack:
+        del d
+
+        def forward(t):
+            return layer(t)[0]
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -252,7 +323,7 @@ def run_ours(args):
             dist.barrier()
 
     def step():
-        return layer(x)
+        return forward(x)
 
     for _ in range(args.warmup):
         step()
@@ -285,7 +356,7 @@ def run_ours(args):
 
     # ---------------------------------------------------------------- per-stage (roofline)
     stages = (stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, args.config)
-              if world == 1 else None)
+              if world == 1 and not stack else None)
 
     # ---------------------------------------------------------------- end to end
     xh = x.cpu().pin_memory()
@@ -299,7 +370,7 @@ def run_ours(args):
         flush.zero_()
         a.record(stream)
         xd.copy_(xh, non_blocking=True)
-        y, _, _ = layer(xd)
+        y = forward(xd)
         oh.copy_(y, non_blocking=True)
         b.record(stream)
         b.synchronize()
@@ -313,7 +384,7 @@ def run_ours(args):
     assert pkg.ops.read_status(dev) == 0
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config in CPU_BASELINE_CONFIGS:
         cb = cpu_baseline(args.config, 1000, args.cpu_budget_s)
         cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
 
@@ -335,7 +406,7 @@ def run_ours(args):
             ep_info = {"layout": "exact splits", "transport": "nccl", "rank0_rows_sent": s_send,
                        "rank0_rows_received": s_recv,
                        "rank0_nvlink_bytes_per_step": (sum(s_send) - s_send[rank] + sum(s_recv) - s_recv[rank])
-                       * (rb + 2 * H), "host_syncs_per_step": 1}
+                       * (rb + 2 * H), "host_syncs_per_step": STACK_LAYERS if stack else 1}
         ep_info.update({"experts_per_rank": E // world, "row_bytes_dispatch": rb, "row_bytes_combine": H * 2})
 
     if rank == 0:
@@ -354,8 +425,8 @@ def run_ours(args):
             "clocks": clocks,
             "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2 + (2 * world * 4 if ep_info and ep_info["host_syncs_per_step"]
-                                                       else 0)},
+                    "d2h_bytes_per_step": T * H * 2 + (2 * world * 4 * ep_info["host_syncs_per_step"]
+                                                       if ep_info else 0)},
             "gpu_launches": launches,
             "cpu_baseline": cpu,
         }
@@ -368,7 +439,8 @@ def run_ours(args):
             line["roofline_note"] = "per-kernel roofline is reported by the N=1 run"
         print(json.dumps(line), flush=True)
     if world > 1:
-        layer.experts.close()
+        for lay in (layers if stack else [layer]):
+            lay.experts.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0
@@ -411,7 +483,7 @@ def stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, 
     g1_gbs = b_g1 / (t_g1 / 1e3) / 1e9
     layer_gbs = b_layer / (ms / 1e3) / 1e9
     flops = 2 * T * k * (H * 2 * I + I * H)
-    if cfg_name == "prefill":
+    if cfg_name in ("prefill", "zipf"):
         # dense block-scaled FP8 x FP4 contraction: the tensor pipe bounds it; its peak is
         # taken as twice the measured dense bf16 rate (the fp8/fp6/fp4 : bf16 rate ratio)
         g1_flops = 2 * T * k * H * 2 * I
