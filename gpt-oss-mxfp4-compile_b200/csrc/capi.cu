@@ -465,8 +465,18 @@ int stage_gemm1(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
 }
 
 // Stage 3: GEMM2 + bias, x routing weight, bf16 scatter-add into out (accumulates).
+// Peer-memory return of the expert-parallel GEMM2 (see GemmParams::ep_*).
+struct EpReturn {
+  const uint64_t* peer_bases;
+  int64_t ret_off, cap;
+  int32_t* counter;
+  int world, rank;
+  int32_t epoch;
+};
+
 int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt, void* out, const WsPtrs& w,
-                GemmLayout lay, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+                GemmLayout lay, int* status, const DeviceInfo& di, int dev, cudaStream_t st,
+                const EpReturn* ep = nullptr) {
   const int64_t Ki = pad128(I);
   GemmJob g2{};
   g2.act = w.inter_codes; g2.act_rows = A; g2.lda = I; g2.wgt = wt.dn_data;
@@ -476,6 +486,11 @@ int stage_gemm2(int64_t A, int E, int64_t H, int64_t I, const ExpertWeights& wt,
   g2.p.out = out; g2.p.ld_out = H; g2.p.bias = wt.dn_bias; g2.p.token_idx = w.sorted_token; g2.p.row_weights = w.sorted_weight;
   g2.sfa_bytes = w.inter_sf_cap;
   g2.sfb_bytes = wt.ldb_dn * E;
+  if (ep != nullptr) {
+    GPTOSS_CHECK(lay.swap, "peer-memory GEMM2 return needs weights-on-M tiles");
+    g2.p.ep_peer_bases = ep->peer_bases; g2.p.ep_ret_off = ep->ret_off; g2.p.ep_cap = ep->cap;
+    g2.p.ep_counter = ep->counter; g2.p.ep_world = ep->world; g2.p.ep_rank = ep->rank; g2.p.ep_epoch = ep->epoch;
+  }
   return run_gemm<kEpiGemm2>(g2, lay.swap, lay.spread, di, dev, st);
 }
 
@@ -1336,6 +1351,7 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
   int32_t* ret_counter = static_cast<int32_t*>(local_base) + kP2pCounterReturn;
   const size_t rp_smem = recv_prologue_smem(R, num_local_experts);
   int prefetch = 0;
+  bool fused_return = false;
   if (R <= kRpMaxRows && rp_smem <= 200 * 1024) {
     // one launch: flag wait, sort by local expert, gather into the blocked layout, zero back_rows
     static uint64_t attr_done = 0;   // one bit per device
@@ -1354,10 +1370,13 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
     rq.sorted_token = p.sorted_token; rq.sorted_expert = p.sorted_expert; rq.sorted_weight = p.sorted_weight;
     rq.counts = p.counts; rq.offsets = p.offsets; rq.sf_offsets_a = p.sfoff_a; rq.sf_offsets_b = p.sfoff_b;
     rq.g4_a = static_cast<int>(Kh / 128); rq.g4_b = static_cast<int>(Ki / 128); rq.spread = lay.spread ? 1 : 0;
-    rq.act_codes = p.act_codes; rq.act_sf = p.act_sf; rq.back_rows = static_cast<__nv_bfloat16*>(back_rows);
+    // weights-on-M GEMM2 stores the rows straight into the sources' return rows
+    rq.act_codes = p.act_codes; rq.act_sf = p.act_sf;
+    rq.back_rows = lay.swap ? nullptr : static_cast<__nv_bfloat16*>(back_rows);
     const int grid = static_cast<int>(std::min<int64_t>(di.sms, std::max<int64_t>(R, 1)));
     GPTOSS_TRY(launch_pdl(ep_recv_prologue_kernel, dim3(grid), dim3(256), rp_smem, st, rq));
     prefetch = kPrefetchTilesAfterPrologue;
+    fused_return = lay.swap;
   } else {
     const int ublocks = static_cast<int>(std::min<int64_t>((R + 255) / 256, 4 * di.sms));
     GPTOSS_TRY(launch_pdl(ep_unpack_meta_p2p_kernel, dim3(ublocks), dim3(256), 0, st, recv, R, H, flags, world_size,
@@ -1382,6 +1401,12 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
   }
   GPTOSS_TRY(stage_gemm1(R, num_local_experts, hidden_size, intermediate_size, w, swiglu_alpha, swiglu_limit, p, lay,
                          status, di, dev, st, prefetch));
+  if (fused_return) {
+    const EpReturn er{peer_bases, p2p_ret_offset(world_size, rank, capacity, rb, H), capacity, ret_counter,
+                      world_size, rank, epoch};
+    return stage_gemm2(R, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, lay, status, di, dev,
+                       st, &er);
+  }
   GPTOSS_TRY(stage_gemm2(R, num_local_experts, hidden_size, intermediate_size, w, back_rows, p, lay, status, di,
                          dev, st));
   return launch_pdl(ep_return_p2p_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, st,

@@ -237,7 +237,7 @@ struct RecvPrologueParams {
   int g4_a, g4_b, spread;
   uint8_t* act_codes;
   uint8_t* act_sf;
-  __nv_bfloat16* back_rows;    // [R, H], zeroed here
+  __nv_bfloat16* back_rows;    // [R, H], zeroed here (nullptr: not needed)
 };
 
 __host__ __device__ inline size_t recv_prologue_smem(int64_t R, int E) {
@@ -349,11 +349,13 @@ __global__ void __launch_bounds__(256) ep_recv_prologue_kernel(const RecvPrologu
       *reinterpret_cast<uint32_t*>(p.act_sf + sfa[e] + blocked_sf_offset(r_in, 4 * a, p.g4_a)) =
           *reinterpret_cast<const uint32_t*>(src + H + 4 * a);
   }
-  const int64_t n16 = static_cast<int64_t>(R) * H / 8;
-  uint4* z = reinterpret_cast<uint4*>(p.back_rows);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < n16;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    z[i] = make_uint4(0, 0, 0, 0);
+  if (p.back_rows != nullptr) {   // null: GEMM2 stores the rows straight into the sources' buffers
+    const int64_t n16 = static_cast<int64_t>(R) * H / 8;
+    uint4* z = reinterpret_cast<uint4*>(p.back_rows);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + tid; i < n16;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      z[i] = make_uint4(0, 0, 0, 0);
+  }
 }
 
 // Source: wait for every owner's return flag, then the combine of ep_combine_kernel over

@@ -31,6 +31,7 @@
 #include <cuda_bf16.h>
 #include "ptx.cuh"
 #include "numerics.cuh"
+#include "ep_p2p.cuh"
 
 namespace gptoss {
 
@@ -66,6 +67,17 @@ struct GemmParams {
   // previous kernel (0: none). The tiles are guessed assuming one activation chunk per
   // expert -- the decode case; a wrong guess only costs bandwidth.
   int prefetch_tiles;
+  // kEpiGemm2 on weights-on-M tiles, expert parallelism over peer memory (ep_world > 0):
+  // output row r is a received row (segment s = r / ep_cap, slot j); its values go straight
+  // into source rank s's return rows (ep_ret_off bytes into s's exchange buffer, row j)
+  // with 16-byte stores instead of being added into `out`, and the last CTA to finish
+  // raises return flag [ep_world + ep_rank] on every peer.
+  const uint64_t* ep_peer_bases;
+  int64_t ep_ret_off;
+  int64_t ep_cap;
+  int32_t* ep_counter;
+  int ep_world, ep_rank;
+  int32_t ep_epoch;
 };
 
 // PAIR: tokens-on-M tiles computed by a CTA pair (cluster of 2, tcgen05 cta_group::2):
@@ -730,10 +742,19 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
                   const __nv_bfloat162 v1 = __floats2bfloat162_rn(__fmul_rn(z0.z, wr), __fmul_rn(z0.w, wr));
                   const __nv_bfloat162 v2 = __floats2bfloat162_rn(__fmul_rn(z1.x, wr), __fmul_rn(z1.y, wr));
                   const __nv_bfloat162 v3 = __floats2bfloat162_rn(__fmul_rn(z1.z, wr), __fmul_rn(z1.w, wr));
-                  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(o + tk * p.ld_out + n0),
-                               "r"(*reinterpret_cast<const uint32_t*>(&v0)), "r"(*reinterpret_cast<const uint32_t*>(&v1)),
-                               "r"(*reinterpret_cast<const uint32_t*>(&v2)), "r"(*reinterpret_cast<const uint32_t*>(&v3))
-                               : "memory");
+                  const uint4 pk4 = make_uint4(*reinterpret_cast<const uint32_t*>(&v0), *reinterpret_cast<const uint32_t*>(&v1),
+                                               *reinterpret_cast<const uint32_t*>(&v2), *reinterpret_cast<const uint32_t*>(&v3));
+                  if (p.ep_world > 0) {   // one received row per output row: a plain store into the source's rows
+                    const int s = static_cast<int>(tk / p.ep_cap);
+                    const int64_t j = tk - static_cast<int64_t>(s) * p.ep_cap;
+                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(p.ep_peer_bases[s]) +
+                                                                         p.ep_ret_off) + j * p.ld_out + n0;
+                    *reinterpret_cast<uint4*>(dst) = pk4;
+                  } else {
+                    asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(o + tk * p.ld_out + n0),
+                                 "r"(pk4.x), "r"(pk4.y), "r"(pk4.z), "r"(pk4.w)
+                                 : "memory");
+                  }
                 }
               }
             }
@@ -756,6 +777,12 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
   // TMEM and the odd CTA's epilogue arrives on the even CTA's barriers.
   if constexpr (PAIR) cluster_sync();
   else __syncthreads();
+  if constexpr (EPI == kEpiGemm2 && SWAP) {
+    // every epilogue store of this CTA is behind the barrier: publish them (one fence per
+    // CTA, then the last CTA raises the return flags)
+    if (p.ep_world > 0 && threadIdx.x == 0)
+      p2p_last_cta_signal(p.ep_counter, p.ep_peer_bases, p.ep_world, p.ep_world + p.ep_rank, p.ep_epoch);
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -177,12 +177,14 @@ def _device_bytes(addr: int, n: int) -> np.ndarray:
 
 
 @pytest.mark.parametrize("world,T,router", [(1, 24, False), (2, 24, True), (4, 24, False), (4, 24, True),
-                                            (2, 80, False), (2, 80, True)])
+                                            (4, 8, True), (2, 80, False), (2, 80, True)])
 def test_p2p_emulated_ranks(pkg, dev, world, T, router):
     # The peer-memory protocol with every rank's exchange buffer on this one GPU: all
     # dispatches, then every owner's expert forward, then every combine, in stream order
     # (each wait finds its flags already raised). T = 24 runs the one-launch dispatch
-    # (router and quantiser fused into a cluster kernel), T = 80 the separate kernels.
+    # (router and quantiser fused into a cluster kernel), T = 80 the separate kernels; the
+    # owners' GEMM2 stores its rows straight into the sources' return rows (16-row chunks
+    # at T = 8, 64-row chunks otherwise).
     E, H, I, k = 8 * world if world > 1 else 8, 512, 512, 4
     d = O.synth_layer(40 + world, E=E, H=H, I=I, T=1)
     wn = O.numpy_weights(d)
