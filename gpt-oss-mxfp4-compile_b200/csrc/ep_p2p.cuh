@@ -9,9 +9,10 @@
 //             the segment past the count carry the empty-slot marker; then it raises
 //             flag[s] of every peer to the call's epoch (release, system scope).
 //   expert    rank q waits (bounded) until flag[s] >= epoch for every s, runs the local
-//             expert forward on its W * cap received rows, and copies each valid output
-//             row back into the ret rows of its source rank s at segment q; then it
-//             raises flag[W + q] of every peer.
+//             expert forward on its W * cap received rows, and each valid output row goes
+//             back into the ret rows of its source rank s at segment q (stored by GEMM2's
+//             epilogue for weights-on-M tiles, else copied by ep_return_p2p_kernel); then
+//             the last CTA of that kernel raises flag[W + q] of every peer.
 //   combine   rank s waits (bounded) until flag[W + q] >= epoch for every q and sums each
 //             token's k returned rows (ascending expert, fp32, one bf16 rounding).
 //
