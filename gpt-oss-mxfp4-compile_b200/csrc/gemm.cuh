@@ -1,21 +1,27 @@
 // Grouped W4A8 GEMM for sm_100a: FP8 e4m3 activations x E2M1 weights, UE8M0 1x32 block
 // scales, fp32 accumulation in TMEM via tcgen05.mma kind::mxf8f6f4.block_scale.
 //
-// One persistent CTA per SM walks a ragged tile list built on the device from the
-// per-expert row counts (no host sync). Warp roles:
+// One persistent CTA per SM (or CTA pair) walks a ragged tile list built on the device
+// from the per-expert row counts (no host sync). Warp roles:
 //   warp 0     TMA producer: activation tile (2-D map, fp8), weight tile (3-D map,
 //              packed e2m1 expanded to the 8-bit smem container by the TMA unit),
-//              plus the 512-byte blocked scale chunks (plain bulk copies).
-//   warp 1     TMEM allocator + single-thread MMA issuer: tcgen05.cp of the scale chunks
-//              into TMEM, then 4 MMAs (K = 32 each) per 128-deep K block.
+//              plus the 512-byte blocked scale chunks (bulk copies, or 256-byte-row
+//              tensor maps for CTA pairs); SWAP tiles load two K blocks per stage.
+//   warp 1     TMEM allocator + MMA issuer: tcgen05.cp of the scale chunks into TMEM,
+//              then 4 MMAs (K = 32 each) per 128-deep K block. SWAP tiles add a second
+//              issuer warp (the last warp) that takes the odd K blocks into a second
+//              partial accumulator.
 //   warps 2+   epilogue: tcgen05.ld of the accumulator and one of three fused tails;
-//              4 warps (SWAP) or 12 warps, three per TMEM lane quarter, each warpgroup
-//              taking one 64-column slice of the 192-column tile (SWAP = false).
+//              4 warps (SWAP; two passes through shared memory) or 12 warps, three per
+//              TMEM lane quarter, each warpgroup taking one 64-column slice of the
+//              192-column tile (SWAP = false).
 //
 // Two orientations:
-//   SWAP = false  M = 128 activation rows, N = 192 weight rows (prefill-sized groups).
-//   SWAP = true   M = 128 weight rows,     N = 64 activation rows (decode: the weights
-//                 stream through the M side so a group of ~4 rows wastes little MMA).
+//   SWAP = false  M = 128 activation rows, N = 192 weight rows (prefill-sized groups;
+//                 PAIR: M = 256 over a CTA pair).
+//   SWAP = true   M = 128 weight rows, N = 16 (SPREAD) or 16/32/64 activation rows
+//                 (decode: the weights stream through the M side so a group of a few
+//                 rows wastes little MMA).
 //
 // Epilogues (all restate cutlass_experts.py:414-450 for the rows a tile owns):
 //   kEpiPlain  D = bf16(alpha[e] * acc) stored row-major (the fp4_group_mm op,
@@ -24,7 +30,8 @@
 //              then FP8 + UE8M0 requantisation written as the next GEMM's A operand
 //              (codes compact row-major, scales in the blocked layout).
 //   kEpiGemm2  y = bf16((float(bf16(acc)) + b_dn[e]) * w_row) added into out[token]
-//              with bf16x2 vector reductions (the scatter_add_ of :445-450).
+//              with bf16x2 vector reductions (the scatter_add_ of :445-450), or stored
+//              into the source rank's return rows over peer memory (expert parallelism).
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -93,7 +100,7 @@ struct GemmConfig {
   static constexpr int kWgtRowsCta = PAIR ? kWgtRows / 2 : kWgtRows;   // weight rows this CTA loads
   // Activation rows per tile. SWAP with reference-layout scales uses 64-row chunks that
   // start 0 or 64 rows into a 128-row scale block (TMEM column offset 0 or 2); SPREAD
-  // uses 16-row chunks (a 2 KB activation slot, so the ring holds 11 stages).
+  // uses 16-row chunks (a 2 KB activation slot per K block).
   static constexpr int kActRows = SWAP ? (SPREAD ? 16 : 64) : 128;
   static constexpr int kColChunks = (kActRows + 31) / 32;   // 32-column TMEM loads per tile
   static constexpr int kTileM = PAIR ? 2 * kActRows : kActRows;   // activation rows per tile
@@ -132,9 +139,10 @@ struct GemmConfig {
   static constexpr uint32_t kEpiStageBytes = SWAP ? 16384 : 0;   // weights-on-M epilogue staging
   static constexpr uint32_t kSmemBytes =
       1024 + kStages * kStageBytes + ((kBarrierBytes + 127) & ~127u) + kEpiStageBytes + 2048;
-  // Epilogue warps: one warpgroup for weights-on-M tiles (their GEMM1 epilogue reduces
-  // across the warpgroup); tokens-on-M tiles give each warpgroup one 64-column slice, so
-  // three warps share every TMEM lane quarter and hide each other's latency.
+  // Epilogue warps: one warpgroup for weights-on-M tiles (their two-pass epilogue
+  // regroups rows through shared memory across the warpgroup); tokens-on-M tiles give
+  // each warpgroup one 64-column slice, so three warps share every TMEM lane quarter and
+  // hide each other's latency.
   static constexpr int kEpiWarps = SWAP ? 4 : 4 * (kWgtRows / 64);
   static constexpr int kThreads = 64 + 32 * kEpiWarps + 32 * (kIssuers - 1);   // 2nd issuer: last warp
 };
