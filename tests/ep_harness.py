@@ -183,3 +183,41 @@ def nccl_worker(rank: int, world: int, port: int, shapes, q):
         q.put((rank, None, repr(e) + traceback.format_exc()))
     finally:
         dist.destroy_process_group()
+
+
+def dead_peer_worker(rank: int, world: int, port: int, q):
+    """Failure detection on the host: both ranks run one expert-parallel step, then rank 1
+    leaves without joining the next one (it exits between steps, nothing in flight). Rank 0's
+    next step must end with an error from the process group (peer gone, or the short
+    timeout), not hang."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    import __graft_entry__ as ge
+
+    pkg = ge.load_package()
+    from gpt_oss_mxfp4_compile_b200 import ep as EP
+
+    d = O.synth_layer(SEED, E=E, H=H, I=I, T=1)
+    wn = O.numpy_weights(d)
+    e_loc = E // world
+    local = pkg.CutlassGptOssExperts(Cfg(e_loc, H, I))
+    mod = EP.ExpertParallelExperts(local, E, kernels=OracleKernels(O.slice_experts(wn, rank * e_loc,
+                                                                                  (rank + 1) * e_loc), H))
+    h, ix, wv = routing_case("random", rank, world, 8)
+    mod(h, ix, wv)                                  # one good step on both ranks
+    if rank == 1:
+        q.put((rank, "left", None))
+        q.close()
+        q.join_thread()                             # the message is out before the process goes
+        os._exit(0)                                 # gone between steps
+    t0 = time.time()
+    try:
+        mod(h, ix, wv)
+        q.put((rank, ("no error", None, time.time() - t0), None))
+    except Exception as e:  # the expected outcome
+        q.put((rank, ("error", type(e).__name__, time.time() - t0), None))
+    q.close()
+    q.join_thread()
+    os._exit(0)                                     # the group is broken; skip its teardown

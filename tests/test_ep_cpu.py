@@ -5,7 +5,7 @@ import numpy as np
 import torch
 
 import oracle as O
-from ep_harness import E, H, I, K, SEED, cpu_worker, routing_case, run_ranks
+from ep_harness import E, H, I, K, SEED, cpu_worker, dead_peer_worker, routing_case, run_ranks
 
 
 def test_oracle_ep_chain_equals_single_device_forward():
@@ -86,3 +86,14 @@ def test_oracle_capacity_layout():
     b0 = O.ep_expert_rows(rows[:cap], H, O.slice_experts(wn, 0, E // 2))
     b1 = O.ep_expert_rows(rows[cap:], H, O.slice_experts(wn, E // 2, E))
     assert torch.equal(O.ep_combine(torch.cat([b0, b1]), pos, ix.numpy()), ref)
+
+
+def test_dead_peer_ends_with_an_error_not_a_hang():
+    # A rank that exits between steps: the surviving rank's next exchange raises (gloo
+    # reports the closed connection or its 5 s timeout) instead of waiting forever.
+    res = run_ranks(dead_peer_worker, 2, timeout=120)
+    (r0, e0), (r1, e1) = res
+    assert e0 is None and e1 is None and r1 == "left"
+    status, kind, elapsed = r0
+    assert status == "error", r0
+    assert elapsed < 60, r0
