@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <cstdarg>
@@ -58,6 +59,15 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 constexpr int kMaxDevices = 64;
+
+// NVTX range around one entry point (visible in Nsight timelines and `ncu --nvtx`; the
+// calls are no-ops while no tool is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Kernels this library launched in this process (every device), for launch accounting.
 std::atomic<uint64_t> g_kernel_launches{0};
@@ -644,6 +654,7 @@ int gptoss_fused_moe_routing(const int64_t* router_indices, const float* routing
                              int top_k, int num_experts, int64_t* sorted_token_idx, int64_t* sorted_expert_idx,
                              float* sorted_weights, int32_t* expert_counts, int32_t* expert_offsets,
                              int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_fused_moe_routing");
   GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && num_experts >= 1 && num_experts <= kMaxExperts,
                "fused_moe_routing: bad sizes (T=%lld k=%d E=%d)", (long long)num_tokens, top_k, num_experts);
   GPTOSS_CHECK(num_tokens * top_k < (1LL << 31), "fused_moe_routing: too many assignments");
@@ -668,6 +679,7 @@ int gptoss_fused_moe_routing(const int64_t* router_indices, const float* routing
 int gptoss_router_topk(const void* hidden, const void* weight, const void* bias, int64_t num_tokens,
                        int64_t hidden_size, int num_experts, int top_k, int64_t* router_indices, void* router_scores,
                        float* routing_weights_f32, void* logits, void* stream) {
+  NvtxRange nvtx_range("gptoss_router_topk");
   GPTOSS_CHECK(num_tokens >= 0, "router: num_tokens < 0");
   GPTOSS_CHECK(hidden_size > 0 && hidden_size % 8 == 0, "router: hidden_size must be a positive multiple of 8");
   GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExperts, "router: num_experts must be in [1, %d]", kMaxExperts);
@@ -686,6 +698,7 @@ int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
 
 int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, uint8_t* codes, uint8_t* scales,
                         void* stream) {
+  NvtxRange nvtx_range("gptoss_quantize_fp8");
   GPTOSS_CHECK(rows >= 0 && cols > 0 && cols % 32 == 0, "quantize: K=%lld must be a positive multiple of 32",
                (long long)cols);
   GPTOSS_CHECK(dtype == GPTOSS_DTYPE_BF16 || dtype == GPTOSS_DTYPE_F32, "quantize: dtype must be bf16 or f32");
@@ -710,6 +723,7 @@ int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, ui
 
 int gptoss_swiglu(const void* x, int dtype, int64_t rows, int64_t cols, void* out, float alpha, float limit,
                   void* stream) {
+  NvtxRange nvtx_range("gptoss_swiglu");
   GPTOSS_CHECK(rows >= 0 && cols > 0 && cols % 2 == 0, "swiglu: last dimension must be even");
   GPTOSS_CHECK(dtype == GPTOSS_DTYPE_BF16 || dtype == GPTOSS_DTYPE_F32, "swiglu: dtype must be bf16 or f32");
   if (rows == 0) return GPTOSS_OK;
@@ -783,6 +797,7 @@ int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t ld
                         int64_t ldb_blockscale, const float* alphas, const int32_t* problem_sizes,
                         const int32_t* expert_offsets, const int32_t* sf_offsets, int gemm_mode, int32_t* status_dev,
                         void* stream) {
+  NvtxRange nvtx_range("gptoss_fp4_group_mm");
   GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExpertsGemm, "fp4_group_mm: num_experts must be in [1, %d]",
                kMaxExpertsGemm);
   GPTOSS_CHECK(k > 0 && k % 128 == 0, "fp4_group_mm: K=%lld must be a multiple of 128 (pad with pad_k_to_tile)",
@@ -829,6 +844,7 @@ int gptoss_moe_experts_forward(const void* hidden, const int64_t* router_indices
                                const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
                                float swiglu_alpha, float swiglu_limit, void* out, void* workspace,
                                size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_experts_forward");
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
@@ -858,6 +874,7 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, cons
                              float swiglu_limit, void* out, int64_t* router_indices_out, void* router_scores_out,
                              void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
                              void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_layer_forward");
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   GPTOSS_CHECK(hidden_size % 8 == 0, "hidden size must be a multiple of 8");
@@ -902,6 +919,7 @@ int gptoss_moe_route_quant(const void* hidden, const int64_t* router_indices, co
                            int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
                            int64_t intermediate_size, void* workspace, size_t workspace_bytes, int gemm_mode,
                            int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_route_quant");
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   DeviceInfo di;
   GPTOSS_TRY(bind_device(workspace, "workspace", &di));
@@ -920,6 +938,7 @@ int gptoss_moe_gemm1(int64_t num_tokens, int top_k, int num_experts, int64_t hid
                      const uint8_t* gate_up_data, const uint8_t* gate_up_scales, int64_t ldb_gate_up,
                      const float* gate_up_bias, float swiglu_alpha, float swiglu_limit, void* workspace,
                      size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_gemm1");
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
@@ -945,6 +964,7 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
                      const uint8_t* down_data, const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
                      void* out, void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
                      void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_gemm2");
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
@@ -1015,6 +1035,7 @@ int gptoss_ep_dispatch(const void* hidden, const int64_t* router_indices, const 
                        int64_t num_tokens, int top_k, int num_experts, int world_size, int64_t hidden_size,
                        int64_t capacity, uint8_t* send_rows, int32_t* send_counts, int32_t* pos_of,
                        void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_dispatch");
   GPTOSS_CHECK(world_size >= 1 && world_size <= kMaxExperts, "ep_dispatch: world_size must be in [1, %d]", kMaxExperts);
   GPTOSS_CHECK(num_experts >= world_size && num_experts % world_size == 0,
                "ep_dispatch: num_experts (%d) must be a multiple of world_size (%d)", num_experts, world_size);
@@ -1072,6 +1093,7 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
                              const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
                              float swiglu_alpha, float swiglu_limit, void* back_rows, void* workspace,
                              size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_expert_forward");
   GPTOSS_TRY(check_dims(num_rows, 1, num_local_experts, hidden_size, intermediate_size));
   GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;
@@ -1125,6 +1147,7 @@ int gptoss_ep_expert_forward(const uint8_t* recv_rows, int64_t num_rows, int num
 int gptoss_ep_combine(const void* back_rows, int64_t num_back_rows, const int32_t* pos_of,
                       const int64_t* router_indices, int64_t num_tokens, int top_k, int64_t hidden_size, void* out,
                       void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_combine");
   GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK, "ep_combine: bad sizes");
   GPTOSS_CHECK(hidden_size > 0 && hidden_size % 2 == 0, "ep_combine: hidden size must be even");
   DeviceInfo di;
@@ -1291,6 +1314,7 @@ int gptoss_ep_p2p_dispatch(const void* hidden, const int64_t* router_indices, co
                            int64_t hidden_size, int64_t capacity, void* local_base, const uint64_t* peer_bases,
                            int32_t epoch, int32_t* send_counts, int32_t* pos_of, void* workspace,
                            size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_p2p_dispatch");
   return ep_p2p_dispatch_impl(hidden, nullptr, router_indices, routing_weights, num_tokens, top_k, num_experts,
                               world_size, rank, hidden_size, capacity, local_base, peer_bases, epoch, send_counts,
                               pos_of, workspace, workspace_bytes, status_dev, stream);
@@ -1302,6 +1326,7 @@ int gptoss_ep_p2p_route_dispatch(const void* hidden, const void* router_weight, 
                                  int32_t epoch, int64_t* router_indices_out, void* router_scores_out,
                                  float* routing_weights_out, int32_t* send_counts, int32_t* pos_of, void* workspace,
                                  size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_p2p_route_dispatch");
   GPTOSS_CHECK(num_tokens == 0 || (router_weight && router_bias && router_indices_out && routing_weights_out),
                "ep_p2p_route_dispatch: null pointer");
   GPTOSS_CHECK(hidden_size % 8 == 0, "ep_p2p_route_dispatch: hidden size must be a multiple of 8");
@@ -1318,6 +1343,7 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
                                  int64_t ldb_down, const float* down_bias, float swiglu_alpha, float swiglu_limit,
                                  void* back_rows, const uint64_t* peer_bases, void* workspace, size_t workspace_bytes,
                                  int gemm_mode, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_p2p_expert_forward");
   GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld && rank >= 0 && rank < world_size,
                "ep_p2p_expert_forward: bad world_size / rank");
   const int64_t R = capacity * world_size;
@@ -1417,6 +1443,7 @@ int gptoss_ep_p2p_expert_forward(void* local_base, int world_size, int rank, int
 int gptoss_ep_p2p_combine(const void* local_base, int world_size, int64_t capacity, int32_t epoch,
                           const int32_t* pos_of, const int64_t* router_indices, int64_t num_tokens, int top_k,
                           int64_t hidden_size, void* out, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_p2p_combine");
   GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld, "ep_p2p_combine: bad world_size");
   GPTOSS_CHECK(num_tokens >= 0 && top_k >= 1 && top_k <= kMaxTopK, "ep_p2p_combine: bad sizes");
   GPTOSS_CHECK(hidden_size > 0 && hidden_size % 32 == 0, "ep_p2p_combine: hidden size must be a multiple of 32");
