@@ -37,16 +37,24 @@ def _stream(dev: torch.device) -> int:
 
 
 # Per (device, stream) scratch of the fused forwards, reused across calls: calls on one
-# stream run in order on the GPU, so one buffer per stream is never used twice at once.
+# stream run in order on the GPU, so one buffer per stream is never used twice at once. A
+# buffer outgrown by a larger call is kept alive, not freed: a CUDA graph captured earlier
+# may still address it. During stream capture every call gets its own buffer from the
+# graph's memory pool.
 _ws_cache = {}
+_ws_retired = []
 _ws_bytes = {}
 
 
 def _scratch(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     key = (dev.index, stream)
     t = _ws_cache.get(key)
     if t is None or t.numel() < nbytes:
-        t = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        if t is not None:
+            _ws_retired.append(t)
+        t = torch.empty(max(nbytes, 256, 2 * t.numel() if t is not None else 0), dtype=torch.uint8, device=dev)
         _ws_cache[key] = t
     return t
 
