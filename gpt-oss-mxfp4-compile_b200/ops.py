@@ -11,6 +11,8 @@ Registered ops (all with register_fake, static output shapes, no host sync unles
   gptoss::quantize_fp8, gptoss::swiglu, gptoss::router_topk,
   gptoss::moe_experts_forward  (the whole CutlassGptOssExperts.forward)
   gptoss::moe_layer_forward    (router + experts)
+  gptoss::route_quant, gptoss::gemm1, gptoss::gemm2   (its three stages on a workspace)
+  gptoss::ep_dispatch, gptoss::ep_expert_forward, gptoss::ep_combine   (expert parallelism)
 """
 from __future__ import annotations
 
@@ -426,6 +428,82 @@ def register_ops() -> None:
             return (torch.empty_like(hidden), hidden.new_empty((T, top_k)),
                     torch.empty((T, top_k), dtype=torch.int64, device=hidden.device))
 
+        # the staged forward on a caller-owned workspace (the three fused stages)
+        @torch.library.custom_op("gptoss::route_quant", mutates_args=("workspace",))
+        def route_quant_op(workspace: torch.Tensor, hidden: torch.Tensor, router_indices: torch.Tensor,
+                           routing_weights: torch.Tensor, num_experts: int, intermediate_size: int,
+                           gemm_mode: int) -> None:
+            route_quant_ws(workspace, hidden, router_indices, routing_weights, num_experts, intermediate_size,
+                           gemm_mode)
+
+        @route_quant_op.register_fake
+        def _(workspace, hidden, router_indices, routing_weights, num_experts, intermediate_size, gemm_mode):
+            return None
+
+        @torch.library.custom_op("gptoss::gemm1", mutates_args=("workspace",))
+        def gemm1_op(workspace: torch.Tensor, num_tokens: int, top_k: int, num_experts: int, hidden_size: int,
+                     intermediate_size: int, gate_up_data: torch.Tensor, gate_up_scales: torch.Tensor,
+                     gate_up_bias: torch.Tensor, alpha: float, limit: float, gemm_mode: int) -> None:
+            gemm1_ws(workspace, num_tokens, top_k, num_experts, hidden_size, intermediate_size, gate_up_data,
+                     gate_up_scales, gate_up_bias, alpha, limit, gemm_mode)
+
+        @gemm1_op.register_fake
+        def _(workspace, num_tokens, top_k, num_experts, hidden_size, intermediate_size, gate_up_data,
+              gate_up_scales, gate_up_bias, alpha, limit, gemm_mode):
+            return None
+
+        @torch.library.custom_op("gptoss::gemm2", mutates_args=("workspace", "out"))
+        def gemm2_op(workspace: torch.Tensor, out: torch.Tensor, num_tokens: int, top_k: int, num_experts: int,
+                     hidden_size: int, intermediate_size: int, down_data: torch.Tensor, down_scales: torch.Tensor,
+                     down_bias: torch.Tensor, gemm_mode: int) -> None:
+            gemm2_ws(workspace, out, num_tokens, top_k, num_experts, hidden_size, intermediate_size, down_data,
+                     down_scales, down_bias, gemm_mode)
+
+        @gemm2_op.register_fake
+        def _(workspace, out, num_tokens, top_k, num_experts, hidden_size, intermediate_size, down_data,
+              down_scales, down_bias, gemm_mode):
+            return None
+
+        # expert parallelism: dispatch / local experts / combine around the caller's exchange
+        @torch.library.custom_op("gptoss::ep_dispatch", mutates_args=())
+        def ep_dispatch_op(hidden: torch.Tensor, router_indices: torch.Tensor, routing_weights: torch.Tensor,
+                           num_experts: int, world_size: int, capacity: int
+                           ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+            return ep_dispatch(hidden, router_indices, routing_weights, num_experts, world_size, capacity)
+
+        @ep_dispatch_op.register_fake
+        def _(hidden, router_indices, routing_weights, num_experts, world_size, capacity):
+            A = router_indices.shape[0] * router_indices.shape[1]
+            dev = hidden.device
+            return (torch.empty((world_size * capacity if capacity else A, ep_row_bytes(hidden.shape[1])),
+                                dtype=torch.uint8, device=dev),
+                    torch.empty(world_size, dtype=torch.int32, device=dev),
+                    torch.empty(A, dtype=torch.int32, device=dev))
+
+        @torch.library.custom_op("gptoss::ep_expert_forward", mutates_args=())
+        def ep_expert_forward_op(recv_rows: torch.Tensor, gate_up_data: torch.Tensor, gate_up_scales: torch.Tensor,
+                                 gate_up_bias: torch.Tensor, down_data: torch.Tensor, down_scales: torch.Tensor,
+                                 down_bias: torch.Tensor, alpha: float, limit: float, gemm_mode: int
+                                 ) -> torch.Tensor:
+            return ep_expert_forward(recv_rows, gate_up_data, gate_up_scales, gate_up_bias, down_data, down_scales,
+                                     down_bias, alpha, limit, gemm_mode)
+
+        @ep_expert_forward_op.register_fake
+        def _(recv_rows, gate_up_data, gate_up_scales, gate_up_bias, down_data, down_scales, down_bias, alpha,
+              limit, gemm_mode):
+            return torch.empty((recv_rows.shape[0], down_data.shape[1]), dtype=torch.bfloat16,
+                               device=recv_rows.device)
+
+        @torch.library.custom_op("gptoss::ep_combine", mutates_args=())
+        def ep_combine_op(back_rows: torch.Tensor, pos_of: torch.Tensor, router_indices: torch.Tensor
+                          ) -> torch.Tensor:
+            return ep_combine(back_rows, pos_of, router_indices)
+
+        @ep_combine_op.register_fake
+        def _(back_rows, pos_of, router_indices):
+            return torch.empty((router_indices.shape[0], back_rows.shape[1]), dtype=torch.bfloat16,
+                               device=back_rows.device)
+
         _registered = True
 
 
@@ -471,21 +549,48 @@ class ExpertsWorkspace:
 
 
 def route_quant(ws: ExpertsWorkspace, hidden, router_indices, routing_weights, gemm_mode: int = GEMM_AUTO):
-    _lib.call("gptoss_moe_route_quant", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(),
-              ws.T, ws.k, ws.E, ws.H, ws.I, ws.ptr, ws.buf.numel(), int(gemm_mode),
-              status_tensor(hidden.device).data_ptr(), _stream(hidden.device))
+    if tuple(router_indices.shape) != (ws.T, ws.k) or tuple(hidden.shape) != (ws.T, ws.H):
+        raise RuntimeError("route_quant: inputs do not match the workspace's (T, k, H)")
+    route_quant_ws(ws.buf, hidden, router_indices, routing_weights, ws.E, ws.I, gemm_mode)
 
 
 def gemm1(ws: ExpertsWorkspace, gu_data, gu_scales, gu_bias, alpha: float = 1.702, limit: float = 7.0,
           gemm_mode: int = GEMM_AUTO):
-    _lib.call("gptoss_moe_gemm1", ws.T, ws.k, ws.E, ws.H, ws.I, gu_data.data_ptr(), gu_scales.data_ptr(),
-              gu_scales.numel() // ws.E, gu_bias.data_ptr(), float(alpha), float(limit), ws.ptr, ws.buf.numel(),
-              int(gemm_mode), status_tensor(gu_data.device).data_ptr(), _stream(gu_data.device))
+    gemm1_ws(ws.buf, ws.T, ws.k, ws.E, ws.H, ws.I, gu_data, gu_scales, gu_bias, alpha, limit, gemm_mode)
 
 
 def gemm2(ws: ExpertsWorkspace, dn_data, dn_scales, dn_bias, out, gemm_mode: int = GEMM_AUTO):
-    _lib.call("gptoss_moe_gemm2", ws.T, ws.k, ws.E, ws.H, ws.I, dn_data.data_ptr(), dn_scales.data_ptr(),
-              dn_scales.numel() // ws.E, dn_bias.data_ptr(), out.data_ptr(), ws.ptr, ws.buf.numel(), int(gemm_mode),
+    gemm2_ws(ws.buf, out, ws.T, ws.k, ws.E, ws.H, ws.I, dn_data, dn_scales, dn_bias, gemm_mode)
+
+
+def route_quant_ws(workspace, hidden, router_indices, routing_weights, num_experts: int, intermediate_size: int,
+                   gemm_mode: int = GEMM_AUTO):
+    """route_quant on a raw workspace tensor (u8, at least workspace_bytes(T, k, E, H, I))."""
+    _cuda(workspace, "workspace")
+    _cuda(hidden, "hidden_states")
+    T, H = hidden.shape
+    k = router_indices.shape[1]
+    _lib.call("gptoss_moe_route_quant", hidden.data_ptr(), router_indices.data_ptr(), routing_weights.data_ptr(),
+              T, k, int(num_experts), H, int(intermediate_size), workspace.data_ptr(), workspace.numel(),
+              int(gemm_mode), status_tensor(hidden.device).data_ptr(), _stream(hidden.device))
+
+
+def gemm1_ws(workspace, T: int, k: int, E: int, H: int, I: int, gu_data, gu_scales, gu_bias, alpha: float = 1.702,
+             limit: float = 7.0, gemm_mode: int = GEMM_AUTO):
+    """gemm1 on a raw workspace tensor."""
+    _cuda(workspace, "workspace")
+    _lib.call("gptoss_moe_gemm1", T, k, E, H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E,
+              gu_bias.data_ptr(), float(alpha), float(limit), workspace.data_ptr(), workspace.numel(),
+              int(gemm_mode), status_tensor(gu_data.device).data_ptr(), _stream(gu_data.device))
+
+
+def gemm2_ws(workspace, out, T: int, k: int, E: int, H: int, I: int, dn_data, dn_scales, dn_bias,
+             gemm_mode: int = GEMM_AUTO):
+    """gemm2 on a raw workspace tensor; adds into `out` [T, H] bf16."""
+    _cuda(workspace, "workspace")
+    _cuda(out, "out")
+    _lib.call("gptoss_moe_gemm2", T, k, E, H, I, dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E,
+              dn_bias.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(), int(gemm_mode),
               status_tensor(dn_data.device).data_ptr(), _stream(dn_data.device))
 
 

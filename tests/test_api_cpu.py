@@ -44,7 +44,8 @@ def test_ops_registered_with_reference_qualnames(pkg):
     pkg.ensure_custom_op_registered()   # idempotent
     assert hasattr(torch.ops.cutlass, "fp4_group_mm")
     assert hasattr(torch.ops.cutlass, "fused_moe_routing")
-    for n in ("moe_experts_forward", "moe_layer_forward", "quantize_fp8", "swiglu", "router_topk"):
+    for n in ("moe_experts_forward", "moe_layer_forward", "quantize_fp8", "swiglu", "router_topk",
+              "route_quant", "gemm1", "gemm2", "ep_dispatch", "ep_expert_forward", "ep_combine"):
         assert hasattr(torch.ops.gptoss, n)
 
 
@@ -65,6 +66,20 @@ def test_fake_kernels_give_static_shapes(pkg):
     assert y.shape == (7, 512) and y.dtype == torch.bfloat16
     q, s = torch.ops.gptoss.quantize_fp8(torch.empty(5, 64, dtype=torch.bfloat16, device=meta))
     assert q.shape == (5, 64) and q.dtype == torch.float8_e4m3fn and s.shape == (5, 2)
+    # expert parallelism: static shapes from the arguments alone
+    rb = pkg.ops.ep_row_bytes(512)
+    rows, counts, pos = torch.ops.gptoss.ep_dispatch(h, idx, w, 32, 4, 40)
+    assert rows.shape == (160, rb) and rows.dtype == torch.uint8 and counts.shape == (4,) and pos.shape == (28,)
+    rows, _, _ = torch.ops.gptoss.ep_dispatch(h, idx, w, 32, 4, 0)
+    assert rows.shape == (28, rb)
+    back = torch.ops.gptoss.ep_expert_forward(
+        torch.empty(28, rb, dtype=torch.uint8, device=meta), torch.empty(8, 512, 256, dtype=torch.uint8, device=meta),
+        torch.empty(8, 16384, dtype=torch.uint8, device=meta), torch.empty(8, 512, device=meta),
+        torch.empty(8, 512, 128, dtype=torch.uint8, device=meta), torch.empty(8, 8192, dtype=torch.uint8, device=meta),
+        torch.empty(8, 512, device=meta), 1.702, 7.0, 0)
+    assert back.shape == (28, 512) and back.dtype == torch.bfloat16
+    out = torch.ops.gptoss.ep_combine(back, pos, idx)
+    assert out.shape == (7, 512) and out.dtype == torch.bfloat16
 
 
 def test_cpu_tensors_are_refused(pkg):
