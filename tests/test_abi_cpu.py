@@ -65,3 +65,16 @@ def test_argument_errors_before_device_access(pkg):
 def test_wrapper_raises_on_failure(pkg):
     with pytest.raises(pkg._lib.GptossError, match="multiple of 32"):
         pkg._lib.call("gptoss_quantize_fp8", None, 0, 4, 31, None, None, None)
+
+
+def test_header_is_plain_c():
+    # FFI hosts (cgo, JNI, N-API, ctypes) consume the header as C: it must compile as C99
+    # on its own, with no CUDA or C++ headers.
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    r = subprocess.run([cc, "-fsyntax-only", "-std=c99", "-Wall", "-Werror", "-x", "c", HEADER],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
