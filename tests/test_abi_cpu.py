@@ -78,3 +78,33 @@ def test_header_is_plain_c():
     r = subprocess.run([cc, "-fsyntax-only", "-std=c99", "-Wall", "-Werror", "-x", "c", HEADER],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_c_program_links_and_calls_host_queries(pkg, tmp_path):
+    # What a C / cgo / JNI host does: include the header, link the library, call entry
+    # points. Only host-side queries run here (no GPU on this machine).
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib = pkg._lib.lib_path()
+    src = tmp_path / "probe.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include "gptoss_moe.h"
+int main(void) {
+  if (gptoss_abi_version() != 1) return 1;
+  size_t ws = gptoss_moe_workspace_bytes(32, 4, 32, 2880, 2880);
+  long long rb = (long long)gptoss_ep_row_bytes(2880);
+  printf("%zu %lld\n", ws, rb);
+  return ws > 0 && rb == 2992 ? 0 : 2;
+}
+""")
+    exe = tmp_path / "probe"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe),
+                        lib, "-Wl,-rpath," + os.path.dirname(lib)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, (r.stdout, r.stderr)
+    assert int(r.stdout.split()[0]) == pkg.ops.workspace_bytes(32, 4, 32, 2880, 2880)
