@@ -639,6 +639,12 @@ int gptoss_abi_version(void) { return 1; }
 
 uint64_t gptoss_kernel_launch_count(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 
+int gptoss_moe_gemm_layout(int gemm_mode, int64_t rows, int num_experts) {
+  if (gemm_mode < 0 || gemm_mode > 3 || rows < 0 || num_experts < 1) return -1;
+  const GemmLayout lay = pick_layout(gemm_mode, rows, num_experts);
+  return !lay.swap ? GPTOSS_GEMM_TOKENS_M : (lay.spread ? GPTOSS_GEMM_SWAP : GPTOSS_GEMM_SWAP_WIDE);
+}
+
 int gptoss_read_status(int32_t* status_dev, int32_t* status_host, void* stream) {
   GPTOSS_CHECK(status_host != nullptr, "status_host is null");
   DeviceInfo di;

@@ -49,6 +49,11 @@ enum { GPTOSS_DTYPE_BF16 = 0, GPTOSS_DTYPE_F32 = 1 };
  * the activation scales in the workspace. */
 enum { GPTOSS_GEMM_AUTO = 0, GPTOSS_GEMM_TOKENS_M = 1, GPTOSS_GEMM_SWAP = 2, GPTOSS_GEMM_SWAP_WIDE = 3 };
 
+/* The orientation a fused forward over `rows` assignments and `num_experts` experts runs
+ * with for `gemm_mode` (AUTO resolved): GPTOSS_GEMM_TOKENS_M / _SWAP / _SWAP_WIDE, or -1 for
+ * bad arguments. Host only. No counterpart in the reference. */
+int gptoss_moe_gemm_layout(int gemm_mode, int64_t rows, int num_experts);
+
 /* Message for the last failing call on this thread ("" if none). */
 const char* gptoss_last_error(void);
 

@@ -108,3 +108,17 @@ int main(void) {
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0, (r.stdout, r.stderr)
     assert int(r.stdout.split()[0]) == pkg.ops.workspace_bytes(32, 4, 32, 2880, 2880)
+
+
+def test_gemm_layout_choice(pkg):
+    # AUTO: 16-row chunks up to 12 rows per expert on average, 64-row chunks up to 80,
+    # tokens on M above (crossovers measured on B200 for H = I = 2880)
+    q = lambda mode, rows, e: pkg._lib.query("gptoss_moe_gemm_layout", mode, rows, e)   # noqa: E731
+    AUTO, TOK, SWAP, WIDE = pkg.ops.GEMM_AUTO, pkg.ops.GEMM_TOKENS_M, pkg.ops.GEMM_SWAP, pkg.ops.GEMM_SWAP_WIDE
+    assert q(AUTO, 32 * 4, 32) == SWAP                     # decode, T = 32
+    assert q(AUTO, 12 * 32, 32) == SWAP and q(AUTO, 12 * 32 + 1, 32) == WIDE
+    assert q(AUTO, 80 * 32, 32) == WIDE and q(AUTO, 80 * 32 + 1, 32) == TOK
+    assert q(AUTO, 8192 * 4, 32) == TOK                    # prefill
+    for m in (TOK, SWAP, WIDE):
+        assert q(m, 8192 * 4, 32) == m and q(m, 4, 32) == m
+    assert q(7, 4, 32) == -1 and q(AUTO, 4, 0) == -1
