@@ -5,15 +5,20 @@ forward over one batch of synthetic tokens).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config decode|prefill|stack|zipf]
   python bench.py --impl reference ...     CPU baseline arm (rank 0 only)
 
-Workload at N=1 is BASELINE config 1 (decode, T=32 tokens, E=32, H=I=2880, top-4,
-seeded synthetic weights/inputs). Under torchrun (N>1) the layer runs expert-parallel:
+Workload at N=1: one GPT-OSS-20B MoE layer at decode (T=32 tokens, E=32, H=I=2880,
+top-4, seeded synthetic weights/inputs). Under torchrun (N>1) the layer runs expert-parallel:
 rank r holds experts [r*E/N, (r+1)*E/N) and its own batch of T tokens (weak scaling);
-dispatch and combine are NCCL all-to-alls. The reported value is the whole-job tokens/s
+dispatch and combine move rows over NVLink (stores into peer-mapped buffers for
+fixed-capacity exchanges, NCCL all-to-alls for exact splits). The reported value is the whole-job tokens/s
 over the max-over-ranks device time.
 
 Timing: W warm-up steps, then exactly K steps, each bracketed by CUDA events on the
-launching stream; before every timed step a 256 MiB buffer is written to flush L2
-(outside the events). Barrier + synchronize on both sides of the timed region.
+launching stream; barrier + synchronize on both sides of the timed region. L2: every
+configuration streams more input than L2 holds (424 MB of expert weights per layer step
+against 126 MB of L2), so by default nothing is flushed between steps; `--l2 write`
+writes a 256 MiB buffer before every timed step instead (its dirty lines are written back
+to HBM inside the next step, so that number also carries the flush's write-back). The
+JSON line reports the no-flush number and, for comparison, the write-flush one.
 """
 from __future__ import annotations
 
@@ -32,20 +37,20 @@ METRIC = "GPT-OSS-20B MoE layer tokens/s; %HBM roofline (decode), %MMA peak (pre
 
 CONFIGS = {
     # name: (T, E, H, I, top_k, skew, description)
-    "decode": (32, 32, 2880, 2880, 4, None, "GPT-OSS-20B MoE layer decode, T=32 (BASELINE config 1)"),
-    "prefill": (8192, 32, 2880, 2880, 4, "prefill", "GPT-OSS-20B MoE layer prefill, T=8192, loads +-50% (BASELINE config 2)"),
+    "decode": (32, 32, 2880, 2880, 4, None, "GPT-OSS-20B MoE layer decode, T=32"),
+    "prefill": (8192, 32, 2880, 2880, 4, "prefill", "GPT-OSS-20B MoE layer prefill, T=8192, loads +-50%"),
     "stack": (4096, 32, 2880, 2880, 4, None,
-              "GPT-OSS-20B-shaped 24-layer stack (RMSNorm -> MoE -> residual), T=4096 (BASELINE config 3)"),
+              "GPT-OSS-20B-shaped 24-layer stack (RMSNorm -> MoE -> residual), T=4096"),
     "zipf": (16384, 128, 2880, 2880, 4, "zipf",
-             "GPT-OSS-120B-shaped MoE layer, 1.5 log-Zipf(1.1) router bias, T=16384 (BASELINE config 4)"),
+             "GPT-OSS-120B-shaped MoE layer, 1.5 log-Zipf(1.1) router bias, T=16384"),
 }
 STACK_LAYERS = 24
 CPU_BASELINE_CONFIGS = ("decode", "prefill")   # the others are minutes of CPU work per step
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from
-# the ncu capture summarised in profiles/ (None until captured for this kernel/config).
-NCU_TRAFFIC_BYTES = {"decode": 294_617_088,     # profiles/moe_gemm_swap_decode_T32.md
-                     "prefill": 769_571_328}    # profiles/moe_gemm_pair_prefill_T8192.md (GEMM1)
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from one
+# ncu capture of that kernel on this workload (None until captured for this kernel/config).
+NCU_TRAFFIC_BYTES = {"decode": 294_617_088,     # GEMM1, weights-on-M tiles, T = 32
+                     "prefill": 769_571_328}    # GEMM1, tokens-on-M CTA-pair tiles, T = 8192
 
 
 
@@ -57,7 +62,11 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=list(CONFIGS), default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-budget-s", type=float, default=45.0)
+    ap.add_argument("--cpu-budget-s", type=float, default=45.0,
+                    help="reference arm: CPU seconds the whole --warmup + --steps run may take; each step "
+                         "times a token sample of the workload sized to fit")
+    ap.add_argument("--l2", choices=["none", "write"], default="none",
+                    help="between timed steps: nothing (inputs larger than L2) or write a 256 MiB buffer")
     ap.add_argument("--ep-transport", choices=["auto", "p2p", "nccl"], default="auto",
                     help="N>1 exchange: stores into peer-mapped buffers (p2p, fixed capacity) or NCCL "
                          "all-to-alls; auto = p2p with the capacity layout, NCCL with exact splits")
@@ -77,7 +86,7 @@ def measured_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def alg_bytes(counts, T, k, H, I):
+def alg_bytes(counts, T, k, H, I, E):
     """Algorithmic HBM bytes of one layer step (unpadded K): weights + scales + fp32
     biases of every touched expert, router weights, activations in/out and the FP8
     intermediates written and read once."""
@@ -89,7 +98,7 @@ def alg_bytes(counts, T, k, H, I):
     inter = A * I + A * (I // 32)         # FP8 intermediate (written by GEMM1, read by GEMM2)
     g1 = gu + act + inter
     g2 = dn + inter + 2 * T * H           # output rows (read-modify-write counted once)
-    layer = g1 + g2 + 32 * H * 2 + 2 * T * H
+    layer = g1 + g2 + E * H * 2 + E * 2 + 2 * T * H   # + router weight and bias, hidden in
     return g1, g2, layer, touched
 
 
@@ -145,9 +154,10 @@ def dist_setup(n_gpus: int):
     return world, rank, local
 
 
-def cpu_baseline(cfg_name: str, steps_cap: int, budget_s: float):
+def cpu_baseline(cfg_name: str, steps: int, warmup: int, budget_s: float):
     """The reference's dequantised PyTorch CPU path (oracle.DequantCPULayer) on the host
-    cores, bounded to ~budget_s of work."""
+    cores: `warmup` untimed and `steps` timed calls, each on the workload's first n
+    tokens, n chosen (from one trial call) so that the whole run takes about budget_s."""
     import torch
     import oracle as O
     T, E, H, I, k, skew, _ = CONFIGS[cfg_name]
@@ -158,24 +168,54 @@ def cpu_baseline(cfg_name: str, steps_cap: int, budget_s: float):
     layer = O.DequantCPULayer(d, top_k=k)
     dequant_s = time.perf_counter() - t0
     h = d["hidden"]
+    n_try = min(T, 512)
     tw = time.perf_counter()
-    layer(h)                                     # warm-up
-    step_est = max(time.perf_counter() - tw, 1e-3)
-    n = max(1, min(steps_cap, int(budget_s / step_est)))
+    layer(h[:n_try])
+    per_tok = max(time.perf_counter() - tw, 1e-4) / n_try     # an upper bound for larger samples
+    n = int(max(1, min(T, budget_s / max(1, steps + warmup) / per_tok)))
+    sample = h[:n]
+    for _ in range(warmup):
+        layer(sample)
     times = []
-    for _ in range(n):
+    for _ in range(steps):
         t = time.perf_counter()
-        layer(h)
+        layer(sample)
         times.append(time.perf_counter() - t)
-    per = statistics.median(times)
-    what = f"{n} full {cfg_name} steps (T={T})"
+    per = statistics.mean(times)
+    what = f"{steps} timed steps of {n} of the workload's {T} tokens"
     if cfg_name == "stack":   # one MoE layer timed; the stack is STACK_LAYERS of them (norms not counted)
         per *= STACK_LAYERS
-        what = f"{n} single-layer steps (T={T}) x {STACK_LAYERS} layers"
-    return {"value": T / per, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{what} of the dequantised bf16 expert path + HF router, "
-                      f"median {per * 1e3:.1f} ms/step; weights dequantised once beforehand ({dequant_s:.1f} s)",
-            "ms_per_step": per * 1e3, "steps_run": n}
+        what += f" (one MoE layer, x {STACK_LAYERS} layers)"
+    return {"value": n / per, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{what} through the dequantised bf16 expert path + HF router, "
+                      f"mean {per * 1e3:.1f} ms/step; weights dequantised once beforehand ({dequant_s:.1f} s)",
+            "ms_per_step": per * 1e3, "steps_run": steps, "tokens_per_step": n}
+
+
+def workload_config(args, world: int) -> dict:
+    """The `config` object both arms print (same keys and values for the same command line)."""
+    T, E, H, I, k, _, desc = CONFIGS[args.config]
+    if world > 1:
+        layout, transport = ep_choice(args, world, T, k)
+        par = (f"ep{world} (E/{world} experts per GPU, "
+               f"{'peer-memory stores' if transport == 'p2p' else 'NCCL all-to-all'})")
+    else:
+        par = "single GPU"
+    l2 = ("none between steps: inputs larger than L2 (each layer step streams 424 MB of expert weights; "
+          "L2 is 126 MB)" if args.l2 == "none" else "256 MiB written before every timed step")
+    return {"workload": desc, "T": T, "T_per_rank": T, "E": E, "hidden": H, "intermediate": I, "top_k": k,
+            "parallelism": par, "l2": l2}
+
+
+def ep_choice(args, world: int, T: int, k: int):
+    """Expert-parallel exchange layout and transport for N > 1."""
+    layout = args.ep_layout
+    if layout == "auto":
+        layout = "capacity" if world * T * k <= 8192 else "exact"
+    transport = args.ep_transport
+    if transport == "auto":
+        transport = "p2p" if layout == "capacity" else "nccl"
+    return layout, transport
 
 
 def run_reference(args):
@@ -183,14 +223,14 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    T = CONFIGS[args.config][0]
-    cb = cpu_baseline(args.config, max(1, args.steps), args.cpu_budget_s)
+    cb = cpu_baseline(args.config, max(1, args.steps), max(0, args.warmup), args.cpu_budget_s)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": cb["steps_run"], "warmup": 1, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (dequantised weights), fp32 accumulate",
-            "data": "synthetic (seeded, SURVEY 8(d) recipe)",
-            "config": {"workload": CONFIGS[args.config][6], "T": T, "world_size": world,
-                       "note": "CPU arm runs on rank 0 only"},
+            "data": "synthetic (seeded: random MXFP4 weights, N(0,1) bf16 hidden)",
+            "config": workload_config(args, world),
+            "reference_note": f"the reference's CPU expert path on {cb['cores']} host cores, rank 0 only; "
+                              f"{cb['tokens_per_step']} tokens per step",
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -299,12 +339,7 @@ def run_ours(args):
         ex.down_proj_bias.data.copy_(d["dn_bias"][lo:hi])
         pkg.load_cutlass_weights(ex, d["gu_blocks"][lo:hi], d["gu_scales"][lo:hi], d["dn_blocks"][lo:hi],
                                  d["dn_scales"][lo:hi], dev)
-        layout = args.ep_layout
-        if layout == "auto":
-            layout = "capacity" if world * T * k <= 8192 else "exact"
-        transport = args.ep_transport
-        if transport == "auto":
-            transport = "p2p" if layout == "capacity" else "nccl"
+        layout, transport = ep_choice(args, world, T, k)
         ep_experts = pkg.ep.ExpertParallelExperts(ex, E, capacity_tokens=T if layout == "capacity" else None,
                                                   transport=transport, top_k=k)
         layer = pkg.ep.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), k, ep_experts)
@@ -332,30 +367,39 @@ def run_ours(args):
 
     # ---------------------------------------------------------------- headline
     K = args.steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    barrier()
-    torch.cuda.synchronize(dev)
-    sampler = clock_sampler_start(dev.index)
-    time.sleep(0.3)
-    launches0 = pkg._lib.query("gptoss_kernel_launch_count")
-    for i in range(K):
-        flush.zero_()
-        ev[i][0].record(stream)
-        step()
-        ev[i][1].record(stream)
-    launches = int(pkg._lib.query("gptoss_kernel_launch_count") - launches0)   # this library's kernels
-    torch.cuda.synchronize(dev)
-    clocks = clock_sampler_stop(sampler)
-    barrier()
-    ms = sum(s.elapsed_time(e) for s, e in ev) / K
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+
+    def timed_loop(l2_mode: str):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        sampler = clock_sampler_start(dev.index)
+        time.sleep(0.3)
+        launches0 = pkg._lib.query("gptoss_kernel_launch_count")
+        for i in range(K):
+            if l2_mode == "write":
+                flush.zero_()
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        n_launch = int(pkg._lib.query("gptoss_kernel_launch_count") - launches0)   # this library's kernels
+        torch.cuda.synchronize(dev)
+        clk = clock_sampler_stop(sampler)
+        barrier()
+        t_ms = sum(s.elapsed_time(e) for s, e in ev) / K
+        if world > 1:
+            t = torch.tensor([t_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_ms = float(t.item())
+        return t_ms, n_launch, clk
+
+    ms, launches, clocks = timed_loop(args.l2)
     value = T * world / (ms / 1e3)
+    other = "write" if args.l2 == "none" else "none"
+    ms_other, _, _ = timed_loop(other)
 
     # ---------------------------------------------------------------- per-stage (roofline)
-    stages = (stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, args.config)
+    stages = (stage_roofline(pkg, layer, ex, x, flush if args.l2 == "write" else None, stream, T, k, E, H, I, K,
+                             ms, dev, args.config)
               if world == 1 and not stack else None)
 
     # ---------------------------------------------------------------- end to end
@@ -367,7 +411,8 @@ def run_ours(args):
     barrier()
     for i in range(Ke + 3):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        flush.zero_()
+        if args.l2 == "write":
+            flush.zero_()
         a.record(stream)
         xd.copy_(xh, non_blocking=True)
         y = forward(xd)
@@ -385,7 +430,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config in CPU_BASELINE_CONFIGS:
-        cb = cpu_baseline(args.config, 1000, args.cpu_budget_s)
+        cb = cpu_baseline(args.config, 50, 2, min(args.cpu_budget_s, 30.0))
         cpu = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
 
     ep_info = None
@@ -415,12 +460,8 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8 e4m3 x fp4 e2m1 (UE8M0 1x32 scales), fp32 accumulate",
             "data": "synthetic (seeded: random MXFP4 weights, N(0,1) bf16 hidden)",
-            "config": {"workload": desc, "T": T, "T_per_rank": T, "E": E, "hidden": H, "intermediate": I,
-                       "top_k": k,
-                       "parallelism": (f"ep{world} (E/{world} experts per GPU, "
-                                       f"{'peer-memory stores' if ep_info and ep_info['transport'] == 'p2p' else 'NCCL all-to-all'})")
-                       if world > 1 else "single GPU",
-                       "l2": "256 MiB written before every timed step (outside the events); weights 424 MB > L2"},
+            "config": workload_config(args, world),
+            "l2_comparison": {"l2": other, "ms_per_step": ms_other, "value": T * world / (ms_other / 1e3)},
             "roofline": stages["roofline"] if stages else None,
             "clocks": clocks,
             "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
@@ -431,7 +472,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
         }
         if stages:
-            line["config"]["experts_touched"] = stages["touched"]
+            line["experts_touched"] = stages["touched"]
             line["layer_hbm"] = stages["layer_hbm"]
             line["mma"] = stages["mma"]
         if ep_info:
@@ -458,7 +499,8 @@ def stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, 
         # hold the stream so every launch of this step is queued before the GPU reaches
         # it (the staged calls go through Python; no host gap may land inside an event pair)
         torch.cuda._sleep(2_000_000)
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
         e0.record(stream)
         _, sc, ix = layer.route(x)
@@ -478,7 +520,7 @@ def stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, 
     t_g1 = statistics.mean(a.elapsed_time(b) for a, b in g1_ms)
     t_g2 = statistics.mean(a.elapsed_time(b) for a, b in g2_ms)
     counts = ws.counts.cpu().tolist()
-    b_g1, b_g2, b_layer, touched = alg_bytes(counts, T, k, H, I)
+    b_g1, b_g2, b_layer, touched = alg_bytes(counts, T, k, H, I, E)
     hbm_peak, bf16_peak, peak_kind = measured_peaks()
     g1_gbs = b_g1 / (t_g1 / 1e3) / 1e9
     layer_gbs = b_layer / (ms / 1e3) / 1e9

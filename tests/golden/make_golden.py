@@ -1,7 +1,7 @@
 """Generates the golden fixtures in this directory from the REFERENCE's own Python.
 
-Run in a container where evil0sheep/gpt-oss-mxfp4-compile is checked out (default
-/root/reference, override with GPTOSS_REFERENCE); the GPU box never runs this.
+Run where a checkout of evil0sheep/gpt-oss-mxfp4-compile is available, with the
+environment variable GPTOSS_REFERENCE pointing at it; the GPU box never runs this.
 
 What runs, unmodified, from the reference:
   * kernels/cutlass_experts.py: quantize_activations_to_fp8 (:197-251), swiglu (:258-276)
@@ -28,7 +28,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("GPTOSS_REFERENCE", "/root/reference")
+REF = os.environ.get("GPTOSS_REFERENCE", "")
 sys.path.insert(0, REPO)
 
 import oracle as O  # noqa: E402  (only synth_layer: the seeded input recipe)
@@ -44,6 +44,8 @@ def sha(*arrays) -> str:
 
 
 def load_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "kernels")):
+        raise SystemExit("set GPTOSS_REFERENCE to a checkout of evil0sheep/gpt-oss-mxfp4-compile")
     spec = importlib.util.spec_from_file_location("cutlass_experts", os.path.join(REF, "kernels", "cutlass_experts.py"))
     ce = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(ce)
@@ -159,8 +161,8 @@ LAYERS = {
     # name: (seed, E, H, I, T, top_k)
     "small": (11, 4, 512, 256, 32, 2),
     "kpad": (12, 4, 288, 288, 32, 2),
-    "decode": (0, 32, 2880, 2880, 32, 4),
-    "cpu_ref": (0, 32, 2880, 2880, 128, 4),
+    "decode": (0, 32, 2880, 2880, 32, 4),     # GPT-OSS-20B layer, decode batch
+    "cpu_ref": (0, 32, 2880, 2880, 128, 4),   # GPT-OSS-20B layer, the CPU baseline batch
 }
 
 

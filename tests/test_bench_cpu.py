@@ -23,6 +23,14 @@ def test_reference_arm_prints_the_contract_line():
     assert j["cpu_baseline"]["kind"] == "port" and j["cpu_baseline"]["cores"] >= 1
     assert j["e2e"]["h2d_bytes_per_step"] == 0 and j["e2e"]["d2h_bytes_per_step"] == 0
     assert "workload" in j["config"]
+    # the same --steps / --warmup and the same config object as the GPU arm prints
+    assert j["steps"] == 2 and j["warmup"] == 1
+    sys.path.insert(0, REPO)
+    import bench
+    ns = type("A", (), {"config": "decode", "l2": "none", "ep_layout": "auto", "ep_transport": "auto"})()
+    assert j["config"] == bench.workload_config(ns, 1)
+    for key in ("T", "E", "hidden", "intermediate", "top_k"):
+        assert key in j["config"], key
 
 
 def test_configs_cover_the_baseline_configs():

@@ -1,7 +1,7 @@
-"""Router + experts (GptOssMoELayer) at the BASELINE configurations.
+"""Router + experts (GptOssMoELayer) at the benchmark workloads.
 
-Config 1 (decode, T=32) is compared with the reference's own output (golden); configs 2
-(prefill T=8192, skewed loads) and 4 (E=128, Zipf, T=16384) are too large for the CPU
+Decode (T=32) is compared with the reference's own output (golden); prefill (T=8192,
+skewed loads) and the 120B-shaped layer (E=128, Zipf, T=16384) are too large for the CPU
 oracle as a whole, so a fixed sample of tokens is recomputed on the CPU (each token's
 output depends only on its own hidden state and routing)."""
 import numpy as np
