@@ -24,6 +24,7 @@ _SIGNATURES = {
     "gptoss_last_error": (ctypes.c_char_p, []),
     "gptoss_abi_version": (_i, []),
     "gptoss_kernel_launch_count": (ctypes.c_uint64, []),
+    "gptoss_set_decode_layer_kernel": (_i, [_i]),
     "gptoss_moe_gemm_layout": (_i, [_i, _c_int64, _i]),
     "gptoss_read_status": (_i, [_vp, _vp, _vp]),
     "gptoss_fused_moe_routing": (_i, [_vp, _vp, _c_int64, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -22,6 +22,7 @@
 #include "gemm.cuh"
 #include "prologue.cuh"
 #include "ep_p2p.cuh"
+#include "decode_layer.cuh"
 
 using namespace gptoss;
 
@@ -318,7 +319,9 @@ int run_gemm(const GemmJob& job, bool swap, bool spread, const DeviceInfo& di, i
 // ---------------------------------------------------------------- workspace layout
 struct Workspace {
   size_t sorted_token, sorted_expert, sorted_weight, counts, offsets, sfoff_a, sfoff_b;
-  size_t act_codes, act_sf, inter_codes, inter_sf, router_idx, router_w, total;
+  size_t act_codes, act_sf, inter_codes, inter_sf, router_idx, router_w;
+  size_t dl_logits, dl_sync;   // decode_layer_kernel: router logits, synchronisation words
+  size_t total;
   int64_t act_sf_cap, inter_sf_cap;
 };
 
@@ -347,6 +350,8 @@ Workspace plan_workspace(int64_t T, int k, int E, int64_t H, int64_t I) {
   w.inter_sf = take(static_cast<size_t>(w.inter_sf_cap));
   w.router_idx = take(sizeof(int64_t) * A);
   w.router_w = take(sizeof(float) * A);
+  w.dl_logits = take(sizeof(float) * T * E);
+  w.dl_sync = take(sizeof(int32_t) * dl_sync_words(E));
   w.total = o;
   return w;
 }
@@ -563,6 +568,82 @@ int run_decode_prologue(const void* hidden, const RouterArgs* ra, const int64_t*
                             dim3(kDpCluster, 1, 1), p);
 }
 
+// ---------------------------------------------------------------- one-launch decode layer
+// decode_layer_kernel runs the whole layer (router or given routing, sort, quantisation,
+// GEMM1, GEMM2) as one persistent launch behind a one-CTA reset of its synchronisation
+// words. It serves batches on the 16-row-chunk weights-on-M layout (SPREAD) that fit its
+// shared-memory routing state; gptoss_set_decode_layer_kernel(0) turns it off (the
+// three-launch path then runs).
+std::atomic<int> g_decode_layer_enabled{1};
+
+bool decode_layer_fits(int64_t T, int k, int E, int64_t H, int64_t I, GemmLayout lay, int sms) {
+  return g_decode_layer_enabled.load(std::memory_order_relaxed) != 0 && lay.swap && lay.spread && T >= 1 &&
+         T <= kDlMaxTokens && T * k <= kDlMaxAssign && E <= kDlMaxExperts && H % 32 == 0 && I % 32 == 0 &&
+         static_cast<size_t>(T) * (E + k) * sizeof(float) <= (DlCfg::kStages - kDlPreStages) * DlCfg::kStageBytes &&
+         sms >= 1;
+}
+
+int run_decode_layer(const void* hidden, const RouterArgs* ra, const int64_t* ridx, const float* rw, int64_t T, int k,
+                     int E, int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit, void* out,
+                     uint8_t* ws, const Workspace& L, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+  const WsPtrs w = ws_ptrs(ws, L);
+  const int64_t A = T * k, Kh = pad128(H), Ki = pad128(I);
+  CUtensorMap ta, ti, tgu, tdn;
+  GPTOSS_TRY(make_act_map(&ta, w.act_codes, A, H, DlCfg::kActRows));
+  GPTOSS_TRY(make_act_map(&ti, w.inter_codes, A, I, DlCfg::kActRows));
+  GPTOSS_TRY(make_wgt_map(&tgu, wt.gu_data, E, 2 * I, Kh, DlCfg::kWgtRowsCta));
+  GPTOSS_TRY(make_wgt_map(&tdn, wt.dn_data, E, H, Ki, DlCfg::kWgtRowsCta));
+  static uint64_t attr_done = 0;   // one bit per device
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_done & (1ull << dev))) {
+      GPTOSS_CUDA(cudaFuncSetAttribute(decode_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(dl_smem_bytes())));
+      attr_done |= (1ull << dev);
+    }
+  }
+  DecodeLayerParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(hidden);
+  if (ra != nullptr) {
+    p.router_w = static_cast<const __nv_bfloat16*>(ra->weight);
+    p.router_b = static_cast<const __nv_bfloat16*>(ra->bias);
+    p.ridx_out = ra->ridx_out;
+    p.scores_out = static_cast<__nv_bfloat16*>(ra->scores_out);
+    p.rw_out = ra->rw_out;
+  } else {
+    p.ridx_in = ridx;
+    p.rw_in = rw;
+  }
+  p.T = static_cast<int>(T); p.H = static_cast<int>(H); p.I = static_cast<int>(I); p.E = E; p.K = k;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.logits = reinterpret_cast<float*>(ws + L.dl_logits);
+  p.sorted_token = w.sorted_token; p.sorted_expert = w.sorted_expert; p.sorted_weight = w.sorted_weight;
+  p.counts = w.counts; p.offsets = w.offsets; p.sf_offsets_a = w.sfoff_a; p.sf_offsets_b = w.sfoff_b;
+  p.act_codes = w.act_codes; p.act_sf = w.act_sf; p.inter_codes = w.inter_codes; p.inter_sf = w.inter_sf;
+  p.sync = reinterpret_cast<int32_t*>(ws + L.dl_sync);
+  p.sfb_gu = wt.gu_scales; p.sfb_stride_gu = wt.ldb_gu; p.bias_gu = wt.gu_bias;
+  p.sfb_dn = wt.dn_scales; p.sfb_stride_dn = wt.ldb_dn; p.bias_dn = wt.dn_bias;
+  p.swiglu_alpha = sw_alpha; p.swiglu_limit = sw_limit;
+  p.kb1 = static_cast<int>(Kh / 128); p.kb2 = static_cast<int>(Ki / 128);
+  p.n_tiles1 = static_cast<int>((2 * I + DlCfg::kWgtRows - 1) / DlCfg::kWgtRows);
+  p.n_tiles2 = static_cast<int>((H + DlCfg::kWgtRows - 1) / DlCfg::kWgtRows);
+  p.err = status;
+  // the epilogue parameters of the two GEMMs (shared-memory tables are filled in on the GPU)
+  GemmParams g1{};
+  g1.num_experts = E; g1.N = static_cast<int>(2 * I); g1.K = static_cast<int>(Kh); g1.num_kb = p.kb1;
+  g1.err = status; g1.out = w.inter_codes; g1.ld_out = I; g1.bias = wt.gu_bias; g1.out_sf = w.inter_sf;
+  g1.out_g4 = p.kb2; g1.out_features = static_cast<int>(I);
+  g1.swiglu_alpha = sw_alpha; g1.swiglu_limit = sw_limit;
+  GemmParams g2{};
+  g2.num_experts = E; g2.N = static_cast<int>(H); g2.K = static_cast<int>(Ki); g2.num_kb = p.kb2;
+  g2.err = status; g2.out = out; g2.ld_out = H; g2.bias = wt.dn_bias;
+  g2.swiglu_alpha = sw_alpha; g2.swiglu_limit = sw_limit;
+  GPTOSS_TRY(launch_pdl(decode_reset_kernel, dim3(1), dim3(256), 0, st, p.sync, dl_sync_words(E)));
+  return launch_pdl(decode_layer_kernel, dim3(di.sms), dim3(DlCfg::kThreads), dl_smem_bytes(), st, ta, ti, tgu, tdn,
+                    p, g1, g2);
+}
+
 // route -> gather/quant -> GEMM1 -> GEMM2 on a routed batch. With `ra` the router runs
 // first (inside the decode prologue, or as router_launch, which also zeroes `out`).
 int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E,
@@ -571,6 +652,9 @@ int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, i
                      cudaStream_t st, const RouterArgs* ra = nullptr) {
   const WsPtrs w = ws_ptrs(ws, L);
   const GemmLayout lay = pick_layout(mode, T * k, E);
+  if (decode_layer_fits(T, k, E, H, I, lay, di.sms))
+    return run_decode_layer(hidden, ra, ridx, rw, T, k, E, H, I, wt, sw_alpha, sw_limit, out, ws, L, status, di, dev,
+                            st);
   size_t smem = 0;
   int slice = 0;
   // While the one-launch decode prologue runs on kDpCluster SMs, GEMM1 (launched behind it
@@ -636,6 +720,10 @@ extern "C" {
 const char* gptoss_last_error(void) { return g_last_error.c_str(); }
 
 int gptoss_abi_version(void) { return 1; }
+
+int gptoss_set_decode_layer_kernel(int enable) {
+  return g_decode_layer_enabled.exchange(enable != 0 ? 1 : 0, std::memory_order_relaxed);
+}
 
 uint64_t gptoss_kernel_launch_count(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 
@@ -998,6 +1086,7 @@ int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router
                                        const uint8_t* down_data, const uint8_t* down_scales, int64_t ldb_down,
                                        const float* down_bias, float swiglu_alpha, float swiglu_limit, void* out,
                                        int gemm_mode, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_experts_forward_noalloc");
   GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
   GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
   DeviceInfo di;

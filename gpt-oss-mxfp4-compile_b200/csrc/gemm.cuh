@@ -166,6 +166,174 @@ __device__ __forceinline__ void load_bias32(const float* b, int valid, float (&o
   }
 }
 
+// Weights-on-M (SWAP) GEMM1 / GEMM2 epilogue of one tile, run by the four epilogue warps
+// (warps 2..5: TMEM lane quarter q = warp % 4). t_acc: the tile's accumulator buffer at this
+// warp's lane quarter; acce_bar_b: the barrier that hands the buffer back to the MMA.
+// out_sf_offsets, token_idx and row_weights may point to shared memory (generic addresses).
+template <bool SPREAD, int EPI>
+__device__ __forceinline__ void swap_epilogue_tile(const GemmParams& p, uint32_t t_acc, uint32_t acce_bar_b, int e,
+                                                   int nt, int ch, int m_e, int row0, int local, float* epi_f,
+                                                   bool has_b, int q, int lane) {
+  using C = GemmConfig<true, SPREAD, false>;
+  constexpr int kEpiTok = C::kActRows < 32 ? C::kActRows : 32;
+  constexpr int kEpiFeat = EPI == kEpiGemm1 ? C::kWgtRows / 2 : C::kWgtRows;
+  constexpr uint32_t kEpiBufBytes = static_cast<uint32_t>(kEpiTok * kEpiFeat * 4);
+  constexpr int kEpiBufs = 2 * kEpiBufBytes <= C::kEpiStageBytes ? 2 : 1;
+  static_assert(kEpiBufBytes <= C::kEpiStageBytes, "epilogue staging too small");
+  // Weights-on-M GEMM1 / GEMM2 epilogue in two passes per chunk of kEpiTok activation
+  // rows. Pass 1 (thread <-> weight row = TMEM lane): accumulator -> bf16 rounding +
+  // bias (GEMM1: SwiGLU of the gate/up lane pair, the two lanes splitting the rows)
+  // into shared memory, and the accumulator goes back to the MMA right after its last
+  // load. Pass 2 regroups by activation row: GEMM1 quantises each 32-feature group in a
+  // team of 4 lanes (8 features each, one 8-byte store); GEMM2 scales 8 outputs by the
+  // routing weight and adds them with one 16-byte bf16x2 reduction.
+  const int wrow_i = nt * C::kWgtRows + 32 * q + lane;    // weight row
+  const bool vcol = wrow_i < p.N;
+  const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
+  const int a_end = min(m_e, ch * C::kActRows + C::kActRows);
+  const int etid = static_cast<int>(threadIdx.x) - 64;   // 0..127
+#pragma unroll 1
+  for (int c = 0; c < C::kColChunks; ++c) {
+    const int a0 = ch * C::kActRows + c * kEpiTok;        // first row inside expert
+    const bool live = a0 < a_end;                         // uniform over the CTA
+    const int nv = min(kEpiTok, a_end - a0);
+    float* sh = epi_f + ((local * C::kColChunks + c) % kEpiBufs) * (kEpiBufBytes / 4);
+    if (live) {
+      float v[kEpiTok];   // accumulator column j (the two issuers' partial sums added)
+      __syncwarp();
+      if constexpr (kEpiTok == 16) {
+        static_assert(kEpiTok != 16 || C::kAccCols == 16, "16-row chunks fill one partial accumulator");
+        uint32_t r[32];   // partial accumulators of both issuers are adjacent: one load
+        tmem_ld_32x32b_x32(t_acc, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          v[j] = has_b ? __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r[16 + j])) : __uint_as_float(r[j]);
+      } else {
+        uint32_t r[32], r2[32];
+        tmem_ld_32x32b_x32(t_acc + c * 32, r);
+        if (has_b) tmem_ld_32x32b_x32(t_acc + C::kAccCols + c * 32, r2);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          v[j] = has_b ? __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r2[j])) : __uint_as_float(r[j]);
+      }
+      if (c == C::kColChunks - 1 || a0 + kEpiTok >= a_end) {   // last load of this tile
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce_bar_b);
+      }
+      if constexpr (EPI == kEpiGemm1) {
+        // lanes (2f, 2f+1) hold gate / up of feature f: the even lane finishes rows
+        // [0, kHalf), the odd lane rows [kHalf, kEpiTok), one exchange per row pair
+        constexpr int kHalf = kEpiTok / 2;
+        const bool odd = (lane & 1) != 0;
+        const int fl = (32 * q + lane) >> 1;
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) {
+          const float vlo = __fadd_rn(bf16_round(v[j]), bsv);
+          const float vhi = __fadd_rn(bf16_round(v[kHalf + j]), bsv);
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? vlo : vhi, 1);
+          const float h = odd ? swiglu_pair(other, vhi, p.swiglu_alpha, p.swiglu_limit)
+                              : swiglu_pair(vlo, other, p.swiglu_alpha, p.swiglu_limit);
+          sh[(odd ? kHalf + j : j) * kEpiFeat + fl] = h;
+        }
+      } else {
+        const int fl = 32 * q + lane;
+#pragma unroll
+        for (int j = 0; j < kEpiTok; ++j) sh[j * kEpiFeat + fl] = __fadd_rn(bf16_round(v[j]), bsv);
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (live) {
+      if constexpr (EPI == kEpiGemm1) {
+        constexpr int kGroups = kEpiFeat / 32;                // quantisation groups per row
+        uint8_t* codes_out = static_cast<uint8_t*>(p.out);
+        uint8_t* sfb_e = p.out_sf + p.out_sf_offsets[e];
+#pragma unroll 1
+        for (int i0 = 0; i0 < kEpiTok * kGroups * 4; i0 += 128) {
+          const int idx = i0 + etid;
+          const int unit = idx >> 2, sub = idx & 3;
+          const int tok = unit / kGroups, grp = unit % kGroups;
+          const float* src = sh + tok * kEpiFeat + grp * 32 + sub * 8;
+          const float4 x0 = *reinterpret_cast<const float4*>(src);
+          const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+          float amax = 0.0f;
+          amax = torch_max_abs(amax, x0.x); amax = torch_max_abs(amax, x0.y);
+          amax = torch_max_abs(amax, x0.z); amax = torch_max_abs(amax, x0.w);
+          amax = torch_max_abs(amax, x1.x); amax = torch_max_abs(amax, x1.y);
+          amax = torch_max_abs(amax, x1.z); amax = torch_max_abs(amax, x1.w);
+#pragma unroll
+          for (int o = 1; o < 4; o <<= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, amax, o);
+            amax = (ob > amax || ob != ob) ? ob : amax;
+          }
+          const uint32_t rb = ue8m0_rounded_bits(amax);
+          const float inv = inv_scale(scale_from_bits(rb));
+          const int f0 = nt * (C::kWgtRows / 2) + grp * 32 + sub * 8;   // intermediate feature
+          if (tok < nv && f0 < p.out_features) {
+            const uint32_t lo = static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x0.x, inv)),
+                                                                 clamp_fp8(__fmul_rn(x0.y, inv)))) |
+                                (static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x0.z, inv)),
+                                                                  clamp_fp8(__fmul_rn(x0.w, inv)))) << 16);
+            const uint32_t hi = static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x1.x, inv)),
+                                                                 clamp_fp8(__fmul_rn(x1.y, inv)))) |
+                                (static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x1.z, inv)),
+                                                                  clamp_fp8(__fmul_rn(x1.w, inv)))) << 16);
+            const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
+            *reinterpret_cast<uint2*>(codes_out + grow * p.ld_out + f0) = make_uint2(lo, hi);
+            if (sub == 0) {
+              const int64_t srow = act_sf_row<SPREAD>(a0 + tok);
+              const int g = f0 >> 5;
+              sfb_e[blocked_sf_offset(srow, g, p.out_g4)] = static_cast<uint8_t>((rb >> 23) & 0xFFu);
+              // the K padding groups of the row's last k-atom read as zero scales in GEMM2
+              if (g == (p.out_features >> 5) - 1)
+                for (int gz = p.out_features >> 5; gz < 4 * p.out_g4; ++gz)
+                  sfb_e[blocked_sf_offset(srow, gz, p.out_g4)] = 0;
+            }
+          }
+        }
+      } else {
+        constexpr int kSegs = kEpiFeat / 8;                   // 8-output segments per row
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int i0 = 0; i0 < kEpiTok * kSegs; i0 += 128) {
+          const int idx = i0 + etid;
+          const int tok = idx / kSegs, seg = idx % kSegs;
+          const int n0 = nt * C::kWgtRows + seg * 8;           // output feature
+          if (tok < nv && n0 < p.N) {
+            const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
+            const int64_t tk = p.token_idx[grow];
+            const float wr = p.row_weights[grow];
+            const float* src = sh + tok * kEpiFeat + seg * 8;
+            const float4 z0 = *reinterpret_cast<const float4*>(src);
+            const float4 z1 = *reinterpret_cast<const float4*>(src + 4);
+            const __nv_bfloat162 v0 = __floats2bfloat162_rn(__fmul_rn(z0.x, wr), __fmul_rn(z0.y, wr));
+            const __nv_bfloat162 v1 = __floats2bfloat162_rn(__fmul_rn(z0.z, wr), __fmul_rn(z0.w, wr));
+            const __nv_bfloat162 v2 = __floats2bfloat162_rn(__fmul_rn(z1.x, wr), __fmul_rn(z1.y, wr));
+            const __nv_bfloat162 v3 = __floats2bfloat162_rn(__fmul_rn(z1.z, wr), __fmul_rn(z1.w, wr));
+            const uint4 pk4 = make_uint4(*reinterpret_cast<const uint32_t*>(&v0), *reinterpret_cast<const uint32_t*>(&v1),
+                                         *reinterpret_cast<const uint32_t*>(&v2), *reinterpret_cast<const uint32_t*>(&v3));
+            if (p.ep_world > 0) {   // one received row per output row: a plain store into the source's rows
+              const int s = static_cast<int>(tk / p.ep_cap);
+              const int64_t j = tk - static_cast<int64_t>(s) * p.ep_cap;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(p.ep_peer_bases[s]) +
+                                                                   p.ep_ret_off) + j * p.ld_out + n0;
+              *reinterpret_cast<uint4*>(dst) = pk4;
+            } else {
+              asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(o + tk * p.ld_out + n0),
+                           "r"(pk4.x), "r"(pk4.y), "r"(pk4.z), "r"(pk4.w)
+                           : "memory");
+            }
+          }
+        }
+      }
+    }
+    // single staging buffer: the next chunk's pass 1 waits for this pass 2
+    if constexpr (kEpiBufs == 1) asm volatile("bar.sync 1, 128;" ::: "memory");
+  }
+}
+
 // tm_aux0 / tm_aux1: SWAP: the 32- and 16-row activation maps; PAIR: the activation and
 // weight scale buffers viewed as rows of 256 bytes (512-byte chunks = 2 rows).
 template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false>
@@ -618,158 +786,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
           }
         }
       } else {
-        // Weights-on-M GEMM1 / GEMM2 epilogue in two passes per chunk of kEpiTok activation
-        // rows. Pass 1 (thread <-> weight row = TMEM lane): accumulator -> bf16 rounding +
-        // bias (GEMM1: SwiGLU of the gate/up lane pair, the two lanes splitting the rows)
-        // into shared memory, and the accumulator goes back to the MMA right after its last
-        // load. Pass 2 regroups by activation row: GEMM1 quantises each 32-feature group in a
-        // team of 4 lanes (8 features each, one 8-byte store); GEMM2 scales 8 outputs by the
-        // routing weight and adds them with one 16-byte bf16x2 reduction.
-        const int wrow_i = nt * C::kWgtRows + 32 * q + lane;    // weight row
-        const bool vcol = wrow_i < p.N;
-        const float bsv = vcol ? p.bias[static_cast<int64_t>(e) * p.N + wrow_i] : 0.0f;
-        const int a_end = min(m_e, ch * C::kActRows + C::kActRows);
-        const int etid = static_cast<int>(threadIdx.x) - 64;   // 0..127
-#pragma unroll 1
-        for (int c = 0; c < C::kColChunks; ++c) {
-          const int a0 = ch * C::kActRows + c * kEpiTok;        // first row inside expert
-          const bool live = a0 < a_end;                         // uniform over the CTA
-          const int nv = min(kEpiTok, a_end - a0);
-          float* sh = epi_f + ((local * C::kColChunks + c) % kEpiBufs) * (kEpiBufBytes / 4);
-          if (live) {
-            float v[kEpiTok];   // accumulator column j (the two issuers' partial sums added)
-            __syncwarp();
-            if constexpr (kEpiTok == 16) {
-              static_assert(kEpiTok != 16 || C::kAccCols == 16, "16-row chunks fill one partial accumulator");
-              uint32_t r[32];   // partial accumulators of both issuers are adjacent: one load
-              tmem_ld_32x32b_x32(t_acc, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                v[j] = has_b ? __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r[16 + j])) : __uint_as_float(r[j]);
-            } else {
-              uint32_t r[32], r2[32];
-              tmem_ld_32x32b_x32(t_acc + c * 32, r);
-              if (has_b) tmem_ld_32x32b_x32(t_acc + C::kAccCols + c * 32, r2);
-              tmem_ld_wait();
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                v[j] = has_b ? __fadd_rn(__uint_as_float(r[j]), __uint_as_float(r2[j])) : __uint_as_float(r[j]);
-            }
-            if (c == C::kColChunks - 1 || a0 + kEpiTok >= a_end) {   // last load of this tile
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(acce_bar(b));
-            }
-            if constexpr (EPI == kEpiGemm1) {
-              // lanes (2f, 2f+1) hold gate / up of feature f: the even lane finishes rows
-              // [0, kHalf), the odd lane rows [kHalf, kEpiTok), one exchange per row pair
-              constexpr int kHalf = kEpiTok / 2;
-              const bool odd = (lane & 1) != 0;
-              const int fl = (32 * q + lane) >> 1;
-#pragma unroll
-              for (int j = 0; j < kHalf; ++j) {
-                const float vlo = __fadd_rn(bf16_round(v[j]), bsv);
-                const float vhi = __fadd_rn(bf16_round(v[kHalf + j]), bsv);
-                const float other = __shfl_xor_sync(0xffffffffu, odd ? vlo : vhi, 1);
-                const float h = odd ? swiglu_pair(other, vhi, p.swiglu_alpha, p.swiglu_limit)
-                                    : swiglu_pair(vlo, other, p.swiglu_alpha, p.swiglu_limit);
-                sh[(odd ? kHalf + j : j) * kEpiFeat + fl] = h;
-              }
-            } else {
-              const int fl = 32 * q + lane;
-#pragma unroll
-              for (int j = 0; j < kEpiTok; ++j) sh[j * kEpiFeat + fl] = __fadd_rn(bf16_round(v[j]), bsv);
-            }
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (live) {
-            if constexpr (EPI == kEpiGemm1) {
-              constexpr int kGroups = kEpiFeat / 32;                // quantisation groups per row
-              uint8_t* codes_out = static_cast<uint8_t*>(p.out);
-              uint8_t* sfb_e = p.out_sf + p.out_sf_offsets[e];
-#pragma unroll 1
-              for (int i0 = 0; i0 < kEpiTok * kGroups * 4; i0 += 128) {
-                const int idx = i0 + etid;
-                const int unit = idx >> 2, sub = idx & 3;
-                const int tok = unit / kGroups, grp = unit % kGroups;
-                const float* src = sh + tok * kEpiFeat + grp * 32 + sub * 8;
-                const float4 x0 = *reinterpret_cast<const float4*>(src);
-                const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
-                float amax = 0.0f;
-                amax = torch_max_abs(amax, x0.x); amax = torch_max_abs(amax, x0.y);
-                amax = torch_max_abs(amax, x0.z); amax = torch_max_abs(amax, x0.w);
-                amax = torch_max_abs(amax, x1.x); amax = torch_max_abs(amax, x1.y);
-                amax = torch_max_abs(amax, x1.z); amax = torch_max_abs(amax, x1.w);
-#pragma unroll
-                for (int o = 1; o < 4; o <<= 1) {
-                  const float ob = __shfl_xor_sync(0xffffffffu, amax, o);
-                  amax = (ob > amax || ob != ob) ? ob : amax;
-                }
-                const uint32_t rb = ue8m0_rounded_bits(amax);
-                const float inv = inv_scale(scale_from_bits(rb));
-                const int f0 = nt * (C::kWgtRows / 2) + grp * 32 + sub * 8;   // intermediate feature
-                if (tok < nv && f0 < p.out_features) {
-                  const uint32_t lo = static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x0.x, inv)),
-                                                                       clamp_fp8(__fmul_rn(x0.y, inv)))) |
-                                      (static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x0.z, inv)),
-                                                                        clamp_fp8(__fmul_rn(x0.w, inv)))) << 16);
-                  const uint32_t hi = static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x1.x, inv)),
-                                                                       clamp_fp8(__fmul_rn(x1.y, inv)))) |
-                                      (static_cast<uint32_t>(cvt_e4m3x2(clamp_fp8(__fmul_rn(x1.z, inv)),
-                                                                        clamp_fp8(__fmul_rn(x1.w, inv)))) << 16);
-                  const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
-                  *reinterpret_cast<uint2*>(codes_out + grow * p.ld_out + f0) = make_uint2(lo, hi);
-                  if (sub == 0) {
-                    const int64_t srow = act_sf_row<SPREAD>(a0 + tok);
-                    const int g = f0 >> 5;
-                    sfb_e[blocked_sf_offset(srow, g, p.out_g4)] = static_cast<uint8_t>((rb >> 23) & 0xFFu);
-                    // the K padding groups of the row's last k-atom read as zero scales in GEMM2
-                    if (g == (p.out_features >> 5) - 1)
-                      for (int gz = p.out_features >> 5; gz < 4 * p.out_g4; ++gz)
-                        sfb_e[blocked_sf_offset(srow, gz, p.out_g4)] = 0;
-                  }
-                }
-              }
-            } else {
-              constexpr int kSegs = kEpiFeat / 8;                   // 8-output segments per row
-              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out);
-#pragma unroll 1
-              for (int i0 = 0; i0 < kEpiTok * kSegs; i0 += 128) {
-                const int idx = i0 + etid;
-                const int tok = idx / kSegs, seg = idx % kSegs;
-                const int n0 = nt * C::kWgtRows + seg * 8;           // output feature
-                if (tok < nv && n0 < p.N) {
-                  const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
-                  const int64_t tk = p.token_idx[grow];
-                  const float wr = p.row_weights[grow];
-                  const float* src = sh + tok * kEpiFeat + seg * 8;
-                  const float4 z0 = *reinterpret_cast<const float4*>(src);
-                  const float4 z1 = *reinterpret_cast<const float4*>(src + 4);
-                  const __nv_bfloat162 v0 = __floats2bfloat162_rn(__fmul_rn(z0.x, wr), __fmul_rn(z0.y, wr));
-                  const __nv_bfloat162 v1 = __floats2bfloat162_rn(__fmul_rn(z0.z, wr), __fmul_rn(z0.w, wr));
-                  const __nv_bfloat162 v2 = __floats2bfloat162_rn(__fmul_rn(z1.x, wr), __fmul_rn(z1.y, wr));
-                  const __nv_bfloat162 v3 = __floats2bfloat162_rn(__fmul_rn(z1.z, wr), __fmul_rn(z1.w, wr));
-                  const uint4 pk4 = make_uint4(*reinterpret_cast<const uint32_t*>(&v0), *reinterpret_cast<const uint32_t*>(&v1),
-                                               *reinterpret_cast<const uint32_t*>(&v2), *reinterpret_cast<const uint32_t*>(&v3));
-                  if (p.ep_world > 0) {   // one received row per output row: a plain store into the source's rows
-                    const int s = static_cast<int>(tk / p.ep_cap);
-                    const int64_t j = tk - static_cast<int64_t>(s) * p.ep_cap;
-                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(p.ep_peer_bases[s]) +
-                                                                         p.ep_ret_off) + j * p.ld_out + n0;
-                    *reinterpret_cast<uint4*>(dst) = pk4;
-                  } else {
-                    asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(o + tk * p.ld_out + n0),
-                                 "r"(pk4.x), "r"(pk4.y), "r"(pk4.z), "r"(pk4.w)
-                                 : "memory");
-                  }
-                }
-              }
-            }
-          }
-          // single staging buffer: the next chunk's pass 1 waits for this pass 2
-          if constexpr (kEpiBufs == 1) asm volatile("bar.sync 1, 128;" ::: "memory");
-        }
+        swap_epilogue_tile<SPREAD, EPI>(p, t_acc, acce_bar(b), e, nt, ch, m_e, row0, local, epi_f, has_b, q, lane);
         continue;   // the accumulator went back to the MMA after its last load
       }
       tc_fence_before();

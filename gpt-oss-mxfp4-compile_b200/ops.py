@@ -99,6 +99,12 @@ def status_tensor(device) -> torch.Tensor:
         return t
 
 
+def set_decode_layer_kernel(enable: bool) -> bool:
+    """Process-wide: decode-sized fused forwards as one persistent launch (True, the
+    default) or as the three-launch path (False). Returns the previous setting."""
+    return bool(_lib.query("gptoss_set_decode_layer_kernel", 1 if enable else 0))
+
+
 def read_status(device) -> int:
     """Returns and clears the device status word (synchronises the current stream)."""
     t = status_tensor(device)

@@ -64,6 +64,16 @@ int gptoss_abi_version(void);
  * for benchmarks; no counterpart in the reference). */
 uint64_t gptoss_kernel_launch_count(void);
 
+/* Decode-sized fused forwards (gptoss_moe_layer_forward, gptoss_moe_experts_forward and
+ * the no-allocation forward with at most 64 tokens, 256 assignments and 128 experts, on
+ * the SWAP orientation) run as one persistent launch that streams the expert weights from
+ * its first cycle and computes the routing on its idle warps (plus a one-CTA launch that
+ * clears its synchronisation words). Its CTAs wait on each other, so it expects the whole
+ * GPU (one CTA per SM). enable = 0 selects the three-launch path (routing prologue, GEMM1,
+ * GEMM2) for those batches instead; outputs agree within the combine's bf16 atomics.
+ * Process-wide; returns the previous setting. No counterpart in the reference. */
+int gptoss_set_decode_layer_kernel(int enable);
+
 /* Copies the 4-byte device status word that kernels set when a bounded wait times out
  * or an expert index is out of range (0 = ok) into *status_host and clears it.
  * Synchronises `stream`. */
@@ -234,18 +244,21 @@ int gptoss_moe_gemm2(int64_t num_tokens, int top_k, int num_experts, int64_t hid
  * it allocate one: runtimes that reserve all device memory up front behind their own pool
  * (an out-of-band cudaMalloc fails there), hosts that bind the C ABI through an FFI and have
  * no device allocator to call, and latency-critical loops that cannot pay for cudaMalloc /
- * cudaFree, which synchronise the device. For them this entry point runs the same five kernels
+ * cudaFree, which synchronise the device. For them this entry point runs the same kernels
  * as gptoss_moe_experts_forward with the workspace in a static device array of
  * GPTOSS_NOALLOC_SCRATCH_BYTES inside this library (every GPU that loads the library holds it
- * until the process exits). Batches whose workspace (gptoss_moe_workspace_bytes) exceeds that
+ * until the process exits). The array is reserved when the library's device code is loaded
+ * onto a GPU, i.e. at this library's first CUDA call on that device, whichever entry point it
+ * is: a runtime that reserves device memory up front must leave that many bytes free, or
+ * that first call fails with an out-of-memory CUDA error. Batches whose workspace (gptoss_moe_workspace_bytes) exceeds that
  * size are rejected with GPTOSS_ERR_INVALID_ARGUMENT — at H = I = 2880 and 32 experts that
  * is about 2,400 token-expert assignments (600 tokens at top-4). The first call on a device
  * does a one-time set-up: it looks up the array's device address (cudaGetSymbolAddress, with
  * that device current) and caches it; make that first call before any stream capture
  * begins. All calls share the one
  * array and it keeps the previous call's contents; every region is rewritten before it is
- * read, so nothing needs clearing, but calls that overlap on the GPU (other streams, other
- * threads) race on it. Inputs, outputs and the status word are the caller's, exactly as in
+ * read and the words that must start at zero are cleared by the call itself, but calls that
+ * overlap on the GPU (other streams, other threads) race on it. Inputs, outputs and the status word are the caller's, exactly as in
  * gptoss_moe_experts_forward; no cudaMalloc, cudaFree or allocating library routine is called. */
 #define GPTOSS_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int gptoss_moe_experts_forward_noalloc(const void* hidden, const int64_t* router_indices,

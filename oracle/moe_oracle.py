@@ -15,7 +15,8 @@ __all__ = [
     "MXFP_BLOCK", "FP8_MAX", "E2M1_VALUES", "pad_k_to_tile",
     "e4m3_encode", "e4m3_decode", "quantize_fp8_ue8m0",
     "blocked_sf_offset", "blocked_sf_cosize", "convert_scales_blocked", "batch_convert_a_scales",
-    "route_stable", "router_topk_hf", "router_logits_fp32",
+    "route_stable", "router_topk_hf", "router_logits_fp32", "router_logits_exact", "router_topk_from_logits",
+    "round_bf16_exact",
     "mxfp4_dequant", "fp8_dequant", "group_mm_bf16", "swiglu_fp32",
     "w4a8_experts_forward", "dequant_fp32_reference", "synth_layer", "synth_router_bias",
     "ep_row_bytes", "ep_dispatch", "ep_expert_rows", "ep_combine", "slice_experts",
@@ -183,6 +184,35 @@ def router_logits_fp32(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.T
     """Logits with fp32 accumulation, fp32 bias add and one rounding to bf16."""
     acc = hidden.float() @ weight.float().T
     return (acc + bias.float()).to(torch.bfloat16)
+
+
+def round_bf16_exact(v: np.ndarray) -> torch.Tensor:
+    """float64 -> bf16, round-to-nearest-even in one step (no float32 intermediate, so
+    no double rounding). Finite normal values only (router logits)."""
+    v = np.asarray(v, dtype=np.float64)
+    f, ex = np.frexp(v)                       # v = f * 2**ex, 0.5 <= |f| < 1
+    q = np.rint(f * 256.0)                    # 8 significant bits, ties to even
+    r = np.ldexp(q, ex - 8)
+    return torch.from_numpy(r.astype(np.float32)).to(torch.bfloat16)
+
+
+def router_logits_exact(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """The exactly rounded F.linear value: bf16 x bf16 products (exact in float64) summed
+    in float64, + bias, one rounding to bf16. An fp32-accumulating F.linear lands on the
+    same bf16 value except where its own rounding error crosses a bf16 rounding boundary."""
+    acc = hidden.double().numpy() @ weight.double().numpy().T + bias.double().numpy()
+    return round_bf16_exact(acc)
+
+
+def router_topk_from_logits(logits: torch.Tensor, top_k: int):
+    """GptOssTopKRouter after its F.linear (bf16 logits in): top-k, softmax over the k
+    logits in bf16. Returns (scores bf16, indices i64). Equal logits are taken in
+    ascending expert order (a stable descending sort); torch.topk leaves their order
+    unspecified, and bf16 logits tie often once router biases spread them apart."""
+    order = torch.sort(logits, dim=-1, descending=True, stable=True).indices[:, :top_k]
+    top_v = torch.gather(logits, 1, order)
+    scores = torch.nn.functional.softmax(top_v, dim=1, dtype=top_v.dtype)
+    return scores, order
 
 
 # --------------------------------------------------------------------------- GEMM

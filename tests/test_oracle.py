@@ -127,3 +127,22 @@ def test_dequant_reference_distance():
     ref = O.dequant_fp32_reference(d["hidden"], idx.numpy(), w.numpy(), wn)
     rel = ((out.float() - ref.float()).abs().mean() / ref.float().abs().mean()).item()
     assert rel < 0.15
+
+
+def test_round_bf16_exact_rounds_once():
+    # 1 + 2^-8 is a tie between 1 and 1 + 2^-7 (ties to even -> 1); just above the tie
+    # rounds up, although float32(1 + 2^-8 + 2^-40) is the tie itself (a float32
+    # intermediate would double-round it down)
+    v = np.array([1.0 + 2.0 ** -8, 1.0 + 2.0 ** -8 + 2.0 ** -40, -(1.0 + 3 * 2.0 ** -8), 3.0, -0.15625])
+    r = O.round_bf16_exact(v).float().numpy()
+    assert r.tolist() == [1.0, 1.0 + 2.0 ** -7, -(1.0 + 2.0 ** -6), 3.0, -0.15625]
+
+
+def test_router_logits_exact_matches_fp32_router_almost_everywhere():
+    d = O.synth_layer(0, E=32, H=2880, I=64, T=32)
+    ex = O.router_logits_exact(d["hidden"], d["router_w"], d["router_b"])
+    f32 = O.router_logits_fp32(d["hidden"], d["router_w"], d["router_b"])
+    # both round the same real number; they can only differ where fp32 accumulation error
+    # crosses a bf16 rounding boundary (a handful of the 1024 logits at most)
+    assert (ex != f32).sum().item() <= 8
+    assert ((ex.float() - f32.float()).abs() <= ex.float().abs() * 2 ** -7 + 1e-30).all()
