@@ -579,7 +579,7 @@ std::atomic<int> g_decode_layer_enabled{1};
 bool decode_layer_fits(int64_t T, int k, int E, int64_t H, int64_t I, GemmLayout lay, int sms) {
   return g_decode_layer_enabled.load(std::memory_order_relaxed) != 0 && lay.swap && lay.spread && T >= 1 &&
          T <= kDlMaxTokens && T * k <= kDlMaxAssign && E <= kDlMaxExperts && H % 32 == 0 && I % 32 == 0 &&
-         static_cast<size_t>(T) * (E + k) * sizeof(float) <= (DlCfg::kStages - kDlPreStages) * DlCfg::kStageBytes &&
+         static_cast<size_t>(T) * (2 * E + k) * sizeof(float) <= (DlCfg::kStages - kDlPreStages) * DlCfg::kStageBytes &&
          sms >= 1;
 }
 

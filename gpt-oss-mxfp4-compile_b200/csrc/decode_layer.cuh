@@ -20,10 +20,11 @@
 //     results), zeroes its slice of `out`, and quantises sorted rows b, b + G, ...
 //     (per-expert counters publish the rows);
 //   * GEMM1 and GEMM2 tiles run back to back on the same ring and TMEM accumulators: one
-//     list holds every GEMM1 tile (expert-major) followed by every GEMM2 tile, and CTA b
-//     takes tiles b, b + G, b + 2G, ... So the experts finish GEMM1 one after another, wave
-//     by wave, and a GEMM2 tile comes up several waves after the last GEMM1 tile of its
-//     expert. A GEMM1 tile's activation loads wait until its expert's rows are all quantised; a
+//     list holds every GEMM1 tile (expert-major) followed by every GEMM2 tile; CTA b starts
+//     with tile b and then takes the next unclaimed tile from a global counter (one tile
+//     ahead of its MMA), so the experts finish GEMM1 one after another, a GEMM2 tile comes up
+//     several waves after the last GEMM1 tile of its expert, and CTAs that stream faster
+//     take more tiles. A GEMM1 tile's activation loads wait until its expert's rows are all quantised; a
 //     GEMM2 tile's wait until all of its expert's GEMM1 tiles have published their FP8
 //     intermediate rows (a per-expert counter) -- in practice they never wait.
 // Synchronisation words live in the workspace and are zeroed by decode_reset_kernel,
@@ -61,7 +62,10 @@ static_assert(kDlPreStages < DlCfg::kStages, "the routing scratch lives in the r
 //   [1]              CTAs whose router dot products are written
 //   [2, 2 + E)       activation rows of expert e quantised (count)
 //   [2 + E, 2 + 2E)  GEMM1 tiles of expert e whose intermediate rows are written
-__host__ __device__ constexpr int dl_sync_words(int E) { return 2 + 2 * E; }
+//   [2 + 2E]         tiles handed out past every CTA's first one (dynamic scheduling)
+__host__ __device__ constexpr int dl_sync_words(int E) { return 3 + 2 * E; }
+
+constexpr int kDlQueue = 16;   // tile indices the producer publishes ahead of the MMA and epilogue
 
 struct DecodeLayerParams {
   const __nv_bfloat16* x;          // [T, H]
@@ -110,6 +114,8 @@ struct DlShared {
   int sexp[kDlMaxAssign];          // sorted position -> expert
   int64_t ridx[kDlMaxAssign];      // assignment -> expert (-1: out of range)
   float rw[kDlMaxAssign];          // assignment -> routing weight
+  uint64_t tq_bar[kDlQueue];       // tile queue: slot (i - 1) % kDlQueue holds the CTA's tile i >= 1
+  int tq[kDlQueue];                // (tile 0 is the CTA index itself); -1 ends the list
 };
 
 __host__ __device__ constexpr uint32_t dl_smem_bytes() {
@@ -143,6 +149,14 @@ __device__ __forceinline__ bool spin_wait_geq(const int32_t* p, int32_t target, 
   }
 }
 
+// Order-preserving key of a router logit for torch.topk order: larger floats -> larger keys,
+// every NaN the largest key, -0 equal to +0; 0 is below every real key.
+__device__ __forceinline__ uint32_t topk_key(float v) {
+  if (v != v) return 0xffffffffu;
+  const uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 enum DlError : int { kDlTimeoutGrid = 0x106, kDlTimeoutAct = 0x107, kDlTimeoutInter = 0x108 };
 
 __global__ void decode_reset_kernel(int32_t* sync, int n) {
@@ -160,6 +174,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   using C = DlCfg;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint32_t s_tmem_base;
+  __shared__ int s_epi_tile;   // the epilogue warps' tile, read from the queue by one thread
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int G = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
@@ -194,6 +209,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
       mbar_init(acce_bar(b), C::kEpiWarps);
     }
     mbar_init(drain_bar, C::kIssuers);
+    for (int j = 0; j < kDlQueue; ++j) mbar_init(smem_u32(&S.tq_bar[j]), 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -209,10 +225,10 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   // expert is touched once.
   const bool guess_live = cta < E * p.n_tiles1;
   const int e_g = cta / p.n_tiles1, nt_g = cta - e_g * p.n_tiles1;
-  // The routing scratch (logits and top-k slots) lives in the epilogue staging buffer when
+  // The routing scratch (logits, their keys, top-k slots) lives in the epilogue staging buffer when
   // it fits -- then the whole ring is loaded ahead -- else in the ring stages past the
   // first kDlPreStages.
-  const bool scratch_in_epi = static_cast<uint32_t>(T) * (E + K) * 4u <= C::kEpiStageBytes;
+  const bool scratch_in_epi = static_cast<uint32_t>(T) * (2 * E + K) * 4u <= C::kEpiStageBytes;
   const int pre = guess_live ? min(scratch_in_epi ? C::kStages : kDlPreStages, (p.kb1 + C::kSubs - 1) / C::kSubs) : 0;
   auto sfb_gu_at = [&](int e, int nt, int kb) {
     return p.sfb_gu + static_cast<int64_t>(e) * p.sfb_stride_gu +
@@ -303,20 +319,33 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     // every CTA: all logits (L2, bypassing L1) -> the routing scratch in ring stages the
     // pre-loads do not use, then one thread per token: top-k + softmax
     float* lg = scratch_in_epi ? epi_f : reinterpret_cast<float*>(smem_gen + kDlPreStages * C::kStageBytes);
-    for (int i = tid; i < np; i += nthr) lg[i] = __ldcg(p.logits + i);
+    float* slot_v = lg + np;
+    uint32_t* keys = reinterpret_cast<uint32_t*>(slot_v + T * K);
+    for (int i = tid; i < np; i += nthr) {
+      const float v = __ldcg(p.logits + i);
+      lg[i] = v;
+      keys[i] = topk_key(v);
+    }
     __syncthreads();
     // top-k in torch.topk order (larger first, NaN above every number, equal values by
     // ascending expert id): thread per (token, expert) counts the experts ranked ahead of
-    // it, so slot rank of token t holds its rank-th choice; then the softmax per token
-    // (the operation order of router_topk_token)
-    float* slot_v = lg + np;
+    // it on order-preserving integer keys (loads batched by the unrolled loop), so slot
+    // `rank` of token t holds its rank-th choice; then one thread per token applies the
+    // softmax over the K values in rank order (the operation order of router_topk_token)
     for (int q = tid; q < np; q += nthr) {
       const int t = q / E, e = q - t * E;
-      const float* row = lg + t * E;
-      const float v = row[e];
+      const uint32_t* kr = keys + t * E;
+      const uint32_t ke = kr[e];
       int rk = 0;
-      for (int f = 0; f < E; ++f) rk += topk_ahead(row[f], f, v, e) ? 1 : 0;
-      if (rk < K) { S.ridx[t * K + rk] = e; slot_v[t * K + rk] = v; }
+#pragma unroll 8
+      for (int f = 0; f < E; ++f) {
+        const uint32_t kf = kr[f];
+        rk += (kf > ke || (kf == ke && f < e)) ? 1 : 0;
+      }
+      if (rk < K) {
+        S.ridx[t * K + rk] = e;
+        slot_v[t * K + rk] = lg[q];
+      }
     }
     __syncthreads();
     for (int t = tid; t < T; t += nthr) {
@@ -404,7 +433,20 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   const int nchunks = S.prefix[E];
   // one tile list: GEMM1 tiles [0, q1), then GEMM2 tiles [q1, q1 + q2); CTA b takes b, b + G, ...
   const int q1 = nchunks * p.n_tiles1, q2 = nchunks * p.n_tiles2;
-  const int ntiles = cta < q1 + q2 ? (q1 + q2 - cta + G - 1) / G : 0;
+  const int qall = q1 + q2;
+  // Tile schedule: CTA b's first tile is tile b (what its pre-loaded stages guessed); every
+  // later one comes from a global counter (first come, first served), so CTAs that stream
+  // faster take more tiles. The producer publishes each tile index through S.tq.
+  const int t_first = cta < qall ? cta : -1;
+  auto queued_tile = [&](int i, bool& ok) -> int {   // tile i >= 1 of this CTA, or -1
+    const int slot = (i - 1) % kDlQueue;
+    if (!mbar_wait(smem_u32(&S.tq_bar[slot]), static_cast<uint32_t>((i - 1) / kDlQueue) & 1u, p.err,
+                   kDevTimeoutMma)) {
+      ok = false;
+      return -1;
+    }
+    return *reinterpret_cast<volatile int*>(&S.tq[slot]);
+  };
 
   // CTA 0: the routing outputs of the API and the routed layout of the workspace
   if (cta == 0) {
@@ -442,9 +484,8 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     nt = local / nch;
     ch = local - nt * nch;
   };
-  // this CTA's i-th tile of the combined list
-  auto tile_of = [&](int i, bool& g2, int& e, int& nt, int& ch) {
-    const int t = cta + i * G;
+  // tile t of the combined list (GEMM1 tiles, then GEMM2 tiles)
+  auto tile_of = [&](int t, bool& g2, int& e, int& nt, int& ch) {
     g2 = t >= q1;
     if (g2) decode(t - q1, p.n_tiles2, e, nt, ch);
     else decode(t, p.n_tiles1, e, nt, ch);
@@ -535,10 +576,19 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
         stage = pre;   // pre <= kStages: the next stage wraps to 0 when every stage was pre-loaded
         if (stage == C::kStages) { stage = 0; phase ^= 1u; }
       }
-      for (int i = 0; i < ntiles && ok; ++i) {
+      int t_next = -1;
+      for (int i = 0; ok; ++i) {
+        const int t = i == 0 ? t_first : (t_next < qall ? t_next : -1);
+        if (i > 0) {                          // publish tile i (or the end of the list)
+          const int slot = (i - 1) % kDlQueue;
+          *reinterpret_cast<volatile int*>(&S.tq[slot]) = t;
+          mbar_arrive(smem_u32(&S.tq_bar[slot]));
+        }
+        if (t < 0) break;
+        t_next = G + atomicAdd(p.sync + 2 + 2 * E, 1);   // the next tile, one tile ahead
         bool g2;
         int e, nt, ch;
-        tile_of(i, g2, e, nt, ch);
+        tile_of(t, g2, e, nt, ch);
         const int num_kb = g2 ? p.kb2 : p.kb1;
         if (!g2 && e != ready_e1) {
           if (!spin_wait_geq(p.sync + 2 + e, S.cnt[e], p.err, kDlTimeoutAct)) { ok = false; break; }
@@ -601,10 +651,12 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
         stage = pre;   // pre <= kStages: the next stage wraps to 0 when every stage was pre-loaded
         if (stage == C::kStages) { stage = 0; phase ^= 1u; }
       }
-      for (int i = 0; i < ntiles && ok; ++i) {
+      for (int i = 0; ok; ++i) {
+        const int t = i == 0 ? t_first : queued_tile(i, ok);
+        if (t < 0) break;
         bool g2;
         int e, nt, ch;
-        tile_of(i, g2, e, nt, ch);
+        tile_of(t, g2, e, nt, ch);
         const int num_kb = g2 ? p.kb2 : p.kb1;
         const int b = i % C::kAccBufs;
         const uint32_t acc_phase = static_cast<uint32_t>(i / C::kAccBufs) & 1u;
@@ -658,10 +710,24 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     const int q = warp & 3;
     bool ok = true;
     bool out_ready = false;
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = 0;; ++i) {
+      // one thread reads the queue and the four warps take the same decision (the named
+      // barriers of the epilogue must stay matched even when a wait gives up)
+      int t = t_first;
+      if (i > 0) {
+        if (tid == 64) {
+          bool okq = true;
+          const int v = queued_tile(i, okq);
+          *reinterpret_cast<volatile int*>(&s_epi_tile) = okq ? v : -2;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        t = *reinterpret_cast<volatile int*>(&s_epi_tile);
+        if (t == -2) ok = false;
+      }
+      if (t < 0) break;
       bool g2;
       int e, nt, ch;
-      tile_of(i, g2, e, nt, ch);
+      tile_of(t, g2, e, nt, ch);
       const int b = i % C::kAccBufs;
       const uint32_t acc_phase = static_cast<uint32_t>(i / C::kAccBufs) & 1u;
       if (ok) ok = mbar_wait(accf_bar(b), acc_phase, p.err, kDevTimeoutEpilogue);
