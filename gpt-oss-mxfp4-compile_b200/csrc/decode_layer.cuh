@@ -58,12 +58,12 @@ using DlCfg = GemmConfig<true, true, false>;
 static_assert(kDlPreStages < DlCfg::kStages, "the routing scratch lives in the ring stages past the pre-loaded ones");
 
 // Synchronisation words (int32, zeroed before every launch):
-//   [0]              CTAs past the routing phase (their slice of `out` zeroed)
+//   [0]              CTAs past the routing phase (their slice of `out` zeroed, their share
+//                    of the activation rows quantised)
 //   [1]              CTAs whose router dot products are written
-//   [2, 2 + E)       activation rows of expert e quantised (count)
-//   [2 + E, 2 + 2E)  GEMM1 tiles of expert e whose intermediate rows are written
-//   [2 + 2E]         tiles handed out past every CTA's first one (dynamic scheduling)
-__host__ __device__ constexpr int dl_sync_words(int E) { return 3 + 2 * E; }
+//   [2, 2 + E)       GEMM1 tiles of expert e whose intermediate rows are written
+//   [2 + E]          tiles handed out past every CTA's first one (dynamic scheduling)
+__host__ __device__ constexpr int dl_sync_words(int E) { return 3 + E; }
 
 constexpr int kDlQueue = 16;   // tile indices the producer publishes ahead of the MMA and epilogue
 
@@ -490,9 +490,9 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     if (g2) decode(t - q1, p.n_tiles2, e, nt, ch);
     else decode(t, p.n_tiles1, e, nt, ch);
   };
-  // quantise sorted rows cta, cta + G, ...: each row's codes and blocked scales, then
-  // count the rows into their expert's counter (a GEMM1 tile's activation loads wait
-  // until all rows of its expert are counted)
+  // quantise sorted rows cta, cta + G, ...: each row's codes and blocked scales; the CTA
+  // then counts itself into sync[0] (the activation loads wait until every CTA has: one
+  // wait per CTA instead of one acquire round trip per expert on the producer's path)
   {
     const int gp = 4 * p.kb1;                 // scale groups per row incl. K padding
     const int gv = H / 32;                    // valid groups
@@ -527,7 +527,6 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     __syncthreads();
     if (tid == 0) {
       __threadfence();
-      for (int r = 0; r < nmine; ++r) atomicAdd(p.sync + 2 + S.sexp[cta + r * G], 1);
       atomicAdd(p.sync + 0, 1);               // this CTA's slice of `out` is zero
     }
   }
@@ -548,8 +547,8 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int ready_e1 = -1, ready_e2 = -1;
-      bool out_ready = false;
+      int ready_e2 = -1;
+      bool all_rows = false;   // every CTA's activation rows quantised and its slice of `out` zeroed
       // activation half of the pre-loaded stages: the first tile's rows, or (the guess was
       // wrong) any in-range rows -- the MMA warps release those stages unused
       if (pre > 0) {
@@ -557,9 +556,9 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
         if (match) {
           int nt0;
           decode(cta, p.n_tiles1, e0, nt0, ch0);
-          ok = spin_wait_geq(p.sync + 2 + e0, S.cnt[e0], p.err, kDlTimeoutAct);
+          ok = spin_wait_geq(p.sync + 0, G, p.err, kDlTimeoutAct);
           fence_proxy_async_global();
-          ready_e1 = e0;
+          all_rows = true;
         }
         const int row = match ? S.off[e0] : 0;
         const int64_t sfa_base = match ? S.sfa[e0] : 0;
@@ -585,22 +584,22 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
           mbar_arrive(smem_u32(&S.tq_bar[slot]));
         }
         if (t < 0) break;
-        t_next = G + atomicAdd(p.sync + 2 + 2 * E, 1);   // the next tile, one tile ahead
+        t_next = G + atomicAdd(p.sync + 2 + E, 1);   // the next tile, one tile ahead
         bool g2;
         int e, nt, ch;
         tile_of(t, g2, e, nt, ch);
         const int num_kb = g2 ? p.kb2 : p.kb1;
-        if (!g2 && e != ready_e1) {
-          if (!spin_wait_geq(p.sync + 2 + e, S.cnt[e], p.err, kDlTimeoutAct)) { ok = false; break; }
+        // One wait per CTA for the activation rows (every CTA counts itself into sync[0] once
+        // its share is quantised): an acquire load is a blocking L2 round trip on the
+        // producer's path, so it is not repeated per expert. GEMM2 tiles wait per expert for
+        // the expert's GEMM1 tiles (in practice they are long done).
+        if (!all_rows) {
+          if (!spin_wait_geq(p.sync + 0, G, p.err, kDlTimeoutAct)) { ok = false; break; }
           fence_proxy_async_global();
-          ready_e1 = e;
+          all_rows = true;
         }
         if (g2 && e != ready_e2) {
-          if (!out_ready) {
-            if (!spin_wait_geq(p.sync + 0, G, p.err, kDlTimeoutGrid)) { ok = false; break; }
-            out_ready = true;
-          }
-          if (!spin_wait_geq(p.sync + 2 + E + e, p.n_tiles1 * S.chunks[e], p.err, kDlTimeoutInter)) {
+          if (!spin_wait_geq(p.sync + 2 + e, p.n_tiles1 * S.chunks[e], p.err, kDlTimeoutInter)) {
             ok = false;
             break;
           }
@@ -755,7 +754,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (tid == 64) {
           __threadfence();
-          atomicAdd(p.sync + 2 + E + e, 1);
+          atomicAdd(p.sync + 2 + e, 1);
         }
       } else {
         swap_epilogue_tile<true, kEpiGemm2>(pg2, t_acc, acce_bar(b), e, nt, ch, S.cnt[e], S.off[e], i, epi_f, has_b,
