@@ -49,7 +49,7 @@ CPU_BASELINE_CONFIGS = ("decode", "prefill")   # the others are minutes of CPU w
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from one
 # ncu capture of that kernel on this workload (None until captured for this kernel/config).
-NCU_TRAFFIC_BYTES = {"decode": None,            # decode_layer_kernel, T = 32 (capture pending)
+NCU_TRAFFIC_BYTES = {"decode": 439_218_944,     # decode_layer_kernel, T = 32
                      "prefill": 769_571_328}    # GEMM1, tokens-on-M CTA-pair tiles, T = 8192
 
 
