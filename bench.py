@@ -65,6 +65,8 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=45.0,
                     help="reference arm: CPU seconds the whole --warmup + --steps run may take; each step "
                          "times a token sample of the workload sized to fit")
+    ap.add_argument("--mma-peak", action="store_true",
+                    help="only measure the block-scaled FP8 x FP4 MMA peak (gptoss_mma_peak) and print it")
     ap.add_argument("--l2", choices=["none", "write"], default="none",
                     help="between timed steps: nothing (inputs larger than L2) or write a 256 MiB buffer")
     ap.add_argument("--ep-transport", choices=["auto", "p2p", "nccl"], default="auto",
@@ -539,14 +541,18 @@ def stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, 
     g1_gbs = b_g1 / (t_g1 / 1e3) / 1e9
     layer_gbs = b_layer / (ms / 1e3) / 1e9
     flops = 2 * T * k * (H * 2 * I + I * H)
+    mma_peak = None
     if cfg_name in ("prefill", "zipf"):
-        # dense block-scaled FP8 x FP4 contraction: the tensor pipe bounds it; its peak is
-        # taken as twice the measured dense bf16 rate (the fp8/fp6/fp4 : bf16 rate ratio)
+        # dense block-scaled FP8 x FP4 contraction: the tensor pipe bounds it; the peak is
+        # this GPU's own kind::mxf8f6f4 rate, measured here (MMA-only probe, CTA pairs, N = 192:
+        # the GEMM's instruction shape)
+        mma_peak = pkg.ops.mma_peak(dev, pair=True, n=192, iters=4000)["tflops"]
         g1_flops = 2 * T * k * H * 2 * I
         g1_tf = g1_flops / (t_g1 / 1e3) / 1e12
         roof = {"bound": "tensor", "kernel": "moe_gemm_kernel (GEMM1 gate_up + SwiGLU + requant, CTA pairs)",
-                "achieved": g1_tf, "peak": 2 * bf16_peak, "unit": "TFLOP/s", "frac": g1_tf / (2 * bf16_peak),
-                "traffic": NCU_TRAFFIC_BYTES.get(cfg_name), "peak_kind": f"{peak_kind} bf16 x 2",
+                "achieved": g1_tf, "peak": mma_peak, "unit": "TFLOP/s", "frac": g1_tf / mma_peak,
+                "traffic": NCU_TRAFFIC_BYTES.get(cfg_name),
+                "peak_kind": "measured in this run: gptoss_mma_peak, kind::mxf8f6f4, CTA pairs, N = 192",
                 "alg_flops_per_launch": g1_flops, "ms_per_launch": t_g1}
     elif launches_per_step <= 2.5:
         roof = {"bound": "hbm",
@@ -567,13 +573,31 @@ def stage_roofline(pkg, layer, ex, x, flush, stream, T, k, E, H, I, K, ms, dev, 
                       "staged_path_ms": {"router+route+quant": t_pre, "gemm1": t_g1, "gemm2": t_g2},
                       "staged_gemm1_gbs": g1_gbs, "staged_gemm2_gbs": b_g2 / (t_g2 / 1e3) / 1e9},
         "mma": {"flops_per_step": flops, "tflops": flops / (ms / 1e3) / 1e12,
-                "frac_of_fp8_dense": flops / (ms / 1e3) / 1e12 / (2 * bf16_peak) if bf16_peak else None,
-                "peak_note": "fp8 dense peak taken as 2 x the measured bf16 rate"},
+                "frac_of_mxf8f6f4_peak": flops / (ms / 1e3) / 1e12 / mma_peak if mma_peak else None,
+                "peak_tflops": mma_peak},
     }
+
+
+def run_mma_peak(args):
+    """One JSON line: the measured dense block-scaled FP8 x FP4 MMA throughput (the
+    tensor-bound roofline denominator) for CTA pairs and single CTAs at N = 256/192/128."""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    dev = torch.device("cuda", 0)
+    sampler = clock_sampler_start(0)
+    time.sleep(0.3)
+    res = [pkg.ops.mma_peak(dev, pair=pair, n=n, iters=4000) for pair in (True, False) for n in (256, 192, 128)]
+    clocks = clock_sampler_stop(sampler)
+    print(json.dumps({"metric": "block-scaled FP8 x FP4 MMA peak (tcgen05.mma kind::mxf8f6f4)", "unit": "TFLOP/s",
+                      "value": max(r["tflops"] for r in res), "results": res, "clocks": clocks}), flush=True)
+    return 0
 
 
 def main():
     args = parse_args()
+    if args.mma_peak:
+        return run_mma_peak(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -29,6 +29,8 @@ _SIGNATURES = {
     "gptoss_read_status": (_i, [_vp, _vp, _vp]),
     "gptoss_fused_moe_routing": (_i, [_vp, _vp, _c_int64, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gptoss_router_topk": (_i, [_vp, _vp, _vp, _c_int64, _c_int64, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    "gptoss_router_topk_from_logits": (_i, [_vp, _c_int64, _i, _i, _vp, _vp, _vp, _vp]),
+    "gptoss_mma_peak": (_i, [_i, _i, _i, _vp, _vp]),
     "gptoss_quantize_fp8": (_i, [_vp, _i, _c_int64, _c_int64, _vp, _vp, _vp]),
     "gptoss_swiglu": (_i, [_vp, _i, _c_int64, _c_int64, _vp, _f, _f, _vp]),
     "gptoss_convert_scales_blocked": (_i, [_vp, _c_int64, _c_int64, _vp, _c_int64, _vp]),

@@ -23,6 +23,7 @@
 #include "prologue.cuh"
 #include "ep_p2p.cuh"
 #include "decode_layer.cuh"
+#include "mma_peak.cuh"
 
 using namespace gptoss;
 
@@ -788,6 +789,59 @@ int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
   return router_launch(hidden, weight, bias, num_tokens, hidden_size, num_experts, top_k, router_indices,
                        router_scores, routing_weights_f32, logits, nullptr, 0, di.sms, dev,
                        static_cast<cudaStream_t>(stream));
+}
+
+int gptoss_mma_peak(int pair, int n, int iters, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_mma_peak");
+  GPTOSS_CHECK(n >= 16 && n <= 256 && n % 16 == 0, "mma_peak: n must be a multiple of 16 in [16, 256]");
+  GPTOSS_CHECK(iters >= 1, "mma_peak: iters must be >= 1");
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  DeviceInfo di;
+  {
+    // bind_device needs a device pointer; the status sink of the current device is one
+    void* sink = nullptr;
+    GPTOSS_CUDA(cudaGetSymbolAddress(&sink, g_status_sink));
+    GPTOSS_TRY(bind_device(sink, "status sink", &di));
+  }
+  // more than half of the shared memory per CTA: one CTA (and one 512-column TMEM
+  // allocation) per SM
+  const size_t smem = 120u * 1024u;
+  static uint64_t attr_done[2] = {0, 0};
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_done[pair ? 1 : 0] & (1ull << dev))) {
+      if (pair) GPTOSS_CUDA(cudaFuncSetAttribute(mma_peak_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      else GPTOSS_CUDA(cudaFuncSetAttribute(mma_peak_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      attr_done[pair ? 1 : 0] |= (1ull << dev);
+    }
+  }
+  int* err = status_dev ? status_dev : di.status_sink;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pair)
+    return launch_pdl_cluster(mma_peak_kernel<true>, dim3(2 * (di.sms / 2)), dim3(128), smem, st, dim3(2, 1, 1), n,
+                              iters, err);
+  return launch_pdl(mma_peak_kernel<false>, dim3(di.sms), dim3(128), smem, st, n, iters, err);
+}
+
+int gptoss_router_topk_from_logits(const void* logits, int64_t num_tokens, int num_experts, int top_k,
+                                   int64_t* router_indices, void* router_scores, float* routing_weights_f32,
+                                   void* stream) {
+  NvtxRange nvtx_range("gptoss_router_topk_from_logits");
+  GPTOSS_CHECK(num_tokens >= 0 && num_tokens < (1LL << 31), "router_topk_from_logits: bad num_tokens");
+  GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExperts, "router_topk_from_logits: num_experts must be in [1, %d]",
+               kMaxExperts);
+  GPTOSS_CHECK(top_k >= 1 && top_k <= kMaxTopK && top_k <= num_experts, "router_topk_from_logits: bad top_k %d", top_k);
+  if (num_tokens == 0) return GPTOSS_OK;
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(logits, "logits", &di));
+  GPTOSS_CHECK(router_indices != nullptr, "router_topk_from_logits: null router_indices");
+  const size_t smem = 32u * static_cast<size_t>(num_experts + 1) * sizeof(float);
+  return launch_pdl(router_topk_logits_kernel, dim3(static_cast<unsigned>((num_tokens + 31) / 32)), dim3(32), smem,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(logits),
+                    static_cast<int>(num_tokens), num_experts, top_k, router_indices,
+                    static_cast<__nv_bfloat16*>(router_scores), routing_weights_f32);
 }
 
 int gptoss_quantize_fp8(const void* x, int dtype, int64_t rows, int64_t cols, uint8_t* codes, uint8_t* scales,

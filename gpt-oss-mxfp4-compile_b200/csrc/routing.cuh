@@ -96,6 +96,27 @@ __device__ __forceinline__ void router_topk_token(const float* lg, int E, int K,
   }
 }
 
+// Top-k + softmax of given bf16 logits [T, E] (router_topk_token, the second half of the
+// router): 32 tokens per CTA, their rows staged in shared memory (padded to E + 1 floats).
+// dynamic smem = 32 * (E + 1) * 4 bytes.
+__global__ void __launch_bounds__(32) router_topk_logits_kernel(const __nv_bfloat16* __restrict__ logits, int T, int E,
+                                                                int K, int64_t* __restrict__ out_idx,
+                                                                __nv_bfloat16* __restrict__ out_scores,
+                                                                float* __restrict__ out_weights_f32) {
+  extern __shared__ float s_rows[];
+  pdl_trigger();
+  pdl_wait();
+  const int t0 = blockIdx.x * 32;
+  const int nt = min(32, T - t0);
+  for (int i = threadIdx.x; i < nt * E; i += 32) {
+    const int r = i / E, e = i - r * E;
+    s_rows[r * (E + 1) + e] = __bfloat162float(logits[static_cast<int64_t>(t0 + r) * E + e]);
+  }
+  __syncwarp();
+  if (static_cast<int>(threadIdx.x) < nt)
+    router_topk_token(s_rows + threadIdx.x * (E + 1), E, K, t0 + threadIdx.x, out_idx, out_scores, out_weights_f32);
+}
+
 // grid = (ceil(T / 16), S); cluster = (1, S, 1) when S > 1; blockDim = 128.
 template <int NT>
 __global__ void __launch_bounds__(128) router_mma_kernel(

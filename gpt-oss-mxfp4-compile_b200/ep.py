@@ -238,16 +238,23 @@ class ExpertParallelMoELayer(nn.Module):
     replicated on every rank."""
 
     def __init__(self, router_weight: torch.Tensor, router_bias: torch.Tensor, top_k: int,
-                 experts: ExpertParallelExperts):
+                 experts: ExpertParallelExperts, router=None):
+        """`router(hidden, weight, bias, top_k) -> (logits, scores, indices)` replaces the
+        fused router op when given (the host-side tests pass the CPU router)."""
         super().__init__()
         self.router_weight = nn.Parameter(router_weight, requires_grad=False)
         self.router_bias = nn.Parameter(router_bias, requires_grad=False)
         self.top_k = top_k
         self.experts = experts
+        self._router = router
 
     def forward(self, hidden_states: torch.Tensor):
-        _ops.register_ops()
         h = hidden_states.reshape(-1, self.experts.hidden_size).contiguous()
+        if self._router is not None:
+            _, scores, idx = self._router(h, self.router_weight.data, self.router_bias.data, int(self.top_k))
+            out = self.experts(h, idx, scores.float())
+            return out.view(hidden_states.shape), scores, idx
+        _ops.register_ops()
         if self.experts.transport == "p2p" and self.top_k == self.experts.top_k:
             out, scores, idx = self.experts.forward_with_router(h, self.router_weight, self.router_bias)
             return out.view(hidden_states.shape), scores, idx

@@ -248,6 +248,42 @@ def fp4_group_mm_impl(output, a, b, a_blockscale, b_blockscales, alphas, problem
               _stream(a.device))
 
 
+def mma_peak(device, pair: bool = True, n: int = 256, iters: int = 4000, repeats: int = 5) -> dict:
+    """Measured dense throughput (TFLOP/s, best of `repeats`) of the block-scaled FP8 x FP4
+    MMA (gptoss_mma_peak): CTA pairs (M = 256) or single CTAs (M = 128), N = n."""
+    dev = torch.device(device)
+    st = _stream(dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    units, M = (sms // 2, 256) if pair else (sms, 128)
+    flops = float(units) * iters * 2 * M * n * 128
+    best = 0.0
+    _lib.call("gptoss_mma_peak", int(pair), int(n), 16, status_tensor(dev).data_ptr(), st)   # warm-up
+    for _ in range(repeats):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        _lib.call("gptoss_mma_peak", int(pair), int(n), int(iters), status_tensor(dev).data_ptr(), st)
+        b.record()
+        b.synchronize()
+        best = max(best, flops / (a.elapsed_time(b) / 1e3) / 1e12)
+    if read_status(dev) != 0:
+        raise RuntimeError("mma_peak: a bounded wait gave up")
+    return {"tflops": best, "pair": bool(pair), "M": M, "N": n, "k_blocks": iters, "units": units}
+
+
+def router_topk_from_logits(logits: torch.Tensor, top_k: int):
+    """Top-k + softmax on given bf16 logits [T, E] (the router's second half) ->
+    (scores bf16 [T, k], indices int64 [T, k])."""
+    _cuda(logits, "logits")
+    _dtype(logits, (torch.bfloat16,), "logits")
+    logits = logits.contiguous()
+    T, E = logits.shape
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=logits.device)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=logits.device)
+    _lib.call("gptoss_router_topk_from_logits", logits.data_ptr(), T, E, int(top_k), idx.data_ptr(),
+              scores.data_ptr(), None, _stream(logits.device))
+    return scores, idx
+
+
 def router_topk_impl(hidden, weight, bias, top_k: int):
     _cuda(hidden, "hidden_states")
     _cuda(weight, "router weight")

@@ -105,6 +105,25 @@ int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
                        int64_t* router_indices, void* router_scores,
                        float* routing_weights_f32, void* logits, void* stream);
 
+/* Throughput probe of the block-scaled FP8 x FP4 tensor-core MMA the GEMMs issue
+ * (tcgen05.mma kind::mxf8f6f4.block_scale, E4M3 x E2M1, UE8M0 scales): one CTA per SM
+ * (pair = 0: M = 128) or one CTA pair per two SMs (pair = 1: M = 256, cta_group::2), each
+ * issuing `iters` 128-deep k blocks of M x n x 128 into one accumulator from operands
+ * resident in shared memory (no memory traffic). n: multiple of 16 in [16, 256]. FLOPs of
+ * one launch = (SMs, or SMs / 2 pairs) x iters x 2 x M x n x 128. The caller times it (CUDA
+ * events on `stream`). No counterpart in the reference; it is the measured denominator of
+ * the tensor-bound GEMM rooflines. */
+int gptoss_mma_peak(int pair, int n, int iters, int32_t* status_dev, void* stream);
+
+/* The second half of the router alone: top-k (ties -> lower expert index, NaN above every
+ * number) and the softmax over the k values rounded to bf16, on given bf16 logits [T, E]
+ * (E <= 256, k <= 8). Same device code as gptoss_router_topk. No counterpart in the
+ * reference (its experts module receives the routing); for callers that run their own
+ * router projection, and for checking the top-k bit for bit against given logits. */
+int gptoss_router_topk_from_logits(const void* logits, int64_t num_tokens, int num_experts, int top_k,
+                                   int64_t* router_indices, void* router_scores, float* routing_weights_f32,
+                                   void* stream);
+
 /* Replaces quantize_activations_to_fp8 (kernels/cutlass_experts.py:197-251):
  * x [M,K] (bf16 or f32, `dtype`) -> codes [M,K] e4m3 bytes + scales [M,K/32] UE8M0,
  * bit-identical to the reference. K % 32 == 0. */

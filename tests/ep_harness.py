@@ -91,6 +91,37 @@ def cpu_worker(rank: int, world: int, port: int, cases, q):
         dist.destroy_process_group()
 
 
+def cpu_layer_worker(rank: int, world: int, port: int, q):
+    """One gloo rank: router + expert-parallel experts (ExpertParallelMoELayer with the CPU
+    router and OracleKernels) on this rank's own tokens vs the single-process oracle."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        import __graft_entry__ as ge
+
+        pkg = ge.load_package()
+        from gpt_oss_mxfp4_compile_b200 import ep as EP
+
+        d = O.synth_layer(SEED, E=E, H=H, I=I, T=1)
+        wn = O.numpy_weights(d)
+        e_loc = E // world
+        local = pkg.CutlassGptOssExperts(Cfg(e_loc, H, I))
+        kern = OracleKernels(O.slice_experts(wn, rank * e_loc, (rank + 1) * e_loc), H)
+        experts = EP.ExpertParallelExperts(local, E, kernels=kern)
+        layer = EP.ExpertParallelMoELayer(d["router_w"], d["router_b"], K, experts, router=O.router_topk_hf)
+        g = torch.Generator().manual_seed(500 + rank)
+        h = torch.randn(24 + 8 * rank, H, generator=g).to(torch.bfloat16)
+        out, scores, idx = layer(h)
+        _, rsc, rix = O.router_topk_hf(h, d["router_w"], d["router_b"], K)
+        ref = O.w4a8_experts_forward(h, rix.numpy(), rsc.float().numpy(), wn)
+        q.put((rank, (bool(torch.equal(idx, rix) and torch.equal(scores, rsc)), bool(torch.equal(out, ref))), None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
 def run_ranks(target, world: int, *args, timeout: float = 240.0):
     """Runs `target(rank, world, port, *args, q)` in `world` spawned processes; returns
     the per-rank results in rank order."""

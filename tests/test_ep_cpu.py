@@ -5,7 +5,7 @@ import numpy as np
 import torch
 
 import oracle as O
-from ep_harness import E, H, I, K, SEED, cpu_worker, dead_peer_worker, routing_case, run_ranks
+from ep_harness import E, H, I, K, SEED, cpu_layer_worker, cpu_worker, dead_peer_worker, routing_case, run_ranks
 
 
 def test_oracle_ep_chain_equals_single_device_forward():
@@ -97,3 +97,15 @@ def test_dead_peer_ends_with_an_error_not_a_hang():
     status, kind, elapsed = r0
     assert status == "error", r0
     assert elapsed < 60, r0
+
+
+def test_gloo_two_ranks_router_and_experts_match_single_device():
+    # ExpertParallelMoELayer end to end on two gloo ranks: each rank routes its own tokens
+    # (the CPU router stands in for the fused router op) and gets the single-device routing
+    # and the single-device oracle output
+    res = run_ranks(cpu_layer_worker, 2)
+    for rank, (out, err) in enumerate(res):
+        assert err is None, f"rank {rank}: {err}"
+        same_routing, same_out = out
+        assert same_routing, f"rank {rank}: routing differs from the single-device router"
+        assert same_out, f"rank {rank}: output differs from the single-device oracle"

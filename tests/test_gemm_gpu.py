@@ -117,3 +117,28 @@ def test_w4a4_mode_not_implemented(pkg, dev):
                                   torch.tensor([[4, 128, 512]], dtype=torch.int32, device=dev),
                                   torch.zeros(1, dtype=torch.int32, device=dev),
                                   torch.zeros(1, dtype=torch.int32, device=dev))
+
+
+@pytest.mark.parametrize("m_list,H,I", [([5, 0, 17, 40], 512, 256), ([3, 9], 288, 288)])
+def test_run_cutlass_gemm_reference_signature(pkg, dev, m_list, H, I):
+    # CutlassGptOssExperts._run_cutlass_gemm keeps the reference's signature
+    # (kernels/cutlass_experts.py:329-374) for subclasses such as the reference's benchmark
+    # variants: unpadded FP8 activations with row-major scales in, K padded inside,
+    # blocked scales built on the GPU, fp4_group_mm on the module's gate_up weights
+    from helpers import build_experts
+    E = len(m_list)
+    d = O.synth_layer(41, E=E, H=H, I=I, T=1)
+    m = build_experts(pkg, d, dev, E, H, I)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(sum(m_list), H, generator=g).to(torch.bfloat16)
+    a_codes, a_sf = O.quantize_fp8_ue8m0(x)
+    counts = torch.tensor(m_list, dtype=torch.int32)
+    offsets = torch.cat([torch.zeros(1, dtype=torch.int32), torch.cumsum(counts, 0)[:-1].to(torch.int32)])
+    out = m._run_cutlass_gemm(torch.from_numpy(a_codes).view(torch.float8_e4m3fn).to(dev),
+                              torch.from_numpy(a_sf).to(dev), m.gate_up_proj_data, m.gate_up_proj_scales,
+                              counts.to(dev), offsets.to(dev), 2 * I, H, m.K_hidden_padded)
+    torch.cuda.synchronize()
+    assert pkg.ops.read_status(dev) == 0
+    ref = O.group_mm_bf16(a_codes, a_sf, d["gu_blocks"].numpy(), d["gu_scales"].numpy(), counts.numpy(),
+                          offsets.numpy())
+    _check(out.cpu(), ref, f"_run_cutlass_gemm m={m_list} H={H}")
