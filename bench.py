@@ -67,6 +67,9 @@ def parse_args():
                          "times a token sample of the workload sized to fit")
     ap.add_argument("--mma-peak", action="store_true",
                     help="only measure the block-scaled FP8 x FP4 MMA peak (gptoss_mma_peak) and print it")
+    ap.add_argument("--w4a4", action="store_true",
+                    help="only measure the W4A4 (NVFP4) mode of fp4_group_mm: the reference's micro-bench "
+                         "shape and a prefill-sized grouped shape, against the measured kind::mxf4nvf4 peak")
     ap.add_argument("--l2", choices=["none", "write"], default="none",
                     help="between timed steps: nothing (inputs larger than L2) or write a 256 MiB buffer")
     ap.add_argument("--ep-transport", choices=["auto", "p2p", "nccl"], default="auto",
@@ -587,10 +590,81 @@ def run_mma_peak(args):
     dev = torch.device("cuda", 0)
     sampler = clock_sampler_start(0)
     time.sleep(0.3)
-    res = [pkg.ops.mma_peak(dev, pair=pair, n=n, iters=4000) for pair in (True, False) for n in (256, 192, 128)]
+    res = [pkg.ops.mma_peak(dev, pair=pair, n=n, iters=4000, kind=kind) for kind in ("mxf8f6f4", "mxf4nvf4")
+           for pair in (True, False) for n in (256, 192, 128)]
     clocks = clock_sampler_stop(sampler)
-    print(json.dumps({"metric": "block-scaled FP8 x FP4 MMA peak (tcgen05.mma kind::mxf8f6f4)", "unit": "TFLOP/s",
-                      "value": max(r["tflops"] for r in res), "results": res, "clocks": clocks}), flush=True)
+    print(json.dumps({"metric": "block-scaled MMA peak (tcgen05.mma kind::mxf8f6f4 / kind::mxf4nvf4)",
+                      "unit": "TFLOP/s",
+                      "value": max(r["tflops"] for r in res if r["kind"] == "mxf8f6f4"),
+                      "value_mxf4nvf4": max(r["tflops"] for r in res if r["kind"] == "mxf4nvf4"),
+                      "results": res, "clocks": clocks}), flush=True)
+    return 0
+
+
+W4A4_SHAPES = {
+    # kernels/benchmark_matmul_mxfp4_cutlass.py:51 (one expert)
+    "reference_microbench": ([256], 4096, 4096),
+    # a prefill-sized gate_up projection: 32 experts x 1024 rows, N = 2 x 2880, K = 2880
+    "grouped_prefill": ([1024] * 32, 5760, 2880),
+}
+
+
+def run_w4a4(args):
+    """One JSON line: W4A4 (NVFP4 x NVFP4) grouped GEMM throughput per shape and tile
+    orientation (CUDA events around `--steps` back-to-back launches after `--warmup`),
+    against the measured kind::mxf4nvf4 peak of single CTAs at N = 192 (the tile the
+    tokens-on-M kernel issues). Random packed codes and sign-clear UE4M3 scale bytes; the
+    scale buffers are filled directly in their blocked layout."""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    pkg.ensure_custom_op_registered()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    peak = pkg.ops.mma_peak(dev, pair=False, n=192, iters=4000, kind="mxf4nvf4")["tflops"]
+    out_lines = {}
+    sampler = clock_sampler_start(0)
+    time.sleep(0.3)
+    for name, (m_list, N, K) in W4A4_SHAPES.items():
+        E, M, G = len(m_list), sum(m_list), K // 16
+        a = torch.randint(0, 256, (M, K // 2), device=dev, dtype=torch.uint8, generator=g)
+        b = torch.randint(0, 256, (E, N, K // 2), device=dev, dtype=torch.uint8, generator=g)
+        blk = lambda rows: ((rows + 127) // 128) * ((G + 3) // 4) * 512   # noqa: E731
+        sf_rows = [0]
+        for m in m_list[:-1]:
+            sf_rows.append(sf_rows[-1] + (m + 127) // 128 * 128)
+        sfa = torch.randint(0x30, 0x41, (sum(blk(m) for m in m_list),), device=dev, dtype=torch.uint8, generator=g)
+        sfb = torch.randint(0x30, 0x41, (E, blk(N)), device=dev, dtype=torch.uint8, generator=g)
+        counts = torch.tensor(m_list, dtype=torch.int32)
+        ps = torch.stack([counts, torch.full((E,), N, dtype=torch.int32), torch.full((E,), K, dtype=torch.int32)],
+                         1).to(dev)
+        offs = torch.cat([torch.zeros(1, dtype=torch.int32), torch.cumsum(counts, 0)[:-1].to(torch.int32)]).to(dev)
+        sfo = torch.tensor(sf_rows, dtype=torch.int32, device=dev)
+        alphas = torch.ones(E, device=dev)
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        flops = 2.0 * M * N * K
+        res = {}
+        for mode_name, mode in (("tokens_m", 1), ("swap", 2)):
+            def call():
+                pkg.ops.fp4_group_mm_impl(out, a, b, sfa, sfb, alphas, ps, offs, sfo, gemm_mode=mode)
+            for _ in range(max(args.warmup, 3)):
+                call()
+            torch.cuda.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            for _ in range(args.steps):
+                call()
+            ev1.record()
+            ev1.synchronize()
+            ms = ev0.elapsed_time(ev1) / args.steps
+            tf = flops / (ms / 1e3) / 1e12
+            res[mode_name] = {"ms_per_call": ms, "tflops": tf, "frac_of_mxf4nvf4_peak": tf / peak}
+        assert pkg.ops.read_status(dev) == 0
+        out_lines[name] = {"experts": E, "M": M, "N": N, "K": K, "flops": flops, **res}
+    clocks = clock_sampler_stop(sampler)
+    print(json.dumps({"metric": "W4A4 (NVFP4) grouped GEMM throughput", "unit": "TFLOP/s",
+                      "peak_mxf4nvf4_tflops": peak, "steps": args.steps, "warmup": args.warmup,
+                      "shapes": out_lines, "clocks": clocks}), flush=True)
     return 0
 
 
@@ -598,6 +672,8 @@ def main():
     args = parse_args()
     if args.mma_peak:
         return run_mma_peak(args)
+    if args.w4a4:
+        return run_w4a4(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

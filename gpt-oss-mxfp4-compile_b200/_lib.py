@@ -30,7 +30,7 @@ _SIGNATURES = {
     "gptoss_fused_moe_routing": (_i, [_vp, _vp, _c_int64, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gptoss_router_topk": (_i, [_vp, _vp, _vp, _c_int64, _c_int64, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "gptoss_router_topk_from_logits": (_i, [_vp, _c_int64, _i, _i, _vp, _vp, _vp, _vp]),
-    "gptoss_mma_peak": (_i, [_i, _i, _i, _vp, _vp]),
+    "gptoss_mma_peak": (_i, [_i, _i, _i, _i, _vp, _vp]),
     "gptoss_quantize_fp8": (_i, [_vp, _i, _c_int64, _c_int64, _vp, _vp, _vp]),
     "gptoss_swiglu": (_i, [_vp, _i, _c_int64, _c_int64, _vp, _f, _f, _vp]),
     "gptoss_convert_scales_blocked": (_i, [_vp, _c_int64, _c_int64, _vp, _c_int64, _vp]),
@@ -39,6 +39,8 @@ _SIGNATURES = {
     "gptoss_batch_blocked_scales_capacity": (_c_int64, [_c_int64, _i, _c_int64]),
     "gptoss_fp4_group_mm": (_i, [_vp, _vp, _c_int64, _c_int64, _vp, _i, _c_int64, _c_int64, _vp, _vp,
                                  _c_int64, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
+    "gptoss_fp4_group_mm_w4a4": (_i, [_vp, _vp, _c_int64, _c_int64, _vp, _i, _c_int64, _c_int64, _vp, _vp,
+                                      _c_int64, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "gptoss_moe_workspace_bytes": (_sz, [_c_int64, _i, _i, _c_int64, _c_int64]),
     "gptoss_moe_experts_forward": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64,
                                         _vp, _vp, _c_int64, _vp, _vp, _vp, _c_int64, _vp,

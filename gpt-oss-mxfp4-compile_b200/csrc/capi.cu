@@ -198,14 +198,18 @@ int make_act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t lda, in
 
 // Weights: 3-D [E, N, K] packed E2M1 (K/2 bytes per row); the TMA unit expands each
 // 8-byte group of 16 codes into a 16-byte slot (the 8-bit container kind::mxf8f6f4 reads).
-int make_wgt_map(CUtensorMap* m, const void* base, int E, int64_t N, int64_t K, int box_rows) {
+// packed: the W4A4 mode, whose MMA reads the packed bytes themselves (a 128-byte box of
+// K/2-byte rows).
+int make_wgt_map(CUtensorMap* m, const void* base, int E, int64_t N, int64_t K, int box_rows, bool packed = false) {
   EncodeTiledFn enc;
   GPTOSS_TRY(get_encode_fn(&enc));
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(E)};
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(packed ? K / 2 : K), static_cast<cuuint64_t>(N),
+                        static_cast<cuuint64_t>(E)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(N * (K / 2))};
   cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = enc(m, packed ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3,
+                   const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GPTOSS_ERR_CUDA, "cuTensorMapEncodeTiled(weights) failed: %d", (int)r);
@@ -240,9 +244,9 @@ struct GemmJob {
   int64_t sfb_bytes;
 };
 
-template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false>
+template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false, bool NVF4 = false>
 int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t st) {
-  using C = GemmConfig<SWAP, SPREAD, PAIR>;
+  using C = GemmConfig<SWAP, SPREAD, PAIR, NVF4>;
   if (job.act_rows <= 0) return GPTOSS_OK;
   CUtensorMap ta, ta32, ta16, tw;
   GPTOSS_TRY(make_act_map(&ta, job.act, job.act_rows, job.lda, C::kActRows));
@@ -256,13 +260,13 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
     ta32 = ta;
     ta16 = ta;
   }
-  GPTOSS_TRY(make_wgt_map(&tw, job.wgt, job.p.num_experts, job.p.N, job.p.K, C::kWgtRowsCta));
+  GPTOSS_TRY(make_wgt_map(&tw, job.wgt, job.p.num_experts, job.p.N, job.p.K, C::kWgtRowsCta, NVF4));
   static uint64_t attr_done = 0;   // one bit per device
   static std::mutex mu;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(attr_done & (1ull << dev))) {
-      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, SPREAD, EPI, PAIR>,
+      GPTOSS_CUDA(cudaFuncSetAttribute(moe_gemm_kernel<SWAP, SPREAD, EPI, PAIR, NVF4>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes)));
       attr_done |= (1ull << dev);
     }
@@ -273,7 +277,7 @@ int launch_gemm(const GemmJob& job, const DeviceInfo& di, int dev, cudaStream_t 
   const int grid = PAIR ? 2 * static_cast<int>(std::min<int64_t>(di.sms / 2, tiles_ub))
                         : static_cast<int>(std::min<int64_t>(di.sms, tiles_ub));
   if (grid <= 0) return GPTOSS_OK;
-  return launch_pdl_cluster(moe_gemm_kernel<SWAP, SPREAD, EPI, PAIR>, dim3(grid), dim3(C::kThreads), C::kSmemBytes,
+  return launch_pdl_cluster(moe_gemm_kernel<SWAP, SPREAD, EPI, PAIR, NVF4>, dim3(grid), dim3(C::kThreads), C::kSmemBytes,
                             st, PAIR ? dim3(2, 1, 1) : dim3(1, 1, 1), ta, ta32, ta16, tw, p);
 }
 
@@ -791,8 +795,37 @@ int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
                        static_cast<cudaStream_t>(stream));
 }
 
-int gptoss_mma_peak(int pair, int n, int iters, int32_t* status_dev, void* stream) {
+}  // extern "C"
+
+namespace {
+template <bool PAIR, bool NVF4>
+int launch_mma_peak(int n, int iters, int* err, const DeviceInfo& di, int dev, cudaStream_t st) {
+  // more than half of the shared memory per CTA: one CTA (and one 512-column TMEM
+  // allocation) per SM
+  const size_t smem = 120u * 1024u;
+  static_assert(kMpSmemBytes <= 120u * 1024u, "peak kernel operands");
+  static uint64_t attr_done = 0;   // one bit per device
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_done & (1ull << dev))) {
+      GPTOSS_CUDA(cudaFuncSetAttribute(mma_peak_kernel<PAIR, NVF4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+      attr_done |= (1ull << dev);
+    }
+  }
+  if (PAIR)
+    return launch_pdl_cluster(mma_peak_kernel<PAIR, NVF4>, dim3(2 * (di.sms / 2)), dim3(128), smem, st,
+                              dim3(2, 1, 1), n, iters, err);
+  return launch_pdl(mma_peak_kernel<PAIR, NVF4>, dim3(di.sms), dim3(128), smem, st, n, iters, err);
+}
+}  // namespace
+
+extern "C" {
+
+int gptoss_mma_peak(int kind, int pair, int n, int iters, int32_t* status_dev, void* stream) {
   NvtxRange nvtx_range("gptoss_mma_peak");
+  GPTOSS_CHECK(kind == 0 || kind == 1, "mma_peak: kind must be 0 (mxf8f6f4) or 1 (mxf4nvf4)");
   GPTOSS_CHECK(n >= 16 && n <= 256 && n % 16 == 0, "mma_peak: n must be a multiple of 16 in [16, 256]");
   GPTOSS_CHECK(iters >= 1, "mma_peak: iters must be >= 1");
   int dev = 0;
@@ -804,25 +837,13 @@ int gptoss_mma_peak(int pair, int n, int iters, int32_t* status_dev, void* strea
     GPTOSS_CUDA(cudaGetSymbolAddress(&sink, g_status_sink));
     GPTOSS_TRY(bind_device(sink, "status sink", &di));
   }
-  // more than half of the shared memory per CTA: one CTA (and one 512-column TMEM
-  // allocation) per SM
-  const size_t smem = 120u * 1024u;
-  static uint64_t attr_done[2] = {0, 0};
-  static std::mutex mu;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!(attr_done[pair ? 1 : 0] & (1ull << dev))) {
-      if (pair) GPTOSS_CUDA(cudaFuncSetAttribute(mma_peak_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      else GPTOSS_CUDA(cudaFuncSetAttribute(mma_peak_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      attr_done[pair ? 1 : 0] |= (1ull << dev);
-    }
-  }
   int* err = status_dev ? status_dev : di.status_sink;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pair)
-    return launch_pdl_cluster(mma_peak_kernel<true>, dim3(2 * (di.sms / 2)), dim3(128), smem, st, dim3(2, 1, 1), n,
-                              iters, err);
-  return launch_pdl(mma_peak_kernel<false>, dim3(di.sms), dim3(128), smem, st, n, iters, err);
+  if (kind == 1)
+    return pair ? launch_mma_peak<true, true>(n, iters, err, di, dev, st)
+                : launch_mma_peak<false, true>(n, iters, err, di, dev, st);
+  return pair ? launch_mma_peak<true, false>(n, iters, err, di, dev, st)
+              : launch_mma_peak<false, false>(n, iters, err, di, dev, st);
 }
 
 int gptoss_router_topk_from_logits(const void* logits, int64_t num_tokens, int num_experts, int top_k,
@@ -977,6 +998,47 @@ int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t ld
   job.p.out = out; job.p.ld_out = n; job.p.alphas = alphas;
   return run_gemm<kEpiPlain>(job, pick_swap(gemm_mode, m_total, num_experts, 48), false, di, dev,
                              static_cast<cudaStream_t>(stream));
+}
+
+int gptoss_fp4_group_mm_w4a4(void* out, const uint8_t* a, int64_t m_total, int64_t lda, const uint8_t* b,
+                             int num_experts, int64_t n, int64_t k, const uint8_t* a_blockscale,
+                             const uint8_t* b_blockscales, int64_t ldb_blockscale, const float* alphas,
+                             const int32_t* problem_sizes, const int32_t* expert_offsets, const int32_t* sf_offsets,
+                             int gemm_mode, int32_t* status_dev, void* stream) {
+  NvtxRange nvtx_range("gptoss_fp4_group_mm_w4a4");
+  GPTOSS_CHECK(num_experts >= 1 && num_experts <= kMaxExpertsGemm,
+               "fp4_group_mm_w4a4: num_experts must be in [1, %d]", kMaxExpertsGemm);
+  GPTOSS_CHECK(k > 0 && k % 64 == 0 && k < (1LL << 30),
+               "fp4_group_mm_w4a4: K=%lld must be a positive multiple of 64 (one 16-code scale atom)", (long long)k);
+  GPTOSS_CHECK(n > 0 && n % 8 == 0 && n < (1LL << 31), "fp4_group_mm_w4a4: N=%lld must be a positive multiple of 8",
+               (long long)n);
+  GPTOSS_CHECK(m_total >= 0 && lda == k / 2, "fp4_group_mm_w4a4: a must be [M, K/2] packed E2M1");
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "fp4_group_mm_w4a4: bad gemm_mode");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(b, "b", &di));
+  GPTOSS_CHECK(aligned(b, 16), "fp4_group_mm_w4a4: b must be 16-byte aligned");
+  GPTOSS_CHECK(ldb_blockscale >= blocked_sf_cosize(n, static_cast<int>(k / 16)) && ldb_blockscale % 16 == 0,
+               "fp4_group_mm_w4a4: b_blockscales holds %lld bytes per expert, need %lld (multiple of 16)",
+               (long long)ldb_blockscale, (long long)blocked_sf_cosize(n, static_cast<int>(k / 16)));
+  GPTOSS_CHECK(problem_sizes && expert_offsets && sf_offsets && b_blockscales, "fp4_group_mm_w4a4: null pointer");
+  if (m_total == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(a && out && a_blockscale && aligned(a, 16) && aligned(out, 16) && aligned(a_blockscale, 16) &&
+                   aligned(b_blockscales, 16),
+               "fp4_group_mm_w4a4: null or misaligned pointer");
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  GemmJob job{};
+  job.act = a; job.act_rows = m_total; job.lda = lda; job.wgt = b;
+  job.p.num_experts = num_experts; job.p.N = static_cast<int>(n); job.p.K = static_cast<int>(k);
+  job.p.num_kb = static_cast<int>((k + 255) / 256); job.p.m_sizes = problem_sizes; job.p.m_stride = 3;
+  job.p.row_offsets = expert_offsets; job.p.sfa_offsets = sf_offsets; job.p.sfa = a_blockscale;
+  job.p.sfb = b_blockscales; job.p.sfb_stride = ldb_blockscale;
+  job.p.err = status_dev ? status_dev : di.status_sink;
+  job.p.out = out; job.p.ld_out = n; job.p.alphas = alphas;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pick_swap(gemm_mode, m_total, num_experts, 48))
+    return launch_gemm<true, false, kEpiPlain, false, true>(job, di, dev, st);
+  return launch_gemm<false, false, kEpiPlain, false, true>(job, di, dev, st);
 }
 
 size_t gptoss_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,

@@ -92,10 +92,17 @@ struct GemmParams {
 // the MMA reads both halves), so per SM the weight bytes per MMA halve and the ring holds
 // 7 stages instead of 5. Each CTA still loads its activation-row scales and the full
 // tile's weight scales.
-template <bool SWAP, bool SPREAD = false, bool PAIR = false>
+//
+// NVF4: the W4A4 mode (NVFP4 x NVFP4: packed E2M1 activations and weights, UE4M3 scales
+// per 16 codes; tcgen05.mma kind::mxf4nvf4 scale_vec::4X, K = 64 per MMA). A k block is
+// still 128 bytes of every operand row (256 codes), so tiles, TMA boxes and descriptors
+// are those of the W4A8 mode; a k block's scales are 4 blocked atoms (64 codes each) per
+// 128 rows instead of one, copied into 4 TMEM column groups that the 4 MMAs read in turn.
+template <bool SWAP, bool SPREAD = false, bool PAIR = false, bool NVF4 = false>
 struct GemmConfig {
   static_assert(SWAP || !SPREAD, "spread activation scales are a SWAP-mode layout");
   static_assert(!(SWAP && PAIR), "CTA pairs are a tokens-on-M layout");
+  static_assert(!(NVF4 && (SPREAD || PAIR)), "NVFP4 tiles: reference scale rows, single CTAs");
   static constexpr int kWgtRows = SWAP ? 128 : 192;   // weight rows per tile
   static constexpr int kWgtRowsCta = PAIR ? kWgtRows / 2 : kWgtRows;   // weight rows this CTA loads
   // Activation rows per tile. SWAP with reference-layout scales uses 64-row chunks that
@@ -111,7 +118,11 @@ struct GemmConfig {
   // 8 KB fp4 weight boxes stream at ~4 TB/s one per stage and ~6.7 TB/s two per stage,
   // at any ring depth), so weights-on-M tiles load two k blocks behind each barrier.
   static constexpr int kSubs = SWAP ? 2 : 1;
-  static constexpr int kStages = SWAP ? (SPREAD ? 5 : 4) : (PAIR ? 7 : 5);
+  static constexpr int kStages = SWAP ? (SPREAD ? 5 : (NVF4 ? 3 : 4)) : (PAIR ? 7 : (NVF4 ? 4 : 5));
+  static constexpr int kKbCodes = NVF4 ? 256 : 128;   // K codes per k block
+  static constexpr int kSfAtoms = NVF4 ? 4 : 1;       // 512-byte scale atoms per 128 rows per k block
+  // global bytes of one weight row per k block (W4A8: 64 packed bytes the TMA expands to 128)
+  static constexpr uint32_t kWgtRowGlobalBytes = NVF4 ? 128u : 64u;
   // MMA issuing threads. A small-N block-scaled MMA costs ~75 cycles of issue, so one
   // thread cannot keep up with the weight stream of weights-on-M tiles: two warps issue
   // alternate k blocks of each stage into two partial accumulators that the epilogue adds.
@@ -122,16 +133,18 @@ struct GemmConfig {
   static constexpr int kWgtSfChunks = SWAP ? 1 : 2;   // 128-row scale blocks per tile
   static constexpr uint32_t kWgtTileBytes = kWgtRowsCta * 128;   // 8-bit container in smem
   static constexpr uint32_t kActTileBytes = kActRows * 128;
-  static constexpr uint32_t kSfActBytes = 512;
-  static constexpr uint32_t kSfWgtBytes = 512 * kWgtSfChunks;
+  static constexpr uint32_t kSfActBytes = 512 * kSfAtoms;
+  static constexpr uint32_t kSfWgtBytes = 512 * kSfAtoms * kWgtSfChunks;
   static constexpr uint32_t kSubBytes =   // one k block: weights | activations | scales
       ((kWgtTileBytes + kActTileBytes + kSfActBytes + kSfWgtBytes + 1023) / 1024) * 1024;
   static constexpr uint32_t kStageBytes = kSubs * kSubBytes;
   static constexpr uint32_t kTmemAccCols = kAccBufs * kAccStride;
-  // scale columns of each issuer: activation 4, then weights 4 per chunk
-  static constexpr uint32_t kSfCols = 4 + 4 * kWgtSfChunks;
+  // scale columns of each issuer: activation 4 per atom, then weights 4 per atom and chunk
+  // (atom-major: the chunks of one atom are adjacent, so a tile that starts 64 rows into a
+  // 128-row block reads across them)
+  static constexpr uint32_t kSfCols = 4 * kSfAtoms * (1 + kWgtSfChunks);
   static constexpr uint32_t kSfActCol = kTmemAccCols;
-  static constexpr uint32_t kSfWgtCol = kTmemAccCols + 4;
+  static constexpr uint32_t kSfWgtCol = kTmemAccCols + 4 * kSfAtoms;
   static constexpr uint32_t kTmemUsed = kTmemAccCols + kIssuers * kSfCols;
   static constexpr uint32_t kTmemCols = kTmemUsed <= 128 ? 128 : kTmemUsed <= 256 ? 256 : 512;
   static_assert(kTmemUsed <= 512, "TMEM budget");
@@ -336,13 +349,20 @@ __device__ __forceinline__ void swap_epilogue_tile(const GemmParams& p, uint32_t
 
 // tm_aux0 / tm_aux1: SWAP: the 32- and 16-row activation maps; PAIR: the activation and
 // weight scale buffers viewed as rows of 256 bytes (512-byte chunks = 2 rows).
-template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false>
-__global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
+// NVF4: the W4A4 mode (plain epilogue only): p.num_kb counts 256-code k blocks, the
+// activation scales of expert e start p.sfa_offsets[e] ROWS into p.sfa (K / 16 bytes a row,
+// matmul_mxfp4_cutlass.cu:95), and a partial last k block issues only its K / 64 MMAs.
+template <bool SWAP, bool SPREAD, int EPI, bool PAIR = false, bool NVF4 = false>
+__global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_act,
                     const __grid_constant__ CUtensorMap tm_aux0,
                     const __grid_constant__ CUtensorMap tm_aux1,
                     const __grid_constant__ CUtensorMap tm_wgt, const GemmParams p) {
-  using C = GemmConfig<SWAP, SPREAD, PAIR>;
+  using C = GemmConfig<SWAP, SPREAD, PAIR, NVF4>;
+  static_assert(!NVF4 || EPI == kEpiPlain, "the W4A4 mode is the plain grouped GEMM");
+  // scale atoms per 128-row block along K, and those of k block kb (fewer in a partial last block)
+  const int g4 = NVF4 ? (p.K >> 6) : p.num_kb;
+  auto atoms_of = [&](int kb) -> int { return NVF4 ? min(C::kSfAtoms, g4 - C::kSfAtoms * kb) : 1; };
   // CTA pair: rank inside the pair, pair index and count (a plain CTA is its own "pair")
   const uint32_t prank = PAIR ? (cluster_ctarank() & 1u) : 0u;
   const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
@@ -402,8 +422,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         if (e >= p.num_experts) break;
         for (int kb = 0; kb < p.num_kb; ++kb) tma_prefetch_3d(&tm_wgt, kb * 128, nt * C::kWgtRows, e);
         bulk_prefetch_l2(p.sfb + static_cast<int64_t>(e) * p.sfb_stride +
-                             static_cast<int64_t>((nt * C::kWgtRows) >> 7) * p.num_kb * 512,
-                         static_cast<uint32_t>(p.num_kb) * 512u);
+                             static_cast<int64_t>((nt * C::kWgtRows) >> 7) * g4 * 512,
+                         static_cast<uint32_t>(g4) * 512u);
       }
     }
   }
@@ -470,18 +490,26 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         const int act_row0 = p.row_offsets[e] + act_in0;
         const int wgt_row0 = nt * C::kWgtRows + static_cast<int>(prank) * C::kWgtRowsCta;
         const int act_blk = static_cast<int>(act_sf_row<SPREAD>(static_cast<int64_t>(act_in0)) >> 7);
-        const int64_t sfa_off = p.sfa_offsets[e] + static_cast<int64_t>(act_blk) * p.num_kb * 512;
+        int64_t sfa_base = NVF4 ? static_cast<int64_t>(p.sfa_offsets[e]) * (p.K >> 4) : p.sfa_offsets[e];
+        if (sfa_base & 15) {   // a bulk copy needs 16-byte alignment: report, then read aligned
+          if (p.err) atomicCAS(p.err, 0, static_cast<int>(kDevMisalignedScales));
+          sfa_base &= ~static_cast<int64_t>(15);
+        }
+        const int64_t sfa_off = sfa_base + static_cast<int64_t>(act_blk) * g4 * 512;
         const int wblk0 = (nt * C::kWgtRows) >> 7;   // scale blocks of the whole tile
         const int nwblk_total = (p.N + 127) >> 7;
         const int nwchunks = min(C::kWgtSfChunks, nwblk_total - wblk0);
-        const int64_t sfb_off = static_cast<int64_t>(e) * p.sfb_stride + static_cast<int64_t>(wblk0) * p.num_kb * 512;
+        const int64_t sfb_off = static_cast<int64_t>(e) * p.sfb_stride + static_cast<int64_t>(wblk0) * g4 * 512;
         const int arows = act_rows_of(e, ch);
         const CUtensorMap* amap = arows == 16 ? &tm_aux1 : (arows == 32 ? &tm_aux0 : &tm_act);
-        const uint32_t tx = (arows * 128u + C::kWgtRowsCta * 64 + C::kSfActBytes + 512u * nwchunks) * (PAIR ? 2u : 1u);
+        const uint32_t tx_fixed = arows * 128u + C::kWgtRowsCta * C::kWgtRowGlobalBytes;
         for (int kb0 = 0; kb0 < p.num_kb; kb0 += C::kSubs) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.err, kDevTimeoutProducer)) { ok = false; break; }
           const int nsub = min(C::kSubs, p.num_kb - kb0);
-          if (leader) mbar_arrive_expect_tx(full_bar(stage), tx * static_cast<uint32_t>(nsub));
+          uint32_t tx = 0;
+          for (int j = 0; j < nsub; ++j)
+            tx += (tx_fixed + 512u * static_cast<uint32_t>(atoms_of(kb0 + j) * (1 + nwchunks))) * (PAIR ? 2u : 1u);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
           for (int j = 0; j < nsub; ++j) {
             const int kb = kb0 + j;
             const uint32_t sb = smem_base + stage * C::kStageBytes + j * C::kSubBytes;
@@ -498,12 +526,17 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
                                  static_cast<int32_t>((sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512) >> 8),
                                  pol_w);
             } else {
+              // x = 128 smem bytes per k block either way: 128 fp8 codes / 128 E2M1 codes
+              // expanded by the TMA (W4A8), or 128 packed bytes (W4A4)
+              // this k block's atoms: kSfAtoms * 512 bytes into each 128-row block's scales
+              const uint32_t sf_bytes = 512u * static_cast<uint32_t>(atoms_of(kb));
+              const int64_t kb_sf = static_cast<int64_t>(kb) * C::kSfAtoms * 512;
               tma_load_2d(s_a, amap, full_bar(stage), kb * 128, act_row0, pol_a);
               tma_load_3d(s_w, &tm_wgt, full_bar(stage), kb * 128, wgt_row0, e, pol_w);
-              bulk_load(s_sfa, p.sfa + sfa_off + kb * 512, 512, full_bar(stage), pol_a);
+              bulk_load(s_sfa, p.sfa + sfa_off + kb_sf, sf_bytes, full_bar(stage), pol_a);
               for (int c = 0; c < nwchunks; ++c)
-                bulk_load(s_sfw + 512u * c, p.sfb + sfb_off + static_cast<int64_t>(c) * p.num_kb * 512 + kb * 512, 512,
-                          full_bar(stage), pol_w);
+                bulk_load(s_sfw + 512u * C::kSfAtoms * c, p.sfb + sfb_off + static_cast<int64_t>(c) * g4 * 512 + kb_sf,
+                          sf_bytes, full_bar(stage), pol_w);
             }
           }
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
@@ -549,8 +582,9 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
         // issue each): descriptors and the instruction word are formed once per tile /
         // stage and advanced by adds (a 32-byte K step is +2 in the descriptor's 16-byte
         // address field).
-        const uint32_t idesc0 = SWAP ? idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, 0, 0)
-                                     : idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, 0, 0);
+        const uint32_t idesc0 = NVF4 ? idesc_mxf4nvf4(C::kMmaM, mma_n)
+                                : SWAP ? idesc_mxf8f6f4(5, 0, C::kMmaM, mma_n, 0, 0)
+                                       : idesc_mxf8f6f4(0, 5, C::kMmaM, mma_n, 0, 0);
         const uint32_t sf_a_t = SWAP ? t_sfw : t_sfa;                       // scales of MMA operand A
         const uint32_t sf_b_t = SWAP ? t_sfa + ashift : t_sfw + wshift;     // scales of MMA operand B
         for (int kb0 = 0; kb0 < p.num_kb; kb0 += C::kSubs) {
@@ -567,6 +601,26 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR>::kThreads, 1)
             if (j >= nsub) break;
             if (j % C::kIssuers != issuer) continue;
             const uint64_t joff = (static_cast<uint64_t>(j) * C::kSubBytes) >> 4;
+            if constexpr (NVF4) {
+              // atom a of the activation scales -> columns 4a; of weight chunk c -> 4 (chunks a + c)
+              const int na = atoms_of(kb0 + j);
+              for (int a = 0; a < na; ++a) {
+                tc_cp_32x128b_warpx4(t_sfa + 4u * a, dsa0 + joff + 32u * a);
+#pragma unroll
+                for (int c = 0; c < C::kWgtSfChunks; ++c)
+                  tc_cp_32x128b_warpx4(t_sfw + 4u * (C::kWgtSfChunks * a + c), dsw0 + joff + 32u * (C::kSfAtoms * c + a));
+              }
+              const uint64_t dw = dw0 + joff, da = da0 + joff;
+              const uint64_t dA = SWAP ? dw : da, dB = SWAP ? da : dw;
+              for (int k = 0; k < na; ++k) {
+                const uint32_t sfa_k = t_sfa + 4u * k, sfw_k = t_sfw + 4u * C::kWgtSfChunks * k;
+                const uint32_t acc = (kb0 != 0 || j >= C::kIssuers || k != 0) ? 1u : 0u;
+                // a 64-code (32-byte) K step is +2 in the descriptor's 16-byte address field
+                mma_mxf4nvf4(d_tmem, dA + 2u * k, dB + 2u * k, idesc0, SWAP ? sfw_k : sfa_k,
+                             SWAP ? sfa_k + ashift : sfw_k + wshift, acc);
+              }
+              continue;
+            }
             if constexpr (PAIR) {
               // each CTA's scale chunks go from its own shared memory into its own TMEM
               tc_cp_32x128b_warpx4_pair(t_sfa, dsa0 + joff);

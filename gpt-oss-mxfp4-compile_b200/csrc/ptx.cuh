@@ -21,6 +21,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 0x103,
   kDevTimeoutDrain = 0x104,
   kDevBadTile = 0x105,
+  kDevMisalignedScales = 0x109,   // an expert's scale offset is not 16-byte aligned (read rounded down)
 };
 
 // A wait that has not completed after this long (wall time) is treated as a hang: the
@@ -232,6 +233,17 @@ __device__ __forceinline__ void mma_mxf8f6f4_pair(uint32_t d_tmem, uint64_t a_de
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void mma_mxf4nvf4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                  uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "setp.ne.b32 P, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], P;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
@@ -266,6 +278,20 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc, u
       "{\n\t.reg .pred P;\n\t"
       "setp.ne.b32 P, %6, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.scale_vec::1X [%0], %1, %2, %3, [%4], [%5], P;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+
+// NVFP4 x NVFP4: packed E2M1 operands (two codes per byte, K = 64 per MMA), one UE4M3
+// scale per 16 codes -- the 4 scales of a row for this MMA are the 4 bytes of one 32-bit
+// TMEM scale column.
+__device__ __forceinline__ void mma_mxf4nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "setp.ne.b32 P, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%4], [%5], P;\n\t"
       "}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
       : "memory");
@@ -333,6 +359,12 @@ __host__ __device__ constexpr uint32_t idesc_mxf8f6f4(uint32_t a_fmt, uint32_t b
                                                       uint32_t b_sf_id) {
   return (b_sf_id << 4) | (a_fmt << 7) | (b_fmt << 10) | ((N >> 3) << 17) | (1u << 23) |
          ((M >> 4) << 24) | (a_sf_id << 29);
+}
+
+// Instruction descriptor of kind::mxf4nvf4 with UE4M3 scales (bit 23 clear): both
+// operands E2M1 (format 1), K-major, dense K = 64; scale ids 0 (4X reads the whole column).
+__host__ __device__ constexpr uint32_t idesc_mxf4nvf4(uint32_t M, uint32_t N) {
+  return (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch

@@ -210,20 +210,27 @@ def fused_moe_routing_impl(router_indices: torch.Tensor, routing_weights: torch.
     return st, se, sw, counts, offsets
 
 
+_FP4X2 = getattr(torch, "float4_e2m1fn_x2", None)
+_SF_DTYPES = (torch.uint8, torch.float8_e4m3fn)
+
+
 def fp4_group_mm_impl(output, a, b, a_blockscale, b_blockscales, alphas, problem_sizes, expert_offsets,
                       sf_offsets, gemm_mode: int = GEMM_AUTO):
-    """W4A8 grouped GEMM into `output` (cutlass_fp4_group_mm, W4A8 mode)."""
+    """Grouped GEMM into `output` (cutlass_fp4_group_mm, matmul_mxfp4_cutlass.cu:1118-1171).
+    The dtype of `a` picks the mode as in the reference (:1157-1166): float8_e4m3fn [M, K]
+    -> W4A8 (UE8M0 1x32 scales, sf_offsets in bytes); packed E2M1 bytes [M, K/2] (uint8) ->
+    W4A4 / NVFP4 (UE4M3 1x16 scales, sf_offsets in rows). Scale tensors may be uint8 or
+    float8_e4m3fn (their bytes are used either way)."""
     _cuda(a, "a")
-    if a.dtype == torch.uint8:
-        raise NotImplementedError("fp4_group_mm: the W4A4 (NVFP4 x NVFP4) mode is not implemented on sm_100a; "
-                                  "pass float8_e4m3fn activations (W4A8)")
-    _dtype(a, (torch.float8_e4m3fn,), "a")
+    w4a4 = a.dtype == torch.uint8 or (_FP4X2 is not None and a.dtype == _FP4X2)
+    if not w4a4:
+        _dtype(a, (torch.float8_e4m3fn,), "a")
     _cuda(b, "b")
-    _dtype(b, (torch.uint8,), "b")
+    _dtype(b, (torch.uint8,) + ((_FP4X2,) if _FP4X2 is not None else ()), "b")
     _cuda(a_blockscale, "a_blockscale")
-    _dtype(a_blockscale, (torch.uint8,), "a_blockscale")
+    _dtype(a_blockscale, _SF_DTYPES, "a_blockscale")
     _cuda(b_blockscales, "b_blockscales")
-    _dtype(b_blockscales, (torch.uint8,), "b_blockscales")
+    _dtype(b_blockscales, _SF_DTYPES, "b_blockscales")
     _cuda(alphas, "alphas")
     _dtype(alphas, (torch.float32,), "alphas")
     _cuda(output, "output")
@@ -242,32 +249,39 @@ def fp4_group_mm_impl(output, a, b, a_blockscale, b_blockscales, alphas, problem
     if output.shape[0] < M or output.shape[1] != N:
         raise RuntimeError(f"output must be [M={M}, N={N}], got {tuple(output.shape)}")
     ldb = b_blockscales.numel() // E
-    _lib.call("gptoss_fp4_group_mm", output.data_ptr(), a.data_ptr(), M, a.shape[1], b.data_ptr(), E, N, K,
+    fn = "gptoss_fp4_group_mm_w4a4" if w4a4 else "gptoss_fp4_group_mm"
+    _lib.call(fn, output.data_ptr(), a.data_ptr(), M, a.shape[1], b.data_ptr(), E, N, K,
               a_blockscale.data_ptr(), b_blockscales.data_ptr(), ldb, alphas.data_ptr(), problem_sizes.data_ptr(),
               expert_offsets.data_ptr(), sf_offsets.data_ptr(), int(gemm_mode), status_tensor(a.device).data_ptr(),
               _stream(a.device))
 
 
-def mma_peak(device, pair: bool = True, n: int = 256, iters: int = 4000, repeats: int = 5) -> dict:
-    """Measured dense throughput (TFLOP/s, best of `repeats`) of the block-scaled FP8 x FP4
-    MMA (gptoss_mma_peak): CTA pairs (M = 256) or single CTAs (M = 128), N = n."""
+def mma_peak(device, pair: bool = True, n: int = 256, iters: int = 4000, repeats: int = 5,
+             kind: str = "mxf8f6f4") -> dict:
+    """Measured dense throughput (TFLOP/s, best of `repeats`) of a block-scaled MMA
+    (gptoss_mma_peak): kind "mxf8f6f4" (FP8 x FP4, the W4A8 GEMMs) or "mxf4nvf4" (NVFP4 x
+    NVFP4, the W4A4 mode); CTA pairs (M = 256) or single CTAs (M = 128), N = n."""
+    kinds = {"mxf8f6f4": (0, 128), "mxf4nvf4": (1, 256)}
+    if kind not in kinds:
+        raise ValueError(f"kind must be one of {sorted(kinds)}")
+    code, kb = kinds[kind]
     dev = torch.device(device)
     st = _stream(dev)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     units, M = (sms // 2, 256) if pair else (sms, 128)
-    flops = float(units) * iters * 2 * M * n * 128
+    flops = float(units) * iters * 2 * M * n * kb
     best = 0.0
-    _lib.call("gptoss_mma_peak", int(pair), int(n), 16, status_tensor(dev).data_ptr(), st)   # warm-up
+    _lib.call("gptoss_mma_peak", code, int(pair), int(n), 16, status_tensor(dev).data_ptr(), st)   # warm-up
     for _ in range(repeats):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        _lib.call("gptoss_mma_peak", int(pair), int(n), int(iters), status_tensor(dev).data_ptr(), st)
+        _lib.call("gptoss_mma_peak", code, int(pair), int(n), int(iters), status_tensor(dev).data_ptr(), st)
         b.record()
         b.synchronize()
         best = max(best, flops / (a.elapsed_time(b) / 1e3) / 1e12)
     if read_status(dev) != 0:
         raise RuntimeError("mma_peak: a bounded wait gave up")
-    return {"tflops": best, "pair": bool(pair), "M": M, "N": n, "k_blocks": iters, "units": units}
+    return {"tflops": best, "kind": kind, "pair": bool(pair), "M": M, "N": n, "k_blocks": iters, "units": units}
 
 
 def router_topk_from_logits(logits: torch.Tensor, top_k: int):

@@ -105,15 +105,17 @@ int gptoss_router_topk(const void* hidden, const void* weight, const void* bias,
                        int64_t* router_indices, void* router_scores,
                        float* routing_weights_f32, void* logits, void* stream);
 
-/* Throughput probe of the block-scaled FP8 x FP4 tensor-core MMA the GEMMs issue
- * (tcgen05.mma kind::mxf8f6f4.block_scale, E4M3 x E2M1, UE8M0 scales): one CTA per SM
- * (pair = 0: M = 128) or one CTA pair per two SMs (pair = 1: M = 256, cta_group::2), each
- * issuing `iters` 128-deep k blocks of M x n x 128 into one accumulator from operands
- * resident in shared memory (no memory traffic). n: multiple of 16 in [16, 256]. FLOPs of
- * one launch = (SMs, or SMs / 2 pairs) x iters x 2 x M x n x 128. The caller times it (CUDA
- * events on `stream`). No counterpart in the reference; it is the measured denominator of
- * the tensor-bound GEMM rooflines. */
-int gptoss_mma_peak(int pair, int n, int iters, int32_t* status_dev, void* stream);
+/* Throughput probe of the block-scaled tensor-core MMAs the GEMMs issue: kind 0 =
+ * tcgen05.mma kind::mxf8f6f4.block_scale (E4M3 x E2M1, UE8M0 1x32 scales, k block 128
+ * codes, the W4A8 mode), kind 1 = kind::mxf4nvf4.block_scale.scale_vec::4X (E2M1 x E2M1,
+ * UE4M3 1x16 scales, k block 256 codes, the W4A4 mode). One CTA per SM (pair = 0: M = 128)
+ * or one CTA pair per two SMs (pair = 1: M = 256, cta_group::2), each issuing `iters` k
+ * blocks of M x n into one accumulator from operands resident in shared memory (no memory
+ * traffic). n: multiple of 16 in [16, 256]. FLOPs of one launch = (SMs, or SMs / 2 pairs) x
+ * iters x 2 x M x n x (128 or 256 codes). The caller times it (CUDA events on `stream`). No
+ * counterpart in the reference; it is the measured denominator of the tensor-bound GEMM
+ * rooflines. */
+int gptoss_mma_peak(int kind, int pair, int n, int iters, int32_t* status_dev, void* stream);
 
 /* The second half of the router alone: top-k (ties -> lower expert index, NaN above every
  * number) and the softmax over the k values rounded to bf16, on given bf16 logits [T, E]
@@ -172,6 +174,25 @@ int gptoss_fp4_group_mm(void* out, const uint8_t* a, int64_t m_total, int64_t ld
                         const int32_t* problem_sizes, const int32_t* expert_offsets,
                         const int32_t* sf_offsets, int gemm_mode, int32_t* status_dev,
                         void* stream);
+
+/* Replaces cutlass_fp4_group_mm, W4A4 mode (NVFP4 x NVFP4; kernels/matmul_mxfp4_cutlass.cu:
+ * 1157-1162 dispatching to run_w4a4_original :180-356, pointer set-up :56-110): for each
+ * expert e with m_e = problem_sizes[3e] rows,
+ *   out[off_e + i, n] = bf16(alphas[e] * sum_k A[off_e + i, k] sfa(i, k/16) * B[e, n, k] sfb(n, k/16))
+ * a [M, K/2] and b [E, N, K/2] packed E2M1 (low nibble = even k), K % 64 == 0, lda == K/2;
+ * scales UE4M3 (float8_e4m3fn bytes with the sign bit clear), one per 16 codes, in the
+ * blocked layout (128-row x 64-code atoms of 512 bytes): expert e's activation scales start
+ * sf_offsets[e] ROWS into a_blockscale (sf_offsets[e] * K/16 bytes, a multiple of 16),
+ * its weight scales at e * ldb_blockscale bytes (ldb >= the blocked size of N x K/16).
+ * alphas [E] f32, expert_offsets [E] int32, out [M, N] bf16. tcgen05.mma kind::mxf4nvf4
+ * block_scale scale_vec::4X on the tiles of gptoss_fp4_group_mm (same gemm_mode choice). */
+int gptoss_fp4_group_mm_w4a4(void* out, const uint8_t* a, int64_t m_total, int64_t lda,
+                             const uint8_t* b, int num_experts, int64_t n, int64_t k,
+                             const uint8_t* a_blockscale, const uint8_t* b_blockscales,
+                             int64_t ldb_blockscale, const float* alphas,
+                             const int32_t* problem_sizes, const int32_t* expert_offsets,
+                             const int32_t* sf_offsets, int gemm_mode, int32_t* status_dev,
+                             void* stream);
 
 /* Workspace (device bytes) for gptoss_moe_experts_forward / gptoss_moe_layer_forward. */
 size_t gptoss_moe_workspace_bytes(int64_t num_tokens, int top_k, int num_experts,

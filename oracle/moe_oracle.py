@@ -1,4 +1,5 @@
-"""CPU restatement of the reference's W4A8 MoE expert path (test infrastructure only).
+"""CPU restatement of the reference's W4A8 MoE expert path and of its W4A4 (NVFP4) grouped
+GEMM mode (test infrastructure only).
 
 Byte and integer work (quantisation bit tricks, e4m3 encoding, blocked layout, routing)
 is numpy; floating point that the reference does in torch (bf16 rounding, matmuls,
@@ -15,6 +16,7 @@ __all__ = [
     "MXFP_BLOCK", "FP8_MAX", "E2M1_VALUES", "pad_k_to_tile",
     "e4m3_encode", "e4m3_decode", "quantize_fp8_ue8m0",
     "blocked_sf_offset", "blocked_sf_cosize", "convert_scales_blocked", "batch_convert_a_scales",
+    "unblock_scales", "nvfp4_dequant", "nvfp4_group_mm",
     "route_stable", "router_topk_hf", "router_logits_fp32", "router_logits_exact", "router_topk_from_logits",
     "round_bf16_exact",
     "mxfp4_dequant", "fp8_dequant", "group_mm_bf16", "swiglu_fp32",
@@ -151,6 +153,51 @@ def batch_convert_a_scales(scales_rowmajor: np.ndarray, counts, offsets) -> tupl
         cur += blk.size
     flat = np.concatenate(parts) if parts else np.zeros(0, dtype=np.uint8)
     return flat, np.asarray(sf, dtype=np.int32)
+
+
+def unblock_scales(buf: np.ndarray, rows: int, groups: int) -> np.ndarray:
+    """Blocked flat buffer -> row-major [rows, groups] (inverse of convert_scales_blocked)."""
+    r, g = np.meshgrid(np.arange(rows), np.arange(groups), indexing="ij")
+    return np.asarray(buf, dtype=np.uint8)[blocked_sf_offset(r, g, (groups + 3) // 4)]
+
+
+# --------------------------------------------------------------------------- NVFP4 (W4A4)
+def nvfp4_dequant(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """Packed E2M1 [R, K/2] (low nibble = even k) x UE4M3 [R, K/16] -> float64 [R, K].
+    UE4M3 is the float8_e4m3fn encoding of a non-negative scale (sign bit clear)."""
+    b = np.asarray(packed, dtype=np.uint8)
+    R = b.shape[0]
+    v = np.stack([E2M1_VALUES[b & 0xF], E2M1_VALUES[b >> 4]], axis=-1).reshape(R, -1).astype(np.float64)
+    K = v.shape[1]
+    s = e4m3_decode(np.asarray(scales, dtype=np.uint8)[:, : K // 16]).astype(np.float64)
+    return (v.reshape(R, K // 16, 16) * s[..., None]).reshape(R, K)
+
+
+def nvfp4_group_mm(a, b, a_sf_blocked, b_sf_blocked, alphas, counts, offsets, sf_offsets_rows) -> torch.Tensor:
+    """cutlass_fp4_group_mm in its W4A4 mode (kernels/matmul_mxfp4_cutlass.cu:52-356, dispatched
+    at :1157-1162), restated as dequantise-and-multiply: rows [off_e, off_e + m_e) of the packed
+    activations `a` [M, K/2] times expert e of `b` [E, N, K/2], bf16(alpha_e * fp32(A @ B^T)).
+    Scales are the blocked UE4M3 layout (one per 16 codes): expert e's activation scales start
+    sf_offsets_rows[e] rows into a_sf_blocked (:95, rows x K/16 bytes), its weight scales
+    e * (b_sf_blocked.size / E) bytes into b_sf_blocked (:99-100). The products are exact;
+    the sum is taken in float64 and rounded once to float32."""
+    a = np.asarray(a, dtype=np.uint8)
+    b = np.asarray(b, dtype=np.uint8)
+    E, N, Kh = b.shape
+    K = 2 * Kh
+    G = K // 16
+    sfa = np.asarray(a_sf_blocked, dtype=np.uint8).reshape(-1)
+    sfb = np.asarray(b_sf_blocked, dtype=np.uint8).reshape(E, -1)
+    out = torch.zeros((a.shape[0], N), dtype=torch.bfloat16)
+    for e, (m, o) in enumerate(zip(np.asarray(counts).tolist(), np.asarray(offsets).tolist())):
+        if m == 0:
+            continue
+        base = int(sf_offsets_rows[e]) * G
+        A = nvfp4_dequant(a[o:o + m], unblock_scales(sfa[base:base + blocked_sf_cosize(m, G)], m, G))
+        B = nvfp4_dequant(b[e], unblock_scales(sfb[e], N, G))
+        acc = torch.from_numpy((A @ B.T).astype(np.float32))
+        out[o:o + m] = (acc * np.float32(alphas[e])).to(torch.bfloat16)
+    return out
 
 
 # --------------------------------------------------------------------------- routing

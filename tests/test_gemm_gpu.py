@@ -107,18 +107,6 @@ def test_orientations_agree(pkg, dev):
     assert (o1.float() - o2.float()).abs().max().item() <= (o1.float().abs().max().item() * 2 ** -7)
 
 
-def test_w4a4_mode_not_implemented(pkg, dev):
-    a = torch.zeros(4, 256, dtype=torch.uint8, device=dev)
-    with pytest.raises(NotImplementedError):
-        pkg.ops.fp4_group_mm_impl(torch.zeros(4, 128, dtype=torch.bfloat16, device=dev), a,
-                                  torch.zeros(1, 128, 256, dtype=torch.uint8, device=dev),
-                                  torch.zeros(512, dtype=torch.uint8, device=dev),
-                                  torch.zeros(1, 2048, dtype=torch.uint8, device=dev), torch.ones(1, device=dev),
-                                  torch.tensor([[4, 128, 512]], dtype=torch.int32, device=dev),
-                                  torch.zeros(1, dtype=torch.int32, device=dev),
-                                  torch.zeros(1, dtype=torch.int32, device=dev))
-
-
 @pytest.mark.parametrize("m_list,H,I", [([5, 0, 17, 40], 512, 256), ([3, 9], 288, 288)])
 def test_run_cutlass_gemm_reference_signature(pkg, dev, m_list, H, I):
     # CutlassGptOssExperts._run_cutlass_gemm keeps the reference's signature

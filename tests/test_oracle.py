@@ -44,8 +44,8 @@ def test_swiglu_matches_reference_golden():
         assert np.array_equal(got, ref), name
 
 
-def _cute_shapes():
-    path = os.path.join(GOLDEN, "cute_sf_layout.txt")
+def _cute_shapes(name="cute_sf_layout.txt"):
+    path = os.path.join(GOLDEN, name)
     lines = open(path).read().strip().splitlines()
     i = 0
     out = []
@@ -65,6 +65,37 @@ def test_blocked_layout_matches_cute():
         assert O.blocked_sf_cosize(rows, G) == cos_a == cos_b
         r, g = np.meshgrid(np.arange(rows), np.arange(G), indexing="ij")
         assert np.array_equal(O.blocked_sf_offset(r, g, (G + 3) // 4), offs), (rows, K)
+
+
+def test_blocked_layout_16_matches_cute():
+    # the NVFP4 mode's layout (Sm1xxBlockScaledConfig<16>): the same closed form with one
+    # group per 16 codes, so an atom spans 64 codes
+    shapes = _cute_shapes("cute_sf_layout16.txt")
+    assert len(shapes) >= 5
+    for rows, K, cos_a, cos_b, offs in shapes:
+        G = K // 16
+        assert O.blocked_sf_cosize(rows, G) == cos_a == cos_b
+        r, g = np.meshgrid(np.arange(rows), np.arange(G), indexing="ij")
+        assert np.array_equal(O.blocked_sf_offset(r, g, (G + 3) // 4), offs), (rows, K)
+        sf = np.random.default_rng(rows).integers(0, 256, (rows, G), dtype=np.uint8)
+        assert np.array_equal(O.unblock_scales(O.convert_scales_blocked(sf), rows, G), sf)
+
+
+def test_nvfp4_oracle_small_case():
+    # one row, one weight row, K = 64: the dot product by hand
+    a = np.zeros((1, 32), np.uint8)
+    b = np.zeros((1, 1, 32), np.uint8)
+    a[0, 0] = 0x2F        # codes k=0: -6 (0xF), k=1: 1.0 (0x2)
+    b[0, 0, 0] = 0x37     # k=0: 6.0, k=1: 1.5
+    a[0, 8] = 0x05        # k=16: 3.0 (second 16-group)
+    b[0, 0, 8] = 0x02     # k=16: 1.0
+    a_sf = np.array([[0x38, 0x40, 0x38, 0x38]], np.uint8)      # 1, 2, 1, 1
+    b_sf = np.array([[[0x30, 0x38, 0x38, 0x38]]], np.uint8)    # 0.5, 1, 1, 1
+    sfa = O.convert_scales_blocked(a_sf)
+    sfb = O.convert_scales_blocked(b_sf[0])[None]
+    out = O.nvfp4_group_mm(a, b, sfa, sfb, np.array([2.0], np.float32), [1], [0], [0])
+    # (-6*6 + 1*1.5) * 1 * 0.5 + 3 * 1 * 2 * 1 = -17.25 + 6 = -11.25; x alpha 2
+    assert out.float().item() == -22.5
 
 
 def test_documented_cosize():
