@@ -73,6 +73,11 @@ _SIGNATURES = {
                                           _c_int64, _vp, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _vp, _vp, _sz, _i,
                                           _vp, _vp]),
     "gptoss_ep_p2p_combine": (_i, [_vp, _i, _c_int64, _c_int32, _vp, _vp, _c_int64, _i, _c_int64, _vp, _vp, _vp]),
+    "gptoss_set_ep_layer_kernel": (_i, [_i]),
+    "gptoss_ep_p2p_layer_fits": (_i, [_c_int64, _i, _i, _i, _c_int64, _c_int64, _c_int64]),
+    "gptoss_ep_p2p_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _c_int64, _i, _i, _i, _i, _c_int64, _c_int64,
+                                         _vp, _vp, _c_int64, _vp, _vp, _vp, _c_int64, _vp, _f, _f, _c_int64, _vp,
+                                         _vp, _c_int32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "gptoss_moe_route_quant": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64, _vp, _sz, _i, _vp, _vp]),
     "gptoss_moe_gemm1": (_i, [_c_int64, _i, _i, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _f, _f, _vp, _sz,
                               _i, _vp, _vp]),

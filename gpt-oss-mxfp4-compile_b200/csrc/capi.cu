@@ -603,7 +603,7 @@ int run_decode_layer(const void* hidden, const RouterArgs* ra, const int64_t* ri
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!(attr_done & (1ull << dev))) {
-      GPTOSS_CUDA(cudaFuncSetAttribute(decode_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GPTOSS_CUDA(cudaFuncSetAttribute(decode_layer_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(dl_smem_bytes())));
       attr_done |= (1ull << dev);
     }
@@ -645,7 +645,7 @@ int run_decode_layer(const void* hidden, const RouterArgs* ra, const int64_t* ri
   g2.err = status; g2.out = out; g2.ld_out = H; g2.bias = wt.dn_bias;
   g2.swiglu_alpha = sw_alpha; g2.swiglu_limit = sw_limit;
   GPTOSS_TRY(launch_pdl(decode_reset_kernel, dim3(1), dim3(256), 0, st, p.sync, dl_sync_words(E)));
-  return launch_pdl(decode_layer_kernel, dim3(di.sms), dim3(DlCfg::kThreads), dl_smem_bytes(), st, ta, ti, tgu, tdn,
+  return launch_pdl(decode_layer_kernel<false>, dim3(di.sms), dim3(DlCfg::kThreads), dl_smem_bytes(), st, ta, ti, tgu, tdn,
                     p, g1, g2);
 }
 
@@ -1672,6 +1672,150 @@ int gptoss_ep_p2p_combine(const void* local_base, int world_size, int64_t capaci
                     flags, world_size, epoch, status_dev ? status_dev : di.status_sink, pos_of, router_indices,
                     num_tokens, top_k, static_cast<int>(hidden_size), capacity * world_size,
                     static_cast<__nv_bfloat16*>(out));
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- one-launch expert-parallel layer
+// decode_layer_kernel<true>: router (or given routing) on this rank's tokens, dispatch into
+// the owners' receive rows, the local experts' GEMMs on the received rows with GEMM2 storing
+// into the sources' return rows, and the combine, in one persistent launch behind a one-CTA
+// reset of its synchronisation words. Serves decode-sized steps: the received rows (W x cap)
+// fit the kernel's shared-memory routing state and the local experts hold few rows each
+// (16-row chunks); gptoss_set_ep_layer_kernel(0) turns it off.
+// The kernel's tiles multiply 16-row activation chunks, so an expert of m rows streams its
+// weight tiles ceil(m / 16) times -- concurrently, from neighbouring CTAs (chunks are the
+// innermost tile index), so mostly out of L2. Up to kEpLayerMaxRowsPerExpert rows per local
+// expert under balanced routing (capacity / local experts: 32 at 8 ranks x 32 tokens x top-4
+// on 32 experts) the one launch wins; above it the five-launch path picks its own layout.
+constexpr int64_t kEpLayerMaxRowsPerExpert = 64;
+std::atomic<int> g_ep_layer_enabled{1};
+
+bool ep_layer_fits(int64_t T, int k, int E, int world, int64_t H, int64_t I, int64_t cap) {
+  if (g_ep_layer_enabled.load(std::memory_order_relaxed) == 0) return false;
+  if (world < 1 || world > kP2pMaxWorld || E % world != 0) return false;
+  const int epr = E / world;
+  return cap <= kEpLayerMaxRowsPerExpert * epr && T >= 1 && T <= kDlMaxTokens && T * k <= kDlMaxAssign &&
+         epr <= kDlMaxExperts &&
+         H % 32 == 0 && I % 32 == 0 && cap >= T * k && world * cap <= kEpMaxRecv &&
+         static_cast<size_t>(T) * (2 * E + k) * sizeof(float) <= (DlCfg::kStages - kDlPreStages) * DlCfg::kStageBytes;
+}
+
+extern "C" {
+
+int gptoss_set_ep_layer_kernel(int enable) {
+  return g_ep_layer_enabled.exchange(enable != 0 ? 1 : 0, std::memory_order_relaxed);
+}
+
+int gptoss_ep_p2p_layer_fits(int64_t num_tokens, int top_k, int num_experts, int world_size, int64_t hidden_size,
+                             int64_t intermediate_size, int64_t capacity) {
+  return ep_layer_fits(num_tokens, top_k, num_experts, world_size, hidden_size, intermediate_size, capacity) ? 1 : 0;
+}
+
+int gptoss_ep_p2p_layer_forward(const void* hidden, const void* router_weight, const void* router_bias,
+                                const int64_t* router_indices, const float* routing_weights, int64_t num_tokens,
+                                int top_k, int num_experts, int world_size, int rank, int64_t hidden_size,
+                                int64_t intermediate_size, const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                                int64_t ldb_gate_up, const float* gate_up_bias, const uint8_t* down_data,
+                                const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                                float swiglu_alpha, float swiglu_limit, int64_t capacity, void* local_base,
+                                const uint64_t* peer_bases, int32_t epoch, void* out, int64_t* router_indices_out,
+                                void* router_scores_out, float* routing_weights_out, int32_t* send_counts,
+                                int32_t* pos_of, void* workspace, size_t workspace_bytes, int32_t* status_dev,
+                                void* stream) {
+  NvtxRange nvtx_range("gptoss_ep_p2p_layer_forward");
+  GPTOSS_CHECK(world_size >= 1 && world_size <= kP2pMaxWorld && rank >= 0 && rank < world_size,
+               "ep_p2p_layer_forward: bad world_size / rank");
+  GPTOSS_CHECK(num_experts % world_size == 0, "ep_p2p_layer_forward: num_experts must be a multiple of world_size");
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  const int epr = num_experts / world_size;
+  GPTOSS_CHECK(ep_layer_fits(num_tokens, top_k, num_experts, world_size, hidden_size, intermediate_size, capacity),
+               "ep_p2p_layer_forward: T=%lld, top_k=%d, E=%d, W=%d, capacity=%lld do not fit the one-launch kernel "
+               "(gptoss_ep_p2p_layer_fits) or it is turned off",
+               (long long)num_tokens, top_k, num_experts, world_size, (long long)capacity);
+  const bool router = router_weight != nullptr;
+  GPTOSS_CHECK(hidden && out && local_base && peer_bases && send_counts && pos_of && workspace &&
+                   (router ? (router_bias && router_indices_out && routing_weights_out)
+                           : (router_indices && routing_weights)),
+               "ep_p2p_layer_forward: null pointer");
+  GPTOSS_CHECK(aligned(hidden, 16) && aligned(out, 16) && aligned(local_base, 256) && aligned(workspace, 256) &&
+                   (!router || aligned(router_weight, 16)),
+               "ep_p2p_layer_forward: misaligned pointer");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  const ExpertWeights wt{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                         down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(wt, hidden_size, intermediate_size, epr));
+  const int64_t R = capacity * world_size;
+  const Workspace L = plan_workspace(R, 1, epr, hidden_size, intermediate_size);
+  if (workspace_bytes < L.total) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, L.total);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* status = status_dev ? status_dev : di.status_sink;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const WsPtrs w = ws_ptrs(ws, L);
+  const int H = static_cast<int>(hidden_size);
+  const int64_t I = intermediate_size, Kh = pad128(hidden_size), Ki = pad128(intermediate_size);
+  const int rb = static_cast<int>(ep_row_bytes(H));
+  CUtensorMap ta, ti, tgu, tdn;
+  GPTOSS_TRY(make_act_map(&ta, w.act_codes, R, hidden_size, DlCfg::kActRows));
+  GPTOSS_TRY(make_act_map(&ti, w.inter_codes, R, I, DlCfg::kActRows));
+  GPTOSS_TRY(make_wgt_map(&tgu, wt.gu_data, epr, 2 * I, Kh, DlCfg::kWgtRowsCta));
+  GPTOSS_TRY(make_wgt_map(&tdn, wt.dn_data, epr, hidden_size, Ki, DlCfg::kWgtRowsCta));
+  static uint64_t attr_done = 0;   // one bit per device
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_done & (1ull << dev))) {
+      GPTOSS_CUDA(cudaFuncSetAttribute(decode_layer_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(dl_smem_bytes<true>())));
+      attr_done |= (1ull << dev);
+    }
+  }
+  DecodeLayerParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(hidden);
+  if (router) {
+    p.router_w = static_cast<const __nv_bfloat16*>(router_weight);
+    p.router_b = static_cast<const __nv_bfloat16*>(router_bias);
+    p.ridx_out = router_indices_out;
+    p.scores_out = static_cast<__nv_bfloat16*>(router_scores_out);
+    p.rw_out = routing_weights_out;
+  } else {
+    p.ridx_in = router_indices;
+    p.rw_in = routing_weights;
+  }
+  p.T = static_cast<int>(num_tokens); p.H = H; p.I = static_cast<int>(I); p.E = num_experts; p.K = top_k;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.logits = reinterpret_cast<float*>(ws + L.dl_logits);
+  p.sorted_token = w.sorted_token; p.sorted_expert = w.sorted_expert; p.sorted_weight = w.sorted_weight;
+  p.counts = w.counts; p.offsets = w.offsets; p.sf_offsets_a = w.sfoff_a; p.sf_offsets_b = w.sfoff_b;
+  p.act_codes = w.act_codes; p.act_sf = w.act_sf; p.inter_codes = w.inter_codes; p.inter_sf = w.inter_sf;
+  p.sync = reinterpret_cast<int32_t*>(ws + L.dl_sync);
+  p.sfb_gu = wt.gu_scales; p.sfb_stride_gu = wt.ldb_gu; p.bias_gu = wt.gu_bias;
+  p.sfb_dn = wt.dn_scales; p.sfb_stride_dn = wt.ldb_dn; p.bias_dn = wt.dn_bias;
+  p.swiglu_alpha = swiglu_alpha; p.swiglu_limit = swiglu_limit;
+  p.kb1 = static_cast<int>(Kh / 128); p.kb2 = static_cast<int>(Ki / 128);
+  p.n_tiles1 = static_cast<int>((2 * I + DlCfg::kWgtRows - 1) / DlCfg::kWgtRows);
+  p.n_tiles2 = static_cast<int>((hidden_size + DlCfg::kWgtRows - 1) / DlCfg::kWgtRows);
+  p.err = status;
+  p.ep_world = world_size; p.ep_rank = rank; p.ep_epr = epr; p.ep_rb = rb; p.ep_cap = capacity;
+  p.ep_local = static_cast<uint8_t*>(local_base); p.ep_peer_bases = peer_bases; p.ep_epoch = epoch;
+  p.ep_send_counts = send_counts; p.ep_pos_of = pos_of;
+  GemmParams g1{};
+  g1.num_experts = epr; g1.N = static_cast<int>(2 * I); g1.K = static_cast<int>(Kh); g1.num_kb = p.kb1;
+  g1.err = status; g1.out = w.inter_codes; g1.ld_out = I; g1.bias = wt.gu_bias; g1.out_sf = w.inter_sf;
+  g1.out_g4 = p.kb2; g1.out_features = static_cast<int>(I);
+  g1.swiglu_alpha = swiglu_alpha; g1.swiglu_limit = swiglu_limit;
+  GemmParams g2{};
+  g2.num_experts = epr; g2.N = H; g2.K = static_cast<int>(Ki); g2.num_kb = p.kb2;
+  g2.err = status; g2.out = out; g2.ld_out = H; g2.bias = wt.dn_bias;
+  g2.swiglu_alpha = swiglu_alpha; g2.swiglu_limit = swiglu_limit;
+  g2.ep_world = world_size; g2.ep_rank = rank; g2.ep_peer_bases = peer_bases; g2.ep_cap = capacity;
+  g2.ep_ret_off = p2p_ret_offset(world_size, rank, capacity, rb, H); g2.ep_epoch = epoch;
+  GPTOSS_TRY(launch_pdl(decode_reset_kernel, dim3(1), dim3(256), 0, st, p.sync, dl_sync_words(epr)));
+  return launch_pdl(decode_layer_kernel<true>, dim3(di.sms), dim3(DlCfg::kThreads), dl_smem_bytes<true>(), st, ta, ti,
+                    tgu, tdn, p, g1, g2);
 }
 
 }  // extern "C"

@@ -46,6 +46,7 @@
 #include "routing.cuh"
 #include "gemm.cuh"
 #include "prologue.cuh"
+#include "ep_p2p.cuh"
 
 namespace gptoss {
 
@@ -103,10 +104,24 @@ struct DecodeLayerParams {
   int kb1, kb2;                    // 128-deep k blocks of GEMM1 (H padded) and GEMM2 (I padded)
   int n_tiles1, n_tiles2;          // 128-row weight tiles of GEMM1 (2I rows) and GEMM2 (H rows)
   int* err;
+  // expert parallelism over peer memory (decode_layer_kernel<true>): E is the global expert
+  // count (the router's), the GEMMs run the ep_epr local experts of rank ep_rank; the
+  // exchange buffers, row format and flag protocol are those of ep_p2p.cuh
+  int ep_world, ep_rank, ep_epr, ep_rb;
+  int64_t ep_cap;                  // rows per (source, owner) segment
+  uint8_t* ep_local;               // this rank's exchange buffer
+  const uint64_t* ep_peer_bases;   // [W] every rank's exchange buffer (this rank's included)
+  int32_t ep_epoch;
+  int32_t* ep_send_counts;         // [W] rows sent to each owner (output)
+  int32_t* ep_pos_of;              // [T, K] the assignment's row in the exchange (output)
 };
 
+// Received rows one rank of the expert-parallel kernel can hold (W x cap <= this).
+constexpr int kEpMaxRecv = 1024;
+
 // Per-CTA routing state in shared memory.
-struct DlShared {
+template <bool EP>
+struct DlSharedT {
   int cnt[kDlMaxExperts], off[kDlMaxExperts], sfa[kDlMaxExperts], sfb[kDlMaxExperts];
   int chunks[kDlMaxExperts], prefix[kDlMaxExperts + 1], run[kDlMaxExperts];
   int64_t tok[kDlMaxAssign];       // sorted position -> token
@@ -117,11 +132,30 @@ struct DlShared {
   uint64_t tq_bar[kDlQueue];       // tile queue: slot (i - 1) % kDlQueue holds the CTA's tile i >= 1
   int tq[kDlQueue];                // (tile 0 is the CTA index itself); -1 ends the list
 };
+// Expert parallelism: the sorted positions index the rows this rank received (up to
+// kEpMaxRecv), and every local assignment keeps its row in the exchange.
+template <>
+struct DlSharedT<true> {
+  int cnt[kDlMaxExperts], off[kDlMaxExperts], sfa[kDlMaxExperts], sfb[kDlMaxExperts];
+  int chunks[kDlMaxExperts], prefix[kDlMaxExperts + 1], run[kDlMaxExperts];
+  int32_t tok[kEpMaxRecv];         // sorted position -> received row (segment x cap + slot)
+  float w[kEpMaxRecv];             // sorted position -> routing weight
+  uint8_t sexp[kEpMaxRecv];        // sorted position -> local expert
+  int64_t ridx[kDlMaxAssign];      // local assignment -> global expert (-1: out of range)
+  float rw[kDlMaxAssign];          // local assignment -> routing weight
+  int32_t dslot[kDlMaxAssign];     // local assignment -> owner x cap + slot (-1: not sent)
+  int dcnt[kP2pMaxWorld];          // rows sent to each owner
+  uint64_t tq_bar[kDlQueue];
+  int tq[kDlQueue];
+};
+using DlShared = DlSharedT<false>;
 
+template <bool EP = false>
 __host__ __device__ constexpr uint32_t dl_smem_bytes() {
   return 1024u + DlCfg::kStages * DlCfg::kStageBytes + ((DlCfg::kBarrierBytes + 255u) & ~255u) +
-         DlCfg::kEpiStageBytes + static_cast<uint32_t>((sizeof(DlShared) + 255) & ~size_t(255));
+         DlCfg::kEpiStageBytes + static_cast<uint32_t>((sizeof(DlSharedT<EP>) + 255) & ~size_t(255));
 }
+static_assert(dl_smem_bytes<true>() <= 227u * 1024u, "expert-parallel decode layer: shared memory");
 
 __device__ __forceinline__ int32_t ld_acquire_gpu(const int32_t* p) {
   int32_t v;
@@ -166,7 +200,22 @@ __global__ void decode_reset_kernel(int32_t* sync, int n) {
 }
 
 // grid = SM count, blockDim = DlCfg::kThreads (producer, MMA issuer, 4 epilogue warps,
-// second MMA issuer), dynamic smem = dl_smem_bytes().
+// second MMA issuer), dynamic smem = dl_smem_bytes<EP>().
+//
+// EP = true: one rank of an expert-parallel layer over NVLink peer memory, the whole step
+// in this launch (the five launches of the ep_p2p.cuh path): the router and top-k on this
+// rank's tokens as above; then dispatch -- every CTA quantises its share of the local
+// assignments straight into the owning ranks' receive rows (segment = this rank, slot =
+// the assignment's stable rank among those to that owner), the last CTA raises this rank's
+// dispatch flag on every peer; receive -- every CTA waits for all W dispatch flags, sorts
+// the W x cap received rows by local expert in its shared memory and copies its share
+// into the GEMM's activation layout; the GEMM tiles of the ep_epr local experts as above,
+// GEMM2's epilogue storing each output row into its source rank's return rows; the last
+// CTA raises this rank's return flag on every peer; combine -- every CTA waits for all W
+// return flags and sums its tokens' k returned rows (ascending expert, fp32, one bf16
+// rounding) into `out`. The weight stream of the first tiles still starts at launch, under
+// the routing and the exchange.
+template <bool EP>
 __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     decode_layer_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_inter,
                         const __grid_constant__ CUtensorMap tm_wgu, const __grid_constant__ CUtensorMap tm_wdn,
@@ -188,9 +237,10 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   const uint32_t drain_bar = bar_base + 8u * (2 * C::kStages + 2 * C::kAccBufs);
   const uint32_t epi_off = C::kStages * C::kStageBytes + ((C::kBarrierBytes + 255u) & ~255u);
   float* const epi_f = reinterpret_cast<float*>(smem_gen + epi_off);
-  DlShared& S = *reinterpret_cast<DlShared*>(smem_gen + epi_off + C::kEpiStageBytes);
+  DlSharedT<EP>& S = *reinterpret_cast<DlSharedT<EP>*>(smem_gen + epi_off + C::kEpiStageBytes);
 
   const int T = p.T, H = p.H, E = p.E, K = p.K, A = T * K;
+  const int EG = EP ? p.ep_epr : E;   // experts the GEMMs run (this rank's, under expert parallelism)
   const bool router = p.router_w != nullptr;
   constexpr uint32_t kTxSub = C::kActRows * 128u + C::kWgtRowsCta * 64u + C::kSfActBytes + 512u;
 
@@ -223,7 +273,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   // ---- weights of the likely first tile, before the routing (and the previous kernel)
   // are known: CTA b starts with GEMM1 tile b, (expert b / n1, weight tile b % n1) when every
   // expert is touched once.
-  const bool guess_live = cta < E * p.n_tiles1;
+  const bool guess_live = cta < EG * p.n_tiles1;
   const int e_g = cta / p.n_tiles1, nt_g = cta - e_g * p.n_tiles1;
   // The routing scratch (logits, their keys, top-k slots) lives in the epilogue staging buffer when
   // it fits -- then the whole ring is loaded ahead -- else in the ring stages past the
@@ -263,8 +313,8 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   pdl_wait();
 
   // ================================================================ routing (all warps)
-  // zero this CTA's slice of `out` (GEMM2 adds into it)
-  {
+  // zero this CTA's slice of `out` (GEMM2 adds into it; expert-parallel: the combine writes it)
+  if constexpr (!EP) {
     const int64_t n16 = static_cast<int64_t>(T) * H / 8;
     const int64_t lo = n16 * cta / G, hi = n16 * (cta + 1) / G;
     uint4* z = reinterpret_cast<uint4*>(p.out);
@@ -371,18 +421,14 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
       S.rw[i] = p.rw_in[i];
     }
   }
-  for (int e = tid; e < E; e += nthr) S.cnt[e] = 0;
-  __syncthreads();
-  for (int i = tid; i < A; i += nthr)
-    if (S.ridx[i] >= 0) atomicAdd(&S.cnt[S.ridx[i]], 1);
-  __syncthreads();
-  if (warp == 0) {
-    // exclusive scans: row offsets, scale offsets (SPREAD rows), 16-row chunks
-    const int per = (E + 31) / 32, q0 = lane * per;
+  // exclusive scans of the GEMM experts' row counts (warp 0): row offsets, scale offsets
+  // (SPREAD rows), 16-row chunks
+  auto scan_counts = [&]() {
+    const int per = (EG + 31) / 32, q0 = lane * per;
     int c_run = 0, a_run = 0, b_run = 0, k_run = 0;
     for (int i = 0; i < per; ++i) {
       const int q = q0 + i;
-      if (q < E) {
+      if (q < EG) {
         c_run += S.cnt[q];
         a_run += static_cast<int>(act_sf_cosize(S.cnt[q], p.kb1 * 4, true));
         b_run += static_cast<int>(act_sf_cosize(S.cnt[q], p.kb2 * 4, true));
@@ -399,7 +445,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     int ce = ci - c_run, ae = ai - a_run, be = bi - b_run, ke = ki - k_run;
     for (int i = 0; i < per; ++i) {
       const int q = q0 + i;
-      if (q < E) {
+      if (q < EG) {
         const int m = S.cnt[q];
         S.off[q] = ce; S.run[q] = ce; S.sfa[q] = ae; S.sfb[q] = be;
         S.chunks[q] = (m + C::kActRows - 1) / C::kActRows;
@@ -410,27 +456,167 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
         ke += S.chunks[q];
       }
     }
-    if (lane == 31) S.prefix[E] = ki;
+    if (lane == 31) S.prefix[EG] = ki;
     __syncwarp();
-    // stable positions, 32 assignments at a time (lanes of one expert rank by lane order)
-    for (int i0 = 0; i0 < A; i0 += 32) {
-      const int i = i0 + lane;
-      const int e = i < A ? static_cast<int>(S.ridx[i]) : -2;
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
-      if (e >= 0) {
-        const int pos = S.run[e] + __popc(peers & ((1u << lane) - 1u));
-        S.tok[pos] = i / K;
-        S.w[pos] = S.rw[i];
-        S.sexp[pos] = e;
+  };
+  // expert parallelism: the exchange rows of this rank's receive buffer
+  const uint8_t* const recv = EP ? p.ep_local + p2p_recv_offset(0, p.ep_cap, p.ep_rb) : nullptr;
+  if constexpr (!EP) {
+    for (int e = tid; e < E; e += nthr) S.cnt[e] = 0;
+    __syncthreads();
+    for (int i = tid; i < A; i += nthr)
+      if (S.ridx[i] >= 0) atomicAdd(&S.cnt[S.ridx[i]], 1);
+    __syncthreads();
+    if (warp == 0) {
+      scan_counts();
+      // stable positions, 32 assignments at a time (lanes of one expert rank by lane order)
+      for (int i0 = 0; i0 < A; i0 += 32) {
+        const int i = i0 + lane;
+        const int e = i < A ? static_cast<int>(S.ridx[i]) : -2;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (e >= 0) {
+          const int pos = S.run[e] + __popc(peers & ((1u << lane) - 1u));
+          S.tok[pos] = i / K;
+          S.w[pos] = S.rw[i];
+          S.sexp[pos] = e;
+        }
+        __syncwarp();
+        if (e >= 0 && lane == __ffs(peers) - 1) S.run[e] += __popc(peers);
+        __syncwarp();
       }
-      __syncwarp();
-      if (e >= 0 && lane == __ffs(peers) - 1) S.run[e] += __popc(peers);
-      __syncwarp();
     }
+    __syncthreads();
+  } else {
+    // ================================================================ dispatch
+    const int W = p.ep_world, epr = p.ep_epr, rb = p.ep_rb;
+    const int64_t cap = p.ep_cap;
+    // owner q = expert / epr; slot j = the assignment's stable rank among those to q
+    if (warp == 0) {
+      for (int q = lane; q < W; q += 32) S.dcnt[q] = 0;
+      __syncwarp();
+      for (int i0 = 0; i0 < A; i0 += 32) {
+        const int i = i0 + lane;
+        const int q = (i < A && S.ridx[i] >= 0) ? static_cast<int>(S.ridx[i] / epr) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, q);
+        if (q >= 0) {
+          const int j = S.dcnt[q] + __popc(peers & ((1u << lane) - 1u));
+          S.dslot[i] = j < cap ? static_cast<int32_t>(q * cap + j) : -1;
+        } else if (i < A) {
+          S.dslot[i] = -1;
+        }
+        __syncwarp();
+        if (q >= 0 && lane == __ffs(peers) - 1) S.dcnt[q] += __popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    if (cta == 0) {   // the routing outputs of the API
+      if (router) {
+        for (int i = tid; i < A; i += nthr) {
+          p.ridx_out[i] = S.ridx[i];
+          if (p.scores_out) p.scores_out[i] = __float2bfloat16_rn(S.rw[i]);
+          p.rw_out[i] = S.rw[i];
+        }
+      }
+      for (int q = tid; q < W; q += nthr) p.ep_send_counts[q] = min(static_cast<int64_t>(S.dcnt[q]), cap);
+      for (int i = tid; i < A; i += nthr) p.ep_pos_of[i] = S.dslot[i];
+    }
+    // this CTA's local assignments cta, cta + G, ...: FP8 codes and UE8M0 scales straight into
+    // the owner's receive row (a row per assignment, in the ep_pack_p2p_row format)
+    {
+      const int gv = H / 32;
+      const int nmine = cta < A ? (A - cta + G - 1) / G : 0;
+      for (int q = tid; q < nmine * gv; q += nthr) {
+        const int r = q / gv, g = q - r * gv;
+        const int i = cta + r * G;
+        const int slot = S.dslot[i];
+        if (slot < 0) continue;
+        const int own = static_cast<int>(slot / cap);
+        const int64_t j = slot - static_cast<int64_t>(own) * cap;
+        uint8_t* row = reinterpret_cast<uint8_t*>(p.ep_peer_bases[own]) + p2p_recv_offset(p.ep_rank, cap, rb) + j * rb;
+        const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(i / K) * H + 32 * g);
+        float v[32];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 w4 = __ldg(src + u);
+          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            v[8 * u + 2 * h] = bf16_bits_lo(wv[h]);
+            v[8 * u + 2 * h + 1] = bf16_bits_hi(wv[h]);
+          }
+        }
+        uint32_t cw[8];
+        const uint8_t sc = quantize_group32(v, cw);
+        uint4* dst = reinterpret_cast<uint4*>(row + 32 * g);
+        dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+        dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+        row[H + g] = sc;
+        if (g == 0) {
+          for (int b = H + gv; b < rb - 8; ++b) row[b] = 0;   // padding travels as zeros
+          int32_t* meta = reinterpret_cast<int32_t*>(row + rb - 8);
+          meta[0] = static_cast<int32_t>(S.ridx[i] % epr);
+          meta[1] = __float_as_int(S.rw[i]);
+        }
+      }
+      // every owner's slots past this rank's count carry the empty-slot marker
+      for (int64_t f = static_cast<int64_t>(cta) * nthr + tid; f < W * cap; f += static_cast<int64_t>(G) * nthr) {
+        const int own = static_cast<int>(f / cap);
+        const int64_t j = f - static_cast<int64_t>(own) * cap;
+        if (j < S.dcnt[own]) continue;
+        int32_t* meta = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(p.ep_peer_bases[own]) +
+                                                   p2p_recv_offset(p.ep_rank, cap, rb) + j * rb + rb - 8);
+        meta[0] = -1;
+        meta[1] = 0;
+      }
+    }
+    __syncthreads();
+    if (tid == 0)
+      p2p_last_cta_signal(reinterpret_cast<int32_t*>(p.ep_local) + kP2pCounterDispatch, p.ep_peer_bases, W,
+                          p.ep_rank, p.ep_epoch);
+    // ================================================================ receive
+    p2p_wait_flags(reinterpret_cast<const int32_t*>(p.ep_local), 0, W, p.ep_epoch, p.err);
+    const int R = static_cast<int>(W * cap);
+    // row headers (local expert, routing weight) in the epilogue staging, free until the GEMMs
+    int* hexp = reinterpret_cast<int*>(epi_f);
+    float* hw = epi_f + kEpMaxRecv;
+    for (int e = tid; e < EG; e += nthr) S.cnt[e] = 0;
+    __syncthreads();
+    for (int r = tid; r < R; r += nthr) {
+      const int32_t* meta = reinterpret_cast<const int32_t*>(recv + static_cast<int64_t>(r) * rb + rb - 8);
+      int e = __ldcg(meta);
+      const float wv = __int_as_float(__ldcg(meta + 1));
+      if (e >= EG || e < -1) {
+        if (cta == 0) atomicCAS(p.err, 0, 0x201);
+        e = -1;
+      }
+      hexp[r] = e;
+      hw[r] = wv;
+      if (e >= 0) atomicAdd(&S.cnt[e], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      scan_counts();
+      // stable positions over the received rows (source rank, then slot)
+      for (int i0 = 0; i0 < R; i0 += 32) {
+        const int r = i0 + lane;
+        const int e = r < R ? hexp[r] : -2;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (e >= 0) {
+          const int pos = S.run[e] + __popc(peers & ((1u << lane) - 1u));
+          S.tok[pos] = r;
+          S.w[pos] = hw[r];
+          S.sexp[pos] = static_cast<uint8_t>(e);
+        }
+        __syncwarp();
+        if (e >= 0 && lane == __ffs(peers) - 1) S.run[e] += __popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  const int total = S.off[E - 1] + S.cnt[E - 1];     // assignments with a valid expert
-  const int nchunks = S.prefix[E];
+  const int total = S.off[EG - 1] + S.cnt[EG - 1];     // rows with a valid expert
+  const int nchunks = S.prefix[EG];
   // one tile list: GEMM1 tiles [0, q1), then GEMM2 tiles [q1, q1 + q2); CTA b takes b, b + G, ...
   const int q1 = nchunks * p.n_tiles1, q2 = nchunks * p.n_tiles2;
   const int qall = q1 + q2;
@@ -449,31 +635,33 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   };
 
   // CTA 0: the routing outputs of the API and the routed layout of the workspace
-  if (cta == 0) {
-    if (router) {
-      for (int i = tid; i < A; i += nthr) {
-        p.ridx_out[i] = S.ridx[i];
-        if (p.scores_out) p.scores_out[i] = __float2bfloat16_rn(S.rw[i]);
-        p.rw_out[i] = S.rw[i];
+  if constexpr (!EP) {
+    if (cta == 0) {
+      if (router) {
+        for (int i = tid; i < A; i += nthr) {
+          p.ridx_out[i] = S.ridx[i];
+          if (p.scores_out) p.scores_out[i] = __float2bfloat16_rn(S.rw[i]);
+          p.rw_out[i] = S.rw[i];
+        }
       }
-    }
-    for (int i = tid; i < A; i += nthr) {
-      const bool v = i < total;
-      p.sorted_token[i] = v ? S.tok[i] : -1;
-      p.sorted_expert[i] = v ? S.sexp[i] : -1;
-      p.sorted_weight[i] = v ? S.w[i] : 0.0f;
-    }
-    for (int e = tid; e < E; e += nthr) {
-      p.counts[e] = S.cnt[e];
-      p.offsets[e] = S.off[e];
-      p.sf_offsets_a[e] = S.sfa[e];
-      p.sf_offsets_b[e] = S.sfb[e];
+      for (int i = tid; i < A; i += nthr) {
+        const bool v = i < total;
+        p.sorted_token[i] = v ? S.tok[i] : -1;
+        p.sorted_expert[i] = v ? S.sexp[i] : -1;
+        p.sorted_weight[i] = v ? S.w[i] : 0.0f;
+      }
+      for (int e = tid; e < E; e += nthr) {
+        p.counts[e] = S.cnt[e];
+        p.offsets[e] = S.off[e];
+        p.sf_offsets_a[e] = S.sfa[e];
+        p.sf_offsets_b[e] = S.sfb[e];
+      }
     }
   }
   // tile t of a GEMM's list -> (expert, weight tile, 16-row chunk); chunks innermost
   auto decode = [&](int t, int n_tiles, int& e, int& nt, int& ch) {
     const int cidx = t / n_tiles;
-    int lo = 0, hi = E - 1;
+    int lo = 0, hi = EG - 1;
     while (lo < hi) {                         // last e with prefix[e] <= cidx
       const int mid = (lo + hi + 1) >> 1;
       if (S.prefix[mid] <= cidx) lo = mid; else hi = mid - 1;
@@ -490,38 +678,57 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     if (g2) decode(t - q1, p.n_tiles2, e, nt, ch);
     else decode(t, p.n_tiles1, e, nt, ch);
   };
-  // quantise sorted rows cta, cta + G, ...: each row's codes and blocked scales; the CTA
-  // then counts itself into sync[0] (the activation loads wait until every CTA has: one
-  // wait per CTA instead of one acquire round trip per expert on the producer's path)
+  // quantise sorted rows cta, cta + G, ... (expert parallelism: copy the received rows): each
+  // row's codes and blocked scales; the CTA then counts itself into sync[0] (the activation
+  // loads wait until every CTA has: one wait per CTA instead of one acquire round trip per
+  // expert on the producer's path)
   {
     const int gp = 4 * p.kb1;                 // scale groups per row incl. K padding
     const int gv = H / 32;                    // valid groups
     const int nmine = cta < total ? (total - cta + G - 1) / G : 0;
-    for (int q = tid; q < nmine * gp; q += nthr) {
-      const int r = q / gp, g = q - r * gp;
-      const int pos = cta + r * G;
-      const int e = S.sexp[pos], j = pos - S.off[e];
-      uint8_t sc = 0;
-      if (g < gv) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.x + S.tok[pos] * H + 32 * g);
-        float v[32];
+    if constexpr (!EP) {
+      for (int q = tid; q < nmine * gp; q += nthr) {
+        const int r = q / gp, g = q - r * gp;
+        const int pos = cta + r * G;
+        const int e = S.sexp[pos], j = pos - S.off[e];
+        uint8_t sc = 0;
+        if (g < gv) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.x + S.tok[pos] * H + 32 * g);
+          float v[32];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint4 w4 = __ldg(src + u);
-          const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          for (int u = 0; u < 4; ++u) {
+            const uint4 w4 = __ldg(src + u);
+            const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            v[8 * u + 2 * h] = bf16_bits_lo(wv[h]);
-            v[8 * u + 2 * h + 1] = bf16_bits_hi(wv[h]);
+            for (int h = 0; h < 4; ++h) {
+              v[8 * u + 2 * h] = bf16_bits_lo(wv[h]);
+              v[8 * u + 2 * h + 1] = bf16_bits_hi(wv[h]);
+            }
           }
+          uint32_t cw[8];
+          sc = quantize_group32(v, cw);
+          uint4* dst = reinterpret_cast<uint4*>(p.act_codes + static_cast<int64_t>(pos) * H + 32 * g);
+          dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+          dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
         }
-        uint32_t cw[8];
-        sc = quantize_group32(v, cw);
-        uint4* dst = reinterpret_cast<uint4*>(p.act_codes + static_cast<int64_t>(pos) * H + 32 * g);
-        dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-        dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+        p.act_sf[S.sfa[e] + blocked_sf_offset(act_sf_row<true>(j), g, p.kb1)] = sc;   // K padding: 0
       }
-      p.act_sf[S.sfa[e] + blocked_sf_offset(act_sf_row<true>(j), g, p.kb1)] = sc;   // K padding: 0
+    } else {
+      const int64_t rb = p.ep_rb;
+      const int nv = H / 16;
+      for (int q = tid; q < nmine * nv; q += nthr) {
+        const int r = q / nv, v = q - r * nv;
+        const int pos = cta + r * G;
+        reinterpret_cast<uint4*>(p.act_codes + static_cast<int64_t>(pos) * H)[v] =
+            __ldcg(reinterpret_cast<const uint4*>(recv + static_cast<int64_t>(S.tok[pos]) * rb) + v);
+      }
+      for (int q = tid; q < nmine * gp; q += nthr) {
+        const int r = q / gp, g = q - r * gp;
+        const int pos = cta + r * G;
+        const int e = S.sexp[pos], j = pos - S.off[e];
+        const uint8_t sc = g < gv ? __ldcg(recv + static_cast<int64_t>(S.tok[pos]) * rb + H + g) : uint8_t{0};
+        p.act_sf[S.sfa[e] + blocked_sf_offset(act_sf_row<true>(j), g, p.kb1)] = sc;   // K padding: 0
+      }
     }
     fence_proxy_async_global();               // the rows are read by other CTAs' TMA copies
     __syncthreads();
@@ -584,7 +791,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
           mbar_arrive(smem_u32(&S.tq_bar[slot]));
         }
         if (t < 0) break;
-        t_next = G + atomicAdd(p.sync + 2 + E, 1);   // the next tile, one tile ahead
+        t_next = G + atomicAdd(p.sync + 2 + EG, 1);   // the next tile, one tile ahead
         bool g2;
         int e, nt, ch;
         tile_of(t, g2, e, nt, ch);
@@ -704,7 +911,8 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     // ================================================================ epilogue
     GemmParams pg1 = pg1_in, pg2 = pg2_in;
     pg1.out_sf_offsets = S.sfb;               // shared-memory copies of the routed layout
-    pg2.token_idx = S.tok;
+    if constexpr (EP) pg2.token_idx32 = S.tok;   // received rows: GEMM2 stores into their sources
+    else pg2.token_idx = S.tok;
     pg2.row_weights = S.w;
     const int q = warp & 3;
     bool ok = true;
@@ -767,6 +975,37 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+  if constexpr (EP) {
+    // ================================================================ return + combine
+    // every GEMM2 store of this CTA is behind the barrier above: the last CTA raises this
+    // rank's return flag on every peer; then every CTA waits for all owners' flags and sums
+    // its tokens' returned rows
+    if (tid == 0)
+      p2p_last_cta_signal(reinterpret_cast<int32_t*>(p.ep_local) + kP2pCounterReturn, p.ep_peer_bases, p.ep_world,
+                          p.ep_world + p.ep_rank, p.ep_epoch);
+    p2p_wait_flags(reinterpret_cast<const int32_t*>(p.ep_local), p.ep_world, p.ep_world, p.ep_epoch, p.err);
+    const __nv_bfloat16* ret =
+        reinterpret_cast<const __nv_bfloat16*>(p.ep_local + p2p_ret_offset(p.ep_world, 0, p.ep_cap, p.ep_rb, H));
+    for (int t = cta; t < T; t += G) {
+      int order[kMaxTopK];
+      for (int j = 0; j < K; ++j) order[j] = j;
+      for (int a = 1; a < K; ++a)             // insertion sort by expert id
+        for (int b = a; b > 0 && S.ridx[t * K + order[b]] < S.ridx[t * K + order[b - 1]]; --b) {
+          const int tmp = order[b]; order[b] = order[b - 1]; order[b - 1] = tmp;
+        }
+      for (int h2 = tid; h2 < H / 2; h2 += nthr) {
+        float a0 = 0.0f, a1 = 0.0f;
+        for (int j = 0; j < K; ++j) {
+          const int pr = S.dslot[t * K + order[j]];
+          if (pr < 0) continue;
+          const __nv_bfloat162 v = __ldcg(reinterpret_cast<const __nv_bfloat162*>(ret + static_cast<int64_t>(pr) * H) + h2);
+          a0 += __bfloat162float(v.x);
+          a1 += __bfloat162float(v.y);
+        }
+        reinterpret_cast<__nv_bfloat162*>(p.out + static_cast<int64_t>(t) * H)[h2] = __floats2bfloat162_rn(a0, a1);
+      }
+    }
   }
 }
 

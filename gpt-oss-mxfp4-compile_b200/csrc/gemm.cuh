@@ -68,6 +68,7 @@ struct GemmParams {
   int out_g4;
   int out_features;             // kEpiGemm1: intermediate width (N / 2)
   const int64_t* token_idx;     // kEpiGemm2
+  const int32_t* token_idx32;   // kEpiGemm2 on weights-on-M tiles: 32-bit row indices when set
   const float* row_weights;     // kEpiGemm2
   float swiglu_alpha, swiglu_limit;
   // Weights-on-M tiles: weight tiles each CTA prefetches into L2 before waiting on the
@@ -316,7 +317,7 @@ __device__ __forceinline__ void swap_epilogue_tile(const GemmParams& p, uint32_t
           const int n0 = nt * C::kWgtRows + seg * 8;           // output feature
           if (tok < nv && n0 < p.N) {
             const int64_t grow = static_cast<int64_t>(row0) + a0 + tok;
-            const int64_t tk = p.token_idx[grow];
+            const int64_t tk = p.token_idx32 != nullptr ? static_cast<int64_t>(p.token_idx32[grow]) : p.token_idx[grow];
             const float wr = p.row_weights[grow];
             const float* src = sh + tok * kEpiFeat + seg * 8;
             const float4 z0 = *reinterpret_cast<const float4*>(src);
@@ -371,6 +372,11 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ int s_chunk_prefix[kMaxExpertsGemm + 1];
   __shared__ int s_chunks[kMaxExpertsGemm];
+  // per-expert metadata read once per CTA: a global load per tile on the producer's path
+  // (under a full memory system, microseconds each) would delay every tile's first stage
+  __shared__ int s_msize[kMaxExpertsGemm];
+  __shared__ int s_row_off[kMaxExpertsGemm];
+  __shared__ long long s_sfa_base[kMaxExpertsGemm];
   __shared__ uint32_t s_tmem_base;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -432,6 +438,14 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
   for (int i = threadIdx.x; i < p.num_experts; i += blockDim.x) {
     const int m = p.m_sizes[i * p.m_stride];
     s_chunks[i] = m > 0 ? (m + C::kTileM - 1) / C::kTileM : 0;
+    s_msize[i] = m;
+    s_row_off[i] = p.row_offsets[i];
+    int64_t sfa_base = NVF4 ? static_cast<int64_t>(p.sfa_offsets[i]) * (p.K >> 4) : p.sfa_offsets[i];
+    if (sfa_base & 15) {   // a bulk copy needs 16-byte alignment: report, then read aligned
+      if (m > 0 && p.err) atomicCAS(p.err, 0, static_cast<int>(kDevMisalignedScales));
+      sfa_base &= ~static_cast<int64_t>(15);
+    }
+    s_sfa_base[i] = sfa_base;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -453,7 +467,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
     if constexpr (!SWAP || SPREAD) {
       return C::kActRows;
     } else {
-      const int left = p.m_sizes[e * p.m_stride] - ch * C::kActRows;
+      const int left = s_msize[e] - ch * C::kActRows;
       return left <= 16 ? 16 : (left <= 32 ? 32 : C::kActRows);
     }
   };
@@ -487,15 +501,10 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
         // this CTA's activation rows (PAIR: its 128-row half of the 256-row tile) and the
         // weight rows it loads (PAIR: its 96-row half of the 192-row tile)
         const int act_in0 = ch * C::kTileM + static_cast<int>(prank) * C::kActRows;
-        const int act_row0 = p.row_offsets[e] + act_in0;
+        const int act_row0 = s_row_off[e] + act_in0;
         const int wgt_row0 = nt * C::kWgtRows + static_cast<int>(prank) * C::kWgtRowsCta;
         const int act_blk = static_cast<int>(act_sf_row<SPREAD>(static_cast<int64_t>(act_in0)) >> 7);
-        int64_t sfa_base = NVF4 ? static_cast<int64_t>(p.sfa_offsets[e]) * (p.K >> 4) : p.sfa_offsets[e];
-        if (sfa_base & 15) {   // a bulk copy needs 16-byte alignment: report, then read aligned
-          if (p.err) atomicCAS(p.err, 0, static_cast<int>(kDevMisalignedScales));
-          sfa_base &= ~static_cast<int64_t>(15);
-        }
-        const int64_t sfa_off = sfa_base + static_cast<int64_t>(act_blk) * g4 * 512;
+        const int64_t sfa_off = s_sfa_base[e] + static_cast<int64_t>(act_blk) * g4 * 512;
         const int wblk0 = (nt * C::kWgtRows) >> 7;   // scale blocks of the whole tile
         const int nwblk_total = (p.N + 127) >> 7;
         const int nwchunks = min(C::kWgtSfChunks, nwblk_total - wblk0);
@@ -694,8 +703,8 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
       }
       tc_fence_after();
       const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + b * C::kAccStride;
-      const int m_e = p.m_sizes[e * p.m_stride];
-      const int row0 = p.row_offsets[e];
+      const int m_e = s_msize[e];
+      const int row0 = s_row_off[e];
       if constexpr (!SWAP) {
         // thread <-> activation row
         const int r_in = ch * C::kTileM + static_cast<int>(prank) * C::kActRows + 32 * q + lane;   // row in expert

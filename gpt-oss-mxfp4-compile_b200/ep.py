@@ -162,6 +162,21 @@ class ExpertParallelExperts(nn.Module):
             self.exchange.close()
             self.exchange = None
 
+    def _p2p_one_launch(self, h, cap: int) -> bool:
+        """Decode-sized steps run as one persistent launch (ops.ep_p2p_layer_forward)."""
+        x = self.experts
+        return _ops.ep_p2p_layer_fits(h.shape[0], self.top_k, self.num_experts, self.world_size, self.hidden_size,
+                                      x.intermediate_size, cap)
+
+    def _p2p_layer(self, h, router_weight, router_bias, idx, w, cap):
+        ex, x = self.exchange, self.experts
+        out, scores, idx, send_counts, _ = _ops.ep_p2p_layer_forward(
+            h, router_weight, router_bias, idx, w, self.top_k, self.num_experts, self.world_size, self.rank,
+            x.gate_up_proj_data, x.gate_up_proj_scales, x.gate_up_proj_bias, x.down_proj_data, x.down_proj_scales,
+            x.down_proj_bias, cap, ex.local, ex.peer_bases, ex.epoch, self._ws, float(x.alpha), float(x.limit))
+        self.last_send_counts = send_counts
+        return out, scores, idx
+
     def _p2p_finish(self, h, idx, send_counts, pos_of, cap):
         """Local experts on the received rows, return rows to their senders, combine."""
         ex, x = self.exchange, self.experts
@@ -183,6 +198,9 @@ class ExpertParallelExperts(nn.Module):
         ex = self.exchange
         ex.epoch += 1
         cap = self.capacity_tokens * self.top_k
+        if self._p2p_one_launch(h, cap):
+            out, scores, idx = self._p2p_layer(h, router_weight, router_bias, None, None, cap)
+            return out, scores, idx
         scores, idx, send_counts, pos_of = _ops.ep_p2p_route_dispatch(
             h, router_weight, router_bias, self.top_k, self.world_size, self.rank, cap, ex.local, ex.peer_bases,
             ex.epoch)
@@ -202,6 +220,8 @@ class ExpertParallelExperts(nn.Module):
             ex = self.exchange
             ex.epoch += 1
             cap = self.capacity_tokens * self.top_k
+            if self._p2p_one_launch(h, cap):
+                return self._p2p_layer(h, None, None, idx, w, cap)[0].view(shape)
             send_counts, pos_of = _ops.ep_p2p_dispatch(h, idx, w, self.num_experts, self.world_size, self.rank, cap,
                                                        ex.local, ex.peer_bases, ex.epoch)
             return self._p2p_finish(h, idx, send_counts, pos_of, cap).view(shape)

@@ -831,6 +831,61 @@ def ep_p2p_expert_forward(local_base: int, world_size: int, rank: int, capacity:
               workspace.numel(), int(gemm_mode), status_tensor(dev).data_ptr(), _stream(dev))
 
 
+def set_ep_layer_kernel(enable: bool) -> bool:
+    """Process-wide: decode-sized expert-parallel steps over peer memory as one persistent
+    launch (True, the default) or as the five-launch path (False). Returns the previous
+    setting."""
+    return bool(_lib.query("gptoss_set_ep_layer_kernel", 1 if enable else 0))
+
+
+def ep_p2p_layer_fits(num_tokens: int, top_k: int, num_experts: int, world_size: int, hidden_size: int,
+                      intermediate_size: int, capacity: int) -> bool:
+    """Whether gptoss_ep_p2p_layer_forward serves this step (and is turned on)."""
+    return bool(_lib.query("gptoss_ep_p2p_layer_fits", int(num_tokens), int(top_k), int(num_experts),
+                           int(world_size), int(hidden_size), int(intermediate_size), int(capacity)))
+
+
+def ep_p2p_layer_forward(hidden, router_weight, router_bias, router_indices, routing_weights, top_k: int,
+                         num_experts: int, world_size: int, rank: int, gu_data, gu_scales, gu_bias, dn_data,
+                         dn_scales, dn_bias, capacity: int, local_base: int, peer_bases, epoch: int, workspace,
+                         alpha: float = 1.702, limit: float = 7.0):
+    """One expert-parallel step in one launch (router, or the given routing when
+    `router_weight` is None; dispatch, local experts, return, combine). Returns
+    (out bf16 [T, H], scores bf16 [T, k] or None, router_indices i64 [T, k], send_counts i32 [W],
+    pos_of i32 [T*k]). `workspace` (u8) holds at least workspace_bytes(W*cap, 1, E/W, H, I)."""
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias)
+    T, H = hidden.shape
+    E_loc = gu_data.shape[0]
+    I = gu_data.shape[1] // 2
+    dev = hidden.device
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    send_counts = torch.empty(world_size, dtype=torch.int32, device=dev)
+    pos_of = torch.empty(max(T * top_k, 1), dtype=torch.int32, device=dev)
+    scores = None
+    if router_weight is not None:
+        _dtype(router_weight, (torch.bfloat16,), "router weight")
+        _dtype(router_bias, (torch.bfloat16,), "router bias")
+        router_indices = torch.empty((T, top_k), dtype=torch.int64, device=dev)
+        scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
+        wf = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+        args = (router_weight.data_ptr(), router_bias.data_ptr(), None, None)
+        outs = (router_indices.data_ptr(), scores.data_ptr(), wf.data_ptr())
+    else:
+        _dtype(router_indices, (torch.int64,), "router_indices")
+        _dtype(routing_weights, (torch.float32,), "routing_weights")
+        args = (None, None, router_indices.data_ptr(), routing_weights.data_ptr())
+        outs = (None, None, None)
+    _lib.call("gptoss_ep_p2p_layer_forward", hidden.data_ptr(), *args, T, int(top_k), int(num_experts),
+              int(world_size), int(rank), H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E_loc,
+              gu_bias.data_ptr(), dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E_loc,
+              dn_bias.data_ptr(), float(alpha), float(limit), int(capacity), int(local_base), peer_bases.data_ptr(),
+              int(epoch), out.data_ptr(), *outs, send_counts.data_ptr(), pos_of.data_ptr(), workspace.data_ptr(),
+              workspace.numel(), status_tensor(dev).data_ptr(), _stream(dev))
+    return out, scores, router_indices, send_counts, pos_of
+
+
 def ep_p2p_combine(local_base: int, world_size: int, capacity: int, epoch: int, pos_of, router_indices,
                    hidden_size: int, device):
     T, k = router_indices.shape

@@ -419,6 +419,38 @@ int gptoss_ep_p2p_combine(const void* local_base, int world_size, int64_t capaci
                           int top_k, int64_t hidden_size, void* out, int32_t* status_dev,
                           void* stream);
 
+/* The same expert-parallel step in ONE persistent launch (no counterpart in the reference,
+ * which has no expert parallelism; it replaces the four calls above at decode sizes):
+ * router (router_weight != NULL: logits, top-k, softmax as gptoss_router_topk, written to
+ * router_indices_out / router_scores_out (may be NULL) / routing_weights_out) or the given
+ * routing (router_weight == NULL: router_indices, routing_weights); the dispatch into the
+ * owners' receive rows; the wait for every sender's flag; the local experts (the
+ * num_experts / world_size experts of this rank, weights as gptoss_moe_experts_forward)
+ * with each output row stored into its source rank's return rows; the return flags; the
+ * wait for every owner's return flag and the combine into out [T, H] bf16. Same buffers,
+ * row format, flags and epochs as the calls above; send_counts [W] and pos_of [T * top_k]
+ * are written as gptoss_ep_p2p_dispatch writes them. workspace: at least
+ * gptoss_moe_workspace_bytes(world_size * capacity, 1, num_experts / world_size, H, I).
+ * Serves steps for which gptoss_ep_p2p_layer_fits() is 1 (T <= 64, T * top_k <= 256,
+ * world_size * capacity <= 1024 received rows, few rows per local expert); every rank must
+ * take it in the same step. gptoss_set_ep_layer_kernel(0) turns it off (returns the previous
+ * setting). */
+int gptoss_set_ep_layer_kernel(int enable);
+int gptoss_ep_p2p_layer_fits(int64_t num_tokens, int top_k, int num_experts, int world_size,
+                             int64_t hidden_size, int64_t intermediate_size, int64_t capacity);
+int gptoss_ep_p2p_layer_forward(const void* hidden, const void* router_weight, const void* router_bias,
+                                const int64_t* router_indices, const float* routing_weights,
+                                int64_t num_tokens, int top_k, int num_experts, int world_size, int rank,
+                                int64_t hidden_size, int64_t intermediate_size,
+                                const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                                int64_t ldb_gate_up, const float* gate_up_bias, const uint8_t* down_data,
+                                const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                                float swiglu_alpha, float swiglu_limit, int64_t capacity, void* local_base,
+                                const uint64_t* peer_bases, int32_t epoch, void* out,
+                                int64_t* router_indices_out, void* router_scores_out,
+                                float* routing_weights_out, int32_t* send_counts, int32_t* pos_of,
+                                void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

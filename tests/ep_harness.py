@@ -216,6 +216,59 @@ def nccl_worker(rank: int, world: int, port: int, shapes, q):
         dist.destroy_process_group()
 
 
+def p2p_layer_worker(rank: int, world: int, port: int, steps: int, q):
+    """One rank on cuda:rank running decode-sized expert-parallel layer steps over peer
+    memory (T = 32 tokens per rank, E = 32, H = I = 2880, capacity T x k): each step once in
+    one launch (decode_layer_kernel<true>) and once in five launches, on the same inputs,
+    and the single-GPU layer on the same tokens. Every rank toggles the path in the same
+    step (all ranks must take the same one)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        import __graft_entry__ as ge
+        from helpers import build_experts, build_layer, rel_l2
+
+        pkg = ge.load_package()
+        pkg.ensure_custom_op_registered()
+        EP = pkg.ep
+        e_tot, hs, isz, T, k = 32, 2880, 2880, 32, 4
+        d = O.synth_layer(SEED, E=e_tot, H=hs, I=isz, T=1)
+        wn = O.numpy_weights(d)
+        full = build_experts(pkg, d, dev, e_tot, hs, isz)
+        local = EP.shard_experts(full, rank, world)
+        epx = EP.ExpertParallelExperts(local, e_tot, capacity_tokens=T, transport="p2p", top_k=k)
+        layer = EP.ExpertParallelMoELayer(d["router_w"].to(dev), d["router_b"].to(dev), k, epx)
+        single = build_layer(pkg, d, dev, e_tot, hs, isz, k)
+        fits = pkg.ops.ep_p2p_layer_fits(T, k, e_tot, world, hs, isz, T * k)
+        results = []
+        g = torch.Generator().manual_seed(700 + rank)
+        for step in range(steps):
+            h = torch.randn(T, hs, generator=g).to(torch.bfloat16).to(dev)
+            o1, s1, i1 = layer(h)                     # one launch
+            prev = pkg.ops.set_ep_layer_kernel(False)
+            o5, s5, i5 = layer(h)                     # five launches
+            pkg.ops.set_ep_layer_kernel(prev)
+            o_s, s_s, i_s = single(h)
+            torch.cuda.synchronize()
+            st = pkg.ops.read_status(dev)
+            ref = O.w4a8_experts_forward(h.cpu(), i1.cpu().numpy(), s1.float().cpu().numpy(), wn)
+            results.append((fits, st, bool(torch.equal(o1, o5)), bool(torch.equal(i1, i5) and torch.equal(s1, s5)),
+                            bool(torch.equal(i1, i_s) and torch.equal(s1, s_s)), rel_l2(o1.cpu(), o_s.cpu()),
+                            rel_l2(o1.cpu(), ref)))
+        epx.close()
+        q.put((rank, results, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        import traceback
+
+        q.put((rank, None, repr(e) + traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
 def dead_peer_worker(rank: int, world: int, port: int, q):
     """Failure detection on the host: both ranks run one expert-parallel step, then rank 1
     leaves without joining the next one (it exits between steps, nothing in flight). Rank 0's

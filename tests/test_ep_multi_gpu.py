@@ -5,7 +5,7 @@ the single-GPU layer's bit for bit."""
 import pytest
 import torch
 
-from ep_harness import nccl_worker, run_ranks
+from ep_harness import nccl_worker, p2p_layer_worker, run_ranks
 
 pytestmark = pytest.mark.gpu
 
@@ -36,3 +36,18 @@ def test_nccl_expert_parallel(world_cap):
             else:
                 _, e_tot, hs, st, same_idx, same_scores, r, _ = row
                 assert st == 0 and same_idx and same_scores and r <= 1e-2, (rank, row)
+
+
+def test_p2p_one_launch_layer_multi_gpu():
+    # decode-sized steps over peer memory in one launch per rank, on every GPU of the box
+    # (up to 8): bit-exact against the five-launch path on the same inputs, routing equal to
+    # the single-GPU layer's, the output within 1e-2 rel-L2 of it and of the oracle, buffers
+    # reused over several epochs
+    world = _world()
+    res = run_ranks(p2p_layer_worker, world, 3, timeout=600)
+    for rank, (out, err) in enumerate(res):
+        assert err is None, f"rank {rank}: {err}"
+        for step, (fits, st, same5, same_route5, same_route1, r_single, r_ref) in enumerate(out):
+            assert fits and st == 0, (rank, step, fits, st)
+            assert same5 and same_route5, (rank, step, "one launch vs five launches")
+            assert same_route1 and r_single <= 1e-2 and r_ref <= 1e-2, (rank, step, r_single, r_ref)
