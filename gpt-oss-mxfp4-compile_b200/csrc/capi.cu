@@ -1689,6 +1689,9 @@ int gptoss_ep_p2p_combine(const void* local_base, int world_size, int64_t capaci
 // expert under balanced routing (capacity / local experts: 32 at 8 ranks x 32 tokens x top-4
 // on 32 experts) the one launch wins; above it the five-launch path picks its own layout.
 constexpr int64_t kEpLayerMaxRowsPerExpert = 64;
+// Expert weights the one-launch kernel pulls into L2 under its routing and exchange phases
+// (about half of the 126 MB L2: all of a rank's experts at 8 ranks of GPT-OSS-20B, 53 MB).
+constexpr int64_t kEpLayerL2PrefetchBytes = 64ll << 20;
 std::atomic<int> g_ep_layer_enabled{1};
 
 bool ep_layer_fits(int64_t T, int k, int E, int world, int64_t H, int64_t I, int64_t cap) {
@@ -1802,6 +1805,11 @@ int gptoss_ep_p2p_layer_forward(const void* hidden, const void* router_weight, c
   p.ep_world = world_size; p.ep_rank = rank; p.ep_epr = epr; p.ep_rb = rb; p.ep_cap = capacity;
   p.ep_local = static_cast<uint8_t*>(local_base); p.ep_peer_bases = peer_bases; p.ep_epoch = epoch;
   p.ep_send_counts = send_counts; p.ep_pos_of = pos_of;
+  p.wgu = wt.gu_data; p.wdn = wt.dn_data;
+  p.wgu_bytes = static_cast<int64_t>(epr) * 2 * I * (Kh / 2);
+  p.wdn_bytes = static_cast<int64_t>(epr) * hidden_size * (Ki / 2);
+  // only when all of this rank's weights fit: a partial warm-up measured no gain at 2 ranks
+  p.l2_prefetch_bytes = p.wgu_bytes + p.wdn_bytes <= kEpLayerL2PrefetchBytes ? kEpLayerL2PrefetchBytes : 0;
   GemmParams g1{};
   g1.num_experts = epr; g1.N = static_cast<int>(2 * I); g1.K = static_cast<int>(Kh); g1.num_kb = p.kb1;
   g1.err = status; g1.out = w.inter_codes; g1.ld_out = I; g1.bias = wt.gu_bias; g1.out_sf = w.inter_sf;

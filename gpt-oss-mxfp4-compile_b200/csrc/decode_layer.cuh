@@ -114,10 +114,18 @@ struct DecodeLayerParams {
   int32_t ep_epoch;
   int32_t* ep_send_counts;         // [W] rows sent to each owner (output)
   int32_t* ep_pos_of;              // [T, K] the assignment's row in the exchange (output)
+  // L2 warm-up while the routing and the exchange run: the first l2_prefetch_bytes of the
+  // local experts' weights in the order the tiles consume them (gate_up experts 0.., then
+  // down experts 0..), each CTA a 1/G share (0: none)
+  const uint8_t* wgu;              // [E, 2I, H/2]
+  const uint8_t* wdn;              // [E, H, I/2]
+  int64_t wgu_bytes, wdn_bytes;    // all local experts of each tensor
+  int64_t l2_prefetch_bytes;
 };
 
 // Received rows one rank of the expert-parallel kernel can hold (W x cap <= this).
 constexpr int kEpMaxRecv = 1024;
+static_assert(3 * kEpMaxRecv * 4 <= DlCfg::kEpiStageBytes, "received-row headers are staged in the epilogue buffer");
 
 // Per-CTA routing state in shared memory.
 template <bool EP>
@@ -145,6 +153,7 @@ struct DlSharedT<true> {
   float rw[kDlMaxAssign];          // local assignment -> routing weight
   int32_t dslot[kDlMaxAssign];     // local assignment -> owner x cap + slot (-1: not sent)
   int dcnt[kP2pMaxWorld];          // rows sent to each owner
+  int rpre[kP2pMaxWorld + 1];      // received rows: exclusive prefix of the sources' counts
   uint64_t tq_bar[kDlQueue];
   int tq[kDlQueue];
 };
@@ -308,6 +317,25 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     const int phi = static_cast<int>(static_cast<int64_t>(np) * (cta + 1) / G);
     for (int pr = plo + warp; pr < phi; pr += nthr / 32)
       if (lane == 0) bulk_prefetch_l2(p.router_w + static_cast<int64_t>(pr % E) * H, static_cast<uint32_t>(H) * 2u);
+  }
+  if constexpr (EP) {
+    // Expert-parallel steps stream only this rank's experts: up to a budget that L2 holds,
+    // pull them into L2 under the routing and the exchange (the tiles that follow the
+    // pre-loaded first stages then read L2 instead of HBM). Weights are not written upstream.
+    if (warp == 3 && lane == 0 && p.l2_prefetch_bytes > 0) {
+      const int64_t total = min(p.l2_prefetch_bytes, p.wgu_bytes + p.wdn_bytes);
+      const int64_t lo = (total * cta / G) & ~static_cast<int64_t>(15);
+      const int64_t hi = cta == G - 1 ? total : (total * (cta + 1) / G) & ~static_cast<int64_t>(15);
+      constexpr int64_t kPiece = 64 * 1024;
+      for (int64_t o = lo; o < hi; o += kPiece) {
+        const int64_t n = min(kPiece, hi - o);
+        if (o < p.wgu_bytes) {
+          bulk_prefetch_l2(p.wgu + o, static_cast<uint32_t>(min(n, p.wgu_bytes - o)));
+        } else {
+          bulk_prefetch_l2(p.wdn + (o - p.wgu_bytes), static_cast<uint32_t>(n));
+        }
+      }
+    }
   }
   pdl_trigger();
   pdl_wait();
@@ -490,6 +518,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     // ================================================================ dispatch
     const int W = p.ep_world, epr = p.ep_epr, rb = p.ep_rb;
     const int64_t cap = p.ep_cap;
+    __syncthreads();   // every thread's S.ridx / S.rw (the top-k's or the given routing) is in
     // owner q = expert / epr; slot j = the assignment's stable rank among those to q
     if (warp == 0) {
       for (int q = lane; q < W; q += 32) S.dcnt[q] = 0;
@@ -518,7 +547,12 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
           p.rw_out[i] = S.rw[i];
         }
       }
-      for (int q = tid; q < W; q += nthr) p.ep_send_counts[q] = min(static_cast<int64_t>(S.dcnt[q]), cap);
+      for (int q = tid; q < W; q += nthr) {
+        const int32_t c = static_cast<int32_t>(min(static_cast<int64_t>(S.dcnt[q]), cap));
+        p.ep_send_counts[q] = c;
+        // the owner reads how many rows this rank sent (published by the dispatch flag)
+        reinterpret_cast<int32_t*>(p.ep_peer_bases[q])[kP2pSendCounts + p.ep_rank] = c;
+      }
       for (int i = tid; i < A; i += nthr) p.ep_pos_of[i] = S.dslot[i];
     }
     // this CTA's local assignments cta, cta + G, ...: FP8 codes and UE8M0 scales straight into
@@ -571,18 +605,33 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
       }
     }
     __syncthreads();
-    if (tid == 0)
+    if (tid < 32)
       p2p_last_cta_signal(reinterpret_cast<int32_t*>(p.ep_local) + kP2pCounterDispatch, p.ep_peer_bases, W,
                           p.ep_rank, p.ep_epoch);
     // ================================================================ receive
     p2p_wait_flags(reinterpret_cast<const int32_t*>(p.ep_local), 0, W, p.ep_epoch, p.err);
-    const int R = static_cast<int>(W * cap);
-    // row headers (local expert, routing weight) in the epilogue staging, free until the GEMMs
-    int* hexp = reinterpret_cast<int*>(epi_f);
-    float* hw = epi_f + kEpMaxRecv;
+    // the valid rows: source s sent rows [0, count_s) of its segment (its count travels with
+    // its flag), so only those headers are read, in (source, slot) order
+    if (tid == 0) {
+      int acc = 0;
+      for (int src = 0; src < W; ++src) {
+        S.rpre[src] = acc;
+        acc += min(max(__ldcg(reinterpret_cast<const int32_t*>(p.ep_local) + kP2pSendCounts + src), 0),
+                   static_cast<int>(cap));
+      }
+      S.rpre[W] = acc;
+    }
     for (int e = tid; e < EG; e += nthr) S.cnt[e] = 0;
     __syncthreads();
-    for (int r = tid; r < R; r += nthr) {
+    const int nvalid = S.rpre[W];
+    // row headers (local expert, routing weight, row) in the epilogue staging, free until the GEMMs
+    int* hexp = reinterpret_cast<int*>(epi_f);
+    float* hw = epi_f + kEpMaxRecv;
+    int* hrow = reinterpret_cast<int*>(epi_f + 2 * kEpMaxRecv);
+    for (int v = tid; v < nvalid; v += nthr) {
+      int src = 0;
+      while (S.rpre[src + 1] <= v) ++src;
+      const int r = static_cast<int>(src * cap) + (v - S.rpre[src]);
       const int32_t* meta = reinterpret_cast<const int32_t*>(recv + static_cast<int64_t>(r) * rb + rb - 8);
       int e = __ldcg(meta);
       const float wv = __int_as_float(__ldcg(meta + 1));
@@ -590,22 +639,23 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
         if (cta == 0) atomicCAS(p.err, 0, 0x201);
         e = -1;
       }
-      hexp[r] = e;
-      hw[r] = wv;
+      hexp[v] = e;
+      hw[v] = wv;
+      hrow[v] = r;
       if (e >= 0) atomicAdd(&S.cnt[e], 1);
     }
     __syncthreads();
     if (warp == 0) {
       scan_counts();
       // stable positions over the received rows (source rank, then slot)
-      for (int i0 = 0; i0 < R; i0 += 32) {
-        const int r = i0 + lane;
-        const int e = r < R ? hexp[r] : -2;
+      for (int i0 = 0; i0 < nvalid; i0 += 32) {
+        const int v = i0 + lane;
+        const int e = v < nvalid ? hexp[v] : -2;
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         if (e >= 0) {
           const int pos = S.run[e] + __popc(peers & ((1u << lane) - 1u));
-          S.tok[pos] = r;
-          S.w[pos] = hw[r];
+          S.tok[pos] = hrow[v];
+          S.w[pos] = hw[v];
           S.sexp[pos] = static_cast<uint8_t>(e);
         }
         __syncwarp();
@@ -981,7 +1031,7 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
     // every GEMM2 store of this CTA is behind the barrier above: the last CTA raises this
     // rank's return flag on every peer; then every CTA waits for all owners' flags and sums
     // its tokens' returned rows
-    if (tid == 0)
+    if (tid < 32)
       p2p_last_cta_signal(reinterpret_cast<int32_t*>(p.ep_local) + kP2pCounterReturn, p.ep_peer_bases, p.ep_world,
                           p.ep_world + p.ep_rank, p.ep_epoch);
     p2p_wait_flags(reinterpret_cast<const int32_t*>(p.ep_local), p.ep_world, p.ep_world, p.ep_epoch, p.err);

@@ -31,10 +31,12 @@ namespace gptoss {
 
 constexpr int kP2pMaxWorld = 64;
 constexpr int kDevTimeoutPeer = 0x301;    // a peer's flag did not arrive within the timeout
-// header: dispatch flags [0, 64), return flags [64, 128), completion counters [128, 130)
+// header (int32 words): dispatch flags [0, 64), return flags [64, 128), completion counters
+// [128, 130), rows each source sent in the current call [192, 256) (written before its flag)
 constexpr uint32_t kP2pFlagBytes = 4 * kP2pMaxWorld * 4;
 constexpr int kP2pCounterDispatch = 2 * kP2pMaxWorld;
 constexpr int kP2pCounterReturn = 2 * kP2pMaxWorld + 1;
+constexpr int kP2pSendCounts = 3 * kP2pMaxWorld;
 
 __host__ __device__ __forceinline__ int64_t p2p_recv_offset(int rank_s, int64_t cap, int64_t rb) {
   return kP2pFlagBytes + static_cast<int64_t>(rank_s) * cap * rb;
@@ -54,6 +56,19 @@ __device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
 }
 __device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(int32_t* p, int32_t v) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Raise flags[slot] of every peer to `epoch`, called by the 32 lanes of one warp after a
+// system-scope fence of everything the caller published: one fence, then the W flag stores
+// in parallel from separate lanes (W release stores from one thread would each wait for the
+// previous one's NVLink round trip).
+__device__ __forceinline__ void p2p_raise_flags_warp(const uint64_t* peer_bases, int world, int slot, int32_t epoch) {
+  __threadfence_system();
+  for (int q = static_cast<int>(threadIdx.x & 31u); q < world; q += 32)
+    st_relaxed_sys(reinterpret_cast<int32_t*>(peer_bases[q]) + slot, epoch);
 }
 
 // Thread 0 waits until flags[first .. first + n) all reach `epoch` (bounded by
@@ -75,18 +90,22 @@ __device__ __forceinline__ void p2p_wait_flags(const int32_t* flags, int first, 
   __syncthreads();
 }
 
-// Called by thread 0 of every CTA after the CTA's stores to the peers: the last CTA to
-// get here raises flags[slot] on every peer to `epoch` (the threadfence-reduction pattern:
-// every CTA fences its stores at system scope before counting itself) and resets the
-// counter for the next call.
+// Called by the 32 lanes of warp 0 of every CTA after the CTA's stores to the peers (behind
+// a CTA barrier): the last CTA to get here raises flags[slot] on every peer to `epoch` (the
+// threadfence-reduction pattern: every CTA fences its stores at system scope before counting
+// itself) and resets the counter for the next call.
 __device__ __forceinline__ void p2p_last_cta_signal(int32_t* counter, const uint64_t* peer_bases, int world,
                                                     int slot, int32_t epoch) {
-  __threadfence_system();
-  const int prev = atomicAdd(counter, 1);
-  if (prev == static_cast<int>(gridDim.x * gridDim.y * gridDim.z) - 1) {
+  int prev = 0;
+  if ((threadIdx.x & 31u) == 0) {
     __threadfence_system();
-    for (int q = 0; q < world; ++q) st_release_sys(reinterpret_cast<int32_t*>(peer_bases[q]) + slot, epoch);
-    atomicExch(counter, 0);
+    prev = atomicAdd(counter, 1);
+  }
+  prev = __shfl_sync(0xffffffffu, prev, 0);
+  if (prev == static_cast<int>(gridDim.x * gridDim.y * gridDim.z) - 1) {
+    p2p_raise_flags_warp(peer_bases, world, slot, epoch);
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) atomicExch(counter, 0);
   }
 }
 
@@ -164,7 +183,7 @@ __global__ void __launch_bounds__(256) ep_pack_p2p_kernel(
   ep_pack_p2p_row(hidden, H, K, experts_per_rank, router_indices, routing_weights, sorted_src, cap, world, rank,
                   dest_counts, dest_offsets, tpr, peer_bases, pos_of);
   __syncthreads();
-  if (threadIdx.x == 0) p2p_last_cta_signal(counter, peer_bases, world, rank, epoch);
+  if (threadIdx.x < 32) p2p_last_cta_signal(counter, peer_bases, world, rank, epoch);
 }
 
 
@@ -206,7 +225,7 @@ __global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16*
     for (int v = threadIdx.x; v < H / 8; v += blockDim.x) dst[v] = src[v];
   }
   __syncthreads();
-  if (threadIdx.x == 0) p2p_last_cta_signal(counter, peer_bases, world, world + rank, epoch);
+  if (threadIdx.x < 32) p2p_last_cta_signal(counter, peer_bases, world, world + rank, epoch);
 }
 
 // ---------------------------------------------------------------- receiving rank, one launch

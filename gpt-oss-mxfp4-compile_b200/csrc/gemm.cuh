@@ -868,7 +868,7 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
   if constexpr (EPI == kEpiGemm2 && SWAP) {
     // every epilogue store of this CTA is behind the barrier: publish them (one fence per
     // CTA, then the last CTA raises the return flags)
-    if (p.ep_world > 0 && threadIdx.x == 0)
+    if (p.ep_world > 0 && threadIdx.x < 32)
       p2p_last_cta_signal(p.ep_counter, p.ep_peer_bases, p.ep_world, p.ep_world + p.ep_rank, p.ep_epoch);
   }
   if (warp == 1) {

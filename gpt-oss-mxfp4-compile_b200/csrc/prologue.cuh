@@ -179,10 +179,7 @@ __device__ __forceinline__ void ep_dispatch_phase4(const DecodePrologueParams& p
   }
   __threadfence_system();
   cluster_sync();
-  if (rank == 0 && tid == 0) {
-    __threadfence_system();
-    for (int q = 0; q < W; ++q) st_release_sys(reinterpret_cast<int32_t*>(p.peer_bases[q]) + p.ep_rank, p.epoch);
-  }
+  if (rank == 0 && tid < 32) p2p_raise_flags_warp(p.peer_bases, W, p.ep_rank, p.epoch);
 }
 
 // grid = kDpCluster CTAs forming one cluster; blockDim = kDpThreads.
