@@ -42,6 +42,11 @@ _SIGNATURES = {
     "gptoss_fp4_group_mm_w4a4": (_i, [_vp, _vp, _c_int64, _c_int64, _vp, _i, _c_int64, _c_int64, _vp, _vp,
                                       _c_int64, _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "gptoss_moe_workspace_bytes": (_sz, [_c_int64, _i, _i, _c_int64, _c_int64]),
+    "gptoss_moe_block_workspace_bytes": (_sz, [_c_int64, _i, _i, _c_int64, _c_int64]),
+    "gptoss_moe_block_forward": (_i, [_vp, _vp, _f, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64,
+                                      _vp, _vp, _c_int64, _vp, _vp, _vp, _c_int64, _vp,
+                                      _f, _f, _vp, _vp, _vp, _vp, _sz, _i, _vp, _vp]),
+    "gptoss_rmsnorm_residual": (_i, [_vp, _vp, _f, _c_int64, _c_int64, _vp, _vp, _vp]),
     "gptoss_moe_experts_forward": (_i, [_vp, _vp, _vp, _c_int64, _i, _i, _c_int64, _c_int64,
                                         _vp, _vp, _c_int64, _vp, _vp, _vp, _c_int64, _vp,
                                         _f, _f, _vp, _vp, _sz, _i, _vp, _vp]),

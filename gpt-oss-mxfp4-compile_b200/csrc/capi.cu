@@ -590,7 +590,8 @@ bool decode_layer_fits(int64_t T, int k, int E, int64_t H, int64_t I, GemmLayout
 
 int run_decode_layer(const void* hidden, const RouterArgs* ra, const int64_t* ridx, const float* rw, int64_t T, int k,
                      int E, int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit, void* out,
-                     uint8_t* ws, const Workspace& L, int* status, const DeviceInfo& di, int dev, cudaStream_t st) {
+                     uint8_t* ws, const Workspace& L, int* status, const DeviceInfo& di, int dev, cudaStream_t st,
+                     bool out_prefilled = false) {
   const WsPtrs w = ws_ptrs(ws, L);
   const int64_t A = T * k, Kh = pad128(H), Ki = pad128(I);
   CUtensorMap ta, ti, tgu, tdn;
@@ -622,6 +623,7 @@ int run_decode_layer(const void* hidden, const RouterArgs* ra, const int64_t* ri
   }
   p.T = static_cast<int>(T); p.H = static_cast<int>(H); p.I = static_cast<int>(I); p.E = E; p.K = k;
   p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_prefilled = out_prefilled ? 1 : 0;
   p.logits = reinterpret_cast<float*>(ws + L.dl_logits);
   p.sorted_token = w.sorted_token; p.sorted_expert = w.sorted_expert; p.sorted_weight = w.sorted_weight;
   p.counts = w.counts; p.offsets = w.offsets; p.sf_offsets_a = w.sfoff_a; p.sf_offsets_b = w.sfoff_b;
@@ -654,29 +656,30 @@ int run_decode_layer(const void* hidden, const RouterArgs* ra, const int64_t* ri
 int experts_pipeline(const void* hidden, const int64_t* ridx, const float* rw, int64_t T, int k, int E,
                      int64_t H, int64_t I, const ExpertWeights& wt, float sw_alpha, float sw_limit, void* out,
                      uint8_t* ws, const Workspace& L, int mode, int* status, const DeviceInfo& di, int dev,
-                     cudaStream_t st, const RouterArgs* ra = nullptr) {
+                     cudaStream_t st, const RouterArgs* ra = nullptr, bool out_prefilled = false) {
   const WsPtrs w = ws_ptrs(ws, L);
   const GemmLayout lay = pick_layout(mode, T * k, E);
   if (decode_layer_fits(T, k, E, H, I, lay, di.sms))
     return run_decode_layer(hidden, ra, ridx, rw, T, k, E, H, I, wt, sw_alpha, sw_limit, out, ws, L, status, di, dev,
-                            st);
+                            st, out_prefilled);
   size_t smem = 0;
   int slice = 0;
   // While the one-launch decode prologue runs on kDpCluster SMs, GEMM1 (launched behind it
   // with programmatic serialisation) pulls its first weight tiles into L2.
   int prefetch = 0;
   if (decode_prologue_fits(T, k, E, H, ra != nullptr, &smem, &slice)) {
-    GPTOSS_TRY(run_decode_prologue(hidden, ra, ridx, rw, T, k, E, H, I, w, lay.spread, out, status, smem, slice, dev, st));
+    GPTOSS_TRY(run_decode_prologue(hidden, ra, ridx, rw, T, k, E, H, I, w, lay.spread, out_prefilled ? nullptr : out,
+                                   status, smem, slice, dev, st));
     prefetch = kPrefetchTilesAfterPrologue;
   } else {
     if (ra != nullptr) {
       GPTOSS_TRY(router_launch(hidden, ra->weight, ra->bias, T, H, E, k, ra->ridx_out, ra->scores_out, ra->rw_out,
-                               nullptr, out, H, di.sms, dev, st));
+                               nullptr, out_prefilled ? nullptr : out, H, di.sms, dev, st));
       ridx = ra->ridx_out;
       rw = ra->rw_out;
     }
     GPTOSS_TRY(stage_route_quant(hidden, ridx, rw, T, k, E, H, I, w, lay.spread, status, st));
-    if (ra == nullptr)
+    if (ra == nullptr && !out_prefilled)
       GPTOSS_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(T * H) * sizeof(__nv_bfloat16), st));
   }
   GPTOSS_TRY(stage_gemm1(T * k, E, H, I, wt, sw_alpha, sw_limit, w, lay, status, di, dev, st, prefetch));
@@ -1112,6 +1115,69 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight, cons
                           status_dev ? status_dev : di.status_sink, di, dev, st, &ra);
 }
 
+
+size_t gptoss_moe_block_workspace_bytes(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                                        int64_t intermediate_size) {
+  if (num_tokens < 0 || top_k < 1 || num_experts < 1 || hidden_size <= 0 || intermediate_size <= 0) return 0;
+  return plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size).total +
+         align256(static_cast<size_t>(num_tokens * hidden_size) * sizeof(__nv_bfloat16));
+}
+
+int gptoss_rmsnorm_residual(const void* x, const void* weight, float eps, int64_t num_tokens, int64_t hidden_size,
+                            void* xn, void* residual_out, void* stream) {
+  NvtxRange nvtx_range("gptoss_rmsnorm_residual");
+  GPTOSS_CHECK(num_tokens >= 0 && num_tokens < (1LL << 31), "rmsnorm: bad num_tokens");
+  GPTOSS_CHECK(hidden_size > 0 && hidden_size % 8 == 0, "rmsnorm: hidden size must be a multiple of 8");
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(x && weight && xn, "rmsnorm: null pointer");
+  GPTOSS_CHECK(aligned(x, 16) && aligned(weight, 16) && aligned(xn, 16) && (!residual_out || aligned(residual_out, 16)),
+               "rmsnorm: misaligned pointer");
+  return launch_pdl(rmsnorm_residual_kernel, dim3(static_cast<unsigned>((num_tokens + 7) / 8)), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                    static_cast<const __nv_bfloat16*>(weight), eps, static_cast<int>(num_tokens),
+                    static_cast<int>(hidden_size), static_cast<__nv_bfloat16*>(xn),
+                    static_cast<__nv_bfloat16*>(residual_out));
+}
+
+int gptoss_moe_block_forward(const void* hidden, const void* norm_weight, float norm_eps, const void* router_weight,
+                             const void* router_bias, int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
+                             int64_t intermediate_size, const uint8_t* gate_up_data, const uint8_t* gate_up_scales,
+                             int64_t ldb_gate_up, const float* gate_up_bias, const uint8_t* down_data,
+                             const uint8_t* down_scales, int64_t ldb_down, const float* down_bias, float swiglu_alpha,
+                             float swiglu_limit, void* out, int64_t* router_indices_out, void* router_scores_out,
+                             void* workspace, size_t workspace_bytes, int gemm_mode, int32_t* status_dev,
+                             void* stream) {
+  NvtxRange nvtx_range("gptoss_moe_block_forward");
+  GPTOSS_TRY(check_dims(num_tokens, top_k, num_experts, hidden_size, intermediate_size));
+  GPTOSS_CHECK(gemm_mode >= 0 && gemm_mode <= 3, "bad gemm_mode");
+  GPTOSS_CHECK(hidden_size % 8 == 0, "hidden size must be a multiple of 8");
+  DeviceInfo di;
+  GPTOSS_TRY(bind_device(gate_up_data, "gate_up_proj_data", &di));
+  ExpertWeights w{gate_up_data, gate_up_scales, ldb_gate_up, gate_up_bias,
+                  down_data, down_scales, ldb_down, down_bias};
+  GPTOSS_TRY(check_expert_weights(w, hidden_size, intermediate_size, num_experts));
+  if (num_tokens == 0) return GPTOSS_OK;
+  GPTOSS_CHECK(hidden && norm_weight && router_weight && router_bias && out && workspace, "block_forward: null pointer");
+  GPTOSS_CHECK(aligned(hidden, 16) && aligned(norm_weight, 16) && aligned(router_weight, 16) && aligned(out, 16) &&
+                   aligned(workspace, 256),
+               "block_forward: misaligned pointer");
+  const Workspace L = plan_workspace(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  const size_t need = gptoss_moe_block_workspace_bytes(num_tokens, top_k, num_experts, hidden_size, intermediate_size);
+  if (workspace_bytes < need) return fail(GPTOSS_ERR_WORKSPACE, "workspace has %zu bytes, need %zu", workspace_bytes, need);
+  int dev = 0;
+  GPTOSS_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* xn = ws + L.total;   // the normalised rows, behind the layer's workspace
+  // out = hidden (the residual GEMM2 adds into), xn = RMSNorm(hidden)
+  GPTOSS_TRY(gptoss_rmsnorm_residual(hidden, norm_weight, norm_eps, num_tokens, hidden_size, xn, out, stream));
+  int64_t* ridx = router_indices_out ? router_indices_out : reinterpret_cast<int64_t*>(ws + L.router_idx);
+  float* rw = reinterpret_cast<float*>(ws + L.router_w);
+  const RouterArgs ra{router_weight, router_bias, ridx, router_scores_out, rw};
+  return experts_pipeline(xn, nullptr, nullptr, num_tokens, top_k, num_experts, hidden_size, intermediate_size,
+                          w, swiglu_alpha, swiglu_limit, out, ws, L, gemm_mode,
+                          status_dev ? status_dev : di.status_sink, di, dev, st, &ra, true);
+}
 
 int gptoss_moe_workspace_layout(int64_t num_tokens, int top_k, int num_experts, int64_t hidden_size,
                                 int64_t intermediate_size, int64_t* offsets_out) {

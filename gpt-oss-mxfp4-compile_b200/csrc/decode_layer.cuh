@@ -121,6 +121,7 @@ struct DecodeLayerParams {
   const uint8_t* wdn;              // [E, H, I/2]
   int64_t wgu_bytes, wdn_bytes;    // all local experts of each tensor
   int64_t l2_prefetch_bytes;
+  int out_prefilled;               // `out` already holds the rows GEMM2 adds into (a residual)
 };
 
 // Received rows one rank of the expert-parallel kernel can hold (W x cap <= this).
@@ -341,8 +342,9 @@ __global__ void __launch_bounds__(DlCfg::kThreads, 1)
   pdl_wait();
 
   // ================================================================ routing (all warps)
-  // zero this CTA's slice of `out` (GEMM2 adds into it; expert-parallel: the combine writes it)
-  if constexpr (!EP) {
+  // zero this CTA's slice of `out` (GEMM2 adds into it; expert-parallel: the combine writes it;
+  // a prefilled `out` -- the residual of a block -- is added into as it is)
+  if (!EP && !p.out_prefilled) {
     const int64_t n16 = static_cast<int64_t>(T) * H / 8;
     const int64_t lo = n16 * cta / G, hi = n16 * (cta + 1) / G;
     uint4* z = reinterpret_cast<uint4*>(p.out);

@@ -843,4 +843,53 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* __
   }
 }
 
+
+// RMSNorm in front of a MoE block (GptOssRMSNorm / F.rms_norm: fp32 mean of squares,
+// rsqrt(mean + eps), x * rsqrt * weight, one rounding to bf16), fused with the residual:
+// one warp per token reads its row once for the sum of squares and once more (from L1/L2)
+// to write the normalised row `xn` and, when `res` is set, a copy of the input into `res` --
+// the rows GEMM2 then adds the expert outputs into, so the block's residual add needs no
+// kernel of its own. x may alias res.
+__global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w,
+                                                               float eps, int T, int H, __nv_bfloat16* xn,
+                                                               __nv_bfloat16* res) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + t * H);
+  const int nv = H / 8;
+  float ss = 0.0f;
+  for (int v = lane; v < nv; v += 32) {
+    const uint4 u = xr[v];
+    const uint32_t a[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float lo = bf16_bits_lo(a[h]), hi = bf16_bits_hi(a[h]);
+      ss = fmaf(lo, lo, ss);
+      ss = fmaf(hi, hi, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), eps));
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(xn + t * H);
+  uint4* cr = res != nullptr ? reinterpret_cast<uint4*>(res + t * H) : nullptr;
+  for (int v = lane; v < nv; v += 32) {
+    const uint4 u = xr[v], g = __ldg(wr + v);
+    const uint32_t a[4] = {u.x, u.y, u.z, u.w}, b[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const __nv_bfloat162 y = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(bf16_bits_lo(a[h]), r), bf16_bits_lo(b[h])),
+                                                     __fmul_rn(__fmul_rn(bf16_bits_hi(a[h]), r), bf16_bits_hi(b[h])));
+      o[h] = *reinterpret_cast<const uint32_t*>(&y);
+    }
+    yr[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    if (cr != nullptr) cr[v] = u;
+  }
+}
+
 }  // namespace gptoss

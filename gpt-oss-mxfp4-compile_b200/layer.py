@@ -44,6 +44,22 @@ class GptOssMoELayer(nn.Module):
                               float(ex.alpha), float(ex.limit), int(ex.gemm_mode))
         return out.view(shape), scores, idx
 
+    def forward_block(self, hidden_states: torch.Tensor, norm_weight: torch.Tensor, norm_eps: float = 1e-5):
+        """The decoder block's MoE half: hidden + self(RMSNorm(hidden)) (the model's
+        residual + mlp(post_attention_layernorm(hidden))), as the MoE kernels alone: the norm
+        and the residual copy are one kernel and GEMM2 adds into the residual rows
+        (gptoss::moe_block_forward). -> (out [..., H] bf16, router_scores, router_indices)."""
+        ensure_custom_op_registered()
+        ex = self.experts
+        shape = hidden_states.shape
+        h = hidden_states.reshape(-1, self.hidden_size).contiguous()
+        fn = _ops.moe_block_forward_impl if _ops.eager_call(h) else torch.ops.gptoss.moe_block_forward
+        out, scores, idx = fn(h, norm_weight, float(norm_eps), self.router_weight, self.router_bias, int(self.top_k),
+                              ex.gate_up_proj_data, ex.gate_up_proj_scales, ex.gate_up_proj_bias,
+                              ex.down_proj_data, ex.down_proj_scales, ex.down_proj_bias,
+                              float(ex.alpha), float(ex.limit), int(ex.gemm_mode))
+        return out.view(shape), scores, idx
+
     def route(self, hidden_states: torch.Tensor):
         """Router only: (logits [T, E] bf16, scores [T, k] bf16, indices [T, k] int64)."""
         ensure_custom_op_registered()

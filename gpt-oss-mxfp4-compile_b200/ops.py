@@ -385,6 +385,48 @@ def moe_layer_forward_impl(hidden, router_weight, router_bias, top_k: int, gu_da
     return out, scores, idx
 
 
+def moe_block_forward_impl(hidden, norm_weight, norm_eps: float, router_weight, router_bias, top_k: int, gu_data,
+                           gu_scales, gu_bias, dn_data, dn_scales, dn_bias, alpha: float, limit: float,
+                           gemm_mode: int = GEMM_AUTO):
+    """hidden + layer(RMSNorm(hidden)) (gptoss_moe_block_forward) -> (out, scores, indices)."""
+    _cuda(hidden, "hidden_states")
+    _dtype(hidden, (torch.bfloat16,), "hidden_states")
+    _cuda(norm_weight, "norm weight")
+    _dtype(norm_weight, (torch.bfloat16,), "norm weight")
+    _cuda(router_weight, "router weight")
+    _dtype(router_weight, (torch.bfloat16,), "router weight")
+    _dtype(router_bias, (torch.bfloat16,), "router bias")
+    _check_weights(gu_data, gu_scales, gu_bias, dn_data, dn_scales, dn_bias)
+    T, H = hidden.shape
+    E = gu_data.shape[0]
+    I = gu_data.shape[1] // 2
+    dev = hidden.device
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=dev)
+    scores = torch.empty((T, top_k), dtype=torch.bfloat16, device=dev)
+    st = _stream(dev)
+    ws = _scratch(dev, st, int(_lib.query("gptoss_moe_block_workspace_bytes", T, top_k, E, H, I)))
+    _lib.call("gptoss_moe_block_forward", hidden.data_ptr(), norm_weight.data_ptr(), float(norm_eps),
+              router_weight.data_ptr(), router_bias.data_ptr(), T, top_k, E, H, I, gu_data.data_ptr(),
+              gu_scales.data_ptr(), gu_scales.numel() // E, gu_bias.data_ptr(), dn_data.data_ptr(),
+              dn_scales.data_ptr(), dn_scales.numel() // E, dn_bias.data_ptr(), float(alpha), float(limit),
+              out.data_ptr(), idx.data_ptr(), scores.data_ptr(), ws.data_ptr(), ws.numel(), int(gemm_mode),
+              status_tensor(dev).data_ptr(), st)
+    return out, scores, idx
+
+
+def rmsnorm_residual(x, weight, eps: float):
+    """(RMSNorm(x) bf16, copy of x) from one kernel (gptoss_rmsnorm_residual)."""
+    _cuda(x, "x")
+    _dtype(x, (torch.bfloat16,), "x")
+    T, H = x.shape
+    xn = torch.empty_like(x)
+    res = torch.empty_like(x)
+    _lib.call("gptoss_rmsnorm_residual", x.data_ptr(), weight.data_ptr(), float(eps), T, H, xn.data_ptr(),
+              res.data_ptr(), _stream(x.device))
+    return xn, res
+
+
 # ------------------------------------------------------------------ registration
 _registered = False
 _reg_lock = threading.Lock()
@@ -480,6 +522,24 @@ def register_ops() -> None:
         @moe_layer_forward.register_fake
         def _(hidden, router_weight, router_bias, top_k, gate_up_data, gate_up_scales, gate_up_bias, down_data,
               down_scales, down_bias, alpha, limit, gemm_mode):
+            T = hidden.shape[0]
+            return (torch.empty_like(hidden), hidden.new_empty((T, top_k)),
+                    torch.empty((T, top_k), dtype=torch.int64, device=hidden.device))
+
+        @torch.library.custom_op("gptoss::moe_block_forward", mutates_args=())
+        def moe_block_forward(hidden: torch.Tensor, norm_weight: torch.Tensor, norm_eps: float,
+                              router_weight: torch.Tensor, router_bias: torch.Tensor, top_k: int,
+                              gate_up_data: torch.Tensor, gate_up_scales: torch.Tensor, gate_up_bias: torch.Tensor,
+                              down_data: torch.Tensor, down_scales: torch.Tensor, down_bias: torch.Tensor,
+                              alpha: float, limit: float, gemm_mode: int
+                              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+            return moe_block_forward_impl(hidden, norm_weight, norm_eps, router_weight, router_bias, top_k,
+                                          gate_up_data, gate_up_scales, gate_up_bias, down_data, down_scales,
+                                          down_bias, alpha, limit, gemm_mode)
+
+        @moe_block_forward.register_fake
+        def _(hidden, norm_weight, norm_eps, router_weight, router_bias, top_k, gate_up_data, gate_up_scales,
+              gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode):
             T = hidden.shape[0]
             return (torch.empty_like(hidden), hidden.new_empty((T, top_k)),
                     torch.empty((T, top_k), dtype=torch.int64, device=hidden.device))

@@ -233,6 +233,29 @@ int gptoss_moe_layer_forward(const void* hidden, const void* router_weight,
                              void* router_scores_out, void* workspace, size_t workspace_bytes,
                              int gemm_mode, int32_t* status_dev, void* stream);
 
+/* The decoder block around the MoE layer, for stacks of layers (the reference's model runs
+ * it as residual + mlp(post_attention_layernorm(hidden)), repro_compile_hftf.py:103-107
+ * compiling the whole model): out = hidden + layer(RMSNorm(hidden)), RMSNorm as GptOssRMSNorm
+ * (fp32 mean of squares, rsqrt(mean + norm_eps), times norm_weight [H] bf16, one rounding).
+ * The norm and the residual copy are one kernel (gptoss_rmsnorm_residual) and GEMM2 adds the
+ * expert outputs straight into the residual rows, so a block is the MoE kernels only. out
+ * may alias hidden. workspace: gptoss_moe_block_workspace_bytes(). */
+size_t gptoss_moe_block_workspace_bytes(int64_t num_tokens, int top_k, int num_experts,
+                                        int64_t hidden_size, int64_t intermediate_size);
+int gptoss_moe_block_forward(const void* hidden, const void* norm_weight, float norm_eps,
+                             const void* router_weight, const void* router_bias, int64_t num_tokens,
+                             int top_k, int num_experts, int64_t hidden_size,
+                             int64_t intermediate_size, const uint8_t* gate_up_data,
+                             const uint8_t* gate_up_scales, int64_t ldb_gate_up,
+                             const float* gate_up_bias, const uint8_t* down_data,
+                             const uint8_t* down_scales, int64_t ldb_down, const float* down_bias,
+                             float swiglu_alpha, float swiglu_limit, void* out,
+                             int64_t* router_indices_out, void* router_scores_out, void* workspace,
+                             size_t workspace_bytes, int gemm_mode, int32_t* status_dev, void* stream);
+/* xn = RMSNorm(x) as above; residual_out (may be NULL, may alias x) = a copy of x. */
+int gptoss_rmsnorm_residual(const void* x, const void* weight, float eps, int64_t num_tokens,
+                            int64_t hidden_size, void* xn, void* residual_out, void* stream);
+
 /* ---- The expert forward as three stages on a shared workspace (same kernels as
  * gptoss_moe_experts_forward; used for per-stage timing and by expert parallelism,
  * which exchanges rows between the stages). */
