@@ -9,11 +9,23 @@ import pytest
 import torch
 
 import oracle as O
-from helpers import assert_output_tolerance, build_layer
+from helpers import build_layer
 
 pytestmark = pytest.mark.gpu
 
 EPS = 1e-5
+
+
+def _assert_block_close(out, ref, what):
+    # the block adds the k expert rows into the residual one bf16 rounding at a time, the
+    # reference adds their bf16 sum once: equal up to a few bf16 ulps of the residual's size
+    o, r = out.float().cpu(), ref.float().cpu()
+    rms = r.pow(2).mean().sqrt().item()
+    rel = ((o - r).norm() / r.norm()).item()
+    ulp = torch.exp2(torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
+    worst = ((o - r).abs() - 4 * ulp).max().item()
+    assert rel <= 1e-2, f"{what}: rel-L2 {rel:.3e}"
+    assert worst <= 5e-2 * rms, f"{what}: {worst:.3e} beyond 4 bf16 ulps (rms {rms:.3e})"
 
 
 def _rms_ref(x, w):
@@ -56,10 +68,10 @@ def test_block_forward(pkg, dev, T):
     assert pkg.ops.read_status(dev) == 0
     assert torch.equal(idx, ix2) and torch.equal(scores, sc2), "routing"
     ref = (t.float() + moe.float()).to(torch.bfloat16)
-    assert_output_tolerance(out.cpu(), ref.cpu(), f"block vs norm + layer + add, T={T}")
+    _assert_block_close(out, ref, f"block vs norm + layer + add, T={T}")
     # and against the oracle on the block's routing
     o_ref = O.w4a8_experts_forward(xn.cpu(), idx.cpu().numpy(), scores.float().cpu().numpy(), O.numpy_weights(d))
-    assert_output_tolerance(out.cpu(), (t.cpu().float() + o_ref.float()).to(torch.bfloat16), f"oracle, T={T}")
+    _assert_block_close(out, (t.cpu().float() + o_ref.float()).to(torch.bfloat16), f"oracle, T={T}")
 
 
 def test_block_stack_in_a_cuda_graph(pkg, dev):
