@@ -94,5 +94,8 @@ def test_block_stack_in_a_cuda_graph(pkg, dev):
         graph.replay()
     torch.cuda.synchronize()
     assert pkg.ops.read_status(dev) == 0
-    # bf16 scatter-adds: the order of the k expert rows can differ between runs
-    assert ((out.float() - eager.float()).abs().max() / eager.float().abs().max()).item() < 2 ** -6
+    # bf16 scatter-adds: the order of the k expert rows can differ between runs, and an ulp of
+    # difference in layer 1's output can move a layer-2 FP8 code or a near-tie in its routing,
+    # so two layers agree to the output gate, not bit for bit (as two eager runs do)
+    rel = ((out.float() - eager.float()).norm() / eager.float().norm()).item()
+    assert rel <= 1e-2, f"graph replay vs eager: rel-L2 {rel:.3e}"
