@@ -1764,7 +1764,7 @@ bool ep_layer_fits(int64_t T, int k, int E, int world, int64_t H, int64_t I, int
   if (g_ep_layer_enabled.load(std::memory_order_relaxed) == 0) return false;
   if (world < 1 || world > kP2pMaxWorld || E % world != 0) return false;
   const int epr = E / world;
-  return cap <= kEpLayerMaxRowsPerExpert * epr && T >= 1 && T <= kDlMaxTokens && T * k <= kDlMaxAssign &&
+  return cap <= kEpLayerMaxRowsPerExpert * epr && T >= 0 && T <= kDlMaxTokens && T * k <= kDlMaxAssign &&
          epr <= kDlMaxExperts &&
          H % 32 == 0 && I % 32 == 0 && cap >= T * k && world * cap <= kEpMaxRecv &&
          static_cast<size_t>(T) * (2 * E + k) * sizeof(float) <= (DlCfg::kStages - kDlPreStages) * DlCfg::kStageBytes;
@@ -1803,9 +1803,12 @@ int gptoss_ep_p2p_layer_forward(const void* hidden, const void* router_weight, c
                "(gptoss_ep_p2p_layer_fits) or it is turned off",
                (long long)num_tokens, top_k, num_experts, world_size, (long long)capacity);
   const bool router = router_weight != nullptr;
-  GPTOSS_CHECK(hidden && out && local_base && peer_bases && send_counts && pos_of && workspace &&
-                   (router ? (router_bias && router_indices_out && routing_weights_out)
-                           : (router_indices && routing_weights)),
+  // a rank without tokens still takes part in the exchange (its peers wait for its flags)
+  GPTOSS_CHECK(local_base && peer_bases && send_counts && workspace &&
+                   (num_tokens == 0 ||
+                    (hidden && out && pos_of &&
+                     (router ? (router_bias && router_indices_out && routing_weights_out)
+                             : (router_indices && routing_weights)))),
                "ep_p2p_layer_forward: null pointer");
   GPTOSS_CHECK(aligned(hidden, 16) && aligned(out, 16) && aligned(local_base, 256) && aligned(workspace, 256) &&
                    (!router || aligned(router_weight, 16)),

@@ -163,10 +163,12 @@ class ExpertParallelExperts(nn.Module):
             self.exchange = None
 
     def _p2p_one_launch(self, h, cap: int) -> bool:
-        """Decode-sized steps run as one persistent launch (ops.ep_p2p_layer_forward)."""
+        """Decode-sized steps run as one persistent launch (ops.ep_p2p_layer_forward). The
+        choice depends only on the group's common sizes (capacity, not this rank's token
+        count), so every rank makes the same one."""
         x = self.experts
-        return _ops.ep_p2p_layer_fits(h.shape[0], self.top_k, self.num_experts, self.world_size, self.hidden_size,
-                                      x.intermediate_size, cap)
+        return _ops.ep_p2p_layer_fits(self.capacity_tokens, self.top_k, self.num_experts, self.world_size,
+                                      self.hidden_size, x.intermediate_size, cap)
 
     def _p2p_layer(self, h, router_weight, router_bias, idx, w, cap):
         ex, x = self.exchange, self.experts

@@ -937,11 +937,11 @@ def ep_p2p_layer_forward(hidden, router_weight, router_bias, router_indices, rou
         _dtype(routing_weights, (torch.float32,), "routing_weights")
         args = (None, None, router_indices.data_ptr(), routing_weights.data_ptr())
         outs = (None, None, None)
-    _lib.call("gptoss_ep_p2p_layer_forward", hidden.data_ptr(), *args, T, int(top_k), int(num_experts),
+    _lib.call("gptoss_ep_p2p_layer_forward", _p(hidden) if T else None, *args, T, int(top_k), int(num_experts),
               int(world_size), int(rank), H, I, gu_data.data_ptr(), gu_scales.data_ptr(), gu_scales.numel() // E_loc,
               gu_bias.data_ptr(), dn_data.data_ptr(), dn_scales.data_ptr(), dn_scales.numel() // E_loc,
               dn_bias.data_ptr(), float(alpha), float(limit), int(capacity), int(local_base), peer_bases.data_ptr(),
-              int(epoch), out.data_ptr(), *outs, send_counts.data_ptr(), pos_of.data_ptr(), workspace.data_ptr(),
+              int(epoch), _p(out) if T else None, *outs, send_counts.data_ptr(), pos_of.data_ptr(), workspace.data_ptr(),
               workspace.numel(), status_tensor(dev).data_ptr(), _stream(dev))
     return out, scores, router_indices, send_counts, pos_of
 
