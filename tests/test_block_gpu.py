@@ -98,4 +98,8 @@ def test_block_stack_in_a_cuda_graph(pkg, dev):
     # difference in layer 1's output can move a layer-2 FP8 code or a near-tie in its routing,
     # so two layers agree to the output gate, not bit for bit (as two eager runs do)
     rel = ((out.float() - eager.float()).norm() / eager.float().norm()).item()
-    assert rel <= 1e-2, f"graph replay vs eager: rel-L2 {rel:.3e}"
+    eager2 = fwd(x)
+    torch.cuda.synchronize()
+    rel_eager = ((eager2.float() - eager.float()).norm() / eager.float().norm()).item()
+    assert rel <= 1e-2, f"graph replay vs eager: rel-L2 {rel:.3e} (two eager runs: {rel_eager:.3e})"
+    assert rel <= max(4 * rel_eager, 1e-3), f"graph replay vs eager {rel:.3e}, two eager runs {rel_eager:.3e}"
