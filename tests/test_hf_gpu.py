@@ -123,3 +123,29 @@ def test_hf_model_with_cutlass_experts(pkg, dev):
     r2 = rel_l2(out2.cpu(), ref.cpu())
     print(f"fused router + experts: logits rel-L2 {r2:.2e} vs the oracle W4A8 model")
     assert r2 <= 0.15
+
+
+def test_hf_model_compiled_like_the_reference(pkg, dev):
+    # the reference's whole-model run (repro_compile_hftf.py:103-107): the GPT-OSS model with
+    # the swapped experts under torch.compile(backend="inductor", mode="reduce-overhead") --
+    # inductor traces the experts' custom ops through their fake kernels and replays the
+    # model as CUDA graphs. The compiled logits agree with the eager model's (both run this
+    # library's experts; they differ only by bf16 scatter-add order and what it moves
+    # downstream, as two eager runs do), and the experts' kernels ran.
+    ids = torch.randint(0, VOCAB, (2, 24), generator=torch.Generator().manual_seed(2)).to(dev)
+    model, ckpt = _model_and_checkpoint(dev)
+    assert pkg.hf.replace_experts_with_cutlass(model, ckpt.__getitem__) == LAYERS
+    with torch.no_grad():
+        eager = model(ids).logits.float()
+        eager2 = model(ids).logits.float()
+        compiled = torch.compile(model, backend="inductor", mode="reduce-overhead")
+        n0 = pkg._lib.query("gptoss_kernel_launch_count")
+        for _ in range(3):                        # warm-up, recording, replays
+            out = compiled(ids).logits.float().clone()
+        n1 = pkg._lib.query("gptoss_kernel_launch_count")
+    torch.cuda.synchronize()
+    assert pkg.ops.read_status(dev) == 0
+    assert n1 > n0, "the compiled model launched none of this library's kernels"
+    r, r_eager = rel_l2(out.cpu(), eager.cpu()), rel_l2(eager2.cpu(), eager.cpu())
+    print(f"compiled vs eager logits: rel-L2 {r:.2e} (two eager runs: {r_eager:.2e})")
+    assert r <= max(0.05, 4 * r_eager)
