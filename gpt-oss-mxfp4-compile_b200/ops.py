@@ -17,6 +17,7 @@ Registered ops (all with register_fake, static output shapes, no host sync unles
 from __future__ import annotations
 
 import ctypes
+import contextlib
 import threading
 
 import torch
@@ -48,8 +49,25 @@ _ws_retired = []
 _ws_bytes = {}
 
 
+_tls = threading.local()
+
+
+@contextlib.contextmanager
+def _fresh_workspace():
+    """Calls through the registered torch ops (traced and compiled code) take a fresh
+    workspace from the caching allocator instead of the per-stream cache: under
+    torch.compile(mode="reduce-overhead") the compiled model runs in CUDA-graph memory pools,
+    and a workspace cached from such a run would keep that pool's memory alive."""
+    prev = getattr(_tls, "fresh", False)
+    _tls.fresh = True
+    try:
+        yield
+    finally:
+        _tls.fresh = prev
+
+
 def _scratch(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
-    if torch.cuda.is_current_stream_capturing():
+    if torch.cuda.is_current_stream_capturing() or getattr(_tls, "fresh", False):
         return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     key = (dev.index, stream)
     t = _ws_cache.get(key)
@@ -502,8 +520,9 @@ def register_ops() -> None:
                                 gate_up_data: torch.Tensor, gate_up_scales: torch.Tensor, gate_up_bias: torch.Tensor,
                                 down_data: torch.Tensor, down_scales: torch.Tensor, down_bias: torch.Tensor,
                                 alpha: float, limit: float, gemm_mode: int) -> torch.Tensor:
-            return moe_experts_forward_impl(hidden, router_indices, routing_weights, gate_up_data, gate_up_scales,
-                                            gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode)
+            with _fresh_workspace():
+                return moe_experts_forward_impl(hidden, router_indices, routing_weights, gate_up_data, gate_up_scales,
+                                                gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode)
 
         @moe_experts_forward.register_fake
         def _(hidden, router_indices, routing_weights, gate_up_data, gate_up_scales, gate_up_bias, down_data,
@@ -516,8 +535,9 @@ def register_ops() -> None:
                               gate_up_bias: torch.Tensor, down_data: torch.Tensor, down_scales: torch.Tensor,
                               down_bias: torch.Tensor, alpha: float, limit: float, gemm_mode: int
                               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-            return moe_layer_forward_impl(hidden, router_weight, router_bias, top_k, gate_up_data, gate_up_scales,
-                                          gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode)
+            with _fresh_workspace():
+                return moe_layer_forward_impl(hidden, router_weight, router_bias, top_k, gate_up_data, gate_up_scales,
+                                              gate_up_bias, down_data, down_scales, down_bias, alpha, limit, gemm_mode)
 
         @moe_layer_forward.register_fake
         def _(hidden, router_weight, router_bias, top_k, gate_up_data, gate_up_scales, gate_up_bias, down_data,
@@ -533,9 +553,10 @@ def register_ops() -> None:
                               down_data: torch.Tensor, down_scales: torch.Tensor, down_bias: torch.Tensor,
                               alpha: float, limit: float, gemm_mode: int
                               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-            return moe_block_forward_impl(hidden, norm_weight, norm_eps, router_weight, router_bias, top_k,
-                                          gate_up_data, gate_up_scales, gate_up_bias, down_data, down_scales,
-                                          down_bias, alpha, limit, gemm_mode)
+            with _fresh_workspace():
+                return moe_block_forward_impl(hidden, norm_weight, norm_eps, router_weight, router_bias, top_k,
+                                              gate_up_data, gate_up_scales, gate_up_bias, down_data, down_scales,
+                                              down_bias, alpha, limit, gemm_mode)
 
         @moe_block_forward.register_fake
         def _(hidden, norm_weight, norm_eps, router_weight, router_bias, top_k, gate_up_data, gate_up_scales,
