@@ -44,8 +44,8 @@ def test_ops_registered_with_reference_qualnames(pkg):
     pkg.ensure_custom_op_registered()   # idempotent
     assert hasattr(torch.ops.cutlass, "fp4_group_mm")
     assert hasattr(torch.ops.cutlass, "fused_moe_routing")
-    for n in ("moe_experts_forward", "moe_layer_forward", "quantize_fp8", "swiglu", "router_topk",
-              "route_quant", "gemm1", "gemm2", "ep_dispatch", "ep_expert_forward", "ep_combine"):
+    for n in ("moe_experts_forward", "moe_layer_forward", "moe_block_forward", "quantize_fp8", "swiglu",
+              "router_topk", "route_quant", "gemm1", "gemm2", "ep_dispatch", "ep_expert_forward", "ep_combine"):
         assert hasattr(torch.ops.gptoss, n)
 
 
@@ -80,6 +80,34 @@ def test_fake_kernels_give_static_shapes(pkg):
     assert back.shape == (28, 512) and back.dtype == torch.bfloat16
     out = torch.ops.gptoss.ep_combine(back, pos, idx)
     assert out.shape == (7, 512) and out.dtype == torch.bfloat16
+    # the decoder block op: out, scores, indices
+    o, sc, ix = torch.ops.gptoss.moe_block_forward(
+        h, torch.empty(512, dtype=torch.bfloat16, device=meta), 1e-5, torch.empty(4, 512, dtype=torch.bfloat16, device=meta),
+        torch.empty(4, dtype=torch.bfloat16, device=meta), 2, torch.empty(4, 512, 256, dtype=torch.uint8, device=meta),
+        torch.empty(4, 16384, dtype=torch.uint8, device=meta), torch.empty(4, 512, device=meta),
+        torch.empty(4, 512, 128, dtype=torch.uint8, device=meta), torch.empty(4, 8192, dtype=torch.uint8, device=meta),
+        torch.empty(4, 512, device=meta), 1.702, 7.0, 0)
+    assert o.shape == (7, 512) and sc.shape == (7, 2) and ix.shape == (7, 2) and ix.dtype == torch.int64
+
+
+def test_one_launch_expert_parallel_gate(pkg):
+    # when a decode-sized expert-parallel step runs as one launch per rank (a pure function of
+    # the group's common sizes, so every rank decides alike): tokens, received rows, rows per
+    # local expert, capacity; and the process-wide switch
+    fits = pkg.ops.ep_p2p_layer_fits
+    assert fits(32, 4, 32, 8, 2880, 2880, 128) and fits(32, 4, 32, 2, 2880, 2880, 128)
+    assert fits(0, 4, 32, 2, 2880, 2880, 128)                  # a rank without tokens takes part
+    assert not fits(65, 4, 32, 1, 2880, 2880, 260)             # > 64 tokens
+    assert not fits(32, 4, 32, 8, 2880, 2880, 160)             # 8 x 160 > 1024 received rows
+    assert not fits(32, 4, 32, 2, 2880, 2880, 100)             # capacity < T x k
+    assert fits(64, 4, 8, 2, 512, 512, 256)                    # 64 rows per local expert
+    assert not fits(64, 4, 8, 2, 512, 512, 272)                # 68
+    assert not fits(32, 4, 30, 4, 2880, 2880, 128)             # E not a multiple of W
+    prev = pkg.ops.set_ep_layer_kernel(False)
+    try:
+        assert not fits(32, 4, 32, 8, 2880, 2880, 128)
+    finally:
+        pkg.ops.set_ep_layer_kernel(prev)
 
 
 def test_cpu_tensors_are_refused(pkg):

@@ -76,18 +76,3 @@ def test_one_launch_matches_five_launch_path(pkg, dev, T, E, H, I, router):
     finally:
         torch.cuda.synchronize()
         pkg.ops.ipc_free(base)
-
-
-def test_fits_gate(pkg):
-    # the one-launch kernel's limits: tokens, received rows, rows per local expert
-    assert pkg.ops.ep_p2p_layer_fits(32, 4, 32, 8, 2880, 2880, 128)
-    assert not pkg.ops.ep_p2p_layer_fits(65, 4, 32, 1, 2880, 2880, 260)        # > 64 tokens
-    assert not pkg.ops.ep_p2p_layer_fits(32, 4, 32, 8, 2880, 2880, 160)        # 8 x 160 > 1024 rows
-    assert not pkg.ops.ep_p2p_layer_fits(32, 4, 32, 2, 2880, 2880, 100)        # capacity < T x k
-    assert pkg.ops.ep_p2p_layer_fits(64, 4, 8, 2, 512, 512, 256)               # 64 rows per local expert
-    assert not pkg.ops.ep_p2p_layer_fits(64, 4, 8, 2, 512, 512, 272)           # 68 rows per local expert
-    prev = pkg.ops.set_ep_layer_kernel(False)
-    try:
-        assert not pkg.ops.ep_p2p_layer_fits(32, 4, 32, 8, 2880, 2880, 128)
-    finally:
-        pkg.ops.set_ep_layer_kernel(prev)
