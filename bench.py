@@ -496,6 +496,11 @@ def run_ours(args):
                 moved = (world - 1) * cap * (rb + 2 * H)
             ep_info = {"layout": "fixed capacity", "transport": epx.transport, "capacity_rows_per_peer": cap,
                        "rank0_rows_used": sent, "rank0_nvlink_bytes_per_step": moved, "host_syncs_per_step": 0}
+            if epx.transport == "p2p":
+                ep_info["kernels"] = ("one persistent launch per rank and step (decode_layer_kernel<true>) behind a "
+                                      "one-CTA reset" if epx._p2p_one_launch(x, cap) else
+                                      "five launches per step (route-dispatch, receive, GEMM1, GEMM2 + return, "
+                                      "combine)")
         else:
             s_send, s_recv = epx.last_splits
             ep_info = {"layout": "exact splits", "transport": "nccl", "rank0_rows_sent": s_send,
