@@ -17,7 +17,7 @@ __all__ = [
     "e4m3_encode", "e4m3_decode", "quantize_fp8_ue8m0",
     "blocked_sf_offset", "blocked_sf_cosize", "convert_scales_blocked", "batch_convert_a_scales",
     "unblock_scales", "nvfp4_dequant", "nvfp4_group_mm",
-    "route_stable", "router_topk_hf", "router_logits_fp32", "router_logits_exact", "router_topk_from_logits",
+    "route_stable", "router_topk_hf", "rmsnorm_hf", "router_logits_fp32", "router_logits_exact", "router_topk_from_logits",
     "round_bf16_exact",
     "mxfp4_dequant", "fp8_dequant", "group_mm_bf16", "swiglu_fp32",
     "w4a8_experts_forward", "dequant_fp32_reference", "synth_layer", "synth_router_bias",
@@ -201,6 +201,15 @@ def nvfp4_group_mm(a, b, a_sf_blocked, b_sf_blocked, alphas, counts, offsets, sf
 
 
 # --------------------------------------------------------------------------- routing
+def rmsnorm_hf(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """GptOssRMSNorm.forward (transformers models/gpt_oss/modeling_gpt_oss.py), the norm in front
+    of every MoE block of the model the reference runs: fp32 mean of squares, rsqrt(mean + eps),
+    the weight times the normalised fp32 row, one rounding to the input dtype."""
+    xf = x.to(torch.float32)
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return (weight * (xf * torch.rsqrt(var + eps))).to(x.dtype)
+
+
 def route_stable(router_indices, routing_weights, num_experts: int):
     """Stable counting sort of the (token, k) assignments by expert
     (benchmark_optimizations.py:170-187). Returns numpy arrays

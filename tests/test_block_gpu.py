@@ -1,10 +1,10 @@
 """The decoder block around the MoE layer (gptoss_moe_block_forward): out = hidden +
 layer(RMSNorm(hidden)) with the norm and the residual copy in one kernel and GEMM2 adding into
-the residual rows. The norm is checked against a plain PyTorch fp32 restatement of
-GptOssRMSNorm (within one bf16 ulp: the sum of squares runs in a different order and rsqrt is
-the hardware's); the block against the same layer on torch's RMSNorm plus a separate add, and
-against the oracle, within the north-star output gate; a CUDA graph of two blocks replays the
-eager result."""
+the residual rows. The norm is checked against the oracle's GptOssRMSNorm restatement (fp32 on
+the CPU, pinned to the transformers module; within one bf16 ulp: the sum of squares runs in a
+different order and rsqrt is the hardware's); the block against the same layer on the same
+normalised rows plus a separate add, and against the oracle's experts, within a few bf16 ulps
+of the residual; a CUDA graph of two blocks replays each block's eager result."""
 import pytest
 import torch
 
@@ -29,9 +29,8 @@ def _assert_block_close(out, ref, what):
 
 
 def _rms_ref(x, w):
-    xf = x.float()
-    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + EPS)
-    return (w.float() * (xf * r)).to(torch.bfloat16)
+    # the oracle's GptOssRMSNorm restatement (pinned to the transformers module on the CPU)
+    return O.rmsnorm_hf(x.cpu(), w.cpu(), EPS).to(x.device)
 
 
 @pytest.mark.parametrize("T,H", [(1, 2880), (37, 512), (4096, 2880)])

@@ -177,3 +177,18 @@ def test_router_logits_exact_matches_fp32_router_almost_everywhere():
     # crosses a bf16 rounding boundary (a handful of the 1024 logits at most)
     assert (ex != f32).sum().item() <= 8
     assert ((ex.float() - f32.float()).abs() <= ex.float().abs() * 2 ** -7 + 1e-30).all()
+
+
+def test_rmsnorm_restatement_matches_hf_module():
+    # the block op's norm is held to this restatement on the GPU; here it is pinned to the
+    # transformers module the reference's model runs (bf16 model, weight in bf16)
+    from transformers.models.gpt_oss.modeling_gpt_oss import GptOssRMSNorm
+    g = torch.Generator().manual_seed(4)
+    for H in (64, 2880):
+        norm = GptOssRMSNorm(H, eps=1e-5).to(torch.bfloat16)
+        with torch.no_grad():
+            norm.weight.copy_((1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16))
+        x = (3 * torch.randn(17, H, generator=g)).to(torch.bfloat16)
+        with torch.no_grad():
+            ref = norm(x)
+        assert torch.equal(O.rmsnorm_hf(x, norm.weight.data, 1e-5), ref)
