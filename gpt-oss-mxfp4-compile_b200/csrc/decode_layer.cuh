@@ -37,6 +37,13 @@
 //
 // Semantics are those of the three-launch path (cutlass_experts.py:376-452 with the router
 // of GptOssTopKRouter in front); the router logits are the exactly rounded F.linear value.
+// With `out_prefilled` the kernel adds into `out` as it is (the residual rows of a decoder
+// block, gptoss_moe_block_forward) instead of zeroing it first.
+//
+// decode_layer_kernel<true> is the same kernel as one rank of an expert-parallel layer: the
+// sort, quantisation and combine phases become dispatch / receive / combine over NVLink peer
+// memory (see the comment at the kernel), the GEMMs run the rank's local experts on the rows
+// it received, and GEMM2 stores into the sources' return rows.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
