@@ -75,8 +75,9 @@ uint64_t gptoss_kernel_launch_count(void);
 int gptoss_set_decode_layer_kernel(int enable);
 
 /* Copies the 4-byte device status word that kernels set when a bounded wait times out
- * or an expert index is out of range (0 = ok) into *status_host and clears it.
- * Synchronises `stream`. */
+ * (0x101-0x104 GEMM roles, 0x106-0x108 the one-launch kernels, 0x301 a peer's flag), an
+ * expert index is out of range (0x201) or an expert's scale offset is not 16-byte aligned
+ * (0x109) -- 0 = ok -- into *status_host and clears it. Synchronises `stream`. */
 int gptoss_read_status(int32_t* status_dev, int32_t* status_host, void* stream);
 
 /* Replaces fused_moe_routing (kernels/matmul_mxfp4_cutlass.cu:1041-1095, registered as
