@@ -90,7 +90,7 @@ _SIGNATURES = {
                               _i, _vp, _vp]),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lock = threading.Lock()
 _lib = None

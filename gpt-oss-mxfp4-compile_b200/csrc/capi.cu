@@ -727,7 +727,7 @@ extern "C" {
 
 const char* gptoss_last_error(void) { return g_last_error.c_str(); }
 
-int gptoss_abi_version(void) { return 1; }
+int gptoss_abi_version(void) { return 2; }
 
 int gptoss_set_decode_layer_kernel(int enable) {
   return g_decode_layer_enabled.exchange(enable != 0 ? 1 : 0, std::memory_order_relaxed);

@@ -33,7 +33,7 @@ enum {
   GPTOSS_OK = 0,
   GPTOSS_ERR_INVALID_ARGUMENT = 1, /* bad shape / dtype / alignment (TORCH_CHECK in the reference) */
   GPTOSS_ERR_CUDA = 2,             /* a CUDA runtime or driver call failed */
-  GPTOSS_ERR_NOT_IMPLEMENTED = 3,  /* e.g. the W4A4 (NVFP4) mode of fp4_group_mm */
+  GPTOSS_ERR_NOT_IMPLEMENTED = 3,  /* a mode this build does not provide */
   GPTOSS_ERR_UNSUPPORTED_DEVICE = 4, /* not a compute-capability 10.x GPU */
   GPTOSS_ERR_WORKSPACE = 5         /* workspace smaller than gptoss_*_workspace_bytes() */
 };
@@ -57,7 +57,7 @@ int gptoss_moe_gemm_layout(int gemm_mode, int64_t rows, int num_experts);
 /* Message for the last failing call on this thread ("" if none). */
 const char* gptoss_last_error(void);
 
-/* ABI version of this header (bumped on any signature change). */
+/* ABI version of this header (bumped on any signature change; 2: gptoss_mma_peak takes a kind). */
 int gptoss_abi_version(void);
 
 /* Kernels this library has launched in this process, on every device (launch accounting

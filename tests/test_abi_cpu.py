@@ -94,7 +94,7 @@ def test_c_program_links_and_calls_host_queries(pkg, tmp_path):
 #include <stdio.h>
 #include "gptoss_moe.h"
 int main(void) {
-  if (gptoss_abi_version() != 1) return 1;
+  if (gptoss_abi_version() != 2) return 1;
   size_t ws = gptoss_moe_workspace_bytes(32, 4, 32, 2880, 2880);
   long long rb = (long long)gptoss_ep_row_bytes(2880);
   printf("%zu %lld\n", ws, rb);
