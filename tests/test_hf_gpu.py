@@ -129,11 +129,19 @@ def test_hf_model_compiled_like_the_reference(pkg, dev):
     # the reference's whole-model run (repro_compile_hftf.py:103-107): the GPT-OSS model with
     # the swapped experts under torch.compile(backend="inductor", mode="reduce-overhead") --
     # inductor traces the experts' custom ops through their fake kernels and replays the
-    # model as CUDA graphs. The compiled logits agree with the eager model's (both run this
-    # library's experts; they differ only by bf16 scatter-add order and what it moves
-    # downstream, as two eager runs do), and the experts' kernels ran.
+    # model as CUDA graphs, and the experts' kernels run. Inductor's own kernels for the rest of
+    # the model (norms, attention, the router) round differently from eager torch, and this
+    # small random model amplifies every rounding (compiled vs eager measured 0.08-0.09 rel-L2,
+    # two eager runs 0.02-0.05), so the logits are held to the whole-model bounds of the eager
+    # tests: within the eager bound of the eager model, and within the bf16 sanity bound of
+    # the oracle-experts model. A broken compiled path lands near 1.
     ids = torch.randint(0, VOCAB, (2, 24), generator=torch.Generator().manual_seed(2)).to(dev)
     model, ckpt = _model_and_checkpoint(dev)
+    with torch.no_grad():
+        for i in range(LAYERS):
+            model.model.layers[i].mlp.experts = OracleExperts(ckpt, f"model.layers.{i}.mlp.experts")
+        ref = model(ids).logits.float()
+    model, _ = _model_and_checkpoint(dev)
     assert pkg.hf.replace_experts_with_cutlass(model, ckpt.__getitem__) == LAYERS
     with torch.no_grad():
         eager = model(ids).logits.float()
@@ -146,6 +154,8 @@ def test_hf_model_compiled_like_the_reference(pkg, dev):
     torch.cuda.synchronize()
     assert pkg.ops.read_status(dev) == 0
     assert n1 > n0, "the compiled model launched none of this library's kernels"
-    r, r_eager = rel_l2(out.cpu(), eager.cpu()), rel_l2(eager2.cpu(), eager.cpu())
-    print(f"compiled vs eager logits: rel-L2 {r:.2e} (two eager runs: {r_eager:.2e})")
-    assert r <= max(0.05, 4 * r_eager)
+    r_ref, r_eager = rel_l2(out.cpu(), ref.cpu()), rel_l2(eager.cpu(), ref.cpu())
+    r_ce, r_ee = rel_l2(out.cpu(), eager.cpu()), rel_l2(eager2.cpu(), eager.cpu())
+    print(f"logits rel-L2 vs the oracle W4A8 model: compiled {r_ref:.2e}, eager {r_eager:.2e}; "
+          f"compiled vs eager {r_ce:.2e}, two eager runs {r_ee:.2e}")
+    assert r_ce <= 0.15 and r_ref <= 0.25
