@@ -62,6 +62,42 @@ def test_argument_errors_before_device_access(pkg):
     assert rc == 1 and b"top_k" in lib.gptoss_last_error()
 
 
+def test_later_entry_points_check_arguments_first(pkg):
+    # the MMA probe, the W4A4 grouped GEMM, the norm kernel, the block op and the one-launch
+    # expert-parallel step validate their sizes on the host and fail with a message
+    lib = pkg._lib.load()
+
+    def fails(rc, text):
+        assert rc == 1 and text in lib.gptoss_last_error(), lib.gptoss_last_error()
+
+    fails(lib.gptoss_mma_peak(2, 1, 256, 10, None, None), b"kind must be")
+    fails(lib.gptoss_mma_peak(0, 1, 200, 10, None, None), b"multiple of 16")
+    fails(lib.gptoss_mma_peak(1, 0, 128, 0, None, None), b"iters")
+    fails(lib.gptoss_fp4_group_mm_w4a4(None, None, 4, 50, None, 1, 256, 100, None, None, 0, None, None, None, None, 0,
+                                       None, None), b"multiple of 64")
+    fails(lib.gptoss_fp4_group_mm_w4a4(None, None, 4, 64, None, 1, 100, 128, None, None, 0, None, None, None, None, 0,
+                                       None, None), b"multiple of 8")
+    fails(lib.gptoss_fp4_group_mm_w4a4(None, None, 4, 128, None, 1, 256, 128, None, None, 0, None, None, None, None, 0,
+                                       None, None), b"[M, K/2]")
+    fails(lib.gptoss_rmsnorm_residual(None, None, 1e-5, 4, 2884, None, None, None), b"multiple of 8")
+    fails(lib.gptoss_rmsnorm_residual(None, None, 1e-5, -1, 2880, None, None, None), b"num_tokens")
+    assert lib.gptoss_rmsnorm_residual(None, None, 1e-5, 0, 2880, None, None, None) == 0   # nothing to do
+    fails(lib.gptoss_moe_block_forward(None, None, 1e-5, None, None, 4, 9, 4, 512, 256, None, None, 0, None, None,
+                                       None, 0, None, 1.702, 7.0, None, None, None, None, 0, 0, None, None),
+          b"top_k")
+    fails(lib.gptoss_ep_p2p_layer_forward(None, None, None, None, None, 4, 4, 32, 3, 0, 512, 256, None, None, 0, None,
+                                          None, None, 0, None, 1.702, 7.0, 16, None, None, 1, None, None, None, None,
+                                          None, None, None, 0, None, None), b"multiple of world_size")
+    fails(lib.gptoss_ep_p2p_layer_forward(None, None, None, None, None, 4, 4, 32, 2, 2, 512, 256, None, None, 0, None,
+                                          None, None, 0, None, 1.702, 7.0, 16, None, None, 1, None, None, None, None,
+                                          None, None, None, 0, None, None), b"world_size / rank")
+    # host-only size answers
+    q = pkg._lib.query
+    e = q("gptoss_moe_workspace_bytes", 32, 4, 32, 2880, 2880)
+    assert q("gptoss_moe_block_workspace_bytes", 32, 4, 32, 2880, 2880) >= e + 32 * 2880 * 2
+    assert q("gptoss_moe_block_workspace_bytes", -1, 4, 32, 2880, 2880) == 0
+
+
 def test_wrapper_raises_on_failure(pkg):
     with pytest.raises(pkg._lib.GptossError, match="multiple of 32"):
         pkg._lib.call("gptoss_quantize_fp8", None, 0, 4, 31, None, None, None)
