@@ -1,7 +1,8 @@
 """Expert parallelism without a GPU: the oracle's EP restatement and the host logic of
 ExpertParallelExperts (count exchange, split bookkeeping, all-to-alls in both directions,
-return positions) on world_size-2 gloo ranks."""
+return positions) on gloo ranks, world sizes 2 and 4."""
 import numpy as np
+import pytest
 import torch
 
 import oracle as O
@@ -66,6 +67,28 @@ def test_gloo_two_ranks_match_single_device_oracle():
         assert s0[0][1] == s1[1][0] and s1[0][0] == s0[1][1]
 
 
+def test_gloo_four_ranks_match_single_device_oracle():
+    # the same host logic with four ranks (two experts each): every rank's output equals the
+    # single-device oracle in both layouts, and the split bookkeeping is consistent across
+    # every pair -- what rank r sends to q is what q receives from r
+    world = 4
+    res = run_ranks(cpu_worker, world, ["random", "rank0", "empty"])
+    for rank, (out, err) in enumerate(res):
+        assert err is None, f"rank {rank}: {err}"
+        for case, shape, eq, _ in out:
+            assert eq, f"rank {rank} case {case}: output differs from the oracle"
+    for ci, case in enumerate(("random", "rank0", "empty")):
+        sends = [res[r][0][ci][3][0] for r in range(world)]
+        recvs = [res[r][0][ci][3][1] for r in range(world)]
+        for r in range(world):
+            for q in range(world):
+                assert sends[r][q] == recvs[q][r], f"{case}: rank {r} -> {q}"
+        if case == "rank0":   # rank 0 owns the only two unpenalised experts: every token's top two
+            assert all(sends[r][0] == 2 * 16 for r in range(world))
+        if case == "empty":   # rank 1 holds no tokens and sends nothing
+            assert sum(sends[1]) == 0 and res[1][0][ci][1] == (0, H)
+
+
 def test_oracle_capacity_layout():
     # fixed-capacity segments: same rows as the compact layout, moved to q*cap, the rest
     # marked empty; the chain through them still equals the single-device forward.
@@ -99,11 +122,12 @@ def test_dead_peer_ends_with_an_error_not_a_hang():
     assert elapsed < 60, r0
 
 
-def test_gloo_two_ranks_router_and_experts_match_single_device():
-    # ExpertParallelMoELayer end to end on two gloo ranks: each rank routes its own tokens
-    # (the CPU router stands in for the fused router op) and gets the single-device routing
-    # and the single-device oracle output
-    res = run_ranks(cpu_layer_worker, 2)
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_router_and_experts_match_single_device(world):
+    # ExpertParallelMoELayer end to end on gloo ranks: each rank routes its own tokens (the
+    # CPU router stands in for the fused router op) and gets the single-device routing and
+    # the single-device oracle output
+    res = run_ranks(cpu_layer_worker, world)
     for rank, (out, err) in enumerate(res):
         assert err is None, f"rank {rank}: {err}"
         same_routing, same_out = out
