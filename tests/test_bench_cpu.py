@@ -39,3 +39,15 @@ def test_configs_cover_the_baseline_configs():
     assert set(bench.CONFIGS) == {"decode", "prefill", "stack", "zipf"}
     T, E, H, I, k, _, _ = bench.CONFIGS["decode"]
     assert (T, E, H, I, k) == (32, 32, 2880, 2880, 4)
+
+
+def test_algorithmic_bytes_follow_the_per_unit_figures():
+    # one touched expert costs 13,253,760 B per layer step (unpadded K: gate_up 8,294,400 +
+    # scales 518,400 + fp32 bias 23,040; down 4,147,200 + 259,200 + 11,520); the router weight
+    # and bias scale with E; the decode config moves 425,813,824 B per step, 32 experts touched
+    sys.path.insert(0, REPO)
+    import bench
+    _, _, full, touched = bench.alg_bytes([1] * 32, 32, 4, 2880, 2880, 32)
+    assert touched == 32 and full == 425_813_824
+    assert full - bench.alg_bytes([1] * 31 + [0], 32, 4, 2880, 2880, 32)[2] == 13_253_760
+    assert bench.alg_bytes([1] * 32 + [0] * 96, 32, 4, 2880, 2880, 128)[2] - full == 96 * (2880 * 2 + 2)
