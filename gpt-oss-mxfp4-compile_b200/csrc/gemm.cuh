@@ -776,8 +776,11 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
 #pragma unroll
                 for (int j = 0; j < 4; ++j) o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
               } else {
-                for (int j = 0; j < 32 && nb + j < p.N; ++j)
-                  o[j] = __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
+                // unrolled with a predicate: a runtime loop bound would index r[] dynamically
+                // and put the whole array in local memory for every tile
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (nb + j < p.N) o[j] = __float2bfloat16_rn(__fmul_rn(alpha, __uint_as_float(r[j])));
               }
             } else {  // kEpiGemm2
               float bsv[32];
@@ -798,12 +801,15 @@ __global__ void __launch_bounds__(GemmConfig<SWAP, SPREAD, PAIR, NVF4>::kThreads
                                "r"(pk[4 * j]), "r"(pk[4 * j + 1]), "r"(pk[4 * j + 2]), "r"(pk[4 * j + 3])
                                : "memory");
               } else {
-                for (int j = 0; j < 16 && nb + 2 * j < p.N; ++j) {
-                  const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
-                  if (nb + 2 * j + 1 < p.N) {
-                    atomicAdd(reinterpret_cast<__nv_bfloat162*>(o + 2 * j), v2);
-                  } else {
-                    atomicAdd(o + 2 * j, v2.x);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {   // unrolled with a predicate, as above (pk[])
+                  if (nb + 2 * j < p.N) {
+                    const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[j]);
+                    if (nb + 2 * j + 1 < p.N) {
+                      atomicAdd(reinterpret_cast<__nv_bfloat162*>(o + 2 * j), v2);
+                    } else {
+                      atomicAdd(o + 2 * j, v2.x);
+                    }
                   }
                 }
               }
